@@ -1,0 +1,158 @@
+/* gpt2q — B200 (sm_100a) GPT-2 forward over group-quantized weights.
+ *
+ * C-ABI boundary of the smelt_b200 library (libgpt2q.so). It replaces the CUDA
+ * executor of LukasParke/smelt's model-lab (experiments/model-lab/src/gpu.rs,
+ * kernels in src/cu/gpt2.cu) and keeps the shape of its Rust API so a thin FFI
+ * crate restores `Gpu::new / step / clear_kv`. Citations below are paths inside
+ * that project.
+ *
+ * Conventions
+ *  - Every call returns an int status: GPT2Q_OK (0) or a negative GPT2Q_E* code.
+ *    Nothing aborts or panics; gpt2q_last_error() gives the message.
+ *  - One handle per GPU. A handle is not thread-safe; distinct handles may be
+ *    driven from distinct threads.
+ *  - Host buffers are caller-owned; gpt2q_create copies every tensor, so the
+ *    caller keeps ownership (gpu.rs:114-127 copies too).
+ *  - Weight payloads use the SMT TENSORS layout (model-lab/src/bin/pack.rs:68-94):
+ *      "core.i8.b32.f16scale"  [rows][cols/32] blocks of 34 B: f16 scale LE + 32 x int8
+ *      "core.i4.b32.f16scale"  [rows][cols/32] blocks of 18 B: f16 scale LE + 16 B, byte j =
+ *                              elem j (low nibble) | elem j+16 (high nibble), two's complement
+ *      "core.f16"              IEEE half, little endian
+ *      "core.f32"              IEEE float (fp32 weights)
+ *    2-D weights are [out, in] (pack.rs transposes HF Conv1D at convert time).
+ *  - Tensor names follow the HF GPT-2 names used by the pack: wte.weight,
+ *    wpe.weight, ln_f.{weight,bias}, h.{L}.ln_1/ln_2.{weight,bias},
+ *    h.{L}.attn.c_attn/c_proj.{weight,bias}, h.{L}.mlp.c_fc/c_proj.{weight,bias}.
+ *  - Greedy argmax follows gpt2.rs:390-396: IEEE total order, ties -> LAST index.
+ */
+#ifndef GPT2Q_H
+#define GPT2Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GPT2Q_OK 0
+#define GPT2Q_EARG -1      /* bad argument / shape / name */
+#define GPT2Q_EOOM -2      /* device allocation failed */
+#define GPT2Q_ECUDA -3     /* CUDA runtime error */
+#define GPT2Q_ENCCL -4     /* NCCL error (tensor-parallel handles) */
+#define GPT2Q_ETIMEOUT -5  /* a bounded device-side wait gave up */
+#define GPT2Q_EUNSUP -6    /* unsupported configuration */
+
+typedef struct gpt2q_handle gpt2q_handle;
+
+/* Model architecture (gpt2.rs:11-19 Meta) plus capacity of this handle. */
+typedef struct gpt2q_config {
+    int32_t n_embd;
+    int32_t n_layer;
+    int32_t n_head;
+    int32_t n_ctx;
+    int32_t vocab;
+    float ln_eps;
+    int32_t max_seqs;   /* KV-cache slots (sequences resident at once); >= 1 */
+    int32_t max_tokens; /* tokens per prefill chunk (activation workspace); 0 = default */
+} gpt2q_config;
+
+/* One tensor record of the SMT TENSORS section (format.rs:17-28 TensorRecord). */
+typedef struct gpt2q_tensor_desc {
+    const char* name;
+    const char* atom;
+    int32_t ndim;
+    int64_t shape[2];
+    const void* data; /* host pointer to the payload */
+    uint64_t len;     /* payload bytes */
+} gpt2q_tensor_desc;
+
+/* Replaces Gpu::new(&Engine) (gpu.rs:75-157): uploads every tensor (quantized
+ * ones stay quantized in HBM), allocates the KV arena for cfg->max_seqs
+ * sequences of n_ctx positions and the activation workspace. */
+int gpt2q_create(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int n_tensors,
+                 int device, gpt2q_handle** out);
+
+/* Tensor-parallel handle (no counterpart in the reference, which is single-GPU,
+ * gpu.rs:76): rank `tp_rank` of `tp_size` keeps its column slice of c_attn
+ * (whole heads) and c_fc and its row slice of attn/mlp c_proj; the two c_proj
+ * outputs per layer are summed with an NCCL all-reduce. nccl_id points to the
+ * 128-byte ncclUniqueId made by rank 0 and shared by the caller. */
+int gpt2q_create_tp(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int n_tensors,
+                    int device, int tp_size, int tp_rank, const void* nccl_id,
+                    gpt2q_handle** out);
+
+/* Frees everything; replaces the Drop of Gpu. Safe on NULL. */
+void gpt2q_destroy(gpt2q_handle* h);
+
+/* Last error message of this handle (or of the last failed create when h is NULL). */
+const char* gpt2q_last_error(const gpt2q_handle* h);
+
+/* Replaces Gpu::clear_kv (gpu.rs:203-209). slots == NULL clears every slot. */
+int gpt2q_reset_kv(gpt2q_handle* h, const int32_t* slots, int n_slots);
+
+/* Exactly Gpu::step (gpu.rs:212-379): batch 1, KV slot 0, token `tok` at
+ * position `pos`; writes vocab fp32 logits to host `logits`. */
+int gpt2q_step(gpt2q_handle* h, uint32_t tok, int32_t pos, float* logits);
+
+/* Batched decode: one token per sequence. Sequence i feeds tok[i] at pos[i]
+ * into KV slot slots[i] (slots == NULL: slot i), attends over positions
+ * 0..pos[i] of that slot. Optional outputs (host, may be NULL): logits
+ * [n_seq][vocab], next_tok [n_seq] (greedy argmax). Engine::step batched over
+ * sequences (gpt2.rs:227-332). */
+int gpt2q_decode(gpt2q_handle* h, const uint32_t* tok, const int32_t* pos, const int32_t* slots,
+                 int n_seq, float* logits, uint32_t* next_tok);
+
+/* Prefill whole prompts starting at position 0. Sequence i owns tokens
+ * [seq_offsets[i], seq_offsets[i+1]) and KV slot slots[i] (NULL: slot i).
+ * Optional host outputs: logits_last [n_seq][vocab] at each prompt's last
+ * position, next_tok [n_seq]. Equivalent to feeding every prompt token through
+ * Engine::step (gpt2.rs:373-381) but computed as one batched pass. */
+int gpt2q_prefill(gpt2q_handle* h, const uint32_t* tokens, const int32_t* seq_offsets,
+                  const int32_t* slots, int n_seq, float* logits_last, uint32_t* next_tok);
+
+/* Continues the sequences of the previous gpt2q_prefill/gpt2q_decode call for
+ * `steps` more greedy decode steps entirely on the device: each step feeds the
+ * previous step's argmax token at position+1. Optional host output
+ * out_tokens [steps][n_seq]. Fails with GPT2Q_EARG when a position would reach n_ctx. */
+int gpt2q_decode_steps(gpt2q_handle* h, int steps, uint32_t* out_tokens);
+
+/* generate_greedy (gpt2.rs:367-388) for a batch of prompts: prefill, then
+ * steps-1 device-side decode steps; out [n_seq][steps]. Prompts are clipped the
+ * same way (positions > n_ctx-1 stop generation; missing tokens are written as
+ * UINT32_MAX). */
+int gpt2q_generate_greedy(gpt2q_handle* h, const uint32_t* tokens, const int32_t* seq_offsets,
+                          int n_seq, int steps, uint32_t* out);
+
+/* Dequantize a weight tensor exactly as Engine::vec_f32 (gpt2.rs:121-142)
+ * into host `out` (n floats). Computed on the device from the uploaded bytes. */
+int gpt2q_dequant(gpt2q_handle* h, const char* name, float* out, uint64_t n);
+
+/* Number of kernel launches issued so far (Gpu::launches, gpu.rs:70). A CUDA
+ * graph replay counts the kernels it contains. */
+uint64_t gpt2q_launches(const gpt2q_handle* h);
+
+/* Launch on this CUDA stream (a cudaStream_t) instead of the handle's own. */
+int gpt2q_set_stream(gpt2q_handle* h, void* stream);
+
+/* Wait for all work of the handle. */
+int gpt2q_sync(gpt2q_handle* h);
+
+/* Per-launch timing (CUDA events around every kernel; disables CUDA graphs
+ * while on). gpt2q_profile_read writes a JSON object
+ * {"kernel": {"launches": n, "ms": t, "bytes": algorithmic bytes}, ...}. */
+int gpt2q_profile(gpt2q_handle* h, int enable);
+int gpt2q_profile_read(gpt2q_handle* h, char* json, size_t cap);
+
+/* Workload utilities for seeded synthetic weights/tokens (no counterpart in the
+ * reference's GPU API): xorshift64* Rng of model-lab/src/gpu_backward.rs:835-856
+ * (Rng::new(seed) = seed ^ 0x9E3779B97F4A7C15) with the Box-Muller normal of
+ * perf-lab/src/bin/atoms.rs:78-83. `state` is advanced in place. */
+uint64_t gpt2q_rng_new(uint64_t seed);
+void gpt2q_rng_normal_f32(uint64_t* state, float* out, size_t n, double stdv);
+void gpt2q_rng_below(uint64_t* state, uint32_t* out, size_t n, uint64_t bound);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GPT2Q_H */

@@ -1,0 +1,551 @@
+// gpt2q CUDA-core kernels for sm_100a: embedding, LayerNorm, dequant-fused linear
+// (decode GEMV / small-M GEMM), flash-decode and causal prefill attention, argmax,
+// and the upload-time repack of the SMT weight atoms.
+//
+// Reference semantics (LukasParke/smelt experiments/model-lab): the CPU step in
+// src/gpt2.rs:227-332 and the NVRTC kernels in src/cu/gpt2.cu. These kernels keep
+// the math (fp32 accumulation of q*f16(scale)*x, population-variance LayerNorm,
+// tanh GELU, exact softmax) but not the launch structure: bias, GELU, residual
+// and the K/V scatter are fused into the linear epilogues, LayerNorm is one warp
+// per row, and attention is tiled with online softmax instead of thread-0 loops.
+#include <float.h>
+
+#include "kernels.h"
+
+namespace gpt2q {
+
+// ------------------------------------------------------------------ helpers
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ------------------------------------------------------------------ embedding
+// x[m] = deq(wte[tok[m]]) + deq(wpe[pos[m]])   (gpt2.rs:229-236, gpu.rs:239-261)
+__global__ void k_embed(QW wte, QW wpe, const uint32_t* __restrict__ tok, const int* __restrict__ pos,
+                        float* __restrict__ x, int d) {
+    const int m = blockIdx.x;
+    const int t = (int)tok[m], p = pos[m];
+    for (int i = threadIdx.x; i < d; i += blockDim.x)
+        x[(size_t)m * d + i] = deq_elem(wte, t, i) + deq_elem(wpe, p, i);
+}
+
+cudaError_t launch_embed(const QW& wte, const QW& wpe, const uint32_t* tok, const int* pos, float* x,
+                         int d, int M, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    k_embed<<<M, 256, 0, st>>>(wte, wpe, tok, pos, x, d);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ LayerNorm
+// One warp per row: mean, population variance, (x-mean)/sqrt(var+eps)*g+b (gpt2.rs:178-185).
+// rows (optional) gathers source rows, e.g. the last prompt position of each sequence.
+__global__ void k_layernorm(const float* __restrict__ x, int ldx, const int* __restrict__ rows,
+                            float* __restrict__ y, int ldy, const float* __restrict__ g,
+                            const float* __restrict__ b, int d, float eps, int M) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const int src = rows ? rows[warp] : warp;
+    const float* xr = x + (size_t)src * ldx;
+    float s = 0.f;
+    for (int i = lane; i < d; i += 32) s += xr[i];
+    const float mean = warp_sum(s) / (float)d;
+    float v = 0.f;
+    for (int i = lane; i < d; i += 32) {
+        float t = xr[i] - mean;
+        v += t * t;
+    }
+    const float var = warp_sum(v) / (float)d;
+    const float den = sqrtf(var + eps);
+    float* yr = y + (size_t)warp * ldy;
+    for (int i = lane; i < d; i += 32) yr[i] = (xr[i] - mean) / den * g[i] + b[i];
+}
+
+cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y, int ldy, const float* g,
+                             const float* b, int d, float eps, int M, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    const int threads = 128, rows_per_block = threads / 32;
+    k_layernorm<<<(M + rows_per_block - 1) / rows_per_block, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d,
+                                                                               eps, M);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ linear (CUDA cores)
+// One half-warp per output row n; its 16 lanes stride over the row in 16-byte chunks
+// (coalesced 256 B per half-warp load). Each chunk is dequantised in registers with
+// the byte-permute conversion, dotted with MT activation rows, and the partial dot
+// of a group is scaled once by the group's f16 scale. Partial sums are reduced with
+// half-warp shuffles; lane mi writes activation row m0+mi through the epilogue.
+template <int ATOM>
+struct ChunkTraits;
+template <>
+struct ChunkTraits<ATOM_Q8> { static constexpr int CE = 16; static constexpr bool SCALED = true; };
+template <>
+struct ChunkTraits<ATOM_Q4> { static constexpr int CE = 32; static constexpr bool SCALED = true; };
+template <>
+struct ChunkTraits<ATOM_F16> { static constexpr int CE = 8; static constexpr bool SCALED = false; };
+template <>
+struct ChunkTraits<ATOM_F32> { static constexpr int CE = 4; static constexpr bool SCALED = false; };
+
+template <int ATOM>
+__device__ __forceinline__ void decode_chunk(const uint4& v, float* f);
+
+template <>
+__device__ __forceinline__ void decode_chunk<ATOM_Q8>(const uint4& v, float* f) {
+    i8x4_to_f32(v.x, f + 0);
+    i8x4_to_f32(v.y, f + 4);
+    i8x4_to_f32(v.z, f + 8);
+    i8x4_to_f32(v.w, f + 12);
+}
+template <>
+__device__ __forceinline__ void decode_chunk<ATOM_Q4>(const uint4& v, float* f) {
+    // word t holds packed bytes 4t..4t+3: low nibbles -> elements 4t.., high -> 16+4t..
+    i4x8_to_f32(v.x, f + 0, f + 16);
+    i4x8_to_f32(v.y, f + 4, f + 20);
+    i4x8_to_f32(v.z, f + 8, f + 24);
+    i4x8_to_f32(v.w, f + 12, f + 28);
+}
+template <>
+__device__ __forceinline__ void decode_chunk<ATOM_F16>(const uint4& v, float* f) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 t = __half22float2(h[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+template <>
+__device__ __forceinline__ void decode_chunk<ATOM_F32>(const uint4& v, float* f) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+}
+
+template <int CE>
+__device__ __forceinline__ float dot_chunk(const float* f, const float* __restrict__ xr) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < CE; i += 4) {
+        float4 xv = __ldg(reinterpret_cast<const float4*>(xr + i));
+        a0 = fmaf(f[i], xv.x, a0);
+        a1 = fmaf(f[i + 1], xv.y, a1);
+        a2 = fmaf(f[i + 2], xv.z, a2);
+        a3 = fmaf(f[i + 3], xv.w, a3);
+    }
+    return (a0 + a1) + (a2 + a3);
+}
+
+template <int ATOM, int MT, int U>
+__global__ void __launch_bounds__(256) k_linear_simt(QW w, const float* __restrict__ X, int ldx, int M,
+                                                     Epi epi) {
+    constexpr int CE = ChunkTraits<ATOM>::CE;
+    const int lane16 = threadIdx.x & 15;
+    const int n = blockIdx.x * (blockDim.x >> 4) + (threadIdx.x >> 4);
+    const bool active = n < w.rows;
+    const int nn = active ? n : (w.rows - 1);
+    const int nch = w.cols / CE;
+    const uint8_t* wrow = w.q + (size_t)nn * w.qstride;
+    const __half* srow = w.s + (size_t)nn * w.sstride;
+
+    for (int m0 = 0; m0 < M; m0 += MT) {
+        float acc[MT];
+#pragma unroll
+        for (int i = 0; i < MT; ++i) acc[i] = 0.f;
+        for (int c0 = lane16; c0 < nch; c0 += 16 * U) {
+            uint4 wv[U];
+            float sc[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + 16 * u;
+                if (c < nch) {
+                    wv[u] = __ldg(reinterpret_cast<const uint4*>(wrow + (size_t)c * 16));
+                    if (ChunkTraits<ATOM>::SCALED)
+                        sc[u] = __half2float(srow[ATOM == ATOM_Q8 ? (c >> 1) : c]);
+                    else
+                        sc[u] = 1.f;
+                } else {
+                    wv[u] = make_uint4(0, 0, 0, 0);
+                    sc[u] = 0.f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + 16 * u;
+                if (c < nch) {
+                    float f[CE];
+                    decode_chunk<ATOM>(wv[u], f);
+#pragma unroll
+                    for (int mi = 0; mi < MT; ++mi) {
+                        if (m0 + mi < M) {
+                            const float* xr = X + (size_t)(m0 + mi) * ldx + (size_t)c * CE;
+                            float p;
+                            if (ATOM == ATOM_Q4) {
+                                // elements 0..15 pair with x[0..15], 16..31 with x[16..31]
+                                p = dot_chunk<32>(f, xr);
+                            } else {
+                                p = dot_chunk<CE>(f, xr);
+                            }
+                            if (ChunkTraits<ATOM>::SCALED)
+                                acc[mi] = fmaf(sc[u], p, acc[mi]);
+                            else
+                                acc[mi] += p;
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int mi = 0; mi < MT; ++mi) {
+            float v = acc[mi];
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            if (active && lane16 == mi && m0 + mi < M) epi_apply(epi, m0 + mi, n, v);
+        }
+    }
+}
+
+template <int ATOM>
+static cudaError_t linear_dispatch(const QW& w, const float* X, int ldx, int M, const Epi& e,
+                                   cudaStream_t st) {
+    // Rows per block: keep at least ~2 blocks per SM on the small matrices.
+    int rpb = 8;
+    if (w.rows < 148 * 2 * 8) rpb = 4;
+    if (w.rows < 148 * 2 * 4) rpb = 2;
+    dim3 grid((w.rows + rpb - 1) / rpb), block(16 * rpb);
+    if (M == 1)
+        k_linear_simt<ATOM, 1, 4><<<grid, block, 0, st>>>(w, X, ldx, M, e);
+    else if (M <= 2)
+        k_linear_simt<ATOM, 2, 4><<<grid, block, 0, st>>>(w, X, ldx, M, e);
+    else if (M <= 4)
+        k_linear_simt<ATOM, 4, 4><<<grid, block, 0, st>>>(w, X, ldx, M, e);
+    else
+        k_linear_simt<ATOM, 8, 2><<<grid, block, 0, st>>>(w, X, ldx, M, e);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, const Epi& e, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    switch (w.atom) {
+        case ATOM_Q8: return linear_dispatch<ATOM_Q8>(w, X, ldx, M, e, st);
+        case ATOM_Q4: return linear_dispatch<ATOM_Q4>(w, X, ldx, M, e, st);
+        case ATOM_F16: return linear_dispatch<ATOM_F16>(w, X, ldx, M, e, st);
+        default: return linear_dispatch<ATOM_F32>(w, X, ldx, M, e, st);
+    }
+}
+
+// ------------------------------------------------------------------ decode attention
+// One block of 4 warps per (head, sequence). Each warp takes 32 keys at a time:
+// lane j scores key t0+j against q (q broadcast from shared memory), the warp does
+// an online-softmax update, then accumulates p_j * V[t0+j] with lane l owning dims
+// 2l, 2l+1 (coalesced 256 B V rows). Warps are merged through shared memory.
+// Semantics: softmax(q.K^T * scale) V over positions 0..pos (gpt2.rs:261-291).
+__global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q, int ldq, KVGeom g,
+                                                     size_t layer_off, const int* __restrict__ slot,
+                                                     const int* __restrict__ pos, float* __restrict__ out,
+                                                     int ldo, float scale) {
+    constexpr int HD = 64;
+    __shared__ float4 qs[HD / 4];
+    __shared__ float wm[4], wl[4];
+    __shared__ float wo[4][HD];
+    const int head = blockIdx.x, b = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int T = pos[b] + 1;
+    const float* K = g.base + (size_t)slot[b] * g.slot_stride + layer_off + (size_t)head * g.head_stride;
+    const float* V = K + g.sel_stride;
+    if (threadIdx.x < HD / 4)
+        qs[threadIdx.x] = *reinterpret_cast<const float4*>(q + (size_t)b * ldq + head * HD + threadIdx.x * 4);
+    __syncthreads();
+
+    float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int t0 = warp * 32; t0 < T; t0 += 128) {
+        const int t = t0 + lane;
+        float s = -INFINITY;
+        if (t < T) {
+            const float4* kr = reinterpret_cast<const float4*>(K + (size_t)t * HD);
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+            for (int i = 0; i < HD / 4; ++i) {
+                float4 kv = __ldg(kr + i);
+                float4 qv = qs[i];
+                a0 = fmaf(qv.x, kv.x, a0);
+                a1 = fmaf(qv.y, kv.y, a1);
+                a2 = fmaf(qv.z, kv.z, a2);
+                a3 = fmaf(qv.w, kv.w, a3);
+            }
+            s = ((a0 + a1) + (a2 + a3)) * scale;
+        }
+        const float mnew = fmaxf(m, warp_max(s));
+        const float corr = expf(m - mnew);
+        const float p = (t < T) ? expf(s - mnew) : 0.f;
+        l = l * corr + warp_sum(p);
+        o0 *= corr;
+        o1 *= corr;
+        const int nv = min(32, T - t0);
+        for (int j = 0; j < nv; ++j) {
+            const float pj = __shfl_sync(0xffffffffu, p, j);
+            const float2 v = __ldg(reinterpret_cast<const float2*>(V + (size_t)(t0 + j) * HD) + lane);
+            o0 = fmaf(pj, v.x, o0);
+            o1 = fmaf(pj, v.y, o1);
+        }
+        m = mnew;
+    }
+    if (lane == 0) {
+        wm[warp] = m;
+        wl[warp] = l;
+    }
+    wo[warp][2 * lane] = o0;
+    wo[warp][2 * lane + 1] = o1;
+    __syncthreads();
+    if (threadIdx.x < HD) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            if (wm[w] != -INFINITY) {
+                const float f = expf(wm[w] - M);
+                L += wl[w] * f;
+                O += wo[w][threadIdx.x] * f;
+            }
+        }
+        out[(size_t)b * ldo + head * HD + threadIdx.x] = O / L;
+    }
+}
+
+cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t layer_off, const int* slot,
+                               const int* pos, float* out, int ldo, int n_head, int B, float scale,
+                               cudaStream_t st) {
+    if (B <= 0) return cudaSuccess;
+    if (g.hd != 64) return cudaErrorInvalidValue;
+    k_attn_decode<<<dim3(n_head, B), 128, 0, st>>>(q, ldq, g, layer_off, slot, pos, out, ldo, scale);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ prefill attention
+// One block of 128 threads per (head, 64-query tile). Thread pair (2i, 2i+1) owns
+// query row i; each half holds 32 of the 64 q/o dims in registers. Keys/values are
+// staged 32 at a time in shared memory with the two halves interleaved so a warp's
+// paired reads hit distinct banks. Causal mask: key t attends iff t <= query position.
+__global__ void __launch_bounds__(128) k_attn_prefill(const float* __restrict__ q, int ldq, KVGeom g,
+                                                      size_t layer_off, const AttnTile* __restrict__ tiles,
+                                                      float* __restrict__ out, int ldo, float scale) {
+    constexpr int HD = 64, KT = 32;
+    __shared__ float Ks[KT][HD];
+    __shared__ float Vs[KT][HD];
+    const AttnTile tile = tiles[blockIdx.y];
+    const int head = blockIdx.x;
+    const int qi = threadIdx.x >> 1, half = threadIdx.x & 1;
+    const int qpos = tile.q0 + qi;
+    const bool valid = qpos < tile.T;
+    const float* K = g.base + (size_t)tile.slot * g.slot_stride + layer_off + (size_t)head * g.head_stride;
+    const float* V = K + g.sel_stride;
+
+    float qr[32], o[32];
+    const float* qrow = q + (size_t)(tile.row0 + (valid ? qpos : tile.q0)) * ldq + head * HD + half * 32;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+        float4 v = *reinterpret_cast<const float4*>(qrow + i);
+        qr[i] = v.x;
+        qr[i + 1] = v.y;
+        qr[i + 2] = v.z;
+        qr[i + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    const int kend = min(tile.T, tile.q0 + 64);
+    for (int k0 = 0; k0 < kend; k0 += KT) {
+        __syncthreads();
+        // 32 rows x 64 floats = 512 float4; element d of a row goes to column (d%32)*2 + d/32.
+        for (int e = threadIdx.x; e < KT * HD / 4; e += 128) {
+            const int r = e / (HD / 4), c4 = (e % (HD / 4)) * 4;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (k0 + r < tile.T) {
+                kv = __ldg(reinterpret_cast<const float4*>(K + (size_t)(k0 + r) * HD + c4));
+                vv = __ldg(reinterpret_cast<const float4*>(V + (size_t)(k0 + r) * HD + c4));
+            }
+            const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, vk[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int dcol = c4 + j;
+                const int col = (dcol & 31) * 2 + (dcol >> 5);
+                Ks[r][col] = kk[j];
+                Vs[r][col] = vk[j];
+            }
+        }
+        __syncthreads();
+        float s[KT];
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < KT; ++j) {
+            float a = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) a = fmaf(qr[i], Ks[j][i * 2 + half], a);
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            s[j] = (valid && k0 + j <= qpos) ? a * scale : -INFINITY;
+            tmax = fmaxf(tmax, s[j]);
+        }
+        const float mnew = fmaxf(m, tmax);
+        if (mnew == -INFINITY) continue;  // nothing visible yet (padding rows only)
+        const float corr = expf(m - mnew);
+        l *= corr;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] *= corr;
+#pragma unroll
+        for (int j = 0; j < KT; ++j) {
+            const float p = expf(s[j] - mnew);
+            l += p;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = fmaf(p, Vs[j][i * 2 + half], o[i]);
+        }
+        m = mnew;
+    }
+    if (valid) {
+        float* orow = out + (size_t)(tile.row0 + qpos) * ldo + head * HD + half * 32;
+        const float inv = 1.0f / l;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) orow[i] = o[i] * inv;
+    }
+}
+
+cudaError_t launch_attn_prefill(const float* q, int ldq, const KVGeom& g, size_t layer_off,
+                                const AttnTile* tiles, int n_tiles, float* out, int ldo, int n_head,
+                                float scale, cudaStream_t st) {
+    if (n_tiles <= 0) return cudaSuccess;
+    if (g.hd != 64) return cudaErrorInvalidValue;
+    k_attn_prefill<<<dim3(n_head, n_tiles), 128, 0, st>>>(q, ldq, g, layer_off, tiles, out, ldo, scale);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ argmax
+// Greedy pick (gpt2.rs:390-396): Iterator::max_by(total_cmp) keeps the LAST maximum,
+// so (key, index) pairs are compared lexicographically with the larger index winning.
+__device__ __forceinline__ void better(int& bk, int& bi, int k, int i) {
+    if (k > bk || (k == bk && i > bi)) {
+        bk = k;
+        bi = i;
+    }
+}
+
+__global__ void __launch_bounds__(512) k_argmax(const float* __restrict__ logits, int V, int ld,
+                                                uint32_t* __restrict__ next, uint32_t* __restrict__ genlog,
+                                                const int* __restrict__ gpos, int n_ctx,
+                                                uint32_t* __restrict__ tok_adv, int* __restrict__ pos_adv) {
+    __shared__ int sk[16], si[16];
+    const int b = blockIdx.x;
+    const float* row = logits + (size_t)b * ld;
+    int bk = INT_MIN, bi = -1;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) better(bk, bi, total_key(row[i]), i);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        int k2 = __shfl_xor_sync(0xffffffffu, bk, o), i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        better(bk, bi, k2, i2);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sk[warp] = bk;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        bk = lane < nw ? sk[lane] : INT_MIN;
+        bi = lane < nw ? si[lane] : -1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            int k2 = __shfl_xor_sync(0xffffffffu, bk, o), i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+            better(bk, bi, k2, i2);
+        }
+        if (lane == 0) {
+            const uint32_t best = (uint32_t)bi;
+            next[b] = best;
+            if (genlog) genlog[(size_t)b * n_ctx + gpos[b]] = best;
+            if (tok_adv) tok_adv[b] = best;
+            if (pos_adv) pos_adv[b] += 1;
+        }
+    }
+}
+
+cudaError_t launch_argmax(const float* logits, int V, int ld, int B, uint32_t* next, uint32_t* genlog,
+                          const int* gpos, int n_ctx, uint32_t* tok_adv, int* pos_adv, cudaStream_t st) {
+    if (B <= 0) return cudaSuccess;
+    k_argmax<<<B, 512, 0, st>>>(logits, V, ld, next, genlog, gpos, n_ctx, tok_adv, pos_adv);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ dequant / repack
+__global__ void k_dequant(QW w, float* __restrict__ out) {
+    const size_t n = (size_t)w.rows * w.cols;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = deq_elem(w, (int)(i / w.cols), (int)(i % w.cols));
+}
+
+cudaError_t launch_dequant(const QW& w, float* out, cudaStream_t st) {
+    k_dequant<<<148 * 8, 256, 0, st>>>(w, out);
+    return cudaGetLastError();
+}
+
+// SMT Q8 payload [rows][nblk][f16 scale | 32 x int8] -> int8 [rows][cols] + f16 [rows][sstride].
+__global__ void k_repack_q8(const uint8_t* __restrict__ raw, int rows, int nblk, uint8_t* __restrict__ q,
+                            __half* __restrict__ s, int sstride) {
+    const size_t total = (size_t)rows * nblk;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / nblk, blk = i % nblk;
+        const uint8_t* src = raw + i * 34;
+        s[r * sstride + blk] = __ushort_as_half((unsigned short)(src[0] | (src[1] << 8)));
+        uint8_t* dst = q + r * (size_t)nblk * 32 + blk * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) dst[j] = src[2 + j];
+    }
+}
+
+// SMT Q4 payload [rows][nblk][f16 scale | 16 packed bytes] -> bytes [rows][nblk*16] + f16 scales.
+__global__ void k_repack_q4(const uint8_t* __restrict__ raw, int rows, int nblk, uint8_t* __restrict__ q,
+                            __half* __restrict__ s, int sstride) {
+    const size_t total = (size_t)rows * nblk;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / nblk, blk = i % nblk;
+        const uint8_t* src = raw + i * 18;
+        s[r * sstride + blk] = __ushort_as_half((unsigned short)(src[0] | (src[1] << 8)));
+        uint8_t* dst = q + r * (size_t)nblk * 16 + blk * 16;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dst[j] = src[2 + j];
+    }
+}
+
+cudaError_t launch_repack_q8(const uint8_t* raw, int rows, int cols, uint8_t* q, __half* s, int sstride,
+                             cudaStream_t st) {
+    k_repack_q8<<<148 * 8, 256, 0, st>>>(raw, rows, cols / 32, q, s, sstride);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_repack_q4(const uint8_t* raw, int rows, int cols, uint8_t* q, __half* s, int sstride,
+                             cudaStream_t st) {
+    k_repack_q4<<<148 * 8, 256, 0, st>>>(raw, rows, cols / 32, q, s, sstride);
+    return cudaGetLastError();
+}
+
+__global__ void k_f16_to_f32(const __half* __restrict__ src, float* __restrict__ dst, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = __half2float(src[i]);
+}
+
+cudaError_t launch_f16_to_f32(const __half* src, float* dst, size_t n, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    k_f16_to_f32<<<148, 256, 0, st>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
+}  // namespace gpt2q

@@ -1,0 +1,50 @@
+// Host-side launchers of the gpt2q CUDA kernels (definitions in kernels.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace gpt2q {
+
+// KV arena geometry: [slot][layer][K|V][head][n_ctx][hd] fp32.
+struct KVGeom {
+    float* base;
+    size_t slot_stride, layer_stride, sel_stride, head_stride;
+    int hd;
+};
+
+// Prefill attention work item: 64 query rows of one sequence.
+struct AttnTile {
+    int row0;  // first activation row of the sequence
+    int q0;    // first query position of the tile
+    int T;     // sequence length
+    int slot;  // KV slot
+};
+
+cudaError_t launch_embed(const QW& wte, const QW& wpe, const uint32_t* tok, const int* pos, float* x,
+                         int d, int M, cudaStream_t st);
+cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y, int ldy, const float* g,
+                             const float* b, int d, float eps, int M, cudaStream_t st);
+// out = epilogue(X[M][K] . W^T) on CUDA cores (fp32 FMA, weights dequantised in registers).
+cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, const Epi& e,
+                               cudaStream_t st);
+cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t layer_off,
+                               const int* slot, const int* pos, float* out, int ldo, int n_head,
+                               int B, float scale, cudaStream_t st);
+cudaError_t launch_attn_prefill(const float* q, int ldq, const KVGeom& g, size_t layer_off,
+                                const AttnTile* tiles, int n_tiles, float* out, int ldo, int n_head,
+                                float scale, cudaStream_t st);
+// Greedy argmax per row (total order, ties -> last index).
+cudaError_t launch_argmax(const float* logits, int V, int ld, int B, uint32_t* next, uint32_t* genlog,
+                          const int* gpos, int n_ctx, uint32_t* tok_adv, int* pos_adv,
+                          cudaStream_t st);
+cudaError_t launch_dequant(const QW& w, float* out, cudaStream_t st);
+// Upload-time layout conversion from the SMT payload (raw, on device).
+cudaError_t launch_repack_q8(const uint8_t* raw, int rows, int cols, uint8_t* q, __half* s, int sstride,
+                             cudaStream_t st);
+cudaError_t launch_repack_q4(const uint8_t* raw, int rows, int cols, uint8_t* q, __half* s, int sstride,
+                             cudaStream_t st);
+cudaError_t launch_f16_to_f32(const __half* src, float* dst, size_t n, cudaStream_t st);
+
+}  // namespace gpt2q

@@ -1,0 +1,1065 @@
+// gpt2q host runtime: the C-ABI of include/gpt2q.h.
+//
+// Replaces the CUDA executor of LukasParke/smelt (experiments/model-lab/src/gpu.rs):
+//  - weights are uploaded once, quantized atoms stay quantized in HBM and are
+//    repacked into a 16-byte aligned layout (int8/nibbles + f16 scale rows);
+//  - the KV cache is one arena [slot][layer][K|V][head][n_ctx][hd] fp32, i.e. a
+//    contiguous cache per sequence (the reference keeps one [n_ctx][d] buffer per
+//    layer for a single sequence, gpu.rs:128-134);
+//  - a decode step is a fixed kernel sequence captured once per batch size in a
+//    CUDA graph; greedy argmax runs on the device and feeds the next step, so a
+//    multi-step decode never returns to the host between tokens.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gpt2q.h"
+#include "gemm.h"
+#include "kernels.h"
+#include "tp.h"
+
+using namespace gpt2q;
+
+namespace {
+
+std::string g_create_error;
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+};
+
+struct Linear {
+    QW w{};
+    float* bias = nullptr;
+    int rows = 0, cols = 0;
+    std::string name;
+    size_t weight_bytes = 0;  // q + scale bytes read by one full pass over W
+};
+
+struct LayerW {
+    float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+    Linear attn, proj, fc, mproj;
+};
+
+struct ProfAgg {
+    uint64_t launches = 0;
+    double ms = 0.0;
+    double bytes = 0.0;
+};
+
+struct ProfRec {
+    std::string name;
+    cudaEvent_t a, b;
+    double bytes;
+};
+
+int atom_id(const std::string& a) {
+    if (a == "core.i8.b32.f16scale") return ATOM_Q8;
+    if (a == "core.i4.b32.f16scale") return ATOM_Q4;
+    if (a == "core.f16") return ATOM_F16;
+    if (a == "core.f32") return ATOM_F32;
+    return -1;
+}
+
+size_t payload_bytes(int atom, size_t numel) {
+    switch (atom) {
+        case ATOM_Q8: return numel / 32 * 34;
+        case ATOM_Q4: return numel / 32 * 18;
+        case ATOM_F16: return numel * 2;
+        default: return numel * 4;
+    }
+}
+
+}  // namespace
+
+struct gpt2q_handle {
+    gpt2q_config cfg{};
+    int device = 0;
+    int hd = 64;
+    int H_local = 0;   // heads held by this handle
+    int d_local = 0;   // H_local * hd
+    int fc_local = 0;  // c_fc rows held by this handle
+    int tp_size = 1, tp_rank = 0;
+    cudaStream_t own_stream = nullptr, stream = nullptr;
+    bool use_graphs = true;
+    std::string err;
+    std::vector<DevBuf> allocs;
+
+    Linear wte, wpe;
+    float *lnf_g = nullptr, *lnf_b = nullptr;
+    std::vector<LayerW> layers;
+    std::map<std::string, const Linear*> lin_by_name;
+    std::map<std::string, std::pair<float*, size_t>> vec_by_name;
+
+    KVGeom kv{};
+    int Mmax = 0;
+    float *x = nullptr, *h = nullptr, *qb = nullptr, *att = nullptr, *f = nullptr, *logits = nullptr;
+    float* tp_red = nullptr;  // tensor-parallel partial sums [Mmax][d]
+    // prefill scratch
+    uint32_t* p_tok = nullptr;
+    int *p_pos = nullptr, *p_slot = nullptr, *p_lastrow = nullptr, *p_lastpos = nullptr;
+    AttnTile* p_tiles = nullptr;
+    int max_tiles = 0;
+    // decode state
+    uint32_t *d_tok = nullptr, *d_next = nullptr, *d_genlog = nullptr;
+    int *d_pos = nullptr, *d_slot = nullptr;
+    int cur_n = 0;
+    std::vector<int> hpos, hslot;  // host mirror of the decode state
+    // host staging (pinned)
+    int* h_stage = nullptr;
+    size_t h_stage_ints = 0;
+
+    std::map<int, std::pair<cudaGraphExec_t, uint64_t>> dec_graphs;  // B -> (graph, kernels)
+    bool capturing = false;
+    uint64_t capture_kernels = 0;
+    uint64_t launches = 0;
+
+    bool prof = false;
+    std::vector<ProfRec> prof_pending;
+    std::map<std::string, ProfAgg> prof_agg;
+
+    GemmPlan gemm;  // tensor-core path for large M
+    TpComm* tp = nullptr;
+
+    int fail(int code, const std::string& m) {
+        err = m;
+        return code;
+    }
+    template <class T>
+    T* dalloc(size_t bytes) {
+        void* p = nullptr;
+        if (bytes == 0) bytes = 16;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+        allocs.push_back({p, bytes});
+        return reinterpret_cast<T*>(p);
+    }
+};
+
+#define CK(call)                                                                        \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            return H->fail(GPT2Q_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+namespace {
+
+// ------------------------------------------------------------------ launch bookkeeping
+int launched(gpt2q_handle* H, const char* name, double bytes, cudaError_t e, cudaEvent_t a, cudaEvent_t b) {
+    if (e != cudaSuccess) return H->fail(GPT2Q_ECUDA, std::string(name) + ": " + cudaGetErrorString(e));
+    if (H->capturing) {
+        H->capture_kernels++;
+    } else {
+        H->launches++;
+    }
+    if (a) {
+        cudaEventRecord(b, H->stream);
+        H->prof_pending.push_back({name, a, b, bytes});
+    }
+    return GPT2Q_OK;
+}
+
+template <class F>
+int run_kernel(gpt2q_handle* H, const char* name, double bytes, F&& f) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (H->prof && !H->capturing) {
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, H->stream);
+    }
+    return launched(H, name, bytes, f(), a, b);
+}
+
+#define RUN(name, bytes, expr)                                              \
+    do {                                                                    \
+        int rc_ = run_kernel(H, name, (double)(bytes), [&]() { return (expr); }); \
+        if (rc_ != GPT2Q_OK) return rc_;                                    \
+    } while (0)
+
+// ------------------------------------------------------------------ upload
+struct Src {
+    const gpt2q_tensor_desc* d = nullptr;
+};
+
+int upload_vec(gpt2q_handle* H, const gpt2q_tensor_desc* t, size_t n, size_t off, size_t cnt, float** out) {
+    int a = atom_id(t->atom);
+    if (t->ndim != 1 || (size_t)t->shape[0] != n)
+        return H->fail(GPT2Q_EARG, std::string("tensor ") + t->name + ": expected 1-D of length " + std::to_string(n));
+    if (a != ATOM_F16 && a != ATOM_F32)
+        return H->fail(GPT2Q_EARG, std::string("tensor ") + t->name + ": 1-D tensors must be core.f16 or core.f32");
+    if (t->len != payload_bytes(a, n)) return H->fail(GPT2Q_EARG, std::string("tensor ") + t->name + ": bad length");
+    float* d = H->dalloc<float>(cnt * 4);
+    if (!d) return H->fail(GPT2Q_EOOM, "cudaMalloc vector");
+    if (a == ATOM_F32) {
+        CK(cudaMemcpy(d, reinterpret_cast<const float*>(t->data) + off, cnt * 4, cudaMemcpyHostToDevice));
+    } else {
+        __half* tmp = nullptr;
+        CK(cudaMalloc(&tmp, cnt * 2));
+        CK(cudaMemcpy(tmp, reinterpret_cast<const uint16_t*>(t->data) + off, cnt * 2, cudaMemcpyHostToDevice));
+        CK(launch_f16_to_f32(tmp, d, cnt, H->stream));
+        CK(cudaStreamSynchronize(H->stream));
+        CK(cudaFree(tmp));
+    }
+    *out = d;
+    H->vec_by_name[t->name] = {d, cnt};
+    return GPT2Q_OK;
+}
+
+// Upload a 2-D weight [rows][cols]; keep the row ranges `rsel` and columns [c0, c1).
+int upload_linear(gpt2q_handle* H, const gpt2q_tensor_desc* t, int rows, int cols,
+                  const std::vector<std::pair<int, int>>& rsel, int c0, int c1, Linear* L) {
+    int a = atom_id(t->atom);
+    if (a < 0) return H->fail(GPT2Q_EARG, std::string("tensor ") + t->name + ": unknown atom " + t->atom);
+    if (t->ndim != 2 || t->shape[0] != rows || t->shape[1] != cols)
+        return H->fail(GPT2Q_EARG, std::string("tensor ") + t->name + ": expected shape [" + std::to_string(rows) +
+                                       ", " + std::to_string(cols) + "]");
+    if (cols % 32 != 0) return H->fail(GPT2Q_EUNSUP, std::string("tensor ") + t->name + ": cols must be a multiple of 32");
+    if (t->len != payload_bytes(a, (size_t)rows * cols))
+        return H->fail(GPT2Q_EARG, std::string("tensor ") + t->name + ": payload length does not match shape/atom");
+    const size_t row_bytes = payload_bytes(a, (size_t)cols);
+    int out_rows = 0;
+    for (auto& r : rsel) out_rows += r.second;
+    const int out_cols = c1 - c0;
+    const size_t out_row_bytes = payload_bytes(a, (size_t)out_cols);
+    const size_t col_off = payload_bytes(a, (size_t)c0);
+    const bool whole = (rsel.size() == 1 && rsel[0].first == 0 && rsel[0].second == rows && c0 == 0 && c1 == cols);
+    std::vector<uint8_t> sliced;
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(t->data);
+    if (!whole) {
+        sliced.resize((size_t)out_rows * out_row_bytes);
+        size_t o = 0;
+        for (auto& r : rsel)
+            for (int i = 0; i < r.second; ++i, ++o)
+                std::memcpy(sliced.data() + o * out_row_bytes, src + (size_t)(r.first + i) * row_bytes + col_off,
+                            out_row_bytes);
+        src = sliced.data();
+    }
+    const size_t raw_bytes = (size_t)out_rows * out_row_bytes;
+    L->rows = out_rows;
+    L->cols = out_cols;
+    L->name = t->name;
+    QW& w = L->w;
+    w.rows = out_rows;
+    w.cols = out_cols;
+    w.atom = a;
+    w.sstride = 0;
+    w.s = nullptr;
+    if (a == ATOM_F16 || a == ATOM_F32) {
+        uint8_t* q = H->dalloc<uint8_t>(raw_bytes);
+        if (!q) return H->fail(GPT2Q_EOOM, "cudaMalloc weight");
+        CK(cudaMemcpy(q, src, raw_bytes, cudaMemcpyHostToDevice));
+        w.q = q;
+        w.qstride = (a == ATOM_F16 ? 2 : 4) * (size_t)out_cols;
+        L->weight_bytes = raw_bytes;
+    } else {
+        const int nblk = out_cols / 32;
+        w.sstride = (nblk + 7) / 8 * 8;
+        w.qstride = (a == ATOM_Q8) ? (size_t)out_cols : (size_t)out_cols / 2;
+        uint8_t* q = H->dalloc<uint8_t>(w.qstride * out_rows);
+        __half* s = H->dalloc<__half>((size_t)w.sstride * out_rows * 2);
+        if (!q || !s) return H->fail(GPT2Q_EOOM, "cudaMalloc weight");
+        CK(cudaMemset(s, 0, (size_t)w.sstride * out_rows * 2));
+        uint8_t* raw = nullptr;
+        CK(cudaMalloc(&raw, raw_bytes));
+        CK(cudaMemcpy(raw, src, raw_bytes, cudaMemcpyHostToDevice));
+        if (a == ATOM_Q8)
+            CK(launch_repack_q8(raw, out_rows, out_cols, q, s, w.sstride, H->stream));
+        else
+            CK(launch_repack_q4(raw, out_rows, out_cols, q, s, w.sstride, H->stream));
+        CK(cudaStreamSynchronize(H->stream));
+        CK(cudaFree(raw));
+        w.q = q;
+        w.s = s;
+        L->weight_bytes = w.qstride * out_rows + (size_t)nblk * 2 * out_rows;
+    }
+    H->lin_by_name[t->name] = L;
+    return GPT2Q_OK;
+}
+
+// ------------------------------------------------------------------ forward pieces
+Epi epi_store(float* out, int ldo, const float* bias) {
+    Epi e{};
+    e.kind = EPI_STORE;
+    e.out = out;
+    e.ldo = ldo;
+    e.bias = bias;
+    return e;
+}
+
+double linear_bytes(const Linear& L, int M, int extra_out_rw) {
+    return (double)L.weight_bytes + (double)M * L.cols * 4 + (double)M * L.rows * 4 * extra_out_rw;
+}
+
+int linear(gpt2q_handle* H, const char* name, const Linear& L, const float* X, int ldx, int M, const Epi& e) {
+    const int extra = (e.kind == EPI_RESID) ? 2 : 1;
+    const double bytes = linear_bytes(L, M, extra);
+    if (H->gemm.usable(L.w, M)) {
+        RUN(name, bytes, launch_linear_tc(H->gemm, L.w, X, ldx, M, e, H->stream));
+    } else {
+        RUN(name, bytes, launch_linear_simt(L.w, X, ldx, M, e, H->stream));
+    }
+    return GPT2Q_OK;
+}
+
+// Residual update of row-split projections under tensor parallelism: y = partial (+bias on
+// rank 0), all-reduce(y), x += y.
+int tp_residual(gpt2q_handle* H, const char* name, const Linear& L, const float* X, int ldx, int M) {
+    const int d = H->cfg.n_embd;
+    Epi e = epi_store(H->tp_red, d, H->tp_rank == 0 ? L.bias : nullptr);
+    int rc = linear(H, name, L, X, ldx, M, e);
+    if (rc) return rc;
+    rc = tp_allreduce_add(H->tp, H->tp_red, H->x, (size_t)M * d, H->stream);
+    if (rc) return H->fail(GPT2Q_ENCCL, tp_last_error(H->tp));
+    if (H->capturing)
+        H->capture_kernels++;
+    else
+        H->launches++;
+    return GPT2Q_OK;
+}
+
+Epi epi_qkv(gpt2q_handle* H, int layer, const int* slot, const int* pos, const float* bias) {
+    Epi e{};
+    e.kind = EPI_QKV;
+    e.bias = bias;
+    e.out = H->qb;
+    e.ldo = H->d_local;
+    e.kv = H->kv.base;
+    e.slot = slot;
+    e.pos = pos;
+    e.d_local = H->d_local;
+    e.hd = H->hd;
+    e.slot_stride = H->kv.slot_stride;
+    e.layer_off = (size_t)layer * H->kv.layer_stride;
+    e.sel_stride = H->kv.sel_stride;
+    e.head_stride = H->kv.head_stride;
+    return e;
+}
+
+// One transformer block over M activation rows (gpt2.rs:238-322). attn_fn runs the
+// attention of this layer (decode or prefill form).
+template <class AttnFn>
+int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, AttnFn&& attn_fn) {
+    const int d = H->cfg.n_embd;
+    const float eps = H->cfg.ln_eps;
+    LayerW& Lw = H->layers[layer];
+    RUN("layernorm", (double)M * d * 8, launch_layernorm(H->x, d, nullptr, H->h, d, Lw.ln1_g, Lw.ln1_b, d, eps, M, H->stream));
+    int rc = linear(H, "linear_qkv", Lw.attn, H->h, d, M, epi_qkv(H, layer, slot, pos, Lw.attn.bias));
+    if (rc) return rc;
+    rc = attn_fn(layer);
+    if (rc) return rc;
+    if (H->tp_size > 1) {
+        rc = tp_residual(H, "linear_attn_proj", Lw.proj, H->att, H->d_local, M);
+    } else {
+        Epi e = epi_store(H->x, d, Lw.proj.bias);
+        e.kind = EPI_RESID;
+        rc = linear(H, "linear_attn_proj", Lw.proj, H->att, H->d_local, M, e);
+    }
+    if (rc) return rc;
+    RUN("layernorm", (double)M * d * 8, launch_layernorm(H->x, d, nullptr, H->h, d, Lw.ln2_g, Lw.ln2_b, d, eps, M, H->stream));
+    {
+        Epi e = epi_store(H->f, H->fc_local, Lw.fc.bias);
+        e.kind = EPI_GELU;
+        rc = linear(H, "linear_fc_gelu", Lw.fc, H->h, d, M, e);
+        if (rc) return rc;
+    }
+    if (H->tp_size > 1) {
+        rc = tp_residual(H, "linear_mlp_proj", Lw.mproj, H->f, H->fc_local, M);
+    } else {
+        Epi e = epi_store(H->x, d, Lw.mproj.bias);
+        e.kind = EPI_RESID;
+        rc = linear(H, "linear_mlp_proj", Lw.mproj, H->f, H->fc_local, M, e);
+    }
+    return rc;
+}
+
+// Decode step for B sequences reading d_tok/d_pos/d_slot; argmax advances the state.
+int enqueue_decode(gpt2q_handle* H, int B) {
+    const int d = H->cfg.n_embd;
+    const float scale = 1.0f / std::sqrt((float)H->hd);
+    RUN("embed", (double)B * d * 6, launch_embed(H->wte.w, H->wpe.w, H->d_tok, H->d_pos, H->x, d, B, H->stream));
+    double kv_bytes = 0;
+    for (int b = 0; b < B && b < (int)H->hpos.size(); ++b) kv_bytes += 2.0 * (H->hpos[b] + 1) * H->d_local * 4;
+    for (int l = 0; l < H->cfg.n_layer; ++l) {
+        int rc = block(H, l, B, H->d_slot, H->d_pos, [&](int layer) {
+            RUN("attn_decode", kv_bytes + (double)B * H->d_local * 8,
+                launch_attn_decode(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->d_slot,
+                                   H->d_pos, H->att, H->d_local, H->H_local, B, scale, H->stream));
+            return GPT2Q_OK;
+        });
+        if (rc) return rc;
+    }
+    RUN("layernorm", (double)B * d * 8,
+        launch_layernorm(H->x, d, nullptr, H->h, d, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, B, H->stream));
+    int rc = linear(H, "linear_head", H->wte, H->h, d, B, epi_store(H->logits, H->cfg.vocab, nullptr));
+    if (rc) return rc;
+    RUN("argmax", (double)B * H->cfg.vocab * 4,
+        launch_argmax(H->logits, H->cfg.vocab, H->cfg.vocab, B, H->d_next, H->d_genlog, H->d_pos, H->cfg.n_ctx,
+                      H->d_tok, H->d_pos, H->stream));
+    return GPT2Q_OK;
+}
+
+int flush_profile(gpt2q_handle* H) {
+    if (H->prof_pending.empty()) return GPT2Q_OK;
+    CK(cudaStreamSynchronize(H->stream));
+    for (auto& r : H->prof_pending) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, r.a, r.b);
+        auto& g = H->prof_agg[r.name];
+        g.launches++;
+        g.ms += ms;
+        g.bytes += r.bytes;
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    H->prof_pending.clear();
+    return GPT2Q_OK;
+}
+
+// Run one decode step for the current state (graph replay when possible).
+int run_decode_step(gpt2q_handle* H, int B) {
+    const bool graph_ok = H->use_graphs && !H->prof && H->stream != nullptr;
+    if (graph_ok) {
+        auto it = H->dec_graphs.find(B);
+        if (it == H->dec_graphs.end()) {
+            cudaGraph_t g = nullptr;
+            CK(cudaStreamBeginCapture(H->stream, cudaStreamCaptureModeThreadLocal));
+            H->capturing = true;
+            H->capture_kernels = 0;
+            int rc = enqueue_decode(H, B);
+            H->capturing = false;
+            cudaError_t ce = cudaStreamEndCapture(H->stream, &g);
+            if (rc) {
+                if (g) cudaGraphDestroy(g);
+                return rc;
+            }
+            if (ce != cudaSuccess) return H->fail(GPT2Q_ECUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+            cudaGraphExec_t ex = nullptr;
+            ce = cudaGraphInstantiate(&ex, g, 0);
+            cudaGraphDestroy(g);
+            if (ce != cudaSuccess) return H->fail(GPT2Q_ECUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+            it = H->dec_graphs.emplace(B, std::make_pair(ex, H->capture_kernels)).first;
+        }
+        CK(cudaGraphLaunch(it->second.first, H->stream));
+        H->launches += it->second.second;
+    } else {
+        int rc = enqueue_decode(H, B);
+        if (rc) return rc;
+        if (H->prof) {
+            rc = flush_profile(H);
+            if (rc) return rc;
+        }
+    }
+    for (int b = 0; b < B; ++b) H->hpos[b] += 1;
+    return GPT2Q_OK;
+}
+
+int check_tokens(gpt2q_handle* H, const uint32_t* tok, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        if (tok[i] >= (uint32_t)H->cfg.vocab)
+            return H->fail(GPT2Q_EARG, "token id " + std::to_string(tok[i]) + " >= vocab");
+    return GPT2Q_OK;
+}
+
+int ensure_stage(gpt2q_handle* H, size_t ints) {
+    if (H->h_stage_ints >= ints) return GPT2Q_OK;
+    if (H->h_stage) cudaFreeHost(H->h_stage);
+    H->h_stage = nullptr;
+    H->h_stage_ints = 0;
+    CK(cudaMallocHost(&H->h_stage, ints * 4));
+    H->h_stage_ints = ints;
+    return GPT2Q_OK;
+}
+
+// Prefill of one chunk of sequences [s0, s1) whose tokens fit the workspace.
+int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, const int32_t* slots, int s0,
+                  int s1) {
+    const int d = H->cfg.n_embd;
+    const int base = offs[s0];
+    const int M = offs[s1] - base;
+    const int ns = s1 - s0;
+    // host staging: tok[M] pos[M] slot[M] lastrow[ns] lastpos[ns] tiles[4*nt]
+    int nt = 0;
+    for (int s = s0; s < s1; ++s) nt += (offs[s + 1] - offs[s] + 63) / 64;
+    if (nt > H->max_tiles) return H->fail(GPT2Q_EARG, "too many attention tiles in one prefill chunk");
+    int rc = ensure_stage(H, (size_t)3 * M + 2 * ns + 4 * (size_t)nt);
+    if (rc) return rc;
+    int* st_tok = H->h_stage;
+    int* st_pos = st_tok + M;
+    int* st_slot = st_pos + M;
+    int* st_lrow = st_slot + M;
+    int* st_lpos = st_lrow + ns;
+    AttnTile* st_tiles = reinterpret_cast<AttnTile*>(st_lpos + ns);
+    int ti = 0;
+    for (int s = s0; s < s1; ++s) {
+        const int T = offs[s + 1] - offs[s];
+        const int r0 = offs[s] - base;
+        const int slot = slots ? slots[s] : s;
+        for (int t = 0; t < T; ++t) {
+            st_tok[r0 + t] = (int)tokens[offs[s] + t];
+            st_pos[r0 + t] = t;
+            st_slot[r0 + t] = slot;
+        }
+        st_lrow[s - s0] = r0 + T - 1;
+        st_lpos[s - s0] = T - 1;
+        for (int q0 = 0; q0 < T; q0 += 64) st_tiles[ti++] = AttnTile{r0, q0, T, slot};
+    }
+    CK(cudaMemcpyAsync(H->p_tok, st_tok, (size_t)M * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->p_pos, st_pos, (size_t)M * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->p_slot, st_slot, (size_t)M * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->p_lastrow, st_lrow, (size_t)ns * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->p_lastpos, st_lpos, (size_t)ns * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->p_tiles, st_tiles, (size_t)nt * sizeof(AttnTile), cudaMemcpyHostToDevice, H->stream));
+
+    const float scale = 1.0f / std::sqrt((float)H->hd);
+    double kv_bytes = 0;
+    for (int s = s0; s < s1; ++s) {
+        const double T = offs[s + 1] - offs[s];
+        kv_bytes += 2.0 * T * H->d_local * 4;
+    }
+    RUN("embed", (double)M * d * 6, launch_embed(H->wte.w, H->wpe.w, H->p_tok, H->p_pos, H->x, d, M, H->stream));
+    for (int l = 0; l < H->cfg.n_layer; ++l) {
+        rc = block(H, l, M, H->p_slot, H->p_pos, [&](int layer) {
+            RUN("attn_prefill", kv_bytes + (double)M * H->d_local * 8,
+                launch_attn_prefill(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->p_tiles, nt,
+                                    H->att, H->d_local, H->H_local, scale, H->stream));
+            return GPT2Q_OK;
+        });
+        if (rc) return rc;
+    }
+    // ln_f + tied head for the last position of each sequence only.
+    RUN("layernorm", (double)ns * d * 8,
+        launch_layernorm(H->x, d, H->p_lastrow, H->h, d, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, ns, H->stream));
+    float* lg = H->logits + (size_t)s0 * H->cfg.vocab;
+    rc = linear(H, "linear_head", H->wte, H->h, d, ns, epi_store(lg, H->cfg.vocab, nullptr));
+    if (rc) return rc;
+    RUN("argmax", (double)ns * H->cfg.vocab * 4,
+        launch_argmax(lg, H->cfg.vocab, H->cfg.vocab, ns, H->d_next + s0, H->d_genlog + (size_t)s0 * H->cfg.n_ctx,
+                      H->p_lastpos, H->cfg.n_ctx, H->d_tok + s0, nullptr, H->stream));
+    // the staging buffer is reused by the next chunk
+    CK(cudaStreamSynchronize(H->stream));
+    if (H->prof) return flush_profile(H);
+    return GPT2Q_OK;
+}
+
+int do_prefill(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, const int32_t* slots, int n_seq) {
+    if (n_seq <= 0 || n_seq > H->cfg.max_seqs) return H->fail(GPT2Q_EARG, "n_seq out of range [1, max_seqs]");
+    if (!tokens || !offs) return H->fail(GPT2Q_EARG, "null tokens/seq_offsets");
+    if (offs[0] != 0) return H->fail(GPT2Q_EARG, "seq_offsets[0] must be 0");
+    std::vector<char> used(H->cfg.max_seqs, 0);
+    for (int s = 0; s < n_seq; ++s) {
+        const int T = offs[s + 1] - offs[s];
+        if (T <= 0 || T > H->cfg.n_ctx) return H->fail(GPT2Q_EARG, "prompt length out of range [1, n_ctx]");
+        const int slot = slots ? slots[s] : s;
+        if (slot < 0 || slot >= H->cfg.max_seqs || used[slot]) return H->fail(GPT2Q_EARG, "bad or repeated slot");
+        used[slot] = 1;
+    }
+    int rc = check_tokens(H, tokens, (size_t)offs[n_seq]);
+    if (rc) return rc;
+    int s0 = 0;
+    while (s0 < n_seq) {
+        int s1 = s0;
+        while (s1 < n_seq && offs[s1 + 1] - offs[s0] <= H->Mmax) s1++;
+        if (s1 == s0) return H->fail(GPT2Q_EARG, "prompt longer than max_tokens");
+        rc = prefill_chunk(H, tokens, offs, slots, s0, s1);
+        if (rc) return rc;
+        s0 = s1;
+    }
+    // decode state: next token at position T for every sequence
+    H->cur_n = n_seq;
+    H->hpos.assign(n_seq, 0);
+    H->hslot.assign(n_seq, 0);
+    rc = ensure_stage(H, (size_t)2 * n_seq);
+    if (rc) return rc;
+    for (int s = 0; s < n_seq; ++s) {
+        H->hpos[s] = offs[s + 1] - offs[s];
+        H->hslot[s] = slots ? slots[s] : s;
+        H->h_stage[s] = H->hpos[s];
+        H->h_stage[n_seq + s] = H->hslot[s];
+    }
+    CK(cudaMemcpyAsync(H->d_pos, H->h_stage, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->d_slot, H->h_stage + n_seq, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaStreamSynchronize(H->stream));
+    return GPT2Q_OK;
+}
+
+int do_decode(gpt2q_handle* H, const uint32_t* tok, const int32_t* pos, const int32_t* slots, int n_seq) {
+    if (n_seq <= 0 || n_seq > H->cfg.max_seqs) return H->fail(GPT2Q_EARG, "n_seq out of range [1, max_seqs]");
+    if (!tok || !pos) return H->fail(GPT2Q_EARG, "null tok/pos");
+    int rc = check_tokens(H, tok, (size_t)n_seq);
+    if (rc) return rc;
+    rc = ensure_stage(H, (size_t)3 * n_seq);
+    if (rc) return rc;
+    std::vector<char> used(H->cfg.max_seqs, 0);
+    H->hpos.assign(n_seq, 0);
+    H->hslot.assign(n_seq, 0);
+    for (int i = 0; i < n_seq; ++i) {
+        const int slot = slots ? slots[i] : i;
+        if (pos[i] < 0 || pos[i] >= H->cfg.n_ctx) return H->fail(GPT2Q_EARG, "pos out of range [0, n_ctx)");
+        if (slot < 0 || slot >= H->cfg.max_seqs || used[slot]) return H->fail(GPT2Q_EARG, "bad or repeated slot");
+        used[slot] = 1;
+        H->h_stage[i] = (int)tok[i];
+        H->h_stage[n_seq + i] = pos[i];
+        H->h_stage[2 * n_seq + i] = slot;
+        H->hpos[i] = pos[i];
+        H->hslot[i] = slot;
+    }
+    CK(cudaMemcpyAsync(H->d_tok, H->h_stage, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->d_pos, H->h_stage + n_seq, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->d_slot, H->h_stage + 2 * n_seq, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
+    H->cur_n = n_seq;
+    return run_decode_step(H, n_seq);
+}
+
+int read_outputs(gpt2q_handle* H, int n, const float* dlogits, float* logits, uint32_t* next) {
+    if (logits)
+        CK(cudaMemcpyAsync(logits, dlogits, (size_t)n * H->cfg.vocab * 4, cudaMemcpyDeviceToHost, H->stream));
+    if (next) CK(cudaMemcpyAsync(next, H->d_next, (size_t)n * 4, cudaMemcpyDeviceToHost, H->stream));
+    CK(cudaStreamSynchronize(H->stream));
+    return GPT2Q_OK;
+}
+
+const gpt2q_tensor_desc* find(const std::map<std::string, const gpt2q_tensor_desc*>& m, const std::string& n) {
+    auto it = m.find(n);
+    return it == m.end() ? nullptr : it->second;
+}
+
+// Column range [c0,c1) of a row-split projection for rank r (multiples of 32 along K).
+std::pair<int, int> k_split(int K, int parts_total, int r0, int r1, int unit) {
+    (void)parts_total;
+    return {r0 * unit, std::min(K, r1 * unit)};
+}
+
+int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int n_tensors, int device,
+                  int tp_size, int tp_rank, const void* nccl_id, gpt2q_handle** out) {
+    if (!cfg || !tensors || !out) {
+        g_create_error = "null argument";
+        return GPT2Q_EARG;
+    }
+    *out = nullptr;
+    std::unique_ptr<gpt2q_handle> H(new gpt2q_handle());
+    H->cfg = *cfg;
+    H->device = device;
+    H->tp_size = tp_size;
+    H->tp_rank = tp_rank;
+    auto bail = [&](int code) {
+        g_create_error = H->err;
+        gpt2q_destroy(H.release());
+        return code;
+    };
+    const gpt2q_config& c = H->cfg;
+    if (c.n_embd <= 0 || c.n_layer <= 0 || c.n_head <= 0 || c.n_ctx <= 0 || c.vocab <= 0 || c.max_seqs <= 0 ||
+        c.n_embd % c.n_head != 0) {
+        H->err = "invalid config";
+        return bail(GPT2Q_EARG);
+    }
+    H->hd = c.n_embd / c.n_head;
+    if (H->hd != 64) {
+        H->err = "head dim must be 64 (all GPT-2 sizes)";
+        return bail(GPT2Q_EUNSUP);
+    }
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || tp_size > c.n_head) {
+        H->err = "invalid tensor-parallel rank/size";
+        return bail(GPT2Q_EARG);
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        H->err = "cudaSetDevice failed";
+        return bail(GPT2Q_ECUDA);
+    }
+    if (cudaStreamCreateWithFlags(&H->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        H->err = "cudaStreamCreate failed";
+        return bail(GPT2Q_ECUDA);
+    }
+    H->stream = H->own_stream;
+    if (const char* e = std::getenv("GPT2Q_NO_GRAPH")) H->use_graphs = (e[0] == '0');
+
+    std::map<std::string, const gpt2q_tensor_desc*> by;
+    for (int i = 0; i < n_tensors; ++i) {
+        if (!tensors[i].name || !tensors[i].atom || !tensors[i].data) {
+            H->err = "tensor descriptor with null field";
+            return bail(GPT2Q_EARG);
+        }
+        by[tensors[i].name] = &tensors[i];
+    }
+    auto need = [&](const std::string& n) -> const gpt2q_tensor_desc* {
+        const gpt2q_tensor_desc* t = find(by, n);
+        if (!t) H->err = "missing tensor '" + n + "'";
+        return t;
+    };
+    const int d = c.n_embd, hd = H->hd;
+    // heads of this rank: contiguous, first (n_head % tp) ranks get one extra
+    const int hbase = c.n_head / tp_size, hrem = c.n_head % tp_size;
+    const int h0 = tp_rank * hbase + std::min(tp_rank, hrem);
+    const int hn = hbase + (tp_rank < hrem ? 1 : 0);
+    H->H_local = hn;
+    H->d_local = hn * hd;
+
+    const gpt2q_tensor_desc* t;
+    int rc;
+    if (!(t = need("wte.weight"))) return bail(GPT2Q_EARG);
+    if ((rc = upload_linear(H.get(), t, c.vocab, d, {{0, c.vocab}}, 0, d, &H->wte))) return bail(rc);
+    if (!(t = need("wpe.weight"))) return bail(GPT2Q_EARG);
+    if ((rc = upload_linear(H.get(), t, c.n_ctx, d, {{0, c.n_ctx}}, 0, d, &H->wpe))) return bail(rc);
+    if (!(t = need("ln_f.weight")) || (rc = upload_vec(H.get(), t, d, 0, d, &H->lnf_g))) return bail(t ? rc : GPT2Q_EARG);
+    if (!(t = need("ln_f.bias")) || (rc = upload_vec(H.get(), t, d, 0, d, &H->lnf_b))) return bail(t ? rc : GPT2Q_EARG);
+    H->layers.resize(c.n_layer);
+    int fc_rows = -1;
+    for (int l = 0; l < c.n_layer; ++l) {
+        LayerW& L = H->layers[l];
+        const std::string p = "h." + std::to_string(l) + ".";
+        auto vec = [&](const std::string& n, size_t len, size_t off, size_t cnt, float** dst) -> int {
+            const gpt2q_tensor_desc* tt = need(p + n);
+            if (!tt) return GPT2Q_EARG;
+            return upload_vec(H.get(), tt, len, off, cnt, dst);
+        };
+        if ((rc = vec("ln_1.weight", d, 0, d, &L.ln1_g)) || (rc = vec("ln_1.bias", d, 0, d, &L.ln1_b)) ||
+            (rc = vec("ln_2.weight", d, 0, d, &L.ln2_g)) || (rc = vec("ln_2.bias", d, 0, d, &L.ln2_b)))
+            return bail(rc);
+        // c_attn: rows [q | k | v], each d wide; keep this rank's heads of each block.
+        if (!(t = need(p + "attn.c_attn.weight"))) return bail(GPT2Q_EARG);
+        std::vector<std::pair<int, int>> qkv_rows = {{h0 * hd, hn * hd}, {d + h0 * hd, hn * hd}, {2 * d + h0 * hd, hn * hd}};
+        if ((rc = upload_linear(H.get(), t, 3 * d, d, qkv_rows, 0, d, &L.attn))) return bail(rc);
+        {
+            const gpt2q_tensor_desc* tb = need(p + "attn.c_attn.bias");
+            if (!tb) return bail(GPT2Q_EARG);
+            // three slices of the bias, concatenated
+            float* dst = H->dalloc<float>((size_t)3 * hn * hd * 4);
+            if (!dst) return bail(GPT2Q_EOOM);
+            for (int k = 0; k < 3; ++k) {
+                float* part = nullptr;
+                if ((rc = upload_vec(H.get(), tb, 3 * d, (size_t)k * d + h0 * hd, (size_t)hn * hd, &part))) return bail(rc);
+                if (cudaMemcpy(dst + (size_t)k * hn * hd, part, (size_t)hn * hd * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+                    return bail(GPT2Q_ECUDA);
+            }
+            L.attn.bias = dst;
+            H->vec_by_name[p + "attn.c_attn.bias"] = {dst, (size_t)3 * hn * hd};
+        }
+        // attn c_proj: [d, d], keep this rank's K columns (its heads' outputs).
+        if (!(t = need(p + "attn.c_proj.weight"))) return bail(GPT2Q_EARG);
+        if ((rc = upload_linear(H.get(), t, d, d, {{0, d}}, h0 * hd, (h0 + hn) * hd, &L.proj))) return bail(rc);
+        if ((rc = vec("attn.c_proj.bias", d, 0, d, &L.proj.bias))) return bail(rc);
+        // mlp c_fc [inter, d]: row split in multiples of 32.
+        if (!(t = need(p + "mlp.c_fc.weight"))) return bail(GPT2Q_EARG);
+        if (t->ndim != 2) {
+            H->err = "mlp.c_fc.weight must be 2-D";
+            return bail(GPT2Q_EARG);
+        }
+        const int inter = (int)t->shape[0];
+        if (fc_rows >= 0 && inter != fc_rows) {
+            H->err = "c_fc rows differ between layers";
+            return bail(GPT2Q_EARG);
+        }
+        fc_rows = inter;
+        if (inter % (32 * tp_size) != 0 && tp_size > 1) {
+            H->err = "c_fc rows must split into multiples of 32";
+            return bail(GPT2Q_EUNSUP);
+        }
+        const int fper = inter / tp_size;
+        const int f0 = tp_rank * fper;
+        if ((rc = upload_linear(H.get(), t, inter, d, {{f0, fper}}, 0, d, &L.fc))) return bail(rc);
+        if ((rc = vec("mlp.c_fc.bias", inter, f0, fper, &L.fc.bias))) return bail(rc);
+        if (!(t = need(p + "mlp.c_proj.weight"))) return bail(GPT2Q_EARG);
+        if ((rc = upload_linear(H.get(), t, d, inter, {{0, d}}, f0, f0 + fper, &L.mproj))) return bail(rc);
+        if ((rc = vec("mlp.c_proj.bias", d, 0, d, &L.mproj.bias))) return bail(rc);
+        H->fc_local = fper;
+    }
+    (void)k_split;
+
+    // KV arena [slot][layer][K|V][head][n_ctx][hd]
+    H->kv.hd = hd;
+    H->kv.head_stride = (size_t)c.n_ctx * hd;
+    H->kv.sel_stride = (size_t)hn * H->kv.head_stride;
+    H->kv.layer_stride = 2 * H->kv.sel_stride;
+    H->kv.slot_stride = (size_t)c.n_layer * H->kv.layer_stride;
+    H->kv.base = H->dalloc<float>(H->kv.slot_stride * c.max_seqs * 4);
+    if (!H->kv.base) {
+        H->err = "cudaMalloc KV arena (" + std::to_string(H->kv.slot_stride * c.max_seqs * 4) + " bytes)";
+        return bail(GPT2Q_EOOM);
+    }
+    if (cudaMemset(H->kv.base, 0, H->kv.slot_stride * c.max_seqs * 4) != cudaSuccess) return bail(GPT2Q_ECUDA);
+
+    const int max_tokens = c.max_tokens > 0 ? c.max_tokens : 8192;
+    H->Mmax = std::max(c.max_seqs, max_tokens);
+    const size_t M = (size_t)H->Mmax;
+    H->max_tiles = (int)(M / 64 + c.max_seqs + 1);
+    H->x = H->dalloc<float>(M * d * 4);
+    H->h = H->dalloc<float>(M * d * 4);
+    H->qb = H->dalloc<float>(M * H->d_local * 4);
+    H->att = H->dalloc<float>(M * H->d_local * 4);
+    H->f = H->dalloc<float>(M * H->fc_local * 4);
+    H->logits = H->dalloc<float>((size_t)c.max_seqs * c.vocab * 4);
+    H->p_tok = H->dalloc<uint32_t>(M * 4);
+    H->p_pos = H->dalloc<int>(M * 4);
+    H->p_slot = H->dalloc<int>(M * 4);
+    H->p_lastrow = H->dalloc<int>((size_t)c.max_seqs * 4);
+    H->p_lastpos = H->dalloc<int>((size_t)c.max_seqs * 4);
+    H->p_tiles = H->dalloc<AttnTile>((size_t)H->max_tiles * sizeof(AttnTile));
+    H->d_tok = H->dalloc<uint32_t>((size_t)c.max_seqs * 4);
+    H->d_next = H->dalloc<uint32_t>((size_t)c.max_seqs * 4);
+    H->d_pos = H->dalloc<int>((size_t)c.max_seqs * 4);
+    H->d_slot = H->dalloc<int>((size_t)c.max_seqs * 4);
+    H->d_genlog = H->dalloc<uint32_t>((size_t)c.max_seqs * c.n_ctx * 4);
+    if (tp_size > 1) H->tp_red = H->dalloc<float>(M * d * 4);
+    if (!H->x || !H->h || !H->qb || !H->att || !H->f || !H->logits || !H->p_tok || !H->p_pos || !H->p_slot ||
+        !H->p_lastrow || !H->p_lastpos || !H->p_tiles || !H->d_tok || !H->d_next || !H->d_pos || !H->d_slot ||
+        !H->d_genlog || (tp_size > 1 && !H->tp_red)) {
+        H->err = "cudaMalloc workspace";
+        return bail(GPT2Q_EOOM);
+    }
+    if (cudaMemset(H->d_genlog, 0xff, (size_t)c.max_seqs * c.n_ctx * 4) != cudaSuccess) return bail(GPT2Q_ECUDA);
+    if (gemm_init(H->gemm, device) != 0) {
+        H->err = "gemm init failed";
+        return bail(GPT2Q_ECUDA);
+    }
+    if (tp_size > 1) {
+        H->tp = tp_create(tp_size, tp_rank, nccl_id, device);
+        if (!H->tp || tp_last_error(H->tp)[0]) {
+            H->err = std::string("NCCL init: ") + (H->tp ? tp_last_error(H->tp) : "failed");
+            return bail(GPT2Q_ENCCL);
+        }
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        H->err = "device sync after upload failed";
+        return bail(GPT2Q_ECUDA);
+    }
+    *out = H.release();
+    return GPT2Q_OK;
+}
+
+}  // namespace
+
+// =================================================================== C-ABI
+extern "C" {
+
+int gpt2q_create(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int n_tensors, int device,
+                 gpt2q_handle** out) {
+    return create_common(cfg, tensors, n_tensors, device, 1, 0, nullptr, out);
+}
+
+int gpt2q_create_tp(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int n_tensors, int device,
+                    int tp_size, int tp_rank, const void* nccl_id, gpt2q_handle** out) {
+    if (tp_size > 1 && !nccl_id) {
+        g_create_error = "nccl_id required for tp_size > 1";
+        return GPT2Q_EARG;
+    }
+    return create_common(cfg, tensors, n_tensors, device, tp_size, tp_rank, nccl_id, out);
+}
+
+void gpt2q_destroy(gpt2q_handle* H) {
+    if (!H) return;
+    cudaSetDevice(H->device);
+    if (H->stream) cudaStreamSynchronize(H->stream);
+    for (auto& g : H->dec_graphs) cudaGraphExecDestroy(g.second.first);
+    H->dec_graphs.clear();
+    for (auto& r : H->prof_pending) {
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    if (H->tp) tp_destroy(H->tp);
+    gemm_destroy(H->gemm);
+    for (auto& a : H->allocs) cudaFree(a.p);
+    if (H->h_stage) cudaFreeHost(H->h_stage);
+    if (H->own_stream) cudaStreamDestroy(H->own_stream);
+    delete H;
+}
+
+const char* gpt2q_last_error(const gpt2q_handle* H) { return H ? H->err.c_str() : g_create_error.c_str(); }
+
+int gpt2q_reset_kv(gpt2q_handle* H, const int32_t* slots, int n_slots) {
+    if (!H) return GPT2Q_EARG;
+    CK(cudaSetDevice(H->device));
+    if (!slots) {
+        CK(cudaMemsetAsync(H->kv.base, 0, H->kv.slot_stride * H->cfg.max_seqs * 4, H->stream));
+    } else {
+        for (int i = 0; i < n_slots; ++i) {
+            if (slots[i] < 0 || slots[i] >= H->cfg.max_seqs) return H->fail(GPT2Q_EARG, "slot out of range");
+            CK(cudaMemsetAsync(H->kv.base + (size_t)slots[i] * H->kv.slot_stride, 0, H->kv.slot_stride * 4, H->stream));
+        }
+    }
+    CK(cudaStreamSynchronize(H->stream));
+    return GPT2Q_OK;
+}
+
+int gpt2q_step(gpt2q_handle* H, uint32_t tok, int32_t pos, float* logits) {
+    if (!H) return GPT2Q_EARG;
+    CK(cudaSetDevice(H->device));
+    const int32_t slot = 0;
+    int rc = do_decode(H, &tok, &pos, &slot, 1);
+    if (rc) return rc;
+    return read_outputs(H, 1, H->logits, logits, nullptr);
+}
+
+int gpt2q_decode(gpt2q_handle* H, const uint32_t* tok, const int32_t* pos, const int32_t* slots, int n_seq,
+                 float* logits, uint32_t* next_tok) {
+    if (!H) return GPT2Q_EARG;
+    CK(cudaSetDevice(H->device));
+    int rc = do_decode(H, tok, pos, slots, n_seq);
+    if (rc) return rc;
+    return read_outputs(H, n_seq, H->logits, logits, next_tok);
+}
+
+int gpt2q_prefill(gpt2q_handle* H, const uint32_t* tokens, const int32_t* seq_offsets, const int32_t* slots,
+                  int n_seq, float* logits_last, uint32_t* next_tok) {
+    if (!H) return GPT2Q_EARG;
+    CK(cudaSetDevice(H->device));
+    int rc = do_prefill(H, tokens, seq_offsets, slots, n_seq);
+    if (rc) return rc;
+    return read_outputs(H, n_seq, H->logits, logits_last, next_tok);
+}
+
+int gpt2q_decode_steps(gpt2q_handle* H, int steps, uint32_t* out_tokens) {
+    if (!H) return GPT2Q_EARG;
+    if (steps < 0) return H->fail(GPT2Q_EARG, "steps < 0");
+    if (H->cur_n <= 0) return H->fail(GPT2Q_EARG, "no sequences to continue (call prefill or decode first)");
+    CK(cudaSetDevice(H->device));
+    const int B = H->cur_n;
+    std::vector<int> start = H->hpos;
+    for (int b = 0; b < B; ++b)
+        if (H->hpos[b] + steps > H->cfg.n_ctx)
+            return H->fail(GPT2Q_EARG, "decode_steps would run past n_ctx");
+    for (int s = 0; s < steps; ++s) {
+        int rc = run_decode_step(H, B);
+        if (rc) return rc;
+    }
+    if (out_tokens && steps > 0) {
+        // genlog[b][p] holds the token predicted from position p
+        std::vector<uint32_t> row(H->cfg.n_ctx);
+        CK(cudaStreamSynchronize(H->stream));
+        for (int b = 0; b < B; ++b) {
+            CK(cudaMemcpy(row.data() + start[b], H->d_genlog + (size_t)b * H->cfg.n_ctx + start[b],
+                          (size_t)steps * 4, cudaMemcpyDeviceToHost));
+            for (int s = 0; s < steps; ++s) out_tokens[(size_t)s * B + b] = row[start[b] + s];
+        }
+    }
+    CK(cudaStreamSynchronize(H->stream));
+    return GPT2Q_OK;
+}
+
+int gpt2q_generate_greedy(gpt2q_handle* H, const uint32_t* tokens, const int32_t* seq_offsets, int n_seq, int steps,
+                          uint32_t* out) {
+    if (!H) return GPT2Q_EARG;
+    if (steps <= 0 || !out) return H->fail(GPT2Q_EARG, "steps must be >= 1 and out non-null");
+    CK(cudaSetDevice(H->device));
+    std::vector<uint32_t> first(n_seq > 0 ? n_seq : 1);
+    int rc = gpt2q_prefill(H, tokens, seq_offsets, nullptr, n_seq, nullptr, first.data());
+    if (rc) return rc;
+    for (size_t i = 0; i < (size_t)n_seq * steps; ++i) out[i] = UINT32_MAX;
+    for (int s = 0; s < n_seq; ++s) out[(size_t)s * steps] = first[s];
+    // sequence s may generate tokens predicted from positions T_s-1 .. n_ctx-1
+    std::vector<int> room(n_seq);
+    int common = steps - 1;
+    for (int s = 0; s < n_seq; ++s) {
+        const int T = seq_offsets[s + 1] - seq_offsets[s];
+        room[s] = std::min(steps - 1, H->cfg.n_ctx - T);
+        common = std::min(common, room[s]);
+    }
+    if (common > 0) {
+        std::vector<uint32_t> buf((size_t)common * n_seq);
+        rc = gpt2q_decode_steps(H, common, buf.data());
+        if (rc) return rc;
+        for (int k = 0; k < common; ++k)
+            for (int s = 0; s < n_seq; ++s) out[(size_t)s * steps + 1 + k] = buf[(size_t)k * n_seq + s];
+    }
+    // sequences with more room continue alone (the others stopped at n_ctx, gpt2.rs:374)
+    for (int k = common; k < steps - 1; ++k) {
+        std::vector<uint32_t> tk;
+        std::vector<int32_t> ps, sl;
+        std::vector<int> who;
+        for (int s = 0; s < n_seq; ++s) {
+            if (k < room[s]) {
+                const int T = seq_offsets[s + 1] - seq_offsets[s];
+                tk.push_back(out[(size_t)s * steps + k]);
+                ps.push_back(T + k);
+                sl.push_back(s);
+                who.push_back(s);
+            }
+        }
+        if (who.empty()) break;
+        std::vector<uint32_t> nx(who.size());
+        rc = gpt2q_decode(H, tk.data(), ps.data(), sl.data(), (int)who.size(), nullptr, nx.data());
+        if (rc) return rc;
+        for (size_t i = 0; i < who.size(); ++i) out[(size_t)who[i] * steps + 1 + k] = nx[i];
+    }
+    return GPT2Q_OK;
+}
+
+int gpt2q_dequant(gpt2q_handle* H, const char* name, float* out, uint64_t n) {
+    if (!H || !name || !out) return GPT2Q_EARG;
+    CK(cudaSetDevice(H->device));
+    auto it = H->lin_by_name.find(name);
+    if (it != H->lin_by_name.end()) {
+        const QW& w = it->second->w;
+        if ((uint64_t)w.rows * w.cols != n) return H->fail(GPT2Q_EARG, "dequant: n does not match tensor size");
+        float* tmp = nullptr;
+        CK(cudaMalloc(&tmp, n * 4));
+        cudaError_t e = launch_dequant(w, tmp, H->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(out, tmp, n * 4, cudaMemcpyDeviceToHost, H->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(H->stream);
+        cudaFree(tmp);
+        if (e != cudaSuccess) return H->fail(GPT2Q_ECUDA, std::string("dequant: ") + cudaGetErrorString(e));
+        return GPT2Q_OK;
+    }
+    auto iv = H->vec_by_name.find(name);
+    if (iv != H->vec_by_name.end()) {
+        if (iv->second.second != n) return H->fail(GPT2Q_EARG, "dequant: n does not match tensor size");
+        CK(cudaMemcpy(out, iv->second.first, n * 4, cudaMemcpyDeviceToHost));
+        return GPT2Q_OK;
+    }
+    return H->fail(GPT2Q_EARG, std::string("dequant: unknown tensor ") + name);
+}
+
+uint64_t gpt2q_launches(const gpt2q_handle* H) { return H ? H->launches : 0; }
+
+int gpt2q_set_stream(gpt2q_handle* H, void* stream) {
+    if (!H) return GPT2Q_EARG;
+    CK(cudaStreamSynchronize(H->stream));
+    H->stream = stream ? reinterpret_cast<cudaStream_t>(stream) : H->own_stream;
+    // graphs were instantiated for launch on any stream; they stay valid
+    return GPT2Q_OK;
+}
+
+int gpt2q_sync(gpt2q_handle* H) {
+    if (!H) return GPT2Q_EARG;
+    CK(cudaSetDevice(H->device));
+    CK(cudaStreamSynchronize(H->stream));
+    return GPT2Q_OK;
+}
+
+int gpt2q_profile(gpt2q_handle* H, int enable) {
+    if (!H) return GPT2Q_EARG;
+    int rc = flush_profile(H);
+    if (rc) return rc;
+    H->prof = enable != 0;
+    if (H->prof) H->prof_agg.clear();
+    return GPT2Q_OK;
+}
+
+int gpt2q_profile_read(gpt2q_handle* H, char* json, size_t cap) {
+    if (!H || !json || cap == 0) return GPT2Q_EARG;
+    int rc = flush_profile(H);
+    if (rc) return rc;
+    std::string s = "{";
+    bool first = true;
+    for (auto& kv : H->prof_agg) {
+        char buf[256];
+        std::snprintf(buf, sizeof buf, "%s\"%s\": {\"launches\": %llu, \"ms\": %.6f, \"bytes\": %.0f}", first ? "" : ", ",
+                      kv.first.c_str(), (unsigned long long)kv.second.launches, kv.second.ms, kv.second.bytes);
+        s += buf;
+        first = false;
+    }
+    s += "}";
+    if (s.size() + 1 > cap) return H->fail(GPT2Q_EARG, "profile_read: buffer too small");
+    std::memcpy(json, s.c_str(), s.size() + 1);
+    return GPT2Q_OK;
+}
+
+}  // extern "C"

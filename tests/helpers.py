@@ -1,0 +1,35 @@
+"""Shared builders for the tests: small GPT-2 shapes, packs and oracle engines."""
+from __future__ import annotations
+
+import functools
+
+import numpy as np
+
+from oracle import oracle as O
+from smelt_b200 import pack as P
+from smelt_b200 import synth
+
+# Small shapes that keep the GPT-2 structure (head dim 64) and run in milliseconds.
+TINY = P.Meta(n_embd=128, n_layer=2, n_head=2, n_ctx=64, vocab=97)
+MINI = P.Meta(n_embd=256, n_layer=3, n_head=4, n_ctx=128, vocab=1031)
+POLICIES = ["auto", "q4auto", "core.f16", "f32"]
+
+
+@functools.lru_cache(maxsize=None)
+def hf(meta: P.Meta, seed: int = 0, bias_std: float = 0.0):
+    return synth.hf_weights(meta, seed=seed, bias_std=bias_std)
+
+
+@functools.lru_cache(maxsize=None)
+def make_pack(meta: P.Meta, policy: str = "auto", seed: int = 0, bias_std: float = 0.0) -> P.Pack:
+    return P.from_hf(meta, hf(meta, seed, bias_std), policy)
+
+
+def oracle_engine(pk: P.Pack, threads: int = 8) -> O.Engine:
+    return O.Engine(pk.meta.as_dict(), {n: (t.shape, t.atom, t.data) for n, t in pk.tensors.items()}, threads)
+
+
+def oracle_prefix_logits(eng: O.Engine, ids) -> np.ndarray:
+    """Logits after every prompt position, by per-token Engine::step (gpt2.rs:373-381)."""
+    kv = eng.empty_kv()
+    return np.stack([eng.step(int(t), p, kv) for p, t in enumerate(ids)])
