@@ -1,0 +1,387 @@
+"""Decode throughput of the quantized GPT-2 forward on B200.
+
+    python bench.py [--gpus N --steps K --warmup W] [--config NAME] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+A step is one decode step of a batch of sequences (one new token per sequence).
+Default workload (`small-int8-b32`): GPT-2 small, int8 per-group-32 weights
+(core.i8.b32.f16scale) from seeded N(0, 0.02) weights, 32 sequences per GPU with
+128-token prompts (ids uniform in [0, 50257)), decoding at positions 128..255.
+Sequences are independent, so N GPUs each run their own 32 sequences with no
+data-path collective (weak scaling).
+
+Printed JSON (rank 0, one line):
+  value      decode tokens/s over all ranks with inputs resident in HBM: the timed
+             region replays K device-side decode steps (CUDA graph per step, greedy
+             argmax feeding the next step), CUDA events on the launch stream,
+             max over ranks;
+  e2e        the same metric through the public C-ABI call gpt2q_decode with host
+             buffers: every step copies its tokens/positions/slots host->device and
+             reads the next tokens device->host inside the timed region;
+  roofline   the dominant kernel of an eager profiled pass: algorithmic bytes per
+             launch / CUDA-event duration, against MEASURED_PEAKS.json hbm_gbs;
+  cpu_baseline  the C++ oracle (restatement of the reference CPU forward) timed on
+             the host cores on a bounded sample (rank 0, N=1 only).
+`--impl reference` times only the reference CPU implementation (the oracle port;
+the Rust reference cannot be built here) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (model, policy, batch per rank, prompt len, decode steps, scaling)
+    "small-int8-b32": ("small", "auto", 32, 128, 128, "weak"),
+    "small-int8-b1": ("small", "auto", 1, 64, 64, "weak"),
+    "small-int4-b256": ("small", "q4auto", 256, 264, 256, "strong"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="small-int8-b32", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-steps", type=int, default=24)
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def algorithmic_step_bytes(pk, positions, d_local=None) -> float:
+    """Bytes one decode step must move: every 2-D weight once, fp32 LN/bias vectors,
+    per sequence the K/V rows 0..pos read and row pos written, embed rows."""
+    meta = pk.meta
+    w = sum(t.data.nbytes for t in pk.tensors.values() if len(t.shape) == 2)
+    vec = sum(t.numel * 4 for t in pk.tensors.values() if len(t.shape) == 1)
+    d = meta.n_embd
+    kv = sum(2.0 * meta.n_layer * d * 4 * (p + 1) + 2.0 * meta.n_layer * d * 4 for p in positions)
+    row_bytes = pk.tensors["wte.weight"].data.nbytes / meta.vocab + pk.tensors["wpe.weight"].data.nbytes / meta.n_ctx
+    return w + vec + kv + len(positions) * row_bytes
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_pack(model: str, policy: str):
+    from smelt_b200 import pack as P
+    from smelt_b200 import synth
+
+    meta = P.CONFIGS[model]
+    return synth.synthetic_pack(meta, policy, seed=0)
+
+
+def prompts_for(rank: int, n: int, plen: int, vocab: int, ragged: bool):
+    from smelt_b200 import synth
+
+    if ragged:
+        lens = synth.ragged_lengths(n, 16, 512, seed=2 + 1000 * rank)
+    else:
+        lens = np.full(n, plen, np.int32)
+    ids = synth.prompt_ids(int(lens.sum()), vocab, seed=1 + 1000 * rank)
+    out, o = [], 0
+    for L in lens:
+        out.append(ids[o:o + L])
+        o += L
+    return out
+
+
+def cpu_baseline(pk, plen: int, sample_steps: int, threads: int):
+    """Oracle (reference CPU forward restated in C++) on a bounded decode sample."""
+    from oracle import oracle as O
+
+    eng = O.Engine(pk.meta.as_dict(), {n: (t.shape, t.atom, t.data) for n, t in pk.tensors.items()}, threads)
+    kv = eng.empty_kv()  # attention cost depends on the position, not on cache contents
+    eng.step(1, plen, kv)  # warm-up
+    t0 = time.perf_counter()
+    for s in range(sample_steps):
+        eng.step((7 * s + 3) % pk.meta.vocab, plen + 1 + s, kv)
+    dt = time.perf_counter() - t0
+    return sample_steps / dt, dt
+
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    model, policy, batch, plen, dec, _scaling = wl
+    pk = build_pack(model, policy)
+    threads = os.cpu_count() or 8
+    from oracle import oracle as O
+
+    eng = O.Engine(pk.meta.as_dict(), {n: (t.shape, t.atom, t.data) for n, t in pk.tensors.items()}, threads)
+    # each step: one decode token for each of 2 sequences (sequential, as the reference runs batches)
+    per_step = 2
+    kvs = [eng.empty_kv() for _ in range(per_step)]
+    for w in range(args.warmup):
+        for j in range(per_step):
+            eng.step(1, plen + w % dec, kvs[j])
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        for j in range(per_step):
+            eng.step((s * 31 + j) % pk.meta.vocab, plen + (args.warmup + s) % dec, kvs[j])
+    dt = time.perf_counter() - t0
+    tok_s = args.steps * per_step / dt
+    line = {
+        "impl": "reference", "metric": "decode tokens/s", "value": tok_s, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": wl[5],
+        "vs_baseline": None, "dtype": "int8xfp32" if policy == "auto" else "int4xfp32", "data": "synthetic",
+        "config": {"workload": args.config, "model": f"gpt2-{model}", "weights": policy, "prompt": plen},
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps x {per_step} sequences x 1 token at positions "
+                                   f"{plen}..{plen + dec - 1}, oracle C++ restatement of gpt2.rs step, "
+                                   f"{threads}-thread row split per matmul"},
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    wl = WORKLOADS[args.config]
+    if args.impl == "reference":
+        run_reference(args, wl)
+        return
+    import torch
+
+    model, policy, batch, plen, dec, scaling = wl
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from smelt_b200.gpu import Gpu
+
+    pk = build_pack(model, policy)
+    meta = pk.meta
+    if scaling == "strong":
+        n_local = batch // world + (1 if rank < batch % world else 0)
+    else:
+        n_local = batch
+    ragged = args.config == "small-int4-b256"
+    prompts = prompts_for(rank, n_local, plen, meta.vocab, ragged)
+    max_plen = max(p.size for p in prompts)
+    g = Gpu(pk, device=local, max_seqs=n_local, max_tokens=max(8192, max_plen))
+    stream = torch.cuda.Stream(device=dev)
+    g.set_stream(stream.cuda_stream)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+
+    # ---- setup: prefill prompts (untimed), warm-up decode steps ----
+    g.prefill(prompts)
+    start_pos = np.array([p.size for p in prompts])
+    room = int(meta.n_ctx - start_pos.max())
+    span = min(dec, room)
+    done = 0  # decode steps taken since prefill
+
+    rewind_tok = np.array([p[-1] for p in prompts], np.uint32)
+    rewind_slots = np.arange(n_local, dtype=np.int32)
+
+    def run_steps(k):
+        # K decode steps cycling over positions start..start+span-1; the step that wraps
+        # back to the first decode position is itself a (host-fed) decode step.
+        nonlocal done
+        while k > 0:
+            if done >= span:
+                g.decode(rewind_tok, start_pos.astype(np.int32), rewind_slots)
+                done = 1
+                k -= 1
+                continue
+            n = min(k, span - done)
+            g.decode_steps(n, n_local, want_tokens=False)
+            done += n
+            k -= n
+
+    run_steps(max(args.warmup, 3))
+    barrier()
+
+    # ---- timed region: K device-resident decode steps ----
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    gpu_id = gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}"
+    positions_timed = []
+    l0 = g.launches
+    with ClockSampler(gpu_id) as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        # positions each timed step sees (for the roofline bytes)
+        d0 = done
+        for s in range(args.steps):
+            dd = (d0 + s) % span if span else 0
+            positions_timed.append(start_pos + dd)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+        run_steps(args.steps)
+        with torch.cuda.stream(stream):
+            ev1.record(stream)
+        barrier()
+        ms = ev0.elapsed_time(ev1)
+        # keep sampling clocks for at least ~1 s of the same work when the timed region was short
+        t_extra = time.perf_counter()
+        while time.perf_counter() - t_extra < max(0.0, 1.0 - ms / 1e3):
+            run_steps(min(args.steps, 32))
+            torch.cuda.synchronize()
+    launches = g.launches - l0
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    total_tokens = n_local * args.steps * (world if scaling == "weak" else 1)
+    if scaling == "strong":
+        total_tokens = batch * args.steps
+    value = total_tokens / (ms_max / 1e3)
+
+    # ---- e2e: the public C-ABI call with host buffers, H2D + D2H every step ----
+    g.set_stream(None)
+    g.prefill(prompts)
+    tok = np.ascontiguousarray(g.decode_steps(1, n_local)[0])
+    pos = (start_pos + 1).astype(np.int32)
+    slots = np.arange(n_local, dtype=np.int32)
+    e2e_steps = min(args.steps, room - 1)
+    barrier()
+    t0 = time.perf_counter()
+    for s in range(e2e_steps):
+        tok = g.decode(tok, pos + s, slots)
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(e2e_t, op=torch.distributed.ReduceOp.MAX)
+    e2e_tokens = n_local * e2e_steps * (world if scaling == "weak" else 1)
+    if scaling == "strong":
+        e2e_tokens = batch * e2e_steps
+    e2e_value = e2e_tokens / float(e2e_t.item())
+
+    # ---- roofline: eager profiled decode steps (CUDA events around every kernel) ----
+    g.prefill(prompts)
+    g.profile(True)
+    g.decode_steps(4, n_local, want_tokens=False)
+    prof = g.profile_read()
+    g.profile(False)
+    top = max(prof.items(), key=lambda kv: kv[1]["ms"])
+    name, rec = top
+    per_launch_bytes = rec["bytes"] / rec["launches"]
+    per_launch_ms = rec["ms"] / rec["launches"]
+    hbm, peak_kind = peaks()
+    achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tfile):
+        with open(tfile) as f:
+            tj = json.load(f)
+        traffic = tj.get(args.config, {}).get(name)
+    step_bytes = statistics.mean(algorithmic_step_bytes(pk, p) for p in positions_timed)
+
+    line = {
+        "metric": "decode tokens/s (GPT-2 small int8)" if policy == "auto" else "decode tokens/s (GPT-2 small int4)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "dtype": "int8xfp32" if policy == "auto" else "int4xfp32", "data": "synthetic",
+        "config": {"workload": args.config, "model": f"gpt2-{model}", "weights": policy,
+                   "batch_per_gpu": n_local, "global_batch": n_local * world if scaling == "weak" else batch,
+                   "prompt": plen, "decode_positions": f"{int(start_pos.min())}..{int(start_pos.max()) + span - 1}",
+                   "kv_dtype": "fp32", "parallelism": f"sequence-sharded x{world}",
+                   "l2": f"inputs larger than L2: {step_bytes / 1e6:.0f} MB moved per step vs 126 MB L2"},
+        "step_hbm_fraction": (step_bytes / (ms_max / args.steps / 1e3) / 1e9) / hbm,
+        "roofline": {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_kind,
+                     "bytes_per_launch": per_launch_bytes, "ms_per_launch": per_launch_ms},
+        "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 4)} for k, v in prof.items()},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": n_local * 12,
+                "d2h_bytes_per_step": n_local * 4, "api": "gpt2q_decode (host tok/pos/slot in, next tokens out)"},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = min(8, os.cpu_count() or 8)
+        tok_s, dt = cpu_baseline(pk, plen, args.cpu_sample_steps, threads)
+        line["cpu_baseline"] = {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": f"{args.cpu_sample_steps} single-sequence decode steps at positions "
+                                          f"{plen + 1}..{plen + args.cpu_sample_steps} ({dt:.1f} s), oracle C++ "
+                                          f"restatement of the reference step, {threads}-thread row split per matmul"}
+    g.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,26 +1,648 @@
-// Tensor-core linear: placeholder until the tcgen05 kernel lands; usable() is false
-// so every linear runs on the CUDA-core path.
+// Tensor-core dequant-fused linear for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   out[m][n] = epilogue( sum_k X[m][k] * deq(W)[n][k] )
+//
+// Precision: each 16-wide k-step issues three MMAs, A_hi*B_hi + A_hi*B_lo + A_lo*B_hi,
+// where x = x_hi + x_lo and w' = w * 2^P = w_hi + w_lo are fp16 pairs. w' = q * f16(scale)
+// * 2^P is exact in fp32 and the pair is exact for it (the power-of-two prescale keeps
+// w_lo a normal fp16), x keeps ~22 bits, and the dropped lo*lo term is ~2^-22 relative:
+// fp32-class results from the fp16 tensor pipe with fp32 TMEM accumulation.
+//
+// The MMA is "swap-AB": weight rows are the MMA M dimension (128 TMEM lanes) and tokens
+// are N (BN columns), so a decode batch of 32 still fills M, and the epilogue's stores
+// along n are coalesced.
+//
+// Two weight sources (template PRESPLIT):
+//  - decode (false): int8 / int4 tiles stream from HBM and are dequantised in the CTA.
+//      warp 0     TMA producer of raw weight tiles [128 rows x 64 k] (64- or 32-byte swizzle)
+//      warps 1-4  one weight row each: q -> w' -> (hi, lo), written into 128-byte-swizzled
+//                 K-major operand tiles; afterwards the epilogue
+//  - prefill (true): one-time exact fp16 hi/lo copies of the weight are TMA-loaded
+//      directly (compute-bound regime; no per-CTA conversion).
+//   warp 5   one thread issues tcgen05.mma kind::f16 into the fp32 TMEM accumulator
+//   warp 6   TMA producer of the activation tiles X_hi / X_lo
+//
+// Split-K (few row tiles, small batch): the splits of one output tile form a thread-block
+// cluster; each CTA parks its partial tile in shared memory and CTA r reduces columns
+// r, r+S, ... by reading all S partials over distributed shared memory in fixed order
+// (deterministic, no global round trip).
+//
+// Programmatic dependent launch: weight loads and their conversion start before the
+// previous kernel has finished; activations are only touched after griddepcontrol.wait.
+// All mbarrier waits are bounded (tcgen05.cuh); a timeout sets the error word.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstdlib>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
 #include "gemm.h"
+#include "tcgen05.cuh"
 
 namespace gpt2q {
 
-bool GemmPlan::usable(const QW& w, int M) const {
-    (void)w;
-    return enabled && M >= min_m;
+namespace {
+
+constexpr int BM = 128, BK = 64, THREADS = 224;
+constexpr int RAW_STAGES = 4;
+constexpr int MAX_SPLITS = 8;  // portable cluster size
+
+template <int BN, bool PRESPLIT>
+struct Cfg {
+    static constexpr int OS = BN >= 256 ? 2 : (BN >= 128 ? 3 : 4);  // operand stages
+    static constexpr int A_BYTES = BM * 128;                          // one of hi/lo
+    static constexpr int B_BYTES = BN * 128;                          // one of hi/lo
+    static constexpr int RAW_BYTES = PRESPLIT ? 0 : BM * 64;          // int8 tile (int4 uses half)
+    static constexpr int OFF_A = 0;
+    static constexpr int OFF_B = OFF_A + OS * 2 * A_BYTES;
+    static constexpr int OFF_RAW = OFF_B + OS * 2 * B_BYTES;
+    static constexpr int OFF_BAR = OFF_RAW + RAW_STAGES * RAW_BYTES;
+    static constexpr int N_BAR = 2 * RAW_STAGES + 2 * OS + 1;
+    static constexpr int SMEM = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem slot, flag, alignment slack
+    // the split-K partial tile [BN][128] fp32 reuses the operand rings once every MMA is done
+    static_assert(BN * BM * 4 <= OFF_RAW, "partial tile must fit in the operand rings");
+};
+
+struct TcParams {
+    QW w;
+    int M, nkb_total, kb_per_split, splits;
+    float post;  // 2^-P
+    float pre;   // 2^P
+    Epi epi;
+    int* err;
+};
+
+__device__ __forceinline__ uint4 pack_hi_lo(const float* f, uint4& lo_out) {
+    uint4 hi, lo;
+    uint32_t* h = &hi.x;
+    uint32_t* l = &lo.x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __half2 hh = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        float2 back = __half22float2(hh);
+        __half2 ll = __floats2half2_rn(f[2 * i] - back.x, f[2 * i + 1] - back.y);
+        h[i] = *reinterpret_cast<uint32_t*>(&hh);
+        l[i] = *reinterpret_cast<uint32_t*>(&ll);
+    }
+    lo_out = lo;
+    return hi;
 }
 
-int gemm_init(GemmPlan& p, int device) {
-    (void)device;
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, const uint4& v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+// Write output chunk j (8 values) of row r into the swizzled hi/lo A tiles.
+__device__ __forceinline__ void put8(uint32_t a_hi, uint32_t a_lo, int r, int j, const float* f) {
+    uint4 lo;
+    uint4 hi = pack_hi_lo(f, lo);
+    const uint32_t off = (uint32_t)r * 128u + (uint32_t)((j ^ (r & 7)) * 16);
+    st_shared_v4(a_hi + off, hi);
+    st_shared_v4(a_lo + off, lo);
+}
+
+template <int ATOM, int BN, bool PRESPLIT>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_linear_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wlo,
+                const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
+                TcParams p) {
+    using C = Cfg<BN, PRESPLIT>;
+    extern __shared__ __align__(1024) uint8_t smem_raw_[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    uint64_t* raw_full = bars;
+    uint64_t* raw_empty = bars + RAW_STAGES;
+    uint64_t* op_full = bars + 2 * RAW_STAGES;
+    uint64_t* op_empty = op_full + C::OS;
+    uint64_t* acc_full = op_empty + C::OS;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BN, n0 = blockIdx.y * BM;
+    const int split = blockIdx.z;
+    const int kb0 = split * p.kb_per_split;
+    const int nkb = min(p.kb_per_split, p.nkb_total - kb0);
+    constexpr int RAW_TX = (ATOM == ATOM_Q8) ? BM * 64 : BM * 32;
+
+    tc::pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < RAW_STAGES; ++i) {
+            tc::mbar_init(&raw_full[i], 1);
+            tc::mbar_init(&raw_empty[i], 128);
+        }
+        for (int i = 0; i < C::OS; ++i) {
+            // decode: X producer (+tx) and 128 converter threads; prefill: both producers (+tx)
+            tc::mbar_init(&op_full[i], PRESPLIT ? 2 : 1 + 128);
+            tc::mbar_init(&op_empty[i], 1);
+        }
+        tc::mbar_init(acc_full, 1);
+        tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, BN);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- weight tile producer (no dependency on earlier kernels) ----------------
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_w);
+            int issued = 0;
+            for (int i = 0; i < nkb; ++i) {
+                if (PRESPLIT) {
+                    const int s = i % C::OS, use = i / C::OS;
+                    if (!tc::mbar_wait(&op_empty[s], (use & 1) ^ 1, p.err)) break;
+                    tc::mbar_arrive_expect_tx(&op_full[s], 2 * C::A_BYTES);
+                    uint8_t* a = smem + C::OFF_A + s * 2 * C::A_BYTES;
+                    tc::tma_load_2d(a, &tm_w, (kb0 + i) * BK, n0, &op_full[s]);
+                    tc::tma_load_2d(a + C::A_BYTES, &tm_wlo, (kb0 + i) * BK, n0, &op_full[s]);
+                } else {
+                    const int s = i % RAW_STAGES, use = i / RAW_STAGES;
+                    if (!tc::mbar_wait(&raw_empty[s], (use & 1) ^ 1, p.err)) break;
+                    tc::mbar_arrive_expect_tx(&raw_full[s], RAW_TX);
+                    const int kx = (kb0 + i) * (ATOM == ATOM_Q8 ? 64 : 32);
+                    tc::tma_load_2d(smem + C::OFF_RAW + s * C::RAW_BYTES, &tm_w, kx, n0, &raw_full[s]);
+                }
+                issued = i + 1;
+            }
+            // drain: every issued copy has landed before the CTA can exit
+            if (PRESPLIT) {
+                for (int i = (issued > C::OS ? issued - C::OS : 0); i < issued; ++i)
+                    tc::mbar_wait(&op_full[i % C::OS], (i / C::OS) & 1, p.err);
+            } else {
+                for (int i = (issued > RAW_STAGES ? issued - RAW_STAGES : 0); i < issued; ++i)
+                    tc::mbar_wait(&raw_full[i % RAW_STAGES], (i / RAW_STAGES) & 1, p.err);
+            }
+        }
+    } else if (warp == 6) {
+        // ---------------- activation tile producer ----------------
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_xhi);
+            tc::prefetch_tmap(&tm_xlo);
+            tc::pdl_wait();  // X was written by the previous kernel
+            int issued = 0;
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % C::OS, use = i / C::OS;
+                if (!tc::mbar_wait(&op_empty[s], (use & 1) ^ 1, p.err)) break;
+                tc::mbar_arrive_expect_tx(&op_full[s], 2 * C::B_BYTES);
+                const int kx = (kb0 + i) * BK;
+                uint8_t* b = smem + C::OFF_B + s * 2 * C::B_BYTES;
+                tc::tma_load_2d(b, &tm_xhi, kx, m0, &op_full[s]);
+                tc::tma_load_2d(b + C::B_BYTES, &tm_xlo, kx, m0, &op_full[s]);
+                issued = i + 1;
+            }
+            for (int i = (issued > C::OS ? issued - C::OS : 0); i < issued; ++i)
+                tc::mbar_wait(&op_full[i % C::OS], (i / C::OS) & 1, p.err);
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_f16_f32(BM, BN);
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % C::OS, use = i / C::OS;
+                if (!tc::mbar_wait(&op_full[s], use & 1, p.err)) break;
+                tc::tc_fence_after();
+                const uint32_t a_hi = tc::smem_u32(smem + C::OFF_A + s * 2 * C::A_BYTES);
+                const uint32_t a_lo = a_hi + C::A_BYTES;
+                const uint32_t b_hi = tc::smem_u32(smem + C::OFF_B + s * 2 * C::B_BYTES);
+                const uint32_t b_lo = b_hi + C::B_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint32_t ko = kk * 32;
+                    const uint64_t dah = tc::desc_sw128(a_hi + ko), dal = tc::desc_sw128(a_lo + ko);
+                    const uint64_t dbh = tc::desc_sw128(b_hi + ko), dbl = tc::desc_sw128(b_lo + ko);
+                    tc::mma_f16(tmem, dah, dbh, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    tc::mma_f16(tmem, dah, dbl, idesc, 1u);
+                    tc::mma_f16(tmem, dal, dbh, idesc, 1u);
+                }
+                tc::mma_commit(&op_empty[s]);
+            }
+            tc::mma_commit(acc_full);
+            tc::mbar_wait(acc_full, 0, p.err);  // every MMA has completed before teardown
+        }
+    } else {
+        // ---------------- converters (warps 1-4), then epilogue ----------------
+        const int t = threadIdx.x - 32;  // weight row within the tile, 0..127
+        if (!PRESPLIT) {
+            const int n = n0 + t;
+            const bool row_ok = n < p.w.rows;
+            const __half* srow = p.w.s + (size_t)(row_ok ? n : 0) * p.w.sstride;
+            bool ok = true;
+            for (int i = 0; i < nkb && ok; ++i) {
+                const int rs = i % RAW_STAGES, ruse = i / RAW_STAGES;
+                const int os = i % C::OS, ouse = i / C::OS;
+                ok = tc::mbar_wait(&raw_full[rs], ruse & 1, p.err) &&
+                     tc::mbar_wait(&op_empty[os], (ouse & 1) ^ 1, p.err);
+                if (!ok) break;
+                const int g0 = (kb0 + i) * 2;  // two 32-groups per 64-k stage
+                float s0 = 0.f, s1 = 0.f;
+                if (row_ok) {
+                    s0 = __half2float(srow[g0]) * p.pre;
+                    if (g0 + 1 < p.w.sstride) s1 = __half2float(srow[g0 + 1]) * p.pre;
+                }
+                const uint32_t raw = tc::smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES);
+                const uint32_t a_hi = tc::smem_u32(smem + C::OFF_A + os * 2 * C::A_BYTES);
+                const uint32_t a_lo = a_hi + C::A_BYTES;
+                if (ATOM == ATOM_Q8) {
+                    // row t: 4 chunks of 16 int8, 64-byte swizzle: chunk c at c ^ ((t >> 1) & 3)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 v = ld_shared_v4(raw + t * 64 + ((c ^ ((t >> 1) & 3)) * 16));
+                        const float sc = (c < 2) ? s0 : s1;
+                        float f[16];
+                        i8x4_to_f32(v.x, f + 0);
+                        i8x4_to_f32(v.y, f + 4);
+                        i8x4_to_f32(v.z, f + 8);
+                        i8x4_to_f32(v.w, f + 12);
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) f[e] *= sc;
+                        put8(a_hi, a_lo, t, 2 * c, f);
+                        put8(a_hi, a_lo, t, 2 * c + 1, f + 8);
+                    }
+                } else {
+                    // row t: 2 chunks of 16 packed bytes (one 32-group each), 32-byte swizzle
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        const uint4 v = ld_shared_v4(raw + t * 32 + ((c ^ ((t >> 2) & 1)) * 16));
+                        const float sc = (c == 0) ? s0 : s1;
+                        float lo[16], hi[16];
+                        i4x8_to_f32(v.x, lo + 0, hi + 0);
+                        i4x8_to_f32(v.y, lo + 4, hi + 4);
+                        i4x8_to_f32(v.z, lo + 8, hi + 8);
+                        i4x8_to_f32(v.w, lo + 12, hi + 12);
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            lo[e] *= sc;
+                            hi[e] *= sc;
+                        }
+                        put8(a_hi, a_lo, t, 4 * c, lo);
+                        put8(a_hi, a_lo, t, 4 * c + 1, lo + 8);
+                        put8(a_hi, a_lo, t, 4 * c + 2, hi);
+                        put8(a_hi, a_lo, t, 4 * c + 3, hi + 8);
+                    }
+                }
+                tc::fence_proxy_async_smem();
+                tc::mbar_arrive(&raw_empty[rs]);
+                tc::mbar_arrive(&op_full[os]);
+            }
+        }
+        // ---- epilogue part 1: TMEM -> (outputs | shared-memory partial) ----
+        const bool acc_ok = tc::mbar_wait(acc_full, 0, p.err);
+        tc::tc_fence_after();
+        tc::pdl_wait();  // outputs / residual inputs belong to earlier kernels
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;  // TMEM lane owned by this thread
+        const int nn = n0 + row;
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+        float* part = reinterpret_cast<float*>(smem);  // [BN][128], operand rings are free now
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            float v[32];
+            tc::tmem_ld32(taddr + c0, v);
+            if (p.splits == 1) {
+                if (acc_ok && nn < p.w.rows) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int m = m0 + c0 + j;
+                        if (m < p.M) epi_apply(p.epi, m, nn, v[j] * p.post);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) part[(c0 + j) * BM + row] = v[j];
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (p.splits > 1) {
+        // ---- epilogue part 2: cluster-wide split-K reduction over distributed shared memory ----
+        tc::cluster_sync();  // every CTA's partial tile is in its shared memory
+        if (warp >= 1 && warp <= 4) {
+            const int row = (warp & 3) * 32 + lane;
+            const int nn = n0 + row;
+            const uint32_t rank = tc::cluster_rank();
+            const uint32_t local = tc::smem_u32(smem);
+            for (int c = (int)rank; c < BN; c += p.splits) {
+                const int m = m0 + c;
+                if (m >= p.M) break;
+                float vals[MAX_SPLITS];
+#pragma unroll
+                for (int sp = 0; sp < MAX_SPLITS; ++sp)
+                    vals[sp] = (sp < p.splits)
+                                   ? tc::ld_cluster_f32(tc::map_cluster(local + (uint32_t)((c * BM + row) * 4), sp))
+                                   : 0.f;
+                float acc = 0.f;
+#pragma unroll
+                for (int sp = 0; sp < MAX_SPLITS; ++sp)
+                    if (sp < p.splits) acc += vals[sp];
+                if (nn < p.w.rows) epi_apply(p.epi, m, nn, acc * p.post);
+            }
+        }
+        tc::cluster_sync();  // no CTA leaves while its partial may still be read
+    }
+    if (warp == 0) tc::tmem_dealloc(tmem, BN);
+}
+
+// fp32 activations -> fp16 hi / lo parts (x = hi + lo to ~22 bits), row-major [M][K].
+__global__ void k_split_hilo(const float* __restrict__ X, int ldx, int M, int K, __half* __restrict__ hi,
+                             __half* __restrict__ lo) {
+    tc::pdl_trigger();
+    tc::pdl_wait();
+    const int per_row = K / 8;
+    const size_t total = (size_t)M * per_row;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / per_row), c = (int)(i % per_row) * 8;
+        const float4 a = *reinterpret_cast<const float4*>(X + (size_t)m * ldx + c);
+        const float4 b = *reinterpret_cast<const float4*>(X + (size_t)m * ldx + c + 4);
+        const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        uint4 l;
+        const uint4 h = pack_hi_lo(f, l);
+        *reinterpret_cast<uint4*>(hi + (size_t)m * K + c) = h;
+        *reinterpret_cast<uint4*>(lo + (size_t)m * K + c) = l;
+    }
+}
+
+// One-time exact split of a quantised weight for the prefill path: w' = deq(w) * 2^P,
+// hi = f16(w'), lo = f16(w' - hi), both [rows][cols].
+__global__ void k_presplit_weight(QW w, float pre, __half* __restrict__ hi, __half* __restrict__ lo) {
+    const size_t n = (size_t)w.rows * w.cols;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float v = deq_elem(w, (int)(i / w.cols), (int)(i % w.cols)) * pre;
+        const __half h = __float2half_rn(v);
+        hi[i] = h;
+        lo[i] = __float2half_rn(v - __half2float(h));
+    }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = std::getenv("GPT2Q_NO_PDL");
+        on = (e && e[0] == '1') ? 0 : 1;
+    }
+    return on == 1;
+}
+
+template <int ATOM, int BN, bool PRESPLIT>
+cudaError_t launch_tc(const CUtensorMap& tw, const CUtensorMap& twlo, const CUtensorMap& txh, const CUtensorMap& txl,
+                      const TcParams& tp, dim3 grid, cudaStream_t st) {
+    auto kern = k_linear_tc<ATOM, BN, PRESPLIT>;
+    const int smem = Cfg<BN, PRESPLIT>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (grid.z > 1) {
+        attrs[na].id = cudaLaunchAttributeClusterDimension;
+        attrs[na].val.clusterDim.x = 1;
+        attrs[na].val.clusterDim.y = 1;
+        attrs[na].val.clusterDim.z = grid.z;
+        ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, kern, tw, twlo, txh, txl, tp);
+}
+
+template <int ATOM, bool PRESPLIT>
+cudaError_t launch_bn(int BN, const CUtensorMap& tw, const CUtensorMap& twlo, const CUtensorMap& txh,
+                      const CUtensorMap& txl, const TcParams& tp, dim3 grid, cudaStream_t st) {
+    switch (BN) {
+        case 32: return launch_tc<ATOM, 32, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
+        case 64: return launch_tc<ATOM, 64, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
+        case 128: return launch_tc<ATOM, 128, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
+        default: return launch_tc<ATOM, 256, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
+    }
+}
+
+}  // namespace
+
+struct WeightTc {
+    CUtensorMap raw;         // int8 / int4 tiles
+    CUtensorMap hi, lo;      // fp16 split copies (prefill)
+    bool has_split = false;
+    float pre = 1.f, post = 1.f;
+};
+
+struct GemmState {
+    std::unordered_map<const void*, WeightTc> w;       // weight payload -> maps
+    std::unordered_map<uint64_t, CUtensorMap> xmaps;   // (K, BN, hi/lo) -> map
+    std::vector<void*> owned;                           // split weight copies
+};
+
+bool GemmPlan::usable(const QW& w, int M) const {
+    if (!enabled || M < min_m || M > Mmax) return false;
+    if (w.atom != ATOM_Q8 && w.atom != ATOM_Q4) return false;
+    if (w.cols % 32 != 0) return false;
+    if (w.cols > Kmax || (w.qstride % 16) != 0) return false;
+    return state->w.count(w.q) != 0;
+}
+
+int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax) {
     p.enabled = false;
+    p.Mmax = Mmax;
+    p.Kmax = Kmax;
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (major != 10 || !encode_fn()) return 0;  // the tensor-core path needs sm_100
+    if (const char* e = std::getenv("GPT2Q_TC_DISABLE"))
+        if (e[0] == '1') return 0;
+    p.min_m = 16;
+    if (const char* e = std::getenv("GPT2Q_TC_MIN_M")) p.min_m = std::max(1, std::atoi(e));
+    p.presplit_min_m = 257;
+    if (const char* e = std::getenv("GPT2Q_TC_PRESPLIT_MIN_M")) p.presplit_min_m = std::max(1, std::atoi(e));
+    const size_t xbytes = (size_t)Mmax * Kmax * 2;
+    if (cudaMalloc(&p.xhi, xbytes) != cudaSuccess || cudaMalloc(&p.xlo, xbytes) != cudaSuccess) return -1;
+    if (cudaMalloc(&p.err, 4) != cudaSuccess || cudaMemset(p.err, 0, 4) != cudaSuccess) return -1;
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    p.state = new GemmState();
+    p.enabled = true;
     return 0;
 }
 
-void gemm_destroy(GemmPlan& p) { p.enabled = false; }
+void gemm_destroy(GemmPlan& p) {
+    if (p.xhi) cudaFree(p.xhi);
+    if (p.xlo) cudaFree(p.xlo);
+    if (p.err) cudaFree(p.err);
+    if (p.state)
+        for (void* q : p.state->owned) cudaFree(q);
+    delete p.state;
+    p = GemmPlan();
+}
+
+// Power-of-two prescale so the fp16 lo part of every weight stays normal:
+// max |q * scale| * 2^P <= 2^14.
+static int prescale_exponent(float max_abs_w) {
+    if (!(max_abs_w > 0.f) || !std::isfinite(max_abs_w)) return 0;
+    int P = (int)std::floor(std::log2(16384.0 / (double)max_abs_w));
+    return std::max(-30, std::min(30, P));
+}
+
+int gemm_register_weight(GemmPlan& p, const QW& w, float max_abs_w, bool presplit, cudaStream_t st) {
+    if (!p.enabled || (w.atom != ATOM_Q8 && w.atom != ATOM_Q4)) return 0;
+    if (w.cols % 32 != 0 || w.cols > p.Kmax) return 0;
+    WeightTc wt;
+    const int P = prescale_exponent(max_abs_w);
+    wt.pre = std::ldexp(1.0f, P);
+    wt.post = std::ldexp(1.0f, -P);
+    const bool q8 = w.atom == ATOM_Q8;
+    if (!make_map_2d(&wt.raw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q, w.qstride, (uint64_t)w.rows, w.qstride,
+                     q8 ? 64 : 32, BM, q8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B))
+        return -1;
+    if (presplit) {
+        const size_t n = (size_t)w.rows * w.cols;
+        void *hi = nullptr, *lo = nullptr;
+        if (cudaMalloc(&hi, n * 2) != cudaSuccess) return -2;
+        p.state->owned.push_back(hi);
+        if (cudaMalloc(&lo, n * 2) != cudaSuccess) return -2;
+        p.state->owned.push_back(lo);
+        k_presplit_weight<<<148 * 8, 256, 0, st>>>(w, wt.pre, reinterpret_cast<__half*>(hi),
+                                                  reinterpret_cast<__half*>(lo));
+        if (cudaGetLastError() != cudaSuccess) return -1;
+        if (!make_map_2d(&wt.hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, hi, (uint64_t)w.cols, (uint64_t)w.rows,
+                         (uint64_t)w.cols * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_map_2d(&wt.lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, lo, (uint64_t)w.cols, (uint64_t)w.rows,
+                         (uint64_t)w.cols * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+            return -1;
+        wt.has_split = true;
+        p.presplit_bytes += 4 * n;
+    }
+    p.state->w[w.q] = wt;
+    return 0;
+}
+
+static const CUtensorMap* xmap(const GemmPlan& p, int K, int BN, bool hi) {
+    const uint64_t key = ((uint64_t)K << 20) | ((uint64_t)BN << 1) | (hi ? 1 : 0);
+    auto it = p.state->xmaps.find(key);
+    if (it != p.state->xmaps.end()) return &it->second;
+    CUtensorMap m;
+    if (!make_map_2d(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, hi ? p.xhi : p.xlo, (uint64_t)K, (uint64_t)p.Mmax,
+                     (uint64_t)K * 2, 64, (uint32_t)BN, CU_TENSOR_MAP_SWIZZLE_128B))
+        return nullptr;
+    return &p.state->xmaps.emplace(key, m).first->second;
+}
+
+cudaError_t launch_split_hilo(const GemmPlan& p, const float* X, int ldx, int M, int K, cudaStream_t st) {
+    const size_t total = (size_t)M * (K / 8);
+    const int blocks = (int)std::max<size_t>(1, std::min<size_t>((total + 255) / 256, 148 * 8));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_split_hilo, X, ldx, M, K, reinterpret_cast<__half*>(p.xhi),
+                              reinterpret_cast<__half*>(p.xlo));
+}
 
 cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const float* X, int ldx, int M, const Epi& e,
                              cudaStream_t st) {
-    (void)p; (void)w; (void)X; (void)ldx; (void)M; (void)e; (void)st;
-    return cudaErrorNotSupported;
+    auto wi = p.state->w.find(w.q);
+    if (wi == p.state->w.end()) return cudaErrorInvalidValue;
+    const WeightTc& wt = wi->second;
+    const int K = w.cols;
+    cudaError_t ce = launch_split_hilo(p, X, ldx, M, K, st);
+    if (ce != cudaSuccess) return ce;
+    const bool presplit = wt.has_split && M >= p.presplit_min_m;
+    const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
+    const int m_tiles = (M + BN - 1) / BN;
+    const int n_tiles = (w.rows + BM - 1) / BM;
+    const int nkb = (K + BK - 1) / BK;
+    int splits = 1;
+    const int tiles = m_tiles * n_tiles;
+    if (tiles < 120) {
+        splits = std::min(std::min(nkb, MAX_SPLITS), (148 + tiles - 1) / tiles);
+        splits = std::max(splits, 1);
+    }
+    int kb_per = (nkb + splits - 1) / splits;
+    splits = (nkb + kb_per - 1) / kb_per;
+    const CUtensorMap* xh = xmap(p, K, BN, true);
+    const CUtensorMap* xl = xmap(p, K, BN, false);
+    if (!xh || !xl) return cudaErrorInvalidValue;
+    TcParams tp;
+    tp.w = w;
+    tp.M = M;
+    tp.nkb_total = nkb;
+    tp.kb_per_split = kb_per;
+    tp.splits = splits;
+    tp.pre = wt.pre;
+    tp.post = wt.post;
+    tp.epi = e;
+    tp.err = p.err;
+    dim3 grid(m_tiles, n_tiles, splits);
+    if (presplit) {
+        if (w.atom == ATOM_Q8) return launch_bn<ATOM_Q8, true>(BN, wt.hi, wt.lo, *xh, *xl, tp, grid, st);
+        return launch_bn<ATOM_Q4, true>(BN, wt.hi, wt.lo, *xh, *xl, tp, grid, st);
+    }
+    if (w.atom == ATOM_Q8) return launch_bn<ATOM_Q8, false>(BN, wt.raw, wt.raw, *xh, *xl, tp, grid, st);
+    return launch_bn<ATOM_Q4, false>(BN, wt.raw, wt.raw, *xh, *xl, tp, grid, st);
+}
+
+int gemm_take_error(GemmPlan& p, cudaStream_t st) {
+    if (!p.enabled || !p.err) return 0;
+    int h = 0;
+    if (cudaMemcpyAsync(&h, p.err, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return -1;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return -1;
+    if (h != 0) cudaMemsetAsync(p.err, 0, 4, st);
+    return h;
 }
 
 }  // namespace gpt2q

@@ -1,21 +1,37 @@
-// Tensor-core (tcgen05 / TMEM) dequant-fused linear for large M (prefill and
-// large-batch decode). See gemm.cu.
+// Tensor-core (tcgen05 / TMEM / TMA) dequant-fused linear for large M (prefill and
+// batched decode). See gemm.cu.
 #pragma once
 #include <cuda_runtime.h>
+#include <stddef.h>
 
 #include "common.cuh"
 
 namespace gpt2q {
 
+struct GemmState;
+
 struct GemmPlan {
     bool enabled = false;
-    int min_m = 1 << 30;  // use the tensor-core path when M >= min_m
+    int min_m = 1 << 30;         // the tensor-core path serves M >= min_m
+    int presplit_min_m = 1 << 30;  // ... and reads the fp16 hi/lo weight copies for M >= this
+    int Mmax = 0, Kmax = 0;
+    void* xhi = nullptr;  // fp16 [Mmax][K] activation hi parts
+    void* xlo = nullptr;  // fp16 [Mmax][K] activation lo parts
+    int* err = nullptr;   // device error word (bounded-wait timeouts)
+    size_t presplit_bytes = 0;
+    GemmState* state = nullptr;
     bool usable(const QW& w, int M) const;
 };
 
-int gemm_init(GemmPlan& p, int device);
+int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax);
 void gemm_destroy(GemmPlan& p);
+// Prepare a weight for the tensor-core path: TMA descriptors, the power-of-two prescale
+// derived from an upper bound of max |dequantised weight| and, when `presplit`, the
+// exact fp16 hi/lo copy used by the compute-bound prefill regime.
+int gemm_register_weight(GemmPlan& p, const QW& w, float max_abs_w, bool presplit, cudaStream_t st);
 cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const float* X, int ldx, int M, const Epi& e,
                              cudaStream_t st);
+// Reads and clears the device error word (0 = no error). Synchronises `st`.
+int gemm_take_error(GemmPlan& p, cudaStream_t st);
 
 }  // namespace gpt2q

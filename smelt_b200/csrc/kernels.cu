@@ -45,35 +45,61 @@ cudaError_t launch_embed(const QW& wte, const QW& wpe, const uint32_t* tok, cons
 
 // ------------------------------------------------------------------ LayerNorm
 // One warp per row: mean, population variance, (x-mean)/sqrt(var+eps)*g+b (gpt2.rs:178-185).
-// rows (optional) gathers source rows, e.g. the last prompt position of each sequence.
-__global__ void k_layernorm(const float* __restrict__ x, int ldx, const int* __restrict__ rows,
-                            float* __restrict__ y, int ldy, const float* __restrict__ g,
-                            const float* __restrict__ b, int d, float eps, int M) {
+// The row is held in registers (NV values per lane, d <= 32*NV) so every load of the row
+// is issued before the first reduction. rows (optional) gathers source rows, e.g. the
+// last prompt position of each sequence.
+template <int NV>
+__global__ void __launch_bounds__(128) k_layernorm(const float* __restrict__ x, int ldx,
+                                                   const int* __restrict__ rows, float* __restrict__ y, int ldy,
+                                                   const float* __restrict__ g, const float* __restrict__ b, int d,
+                                                   float eps, int M) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= M) return;
     const int src = rows ? rows[warp] : warp;
     const float* xr = x + (size_t)src * ldx;
-    float s = 0.f;
-    for (int i = lane; i < d; i += 32) s += xr[i];
-    const float mean = warp_sum(s) / (float)d;
-    float v = 0.f;
-    for (int i = lane; i < d; i += 32) {
-        float t = xr[i] - mean;
-        v += t * t;
+    float v[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = (i < d) ? xr[i] : 0.f;
     }
-    const float var = warp_sum(v) / (float)d;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) s += v[j];
+    const float mean = warp_sum(s) / (float)d;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int i = lane + 32 * j;
+        const float t = (i < d) ? v[j] - mean : 0.f;
+        q += t * t;
+    }
+    const float var = warp_sum(q) / (float)d;
     const float den = sqrtf(var + eps);
     float* yr = y + (size_t)warp * ldy;
-    for (int i = lane; i < d; i += 32) yr[i] = (xr[i] - mean) / den * g[i] + b[i];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int i = lane + 32 * j;
+        if (i < d) yr[i] = (v[j] - mean) / den * g[i] + b[i];
+    }
 }
 
 cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y, int ldy, const float* g,
                              const float* b, int d, float eps, int M, cudaStream_t st) {
     if (M <= 0) return cudaSuccess;
     const int threads = 128, rows_per_block = threads / 32;
-    k_layernorm<<<(M + rows_per_block - 1) / rows_per_block, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d,
-                                                                               eps, M);
+    const int grid = (M + rows_per_block - 1) / rows_per_block;
+    if (d <= 32 * 8)
+        k_layernorm<8><<<grid, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d, eps, M);
+    else if (d <= 32 * 24)
+        k_layernorm<24><<<grid, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d, eps, M);
+    else if (d <= 32 * 32)
+        k_layernorm<32><<<grid, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d, eps, M);
+    else if (d <= 32 * 56)
+        k_layernorm<56><<<grid, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d, eps, M);
+    else
+        return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
 
@@ -292,11 +318,14 @@ __global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q
         o0 *= corr;
         o1 *= corr;
         const int nv = min(32, T - t0);
-        for (int j = 0; j < nv; ++j) {
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
             const float pj = __shfl_sync(0xffffffffu, p, j);
-            const float2 v = __ldg(reinterpret_cast<const float2*>(V + (size_t)(t0 + j) * HD) + lane);
-            o0 = fmaf(pj, v.x, o0);
-            o1 = fmaf(pj, v.y, o1);
+            if (j < nv) {
+                const float2 v = __ldg(reinterpret_cast<const float2*>(V + (size_t)(t0 + j) * HD) + lane);
+                o0 = fmaf(pj, v.x, o0);
+                o1 = fmaf(pj, v.y, o1);
+            }
         }
         m = mnew;
     }
@@ -545,6 +574,25 @@ __global__ void k_f16_to_f32(const __half* __restrict__ src, float* __restrict__
 cudaError_t launch_f16_to_f32(const __half* src, float* dst, size_t n, cudaStream_t st) {
     if (n == 0) return cudaSuccess;
     k_f16_to_f32<<<148, 256, 0, st>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
+// Bounded busy-wait used only by the profiling mode: it keeps the stream busy while
+// the host enqueues the timed kernels, so per-kernel events measure kernel time and
+// not host launch gaps. Ends after `ns` nanoseconds of globaltimer, whatever happens.
+__global__ void k_sleep(unsigned long long ns) {
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (int i = 0; i < (1 << 20); ++i) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 >= ns) break;
+        __nanosleep(1000);
+    }
+}
+
+cudaError_t launch_sleep(unsigned long long ns, cudaStream_t st) {
+    k_sleep<<<1, 1, 0, st>>>(ns);
     return cudaGetLastError();
 }
 

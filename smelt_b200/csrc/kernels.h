@@ -45,6 +45,8 @@ cudaError_t launch_repack_q8(const uint8_t* raw, int rows, int cols, uint8_t* q,
                              cudaStream_t st);
 cudaError_t launch_repack_q4(const uint8_t* raw, int rows, int cols, uint8_t* q, __half* s, int sstride,
                              cudaStream_t st);
+// Bounded host-lag helper for profiling (see kernels.cu).
+cudaError_t launch_sleep(unsigned long long ns, cudaStream_t st);
 cudaError_t launch_f16_to_f32(const __half* src, float* dst, size_t n, cudaStream_t st);
 
 }  // namespace gpt2q

@@ -44,6 +44,7 @@ struct Linear {
     int rows = 0, cols = 0;
     std::string name;
     size_t weight_bytes = 0;  // q + scale bytes read by one full pass over W
+    float max_abs_w = 0.f;    // upper bound of |dequantised weight| (tensor-core prescale)
 };
 
 struct LayerW {
@@ -62,6 +63,12 @@ struct ProfRec {
     cudaEvent_t a, b;
     double bytes;
 };
+
+float half_bits_to_float(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
 
 int atom_id(const std::string& a) {
     if (a == "core.i8.b32.f16scale") return ATOM_Q8;
@@ -126,6 +133,7 @@ struct gpt2q_handle {
 
     bool prof = false;
     std::vector<ProfRec> prof_pending;
+    std::vector<cudaEvent_t> ev_pool;
     std::map<std::string, ProfAgg> prof_agg;
 
     GemmPlan gemm;  // tensor-core path for large M
@@ -169,12 +177,23 @@ int launched(gpt2q_handle* H, const char* name, double bytes, cudaError_t e, cud
     return GPT2Q_OK;
 }
 
+cudaEvent_t pooled_event(gpt2q_handle* H) {
+    if (H->ev_pool.empty()) {
+        cudaEvent_t e = nullptr;
+        cudaEventCreate(&e);
+        return e;
+    }
+    cudaEvent_t e = H->ev_pool.back();
+    H->ev_pool.pop_back();
+    return e;
+}
+
 template <class F>
 int run_kernel(gpt2q_handle* H, const char* name, double bytes, F&& f) {
     cudaEvent_t a = nullptr, b = nullptr;
     if (H->prof && !H->capturing) {
-        cudaEventCreate(&a);
-        cudaEventCreate(&b);
+        a = pooled_event(H);
+        b = pooled_event(H);
         cudaEventRecord(a, H->stream);
     }
     return launched(H, name, bytes, f(), a, b);
@@ -201,11 +220,14 @@ int upload_vec(gpt2q_handle* H, const gpt2q_tensor_desc* t, size_t n, size_t off
     float* d = H->dalloc<float>(cnt * 4);
     if (!d) return H->fail(GPT2Q_EOOM, "cudaMalloc vector");
     if (a == ATOM_F32) {
-        CK(cudaMemcpy(d, reinterpret_cast<const float*>(t->data) + off, cnt * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(d, reinterpret_cast<const float*>(t->data) + off, cnt * 4, cudaMemcpyHostToDevice,
+                           H->stream));
+        CK(cudaStreamSynchronize(H->stream));
     } else {
         __half* tmp = nullptr;
         CK(cudaMalloc(&tmp, cnt * 2));
-        CK(cudaMemcpy(tmp, reinterpret_cast<const uint16_t*>(t->data) + off, cnt * 2, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(tmp, reinterpret_cast<const uint16_t*>(t->data) + off, cnt * 2, cudaMemcpyHostToDevice,
+                           H->stream));
         CK(launch_f16_to_f32(tmp, d, cnt, H->stream));
         CK(cudaStreamSynchronize(H->stream));
         CK(cudaFree(tmp));
@@ -245,6 +267,17 @@ int upload_linear(gpt2q_handle* H, const gpt2q_tensor_desc* t, int rows, int col
         src = sliced.data();
     }
     const size_t raw_bytes = (size_t)out_rows * out_row_bytes;
+    if (a == ATOM_Q8 || a == ATOM_Q4) {
+        const size_t blk = (a == ATOM_Q8) ? 34 : 18;
+        const float qmax = (a == ATOM_Q8) ? 127.f : 8.f;
+        float smax = 0.f;
+        for (size_t o = 0; o + blk <= raw_bytes; o += blk) {
+            const uint16_t hb = (uint16_t)(src[o] | (src[o + 1] << 8));
+            const float sv = std::fabs(half_bits_to_float(hb));
+            if (sv > smax && std::isfinite(sv)) smax = sv;
+        }
+        L->max_abs_w = smax * qmax;
+    }
     L->rows = out_rows;
     L->cols = out_cols;
     L->name = t->name;
@@ -257,7 +290,8 @@ int upload_linear(gpt2q_handle* H, const gpt2q_tensor_desc* t, int rows, int col
     if (a == ATOM_F16 || a == ATOM_F32) {
         uint8_t* q = H->dalloc<uint8_t>(raw_bytes);
         if (!q) return H->fail(GPT2Q_EOOM, "cudaMalloc weight");
-        CK(cudaMemcpy(q, src, raw_bytes, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(q, src, raw_bytes, cudaMemcpyHostToDevice, H->stream));
+        CK(cudaStreamSynchronize(H->stream));
         w.q = q;
         w.qstride = (a == ATOM_F16 ? 2 : 4) * (size_t)out_cols;
         L->weight_bytes = raw_bytes;
@@ -268,10 +302,10 @@ int upload_linear(gpt2q_handle* H, const gpt2q_tensor_desc* t, int rows, int col
         uint8_t* q = H->dalloc<uint8_t>(w.qstride * out_rows);
         __half* s = H->dalloc<__half>((size_t)w.sstride * out_rows * 2);
         if (!q || !s) return H->fail(GPT2Q_EOOM, "cudaMalloc weight");
-        CK(cudaMemset(s, 0, (size_t)w.sstride * out_rows * 2));
+        CK(cudaMemsetAsync(s, 0, (size_t)w.sstride * out_rows * 2, H->stream));
         uint8_t* raw = nullptr;
         CK(cudaMalloc(&raw, raw_bytes));
-        CK(cudaMemcpy(raw, src, raw_bytes, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(raw, src, raw_bytes, cudaMemcpyHostToDevice, H->stream));
         if (a == ATOM_Q8)
             CK(launch_repack_q8(raw, out_rows, out_cols, q, s, w.sstride, H->stream));
         else
@@ -418,8 +452,8 @@ int flush_profile(gpt2q_handle* H) {
         g.launches++;
         g.ms += ms;
         g.bytes += r.bytes;
-        cudaEventDestroy(r.a);
-        cudaEventDestroy(r.b);
+        H->ev_pool.push_back(r.a);
+        H->ev_pool.push_back(r.b);
     }
     H->prof_pending.clear();
     return GPT2Q_OK;
@@ -452,6 +486,7 @@ int run_decode_step(gpt2q_handle* H, int B) {
         CK(cudaGraphLaunch(it->second.first, H->stream));
         H->launches += it->second.second;
     } else {
+        if (H->prof) CK(launch_sleep(20000000ull, H->stream));  // host runs ahead of the GPU
         int rc = enqueue_decode(H, B);
         if (rc) return rc;
         if (H->prof) {
@@ -521,6 +556,7 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
     CK(cudaMemcpyAsync(H->p_tiles, st_tiles, (size_t)nt * sizeof(AttnTile), cudaMemcpyHostToDevice, H->stream));
 
     const float scale = 1.0f / std::sqrt((float)H->hd);
+    if (H->prof) CK(launch_sleep(20000000ull, H->stream));
     double kv_bytes = 0;
     for (int s = s0; s < s1; ++s) {
         const double T = offs[s + 1] - offs[s];
@@ -620,12 +656,19 @@ int do_decode(gpt2q_handle* H, const uint32_t* tok, const int32_t* pos, const in
     return run_decode_step(H, n_seq);
 }
 
+int check_device_error(gpt2q_handle* H) {
+    const int e = gemm_take_error(H->gemm, H->stream);
+    if (e > 0) return H->fail(GPT2Q_ETIMEOUT, "a bounded device-side wait timed out (error word " + std::to_string(e) + ")");
+    if (e < 0) return H->fail(GPT2Q_ECUDA, "reading the device error word failed");
+    return GPT2Q_OK;
+}
+
 int read_outputs(gpt2q_handle* H, int n, const float* dlogits, float* logits, uint32_t* next) {
     if (logits)
         CK(cudaMemcpyAsync(logits, dlogits, (size_t)n * H->cfg.vocab * 4, cudaMemcpyDeviceToHost, H->stream));
     if (next) CK(cudaMemcpyAsync(next, H->d_next, (size_t)n * 4, cudaMemcpyDeviceToHost, H->stream));
     CK(cudaStreamSynchronize(H->stream));
-    return GPT2Q_OK;
+    return check_device_error(H);
 }
 
 const gpt2q_tensor_desc* find(const std::map<std::string, const gpt2q_tensor_desc*>& m, const std::string& n) {
@@ -737,7 +780,8 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
             for (int k = 0; k < 3; ++k) {
                 float* part = nullptr;
                 if ((rc = upload_vec(H.get(), tb, 3 * d, (size_t)k * d + h0 * hd, (size_t)hn * hd, &part))) return bail(rc);
-                if (cudaMemcpy(dst + (size_t)k * hn * hd, part, (size_t)hn * hd * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+                if (cudaMemcpyAsync(dst + (size_t)k * hn * hd, part, (size_t)hn * hd * 4, cudaMemcpyDeviceToDevice,
+                                    H->stream) != cudaSuccess)
                     return bail(GPT2Q_ECUDA);
             }
             L.attn.bias = dst;
@@ -785,7 +829,8 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
         H->err = "cudaMalloc KV arena (" + std::to_string(H->kv.slot_stride * c.max_seqs * 4) + " bytes)";
         return bail(GPT2Q_EOOM);
     }
-    if (cudaMemset(H->kv.base, 0, H->kv.slot_stride * c.max_seqs * 4) != cudaSuccess) return bail(GPT2Q_ECUDA);
+    if (cudaMemsetAsync(H->kv.base, 0, H->kv.slot_stride * c.max_seqs * 4, H->stream) != cudaSuccess)
+        return bail(GPT2Q_ECUDA);
 
     const int max_tokens = c.max_tokens > 0 ? c.max_tokens : 8192;
     H->Mmax = std::max(c.max_seqs, max_tokens);
@@ -815,10 +860,24 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
         H->err = "cudaMalloc workspace";
         return bail(GPT2Q_EOOM);
     }
-    if (cudaMemset(H->d_genlog, 0xff, (size_t)c.max_seqs * c.n_ctx * 4) != cudaSuccess) return bail(GPT2Q_ECUDA);
-    if (gemm_init(H->gemm, device) != 0) {
-        H->err = "gemm init failed";
+    if (cudaMemsetAsync(H->d_genlog, 0xff, (size_t)c.max_seqs * c.n_ctx * 4, H->stream) != cudaSuccess)
         return bail(GPT2Q_ECUDA);
+    {
+        const int Kmax = std::max(std::max(d, H->fc_local), H->d_local);
+        if (gemm_init(H->gemm, device, H->Mmax, Kmax) != 0) {
+            H->err = "tensor-core linear init failed";
+            return bail(GPT2Q_ECUDA);
+        }
+        for (auto& kv : H->lin_by_name) {
+            const Linear* L = kv.second;
+            // layer weights also get the fp16 hi/lo copy for compute-bound prefill; the tied
+            // head only ever multiplies the last position of each prompt
+            const bool presplit = kv.first.rfind("h.", 0) == 0;
+            if (gemm_register_weight(H->gemm, L->w, L->max_abs_w, presplit, H->stream) != 0) {
+                H->err = "tensor map for " + kv.first + " failed";
+                return bail(GPT2Q_ECUDA);
+            }
+        }
     }
     if (tp_size > 1) {
         H->tp = tp_create(tp_size, tp_rank, nccl_id, device);
@@ -827,7 +886,7 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
             return bail(GPT2Q_ENCCL);
         }
     }
-    if (cudaDeviceSynchronize() != cudaSuccess) {
+    if (cudaStreamSynchronize(H->stream) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
         H->err = "device sync after upload failed";
         return bail(GPT2Q_ECUDA);
     }
@@ -864,6 +923,7 @@ void gpt2q_destroy(gpt2q_handle* H) {
         cudaEventDestroy(r.a);
         cudaEventDestroy(r.b);
     }
+    for (auto e : H->ev_pool) cudaEventDestroy(e);
     if (H->tp) tp_destroy(H->tp);
     gemm_destroy(H->gemm);
     for (auto& a : H->allocs) cudaFree(a.p);
@@ -935,13 +995,14 @@ int gpt2q_decode_steps(gpt2q_handle* H, int steps, uint32_t* out_tokens) {
         std::vector<uint32_t> row(H->cfg.n_ctx);
         CK(cudaStreamSynchronize(H->stream));
         for (int b = 0; b < B; ++b) {
-            CK(cudaMemcpy(row.data() + start[b], H->d_genlog + (size_t)b * H->cfg.n_ctx + start[b],
-                          (size_t)steps * 4, cudaMemcpyDeviceToHost));
+            CK(cudaMemcpyAsync(row.data() + start[b], H->d_genlog + (size_t)b * H->cfg.n_ctx + start[b],
+                               (size_t)steps * 4, cudaMemcpyDeviceToHost, H->stream));
+            CK(cudaStreamSynchronize(H->stream));
             for (int s = 0; s < steps; ++s) out_tokens[(size_t)s * B + b] = row[start[b] + s];
         }
     }
     CK(cudaStreamSynchronize(H->stream));
-    return GPT2Q_OK;
+    return check_device_error(H);
 }
 
 int gpt2q_generate_greedy(gpt2q_handle* H, const uint32_t* tokens, const int32_t* seq_offsets, int n_seq, int steps,
@@ -1011,7 +1072,8 @@ int gpt2q_dequant(gpt2q_handle* H, const char* name, float* out, uint64_t n) {
     auto iv = H->vec_by_name.find(name);
     if (iv != H->vec_by_name.end()) {
         if (iv->second.second != n) return H->fail(GPT2Q_EARG, "dequant: n does not match tensor size");
-        CK(cudaMemcpy(out, iv->second.first, n * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpyAsync(out, iv->second.first, n * 4, cudaMemcpyDeviceToHost, H->stream));
+        CK(cudaStreamSynchronize(H->stream));
         return GPT2Q_OK;
     }
     return H->fail(GPT2Q_EARG, std::string("dequant: unknown tensor ") + name);
@@ -1039,7 +1101,14 @@ int gpt2q_profile(gpt2q_handle* H, int enable) {
     int rc = flush_profile(H);
     if (rc) return rc;
     H->prof = enable != 0;
-    if (H->prof) H->prof_agg.clear();
+    if (H->prof) {
+        H->prof_agg.clear();
+        while (H->ev_pool.size() < 2048) {
+            cudaEvent_t e = nullptr;
+            CK(cudaEventCreate(&e));
+            H->ev_pool.push_back(e);
+        }
+    }
     return GPT2Q_OK;
 }
 

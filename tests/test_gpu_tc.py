@@ -1,0 +1,71 @@
+"""Tensor-core (tcgen05) linear path vs the CPU oracle and vs the CUDA-core path.
+
+GPT2Q_TC_MIN_M=1 forces every int8/int4 linear through the tcgen05 kernel (even
+single-token decode); GPT2Q_TC_DISABLE=1 forces the CUDA-core kernel. Both are read
+when a handle is created.
+"""
+import numpy as np
+import pytest
+
+from smelt_b200.gpu import Gpu
+
+from .helpers import MINI, TINY, make_pack, oracle_engine, oracle_prefix_logits
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 2e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    from smelt_b200 import build
+    build.build()
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+@pytest.mark.parametrize("meta", [TINY, MINI])
+def test_tc_step_matches_oracle(meta, policy, monkeypatch):
+    monkeypatch.setenv("GPT2Q_TC_MIN_M", "1")
+    pk = make_pack(meta, policy, 0, 0.02)
+    eng = oracle_engine(pk)
+    ids = ((np.arange(30) * 53 + 3) % meta.vocab).astype(np.uint32)
+    ref = oracle_prefix_logits(eng, ids)
+    with Gpu(pk) as g:
+        got = np.stack([g.step(int(t), p) for p, t in enumerate(ids)])
+    err = np.abs(got - ref).max()
+    assert err <= LOGIT_TOL, err
+    assert err <= 1e-3, f"tensor-core path less accurate than expected: {err}"
+    assert np.array_equal(got.argmax(-1), ref.argmax(-1))
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+def test_tc_batched_decode_matches_cuda_core_path(policy, monkeypatch):
+    pk = make_pack(MINI, policy, 0, 0.02)
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, MINI.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 60, 40)]
+    res = {}
+    for mode in ("simt", "tc"):
+        monkeypatch.setenv("GPT2Q_TC_DISABLE", "1" if mode == "simt" else "0")
+        monkeypatch.setenv("GPT2Q_TC_MIN_M", "16")
+        with Gpu(pk, max_seqs=len(prompts)) as g:
+            nxt, lg0 = g.prefill(prompts, want_logits=True)
+            toks = g.decode_steps(8, len(prompts))
+            nxt2, lg = g.decode(toks[-1], [p.size + 8 for p in prompts], want_logits=True)
+        res[mode] = (nxt, lg0, toks, nxt2, lg)
+    a, b = res["simt"], res["tc"]
+    assert np.abs(a[1] - b[1]).max() <= 1e-3
+    assert np.abs(a[4] - b[4]).max() <= 1e-3
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[2], b[2]) and np.array_equal(a[3], b[3])
+
+
+def test_tc_large_prefill_matches_oracle():
+    pk = make_pack(MINI, "auto", 0, 0.02)
+    eng = oracle_engine(pk)
+    rng = np.random.default_rng(9)
+    lens = [128, 7, 100, 128, 33, 64, 128, 90, 1, 128, 128, 77, 55, 128, 128, 120]
+    prompts = [rng.integers(0, MINI.vocab, n).astype(np.uint32) for n in lens]
+    with Gpu(pk, max_seqs=len(prompts)) as g:
+        nxt, lg = g.prefill(prompts, want_logits=True)
+    for i in (0, 1, 8, 15):
+        ref = oracle_prefix_logits(eng, prompts[i])[-1]
+        assert np.abs(lg[i] - ref).max() <= 1e-3
+        assert nxt[i] == int(np.argmax(ref[::-1]) and (len(ref) - 1 - np.argmax(ref[::-1])))
