@@ -38,6 +38,10 @@ struct Epi {
     const float* bias;  // may be null
     float* out;
     int ldo;
+    // EPI_GELU: optional fp16 hi/lo copies of the output (x = hi + lo), row stride ldo,
+    // read by the tensor-core linear that consumes this activation
+    __half* out_hi;
+    __half* out_lo;
     // EPI_QKV
     float* kv;             // KV arena base
     const int* slot;       // per row m
@@ -68,10 +72,18 @@ __device__ __forceinline__ void epi_apply(const Epi& e, int m, int n, float acc)
             *p = *p + (v + b);
             break;
         }
-        case EPI_GELU:
+        case EPI_GELU: {
             if (e.bias) v += e.bias[n];
-            e.out[(size_t)m * e.ldo + n] = gelu_tanh(v);
+            const float gv = gelu_tanh(v);
+            const size_t o = (size_t)m * e.ldo + n;
+            e.out[o] = gv;
+            if (e.out_hi) {
+                const __half h = __float2half_rn(gv);
+                e.out_hi[o] = h;
+                e.out_lo[o] = __float2half_rn(gv - __half2float(h));
+            }
             break;
+        }
         default: {  // EPI_QKV
             if (e.bias) v += e.bias[n];
             if (n < e.d_local) {
@@ -145,6 +157,19 @@ __device__ __forceinline__ float deq_elem(const QW& w, int r, int c) {
 __device__ __forceinline__ int total_key(float f) {
     int b = __float_as_int(f);
     return b ^ (int)(((unsigned)(b >> 31)) >> 1);
+}
+
+// (total-order key, index) packed so that unsigned 64-bit max picks the largest value
+// and, among equal values, the LAST index (Iterator::max_by, gpt2.rs:390-396).
+__device__ __forceinline__ unsigned long long argmax_pack(float v, int idx) {
+    const unsigned k = (unsigned)total_key(v) ^ 0x80000000u;
+    return ((unsigned long long)k << 32) | (unsigned)idx;
+}
+
+// fp32 -> fp16 pair with x ~= hi + lo (about 22 significant bits).
+__device__ __forceinline__ void split_hl(float x, __half& hi, __half& lo) {
+    hi = __float2half_rn(x);
+    lo = __float2half_rn(x - __half2float(hi));
 }
 
 }  // namespace gpt2q

@@ -40,6 +40,7 @@
 #include <vector>
 
 #include "gemm.h"
+#include "kernels.h"
 #include "tcgen05.cuh"
 
 namespace gpt2q {
@@ -358,25 +359,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 0) tc::tmem_dealloc(tmem, BN);
 }
 
-// fp32 activations -> fp16 hi / lo parts (x = hi + lo to ~22 bits), row-major [M][K].
-__global__ void k_split_hilo(const float* __restrict__ X, int ldx, int M, int K, __half* __restrict__ hi,
-                             __half* __restrict__ lo) {
-    tc::pdl_trigger();
-    tc::pdl_wait();
-    const int per_row = K / 8;
-    const size_t total = (size_t)M * per_row;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int m = (int)(i / per_row), c = (int)(i % per_row) * 8;
-        const float4 a = *reinterpret_cast<const float4*>(X + (size_t)m * ldx + c);
-        const float4 b = *reinterpret_cast<const float4*>(X + (size_t)m * ldx + c + 4);
-        const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        uint4 l;
-        const uint4 h = pack_hi_lo(f, l);
-        *reinterpret_cast<uint4*>(hi + (size_t)m * K + c) = h;
-        *reinterpret_cast<uint4*>(lo + (size_t)m * K + c) = l;
-    }
-}
-
 // One-time exact split of a quantised weight for the prefill path: w' = deq(w) * 2^P,
 // hi = f16(w'), lo = f16(w' - hi), both [rows][cols].
 __global__ void k_presplit_weight(QW w, float pre, __half* __restrict__ hi, __half* __restrict__ lo) {
@@ -417,15 +399,6 @@ bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
     cuuint32_t es[2] = {1, 1};
     return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-bool pdl_enabled() {
-    static int on = -1;
-    if (on < 0) {
-        const char* e = std::getenv("GPT2Q_NO_PDL");
-        on = (e && e[0] == '1') ? 0 : 1;
-    }
-    return on == 1;
 }
 
 template <int ATOM, int BN, bool PRESPLIT>
@@ -479,10 +452,21 @@ struct WeightTc {
     float pre = 1.f, post = 1.f;
 };
 
+struct XKey {
+    const void* buf;
+    int K, ld, BN;
+    bool operator==(const XKey& o) const { return buf == o.buf && K == o.K && ld == o.ld && BN == o.BN; }
+};
+struct XKeyHash {
+    size_t operator()(const XKey& k) const {
+        return std::hash<const void*>()(k.buf) ^ ((size_t)k.K << 1) ^ ((size_t)k.ld << 17) ^ ((size_t)k.BN << 33);
+    }
+};
+
 struct GemmState {
-    std::unordered_map<const void*, WeightTc> w;       // weight payload -> maps
-    std::unordered_map<uint64_t, CUtensorMap> xmaps;   // (K, BN, hi/lo) -> map
-    std::vector<void*> owned;                           // split weight copies
+    std::unordered_map<const void*, WeightTc> w;                 // weight payload -> maps
+    std::unordered_map<XKey, CUtensorMap, XKeyHash> xmaps;       // activation buffer -> map
+    std::vector<void*> owned;                                     // split weight copies
 };
 
 bool GemmPlan::usable(const QW& w, int M) const {
@@ -506,8 +490,6 @@ int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax) {
     if (const char* e = std::getenv("GPT2Q_TC_MIN_M")) p.min_m = std::max(1, std::atoi(e));
     p.presplit_min_m = 257;
     if (const char* e = std::getenv("GPT2Q_TC_PRESPLIT_MIN_M")) p.presplit_min_m = std::max(1, std::atoi(e));
-    const size_t xbytes = (size_t)Mmax * Kmax * 2;
-    if (cudaMalloc(&p.xhi, xbytes) != cudaSuccess || cudaMalloc(&p.xlo, xbytes) != cudaSuccess) return -1;
     if (cudaMalloc(&p.err, 4) != cudaSuccess || cudaMemset(p.err, 0, 4) != cudaSuccess) return -1;
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     p.state = new GemmState();
@@ -516,8 +498,6 @@ int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax) {
 }
 
 void gemm_destroy(GemmPlan& p) {
-    if (p.xhi) cudaFree(p.xhi);
-    if (p.xlo) cudaFree(p.xlo);
     if (p.err) cudaFree(p.err);
     if (p.state)
         for (void* q : p.state->owned) cudaFree(q);
@@ -566,41 +546,24 @@ int gemm_register_weight(GemmPlan& p, const QW& w, float max_abs_w, bool prespli
     return 0;
 }
 
-static const CUtensorMap* xmap(const GemmPlan& p, int K, int BN, bool hi) {
-    const uint64_t key = ((uint64_t)K << 20) | ((uint64_t)BN << 1) | (hi ? 1 : 0);
+// Tensor map of one fp16 activation buffer [Mmax][ld] viewed as [Mmax][K], box 64 x BN.
+static const CUtensorMap* xmap(const GemmPlan& p, const __half* buf, int K, int ld, int BN) {
+    const XKey key{buf, K, ld, BN};
     auto it = p.state->xmaps.find(key);
     if (it != p.state->xmaps.end()) return &it->second;
     CUtensorMap m;
-    if (!make_map_2d(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, hi ? p.xhi : p.xlo, (uint64_t)K, (uint64_t)p.Mmax,
-                     (uint64_t)K * 2, 64, (uint32_t)BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!make_map_2d(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, buf, (uint64_t)K, (uint64_t)p.Mmax, (uint64_t)ld * 2, 64,
+                     (uint32_t)BN, CU_TENSOR_MAP_SWIZZLE_128B))
         return nullptr;
     return &p.state->xmaps.emplace(key, m).first->second;
 }
 
-cudaError_t launch_split_hilo(const GemmPlan& p, const float* X, int ldx, int M, int K, cudaStream_t st) {
-    const size_t total = (size_t)M * (K / 8);
-    const int blocks = (int)std::max<size_t>(1, std::min<size_t>((total + 255) / 256, 148 * 8));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(256);
-    cfg.stream = st;
-    cudaLaunchAttribute at;
-    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at.val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = &at;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_split_hilo, X, ldx, M, K, reinterpret_cast<__half*>(p.xhi),
-                              reinterpret_cast<__half*>(p.xlo));
-}
-
-cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const float* X, int ldx, int M, const Epi& e,
+cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, int M, const Epi& e,
                              cudaStream_t st) {
     auto wi = p.state->w.find(w.q);
     if (wi == p.state->w.end()) return cudaErrorInvalidValue;
     const WeightTc& wt = wi->second;
     const int K = w.cols;
-    cudaError_t ce = launch_split_hilo(p, X, ldx, M, K, st);
-    if (ce != cudaSuccess) return ce;
     const bool presplit = wt.has_split && M >= p.presplit_min_m;
     const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
     const int m_tiles = (M + BN - 1) / BN;
@@ -614,8 +577,8 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const float* X, int
     }
     int kb_per = (nkb + splits - 1) / splits;
     splits = (nkb + kb_per - 1) / kb_per;
-    const CUtensorMap* xh = xmap(p, K, BN, true);
-    const CUtensorMap* xl = xmap(p, K, BN, false);
+    const CUtensorMap* xh = xmap(p, x.hi, K, x.ld, BN);
+    const CUtensorMap* xl = xmap(p, x.lo, K, x.ld, BN);
     if (!xh || !xl) return cudaErrorInvalidValue;
     TcParams tp;
     tp.w = w;

@@ -10,13 +10,19 @@ namespace gpt2q {
 
 struct GemmState;
 
+// Activation operand of the tensor-core linear: x = hi + lo, fp16 [Mmax][ld] buffers
+// written by the producing kernel (LayerNorm, attention, GELU epilogue).
+struct XSplit {
+    const __half* hi;
+    const __half* lo;
+    int ld;
+};
+
 struct GemmPlan {
     bool enabled = false;
     int min_m = 1 << 30;         // the tensor-core path serves M >= min_m
     int presplit_min_m = 1 << 30;  // ... and reads the fp16 hi/lo weight copies for M >= this
     int Mmax = 0, Kmax = 0;
-    void* xhi = nullptr;  // fp16 [Mmax][K] activation hi parts
-    void* xlo = nullptr;  // fp16 [Mmax][K] activation lo parts
     int* err = nullptr;   // device error word (bounded-wait timeouts)
     size_t presplit_bytes = 0;
     GemmState* state = nullptr;
@@ -29,7 +35,7 @@ void gemm_destroy(GemmPlan& p);
 // derived from an upper bound of max |dequantised weight| and, when `presplit`, the
 // exact fp16 hi/lo copy used by the compute-bound prefill regime.
 int gemm_register_weight(GemmPlan& p, const QW& w, float max_abs_w, bool presplit, cudaStream_t st);
-cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const float* X, int ldx, int M, const Epi& e,
+cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, int M, const Epi& e,
                              cudaStream_t st);
 // Reads and clears the device error word (0 = no error). Synchronises `st`.
 int gemm_take_error(GemmPlan& p, cudaStream_t st);

@@ -10,9 +10,40 @@
 // per row, and attention is tiled with online softmax instead of thread-0 loops.
 #include <float.h>
 
+#include <cstdlib>
+
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace gpt2q {
+
+bool pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = std::getenv("GPT2Q_NO_PDL");
+        on = (e && e[0] == '1') ? 0 : 1;
+    }
+    return on == 1;
+}
+
+// Every kernel here is launched as a programmatic dependent of the previous kernel in
+// the stream: it lets its own dependents start early (pdl_trigger) and waits for its
+// inputs (pdl_wait) before touching activations.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 // ------------------------------------------------------------------ helpers
 __device__ __forceinline__ float warp_sum(float v) {
@@ -30,6 +61,8 @@ __device__ __forceinline__ float warp_max(float v) {
 // x[m] = deq(wte[tok[m]]) + deq(wpe[pos[m]])   (gpt2.rs:229-236, gpu.rs:239-261)
 __global__ void k_embed(QW wte, QW wpe, const uint32_t* __restrict__ tok, const int* __restrict__ pos,
                         float* __restrict__ x, int d) {
+    tc::pdl_trigger();
+    tc::pdl_wait();
     const int m = blockIdx.x;
     const int t = (int)tok[m], p = pos[m];
     for (int i = threadIdx.x; i < d; i += blockDim.x)
@@ -39,68 +72,132 @@ __global__ void k_embed(QW wte, QW wpe, const uint32_t* __restrict__ tok, const 
 cudaError_t launch_embed(const QW& wte, const QW& wpe, const uint32_t* tok, const int* pos, float* x,
                          int d, int M, cudaStream_t st) {
     if (M <= 0) return cudaSuccess;
-    k_embed<<<M, 256, 0, st>>>(wte, wpe, tok, pos, x, d);
-    return cudaGetLastError();
+    return launch_pdl(k_embed, dim3(M), dim3(256), 0, st, wte, wpe, tok, pos, x, d);
 }
 
 // ------------------------------------------------------------------ LayerNorm
-// One warp per row: mean, population variance, (x-mean)/sqrt(var+eps)*g+b (gpt2.rs:178-185).
-// The row is held in registers (NV values per lane, d <= 32*NV) so every load of the row
-// is issued before the first reduction. rows (optional) gathers source rows, e.g. the
-// last prompt position of each sequence.
-template <int NV>
-__global__ void __launch_bounds__(128) k_layernorm(const float* __restrict__ x, int ldx,
-                                                   const int* __restrict__ rows, float* __restrict__ y, int ldy,
-                                                   const float* __restrict__ g, const float* __restrict__ b, int d,
-                                                   float eps, int M) {
+// One warp per row: mean, population variance, (x-mean)/sqrt(var+eps)*g+b (gpt2.rs:178-185),
+// computed as (x-mean) * (1/sqrt(var+eps)) * g + b (within 1 ulp of the division; an IEEE
+// division per element costs more than the whole row otherwise). The row is held in
+// registers as VEC-wide vectors (NV per lane, d = 32*VEC*NV) so every load is issued before
+// the first reduction. Optional outputs: fp16 hi/lo copies for a tensor-core consumer.
+// rows (optional) gathers source rows, e.g. the last prompt position of each sequence.
+template <int VEC>
+struct VecT;
+template <>
+struct VecT<4> { using T = float4; };
+template <>
+struct VecT<2> { using T = float2; };
+
+__device__ __forceinline__ void vec_get(const float4& v, float* f) { f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w; }
+__device__ __forceinline__ void vec_get(const float2& v, float* f) { f[0] = v.x; f[1] = v.y; }
+__device__ __forceinline__ float4 vec_make4(const float* f) { return make_float4(f[0], f[1], f[2], f[3]); }
+
+template <int VEC, int NV>
+__global__ void __launch_bounds__(128) k_layernorm(const float* __restrict__ x, int ldx, const int* __restrict__ rows,
+                                                   float* __restrict__ y, int ldy, __half* __restrict__ yhi,
+                                                   __half* __restrict__ ylo, const float* __restrict__ g,
+                                                   const float* __restrict__ b, float eps, int M) {
+    using V = typename VecT<VEC>::T;
+    constexpr int D = 32 * VEC * NV;
+    tc::pdl_trigger();
+    tc::pdl_wait();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const int src = rows ? rows[warp] : warp;
+    const V* xr = reinterpret_cast<const V*>(x + (size_t)src * ldx);
+    float v[NV][VEC];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) vec_get(xr[lane + 32 * j], v[j]);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) s += v[j][e];
+    const float mean = warp_sum(s) / (float)D;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+            const float t = v[j][e] - mean;
+            q += t * t;
+        }
+    const float var = warp_sum(q) / (float)D;
+    const float rstd = __frcp_rn(sqrtf(var + eps));
+    const V* gv = reinterpret_cast<const V*>(g);
+    const V* bv = reinterpret_cast<const V*>(b);
+    float* yr = y + (size_t)warp * ldy;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        float gg[VEC], bb[VEC], o[VEC];
+        vec_get(gv[lane + 32 * j], gg);
+        vec_get(bv[lane + 32 * j], bb);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = (v[j][e] - mean) * rstd * gg[e] + bb[e];
+        const int i0 = (lane + 32 * j) * VEC;
+        if (VEC == 4) {
+            *reinterpret_cast<float4*>(yr + i0) = vec_make4(o);
+        } else {
+            *reinterpret_cast<float2*>(yr + i0) = make_float2(o[0], o[1]);
+        }
+        if (yhi) {
+            __half h[VEC], l[VEC];
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) split_hl(o[e], h[e], l[e]);
+            __half* ph = yhi + (size_t)warp * ldy + i0;
+            __half* pl = ylo + (size_t)warp * ldy + i0;
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) {
+                *reinterpret_cast<__half2*>(ph + e) = __halves2half2(h[e], h[e + 1]);
+                *reinterpret_cast<__half2*>(pl + e) = __halves2half2(l[e], l[e + 1]);
+            }
+        }
+    }
+}
+
+// Any d (multiple of 2): strided scalar form of the same computation.
+__global__ void __launch_bounds__(128) k_layernorm_any(const float* __restrict__ x, int ldx,
+                                                       const int* __restrict__ rows, float* __restrict__ y, int ldy,
+                                                       __half* __restrict__ yhi, __half* __restrict__ ylo,
+                                                       const float* __restrict__ g, const float* __restrict__ b, int d,
+                                                       float eps, int M) {
+    tc::pdl_trigger();
+    tc::pdl_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= M) return;
     const int src = rows ? rows[warp] : warp;
     const float* xr = x + (size_t)src * ldx;
-    float v[NV];
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int i = lane + 32 * j;
-        v[j] = (i < d) ? xr[i] : 0.f;
-    }
     float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < NV; ++j) s += v[j];
+    for (int i = lane; i < d; i += 32) s += xr[i];
     const float mean = warp_sum(s) / (float)d;
     float q = 0.f;
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int i = lane + 32 * j;
-        const float t = (i < d) ? v[j] - mean : 0.f;
+    for (int i = lane; i < d; i += 32) {
+        const float t = xr[i] - mean;
         q += t * t;
     }
-    const float var = warp_sum(q) / (float)d;
-    const float den = sqrtf(var + eps);
-    float* yr = y + (size_t)warp * ldy;
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int i = lane + 32 * j;
-        if (i < d) yr[i] = (v[j] - mean) / den * g[i] + b[i];
+    const float rstd = __frcp_rn(sqrtf(warp_sum(q) / (float)d + eps));
+    for (int i = lane; i < d; i += 32) {
+        const float o = (xr[i] - mean) * rstd * g[i] + b[i];
+        y[(size_t)warp * ldy + i] = o;
+        if (yhi) split_hl(o, yhi[(size_t)warp * ldy + i], ylo[(size_t)warp * ldy + i]);
     }
 }
 
-cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y, int ldy, const float* g,
-                             const float* b, int d, float eps, int M, cudaStream_t st) {
+cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y, int ldy, __half* yhi, __half* ylo,
+                             const float* g, const float* b, int d, float eps, int M, cudaStream_t st) {
     if (M <= 0) return cudaSuccess;
-    const int threads = 128, rows_per_block = threads / 32;
-    const int grid = (M + rows_per_block - 1) / rows_per_block;
-    if (d <= 32 * 8)
-        k_layernorm<8><<<grid, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d, eps, M);
-    else if (d <= 32 * 24)
-        k_layernorm<24><<<grid, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d, eps, M);
-    else if (d <= 32 * 32)
-        k_layernorm<32><<<grid, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d, eps, M);
-    else if (d <= 32 * 56)
-        k_layernorm<56><<<grid, threads, 0, st>>>(x, ldx, rows, y, ldy, g, b, d, eps, M);
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    const dim3 grid((M + 3) / 4), block(128);
+    const bool al = (ldx % 4 == 0) && (ldy % 4 == 0);
+    if (al && d == 768) return launch_pdl(k_layernorm<4, 6>, grid, block, 0, st, x, ldx, rows, y, ldy, yhi, ylo, g, b, eps, M);
+    if (al && d == 1024) return launch_pdl(k_layernorm<4, 8>, grid, block, 0, st, x, ldx, rows, y, ldy, yhi, ylo, g, b, eps, M);
+    if (al && d == 1280) return launch_pdl(k_layernorm<4, 10>, grid, block, 0, st, x, ldx, rows, y, ldy, yhi, ylo, g, b, eps, M);
+    if (al && d == 1600) return launch_pdl(k_layernorm<2, 25>, grid, block, 0, st, x, ldx, rows, y, ldy, yhi, ylo, g, b, eps, M);
+    if (al && d == 128) return launch_pdl(k_layernorm<4, 1>, grid, block, 0, st, x, ldx, rows, y, ldy, yhi, ylo, g, b, eps, M);
+    if (al && d == 256) return launch_pdl(k_layernorm<4, 2>, grid, block, 0, st, x, ldx, rows, y, ldy, yhi, ylo, g, b, eps, M);
+    return launch_pdl(k_layernorm_any, grid, block, 0, st, x, ldx, rows, y, ldy, yhi, ylo, g, b, d, eps, M);
 }
 
 // ------------------------------------------------------------------ linear (CUDA cores)
@@ -174,6 +271,8 @@ template <int ATOM, int MT, int U>
 __global__ void __launch_bounds__(256) k_linear_simt(QW w, const float* __restrict__ X, int ldx, int M,
                                                      Epi epi) {
     constexpr int CE = ChunkTraits<ATOM>::CE;
+    tc::pdl_trigger();
+    tc::pdl_wait();
     const int lane16 = threadIdx.x & 15;
     const int n = blockIdx.x * (blockDim.x >> 4) + (threadIdx.x >> 4);
     const bool active = n < w.rows;
@@ -249,15 +348,10 @@ static cudaError_t linear_dispatch(const QW& w, const float* X, int ldx, int M, 
     if (w.rows < 148 * 2 * 8) rpb = 4;
     if (w.rows < 148 * 2 * 4) rpb = 2;
     dim3 grid((w.rows + rpb - 1) / rpb), block(16 * rpb);
-    if (M == 1)
-        k_linear_simt<ATOM, 1, 4><<<grid, block, 0, st>>>(w, X, ldx, M, e);
-    else if (M <= 2)
-        k_linear_simt<ATOM, 2, 4><<<grid, block, 0, st>>>(w, X, ldx, M, e);
-    else if (M <= 4)
-        k_linear_simt<ATOM, 4, 4><<<grid, block, 0, st>>>(w, X, ldx, M, e);
-    else
-        k_linear_simt<ATOM, 8, 2><<<grid, block, 0, st>>>(w, X, ldx, M, e);
-    return cudaGetLastError();
+    if (M == 1) return launch_pdl(k_linear_simt<ATOM, 1, 4>, grid, block, 0, st, w, X, ldx, M, e);
+    if (M <= 2) return launch_pdl(k_linear_simt<ATOM, 2, 4>, grid, block, 0, st, w, X, ldx, M, e);
+    if (M <= 4) return launch_pdl(k_linear_simt<ATOM, 4, 4>, grid, block, 0, st, w, X, ldx, M, e);
+    return launch_pdl(k_linear_simt<ATOM, 8, 2>, grid, block, 0, st, w, X, ldx, M, e);
 }
 
 cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, const Epi& e, cudaStream_t st) {
@@ -271,19 +365,23 @@ cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, cons
 }
 
 // ------------------------------------------------------------------ decode attention
-// One block of 4 warps per (head, sequence). Each warp takes 32 keys at a time:
-// lane j scores key t0+j against q (q broadcast from shared memory), the warp does
-// an online-softmax update, then accumulates p_j * V[t0+j] with lane l owning dims
-// 2l, 2l+1 (coalesced 256 B V rows). Warps are merged through shared memory.
+// One block of 4 warps per (head, sequence). Each warp takes 32 keys at a time: lane j
+// scores key t0+j against q (q broadcast from shared memory); the V rows of the same 32
+// keys are loaded in the same burst (lane l owns dims 2l, 2l+1, coalesced 256-byte rows),
+// so one memory round trip serves the whole block. The warp does an online-softmax update
+// and the four warps are merged through shared memory.
 // Semantics: softmax(q.K^T * scale) V over positions 0..pos (gpt2.rs:261-291).
 __global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q, int ldq, KVGeom g,
                                                      size_t layer_off, const int* __restrict__ slot,
                                                      const int* __restrict__ pos, float* __restrict__ out,
-                                                     int ldo, float scale) {
+                                                     __half* __restrict__ ohi, __half* __restrict__ olo, int ldo,
+                                                     float scale) {
     constexpr int HD = 64;
     __shared__ float4 qs[HD / 4];
     __shared__ float wm[4], wl[4];
     __shared__ float wo[4][HD];
+    tc::pdl_trigger();
+    tc::pdl_wait();
     const int head = blockIdx.x, b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int T = pos[b] + 1;
@@ -296,36 +394,37 @@ __global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q
     float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
     for (int t0 = warp * 32; t0 < T; t0 += 128) {
         const int t = t0 + lane;
-        float s = -INFINITY;
-        if (t < T) {
-            const float4* kr = reinterpret_cast<const float4*>(K + (size_t)t * HD);
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        const int nv = min(32, T - t0);
+        // one burst: this lane's K row and the V slice of all 32 rows
+        float4 kr[HD / 4];
+        const float4* kp = reinterpret_cast<const float4*>(K + (size_t)min(t, T - 1) * HD);
 #pragma unroll
-            for (int i = 0; i < HD / 4; ++i) {
-                float4 kv = __ldg(kr + i);
-                float4 qv = qs[i];
-                a0 = fmaf(qv.x, kv.x, a0);
-                a1 = fmaf(qv.y, kv.y, a1);
-                a2 = fmaf(qv.z, kv.z, a2);
-                a3 = fmaf(qv.w, kv.w, a3);
-            }
-            s = ((a0 + a1) + (a2 + a3)) * scale;
+        for (int i = 0; i < HD / 4; ++i) kr[i] = __ldg(kp + i);
+        float2 vv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            vv[j] = __ldg(reinterpret_cast<const float2*>(V + (size_t)(t0 + min(j, nv - 1)) * HD) + lane);
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD / 4; ++i) {
+            const float4 qv = qs[i];
+            a0 = fmaf(qv.x, kr[i].x, a0);
+            a1 = fmaf(qv.y, kr[i].y, a1);
+            a2 = fmaf(qv.z, kr[i].z, a2);
+            a3 = fmaf(qv.w, kr[i].w, a3);
         }
+        const float s = (t < T) ? ((a0 + a1) + (a2 + a3)) * scale : -INFINITY;
         const float mnew = fmaxf(m, warp_max(s));
         const float corr = expf(m - mnew);
         const float p = (t < T) ? expf(s - mnew) : 0.f;
         l = l * corr + warp_sum(p);
         o0 *= corr;
         o1 *= corr;
-        const int nv = min(32, T - t0);
-#pragma unroll 8
+#pragma unroll
         for (int j = 0; j < 32; ++j) {
-            const float pj = __shfl_sync(0xffffffffu, p, j);
-            if (j < nv) {
-                const float2 v = __ldg(reinterpret_cast<const float2*>(V + (size_t)(t0 + j) * HD) + lane);
-                o0 = fmaf(pj, v.x, o0);
-                o1 = fmaf(pj, v.y, o1);
-            }
+            const float pj = __shfl_sync(0xffffffffu, p, j);  // 0 for j >= nv
+            o0 = fmaf(pj, vv[j].x, o0);
+            o1 = fmaf(pj, vv[j].y, o1);
         }
         m = mnew;
     }
@@ -349,17 +448,20 @@ __global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q
                 O += wo[w][threadIdx.x] * f;
             }
         }
-        out[(size_t)b * ldo + head * HD + threadIdx.x] = O / L;
+        const float r = O / L;
+        const size_t o = (size_t)b * ldo + head * HD + threadIdx.x;
+        out[o] = r;
+        if (ohi) split_hl(r, ohi[o], olo[o]);
     }
 }
 
 cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t layer_off, const int* slot,
-                               const int* pos, float* out, int ldo, int n_head, int B, float scale,
-                               cudaStream_t st) {
+                               const int* pos, float* out, __half* ohi, __half* olo, int ldo, int n_head, int B,
+                               float scale, cudaStream_t st) {
     if (B <= 0) return cudaSuccess;
     if (g.hd != 64) return cudaErrorInvalidValue;
-    k_attn_decode<<<dim3(n_head, B), 128, 0, st>>>(q, ldq, g, layer_off, slot, pos, out, ldo, scale);
-    return cudaGetLastError();
+    return launch_pdl(k_attn_decode, dim3(n_head, B), dim3(128), 0, st, q, ldq, g, layer_off, slot, pos, out, ohi,
+                      olo, ldo, scale);
 }
 
 // ------------------------------------------------------------------ prefill attention
@@ -369,10 +471,13 @@ cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t 
 // paired reads hit distinct banks. Causal mask: key t attends iff t <= query position.
 __global__ void __launch_bounds__(128) k_attn_prefill(const float* __restrict__ q, int ldq, KVGeom g,
                                                       size_t layer_off, const AttnTile* __restrict__ tiles,
-                                                      float* __restrict__ out, int ldo, float scale) {
+                                                      float* __restrict__ out, __half* __restrict__ ohi,
+                                                      __half* __restrict__ olo, int ldo, float scale) {
     constexpr int HD = 64, KT = 32;
     __shared__ float Ks[KT][HD];
     __shared__ float Vs[KT][HD];
+    tc::pdl_trigger();
+    tc::pdl_wait();
     const AttnTile tile = tiles[blockIdx.y];
     const int head = blockIdx.x;
     const int qi = threadIdx.x >> 1, half = threadIdx.x & 1;
@@ -442,76 +547,93 @@ __global__ void __launch_bounds__(128) k_attn_prefill(const float* __restrict__ 
         m = mnew;
     }
     if (valid) {
-        float* orow = out + (size_t)(tile.row0 + qpos) * ldo + head * HD + half * 32;
+        const size_t base = (size_t)(tile.row0 + qpos) * ldo + head * HD + half * 32;
         const float inv = 1.0f / l;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) orow[i] = o[i] * inv;
+        for (int i = 0; i < 32; ++i) {
+            const float r = o[i] * inv;
+            out[base + i] = r;
+            if (ohi) split_hl(r, ohi[base + i], olo[base + i]);
+        }
     }
 }
 
 cudaError_t launch_attn_prefill(const float* q, int ldq, const KVGeom& g, size_t layer_off,
-                                const AttnTile* tiles, int n_tiles, float* out, int ldo, int n_head,
-                                float scale, cudaStream_t st) {
+                                const AttnTile* tiles, int n_tiles, float* out, __half* ohi, __half* olo, int ldo,
+                                int n_head, float scale, cudaStream_t st) {
     if (n_tiles <= 0) return cudaSuccess;
     if (g.hd != 64) return cudaErrorInvalidValue;
-    k_attn_prefill<<<dim3(n_head, n_tiles), 128, 0, st>>>(q, ldq, g, layer_off, tiles, out, ldo, scale);
-    return cudaGetLastError();
+    return launch_pdl(k_attn_prefill, dim3(n_head, n_tiles), dim3(128), 0, st, q, ldq, g, layer_off, tiles, out, ohi,
+                      olo, ldo, scale);
 }
 
 // ------------------------------------------------------------------ argmax
-// Greedy pick (gpt2.rs:390-396): Iterator::max_by(total_cmp) keeps the LAST maximum,
-// so (key, index) pairs are compared lexicographically with the larger index winning.
-__device__ __forceinline__ void better(int& bk, int& bi, int k, int i) {
-    if (k > bk || (k == bk && i > bi)) {
-        bk = k;
-        bi = i;
-    }
+// Greedy pick (gpt2.rs:390-396): Iterator::max_by(total_cmp) keeps the LAST maximum.
+// (total-order key, index) pairs pack into one u64 whose max is exactly that element, so
+// the row is split over many blocks: each reduces its chunk and does one atomicMax on the
+// row's slot (max is order-independent: deterministic); the finaliser reads and clears it.
+constexpr int ARGMAX_CHUNK = 4096;
+
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) {
+    return a > b ? a : b;
 }
 
-__global__ void __launch_bounds__(512) k_argmax(const float* __restrict__ logits, int V, int ld,
-                                                uint32_t* __restrict__ next, uint32_t* __restrict__ genlog,
-                                                const int* __restrict__ gpos, int n_ctx,
-                                                uint32_t* __restrict__ tok_adv, int* __restrict__ pos_adv) {
-    __shared__ int sk[16], si[16];
-    const int b = blockIdx.x;
+__global__ void __launch_bounds__(256) k_argmax_partial(const float* __restrict__ logits, int V, int ld,
+                                                        unsigned long long* __restrict__ best) {
+    __shared__ unsigned long long sm[8];
+    tc::pdl_trigger();
+    tc::pdl_wait();
+    const int b = blockIdx.y;
+    const int base = blockIdx.x * ARGMAX_CHUNK;
     const float* row = logits + (size_t)b * ld;
-    int bk = INT_MIN, bi = -1;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) better(bk, bi, total_key(row[i]), i);
+    float v[ARGMAX_CHUNK / 256];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        int k2 = __shfl_xor_sync(0xffffffffu, bk, o), i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-        better(bk, bi, k2, i2);
+    for (int j = 0; j < ARGMAX_CHUNK / 256; ++j) {
+        const int i = base + j * 256 + threadIdx.x;
+        v[j] = (i < V) ? row[i] : 0.f;
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) {
-        sk[warp] = bk;
-        si[warp] = bi;
+    unsigned long long bk = 0;
+#pragma unroll
+    for (int j = 0; j < ARGMAX_CHUNK / 256; ++j) {
+        const int i = base + j * 256 + threadIdx.x;
+        if (i < V) bk = umax64(bk, argmax_pack(v[j], i));
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) bk = umax64(bk, __shfl_xor_sync(0xffffffffu, bk, o));
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = bk;
     __syncthreads();
-    if (warp == 0) {
-        const int nw = blockDim.x >> 5;
-        bk = lane < nw ? sk[lane] : INT_MIN;
-        bi = lane < nw ? si[lane] : -1;
+    if (threadIdx.x == 0) {
+        unsigned long long r = sm[0];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            int k2 = __shfl_xor_sync(0xffffffffu, bk, o), i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-            better(bk, bi, k2, i2);
-        }
-        if (lane == 0) {
-            const uint32_t best = (uint32_t)bi;
-            next[b] = best;
-            if (genlog) genlog[(size_t)b * n_ctx + gpos[b]] = best;
-            if (tok_adv) tok_adv[b] = best;
-            if (pos_adv) pos_adv[b] += 1;
-        }
+        for (int w = 1; w < 8; ++w) r = umax64(r, sm[w]);
+        atomicMax(best + b, r);
     }
 }
 
-cudaError_t launch_argmax(const float* logits, int V, int ld, int B, uint32_t* next, uint32_t* genlog,
-                          const int* gpos, int n_ctx, uint32_t* tok_adv, int* pos_adv, cudaStream_t st) {
+__global__ void k_argmax_finalize(unsigned long long* __restrict__ best, int B, uint32_t* __restrict__ next,
+                                  uint32_t* __restrict__ genlog, const int* __restrict__ gpos, int n_ctx,
+                                  uint32_t* __restrict__ tok_adv, int* __restrict__ pos_adv) {
+    tc::pdl_trigger();
+    tc::pdl_wait();
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        const uint32_t tok = (uint32_t)(best[b] & 0xffffffffull);
+        best[b] = 0ull;
+        next[b] = tok;
+        if (genlog) genlog[(size_t)b * n_ctx + gpos[b]] = tok;
+        if (tok_adv) tok_adv[b] = tok;
+        if (pos_adv) pos_adv[b] += 1;
+    }
+}
+
+cudaError_t launch_argmax(const float* logits, int V, int ld, int B, unsigned long long* best, uint32_t* next,
+                          uint32_t* genlog, const int* gpos, int n_ctx, uint32_t* tok_adv, int* pos_adv,
+                          cudaStream_t st) {
     if (B <= 0) return cudaSuccess;
-    k_argmax<<<B, 512, 0, st>>>(logits, V, ld, next, genlog, gpos, n_ctx, tok_adv, pos_adv);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(k_argmax_partial, dim3((V + ARGMAX_CHUNK - 1) / ARGMAX_CHUNK, B), dim3(256), 0, st,
+                               logits, V, ld, best);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_argmax_finalize, dim3(1), dim3(256), 0, st, best, B, next, genlog, gpos, n_ctx, tok_adv,
+                      pos_adv);
 }
 
 // ------------------------------------------------------------------ dequant / repack

@@ -24,21 +24,26 @@ struct AttnTile {
 
 cudaError_t launch_embed(const QW& wte, const QW& wpe, const uint32_t* tok, const int* pos, float* x,
                          int d, int M, cudaStream_t st);
-cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y, int ldy, const float* g,
-                             const float* b, int d, float eps, int M, cudaStream_t st);
+// y = LayerNorm(x rows) and, when yhi != null, its fp16 hi/lo split (row stride ldy).
+cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y, int ldy, __half* yhi, __half* ylo,
+                             const float* g, const float* b, int d, float eps, int M, cudaStream_t st);
 // out = epilogue(X[M][K] . W^T) on CUDA cores (fp32 FMA, weights dequantised in registers).
 cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, const Epi& e,
                                cudaStream_t st);
-cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t layer_off,
-                               const int* slot, const int* pos, float* out, int ldo, int n_head,
-                               int B, float scale, cudaStream_t st);
+cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t layer_off, const int* slot,
+                               const int* pos, float* out, __half* ohi, __half* olo, int ldo, int n_head, int B,
+                               float scale, cudaStream_t st);
 cudaError_t launch_attn_prefill(const float* q, int ldq, const KVGeom& g, size_t layer_off,
-                                const AttnTile* tiles, int n_tiles, float* out, int ldo, int n_head,
-                                float scale, cudaStream_t st);
-// Greedy argmax per row (total order, ties -> last index).
-cudaError_t launch_argmax(const float* logits, int V, int ld, int B, uint32_t* next, uint32_t* genlog,
-                          const int* gpos, int n_ctx, uint32_t* tok_adv, int* pos_adv,
+                                const AttnTile* tiles, int n_tiles, float* out, __half* ohi, __half* olo, int ldo,
+                                int n_head, float scale, cudaStream_t st);
+// Greedy argmax per row (total order, ties -> last index). `best` holds one zeroed u64 per
+// row; the finaliser consumes and re-zeroes it, writes next[], and optionally logs the
+// token at genlog[b][gpos[b]], feeds it back (tok_adv) and advances pos_adv.
+cudaError_t launch_argmax(const float* logits, int V, int ld, int B, unsigned long long* best, uint32_t* next,
+                          uint32_t* genlog, const int* gpos, int n_ctx, uint32_t* tok_adv, int* pos_adv,
                           cudaStream_t st);
+// Programmatic dependent launch on/off (GPT2Q_NO_PDL=1 disables it).
+bool pdl_enabled();
 cudaError_t launch_dequant(const QW& w, float* out, cudaStream_t st);
 // Upload-time layout conversion from the SMT payload (raw, on device).
 cudaError_t launch_repack_q8(const uint8_t* raw, int rows, int cols, uint8_t* q, __half* s, int sstride,

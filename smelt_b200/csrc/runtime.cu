@@ -111,6 +111,9 @@ struct gpt2q_handle {
     KVGeom kv{};
     int Mmax = 0;
     float *x = nullptr, *h = nullptr, *qb = nullptr, *att = nullptr, *f = nullptr, *logits = nullptr;
+    // fp16 hi/lo copies of the linear inputs (h: LayerNorm out, att: attention out, f: GELU out)
+    __half *h_hi = nullptr, *h_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr, *f_hi = nullptr, *f_lo = nullptr;
+    unsigned long long* best = nullptr;  // argmax slots, one per sequence
     float* tp_red = nullptr;  // tensor-parallel partial sums [Mmax][d]
     // prefill scratch
     uint32_t* p_tok = nullptr;
@@ -334,23 +337,33 @@ double linear_bytes(const Linear& L, int M, int extra_out_rw) {
     return (double)L.weight_bytes + (double)M * L.cols * 4 + (double)M * L.rows * 4 * extra_out_rw;
 }
 
-int linear(gpt2q_handle* H, const char* name, const Linear& L, const float* X, int ldx, int M, const Epi& e) {
+// Linear input: fp32 rows for the CUDA-core kernel and their fp16 hi/lo split for the
+// tensor-core kernel (both written by the producer).
+struct In {
+    const float* f;
+    const __half* hi;
+    const __half* lo;
+    int ld;
+};
+
+int linear(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int M, const Epi& e) {
     const int extra = (e.kind == EPI_RESID) ? 2 : 1;
     const double bytes = linear_bytes(L, M, extra);
-    if (H->gemm.usable(L.w, M)) {
-        RUN(name, bytes, launch_linear_tc(H->gemm, L.w, X, ldx, M, e, H->stream));
+    if (X.hi && H->gemm.usable(L.w, M)) {
+        const XSplit xs{X.hi, X.lo, X.ld};
+        RUN(name, bytes, launch_linear_tc(H->gemm, L.w, xs, M, e, H->stream));
     } else {
-        RUN(name, bytes, launch_linear_simt(L.w, X, ldx, M, e, H->stream));
+        RUN(name, bytes, launch_linear_simt(L.w, X.f, X.ld, M, e, H->stream));
     }
     return GPT2Q_OK;
 }
 
 // Residual update of row-split projections under tensor parallelism: y = partial (+bias on
 // rank 0), all-reduce(y), x += y.
-int tp_residual(gpt2q_handle* H, const char* name, const Linear& L, const float* X, int ldx, int M) {
+int tp_residual(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int M) {
     const int d = H->cfg.n_embd;
     Epi e = epi_store(H->tp_red, d, H->tp_rank == 0 ? L.bias : nullptr);
-    int rc = linear(H, name, L, X, ldx, M, e);
+    int rc = linear(H, name, L, X, M, e);
     if (rc) return rc;
     rc = tp_allreduce_add(H->tp, H->tp_red, H->x, (size_t)M * d, H->stream);
     if (rc) return H->fail(GPT2Q_ENCCL, tp_last_error(H->tp));
@@ -386,32 +399,39 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     const int d = H->cfg.n_embd;
     const float eps = H->cfg.ln_eps;
     LayerW& Lw = H->layers[layer];
-    RUN("layernorm", (double)M * d * 8, launch_layernorm(H->x, d, nullptr, H->h, d, Lw.ln1_g, Lw.ln1_b, d, eps, M, H->stream));
-    int rc = linear(H, "linear_qkv", Lw.attn, H->h, d, M, epi_qkv(H, layer, slot, pos, Lw.attn.bias));
+    const In hin{H->h, H->h_hi, H->h_lo, d};
+    const In ain{H->att, H->att_hi, H->att_lo, H->d_local};
+    const In fin{H->f, H->f_hi, H->f_lo, H->fc_local};
+    RUN("layernorm", (double)M * d * 8,
+        launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln1_g, Lw.ln1_b, d, eps, M, H->stream));
+    int rc = linear(H, "linear_qkv", Lw.attn, hin, M, epi_qkv(H, layer, slot, pos, Lw.attn.bias));
     if (rc) return rc;
     rc = attn_fn(layer);
     if (rc) return rc;
     if (H->tp_size > 1) {
-        rc = tp_residual(H, "linear_attn_proj", Lw.proj, H->att, H->d_local, M);
+        rc = tp_residual(H, "linear_attn_proj", Lw.proj, ain, M);
     } else {
         Epi e = epi_store(H->x, d, Lw.proj.bias);
         e.kind = EPI_RESID;
-        rc = linear(H, "linear_attn_proj", Lw.proj, H->att, H->d_local, M, e);
+        rc = linear(H, "linear_attn_proj", Lw.proj, ain, M, e);
     }
     if (rc) return rc;
-    RUN("layernorm", (double)M * d * 8, launch_layernorm(H->x, d, nullptr, H->h, d, Lw.ln2_g, Lw.ln2_b, d, eps, M, H->stream));
+    RUN("layernorm", (double)M * d * 8,
+        launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln2_g, Lw.ln2_b, d, eps, M, H->stream));
     {
         Epi e = epi_store(H->f, H->fc_local, Lw.fc.bias);
         e.kind = EPI_GELU;
-        rc = linear(H, "linear_fc_gelu", Lw.fc, H->h, d, M, e);
+        e.out_hi = H->f_hi;
+        e.out_lo = H->f_lo;
+        rc = linear(H, "linear_fc_gelu", Lw.fc, hin, M, e);
         if (rc) return rc;
     }
     if (H->tp_size > 1) {
-        rc = tp_residual(H, "linear_mlp_proj", Lw.mproj, H->f, H->fc_local, M);
+        rc = tp_residual(H, "linear_mlp_proj", Lw.mproj, fin, M);
     } else {
         Epi e = epi_store(H->x, d, Lw.mproj.bias);
         e.kind = EPI_RESID;
-        rc = linear(H, "linear_mlp_proj", Lw.mproj, H->f, H->fc_local, M, e);
+        rc = linear(H, "linear_mlp_proj", Lw.mproj, fin, M, e);
     }
     return rc;
 }
@@ -427,18 +447,23 @@ int enqueue_decode(gpt2q_handle* H, int B) {
         int rc = block(H, l, B, H->d_slot, H->d_pos, [&](int layer) {
             RUN("attn_decode", kv_bytes + (double)B * H->d_local * 8,
                 launch_attn_decode(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->d_slot,
-                                   H->d_pos, H->att, H->d_local, H->H_local, B, scale, H->stream));
+                                   H->d_pos, H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, B, scale,
+                                   H->stream));
             return GPT2Q_OK;
         });
         if (rc) return rc;
     }
     RUN("layernorm", (double)B * d * 8,
-        launch_layernorm(H->x, d, nullptr, H->h, d, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, B, H->stream));
-    int rc = linear(H, "linear_head", H->wte, H->h, d, B, epi_store(H->logits, H->cfg.vocab, nullptr));
+        launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, B,
+                         H->stream));
+    int rc = linear(H, "linear_head", H->wte, In{H->h, H->h_hi, H->h_lo, d}, B,
+                    epi_store(H->logits, H->cfg.vocab, nullptr));
     if (rc) return rc;
     RUN("argmax", (double)B * H->cfg.vocab * 4,
-        launch_argmax(H->logits, H->cfg.vocab, H->cfg.vocab, B, H->d_next, H->d_genlog, H->d_pos, H->cfg.n_ctx,
-                      H->d_tok, H->d_pos, H->stream));
+        launch_argmax(H->logits, H->cfg.vocab, H->cfg.vocab, B, H->best, H->d_next, H->d_genlog, H->d_pos,
+                      H->cfg.n_ctx, H->d_tok, H->d_pos, H->stream));
+    H->launches += H->capturing ? 0 : 1;  // argmax is two kernels
+    if (H->capturing) H->capture_kernels++;
     return GPT2Q_OK;
 }
 
@@ -567,20 +592,23 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
         rc = block(H, l, M, H->p_slot, H->p_pos, [&](int layer) {
             RUN("attn_prefill", kv_bytes + (double)M * H->d_local * 8,
                 launch_attn_prefill(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->p_tiles, nt,
-                                    H->att, H->d_local, H->H_local, scale, H->stream));
+                                    H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, scale, H->stream));
             return GPT2Q_OK;
         });
         if (rc) return rc;
     }
     // ln_f + tied head for the last position of each sequence only.
     RUN("layernorm", (double)ns * d * 8,
-        launch_layernorm(H->x, d, H->p_lastrow, H->h, d, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, ns, H->stream));
+        launch_layernorm(H->x, d, H->p_lastrow, H->h, d, H->h_hi, H->h_lo, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, ns,
+                         H->stream));
     float* lg = H->logits + (size_t)s0 * H->cfg.vocab;
-    rc = linear(H, "linear_head", H->wte, H->h, d, ns, epi_store(lg, H->cfg.vocab, nullptr));
+    rc = linear(H, "linear_head", H->wte, In{H->h, H->h_hi, H->h_lo, d}, ns, epi_store(lg, H->cfg.vocab, nullptr));
     if (rc) return rc;
     RUN("argmax", (double)ns * H->cfg.vocab * 4,
-        launch_argmax(lg, H->cfg.vocab, H->cfg.vocab, ns, H->d_next + s0, H->d_genlog + (size_t)s0 * H->cfg.n_ctx,
-                      H->p_lastpos, H->cfg.n_ctx, H->d_tok + s0, nullptr, H->stream));
+        launch_argmax(lg, H->cfg.vocab, H->cfg.vocab, ns, H->best + s0, H->d_next + s0,
+                      H->d_genlog + (size_t)s0 * H->cfg.n_ctx, H->p_lastpos, H->cfg.n_ctx, H->d_tok + s0, nullptr,
+                      H->stream));
+    H->launches += 1;  // argmax is two kernels
     // the staging buffer is reused by the next chunk
     CK(cudaStreamSynchronize(H->stream));
     if (H->prof) return flush_profile(H);
@@ -842,6 +870,13 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     H->att = H->dalloc<float>(M * H->d_local * 4);
     H->f = H->dalloc<float>(M * H->fc_local * 4);
     H->logits = H->dalloc<float>((size_t)c.max_seqs * c.vocab * 4);
+    H->h_hi = H->dalloc<__half>(M * d * 2);
+    H->h_lo = H->dalloc<__half>(M * d * 2);
+    H->att_hi = H->dalloc<__half>(M * H->d_local * 2);
+    H->att_lo = H->dalloc<__half>(M * H->d_local * 2);
+    H->f_hi = H->dalloc<__half>(M * H->fc_local * 2);
+    H->f_lo = H->dalloc<__half>(M * H->fc_local * 2);
+    H->best = H->dalloc<unsigned long long>((size_t)c.max_seqs * 8);
     H->p_tok = H->dalloc<uint32_t>(M * 4);
     H->p_pos = H->dalloc<int>(M * 4);
     H->p_slot = H->dalloc<int>(M * 4);
@@ -856,11 +891,13 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     if (tp_size > 1) H->tp_red = H->dalloc<float>(M * d * 4);
     if (!H->x || !H->h || !H->qb || !H->att || !H->f || !H->logits || !H->p_tok || !H->p_pos || !H->p_slot ||
         !H->p_lastrow || !H->p_lastpos || !H->p_tiles || !H->d_tok || !H->d_next || !H->d_pos || !H->d_slot ||
-        !H->d_genlog || (tp_size > 1 && !H->tp_red)) {
+        !H->d_genlog || (tp_size > 1 && !H->tp_red) || !H->h_hi || !H->h_lo || !H->att_hi || !H->att_lo ||
+        !H->f_hi || !H->f_lo || !H->best) {
         H->err = "cudaMalloc workspace";
         return bail(GPT2Q_EOOM);
     }
-    if (cudaMemsetAsync(H->d_genlog, 0xff, (size_t)c.max_seqs * c.n_ctx * 4, H->stream) != cudaSuccess)
+    if (cudaMemsetAsync(H->d_genlog, 0xff, (size_t)c.max_seqs * c.n_ctx * 4, H->stream) != cudaSuccess ||
+        cudaMemsetAsync(H->best, 0, (size_t)c.max_seqs * 8, H->stream) != cudaSuccess)
         return bail(GPT2Q_ECUDA);
     {
         const int Kmax = std::max(std::max(d, H->fc_local), H->d_local);

@@ -148,8 +148,8 @@ def test_launch_counter_counts_graph_kernels():
         n0 = g.launches
         g.step(2, 1)
         per_step = g.launches - n0
-    # embed + 7 per layer + ln_f + head + argmax
-    assert per_step == 1 + 7 * TINY.n_layer + 3
+    # embed + 7 per layer + ln_f + head + argmax (partial + finalize)
+    assert per_step == 1 + 7 * TINY.n_layer + 4
 
 
 @pytest.mark.parametrize("policy", ["f32", "auto", "q4auto"])
