@@ -29,6 +29,10 @@
 
 using namespace gpt2q;
 
+namespace gpt2q {
+void set_global_error(const std::string& msg);
+}
+
 namespace {
 
 std::string g_create_error;
@@ -932,6 +936,9 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
 }
 
 }  // namespace
+
+// Message for gpt2q_last_error(NULL), used by calls that have no handle.
+void gpt2q::set_global_error(const std::string& msg) { g_create_error = msg; }
 
 // =================================================================== C-ABI
 extern "C" {
