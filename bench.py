@@ -139,19 +139,21 @@ def build_pack(model: str, policy: str):
     return synth.synthetic_pack(meta, policy, seed=0)
 
 
-def prompts_for(rank: int, n: int, plen: int, vocab: int, ragged: bool):
-    from smelt_b200 import synth
+def prompts_for(rank: int, world: int, n: int, plen: int, vocab: int, ragged: bool):
+    """This rank's prompts. Weak scaling (fixed prompts): every rank draws its own n
+    prompts. Strong scaling (ragged): the n global prompts are drawn once and split into
+    contiguous ranges balanced by token count (smelt_b200.shard)."""
+    from smelt_b200 import shard, synth
 
     if ragged:
-        lens = synth.ragged_lengths(n, 16, 512, seed=2 + 1000 * rank)
-    else:
-        lens = np.full(n, plen, np.int32)
+        lens = synth.ragged_lengths(n, 16, 512, seed=2)
+        ids = synth.prompt_ids(int(lens.sum()), vocab, seed=1)
+        offs = np.concatenate([[0], np.cumsum(lens)])
+        lo, hi = shard.shard_sequences(lens, world)[rank]
+        return [ids[offs[i]:offs[i + 1]] for i in range(lo, hi)]
+    lens = np.full(n, plen, np.int32)
     ids = synth.prompt_ids(int(lens.sum()), vocab, seed=1 + 1000 * rank)
-    out, o = [], 0
-    for L in lens:
-        out.append(ids[o:o + L])
-        o += L
-    return out
+    return [ids[i * plen:(i + 1) * plen] for i in range(n)]
 
 
 def cpu_baseline(pk, plen: int, sample_steps: int, threads: int):
@@ -229,12 +231,9 @@ def main():
 
     pk = build_pack(model, policy)
     meta = pk.meta
-    if scaling == "strong":
-        n_local = batch // world + (1 if rank < batch % world else 0)
-    else:
-        n_local = batch
     ragged = args.config == "small-int4-b256"
-    prompts = prompts_for(rank, n_local, plen, meta.vocab, ragged)
+    prompts = prompts_for(rank, world, batch, plen, meta.vocab, ragged)
+    n_local = len(prompts)
     max_plen = max(p.size for p in prompts)
     g = Gpu(pk, device=local, max_seqs=n_local, max_tokens=max(8192, max_plen))
     stream = torch.cuda.Stream(device=dev)
