@@ -18,8 +18,9 @@ Printed JSON (rank 0, one line):
   e2e        the same metric through the public C-ABI call gpt2q_decode with host
              buffers: every step copies its tokens/positions/slots host->device and
              reads the next tokens device->host inside the timed region;
-  roofline   the dominant kernel of an eager profiled pass: algorithmic bytes per
-             launch / CUDA-event duration, against MEASURED_PEAKS.json hbm_gbs;
+  roofline   the kernel with the largest time share of a decode step: algorithmic bytes
+             per launch / steady-state launch time (its launch replayed 20x in a CUDA graph,
+             CUDA events on the launch stream), against MEASURED_PEAKS.json hbm_gbs;
   cpu_baseline  the C++ oracle (restatement of the reference CPU forward) timed on
              the host cores on a bounded sample (rank 0, N=1 only).
 `--impl reference` times only the reference CPU implementation (the oracle port;
@@ -327,16 +328,13 @@ def main():
         e2e_tokens = batch * e2e_steps
     e2e_value = e2e_tokens / float(e2e_t.item())
 
-    # ---- roofline: eager profiled decode steps (CUDA events around every kernel) ----
+    # ---- roofline: every kernel type of one decode step timed in steady state (its first
+    # launch replayed back to back in a CUDA graph, CUDA events on the launch stream) ----
     g.prefill(prompts)
-    g.profile(True)
-    g.decode_steps(4, n_local, want_tokens=False)
-    prof = g.profile_read()
-    g.profile(False)
-    top = max(prof.items(), key=lambda kv: kv[1]["ms"])
-    name, rec = top
-    per_launch_bytes = rec["bytes"] / rec["launches"]
-    per_launch_ms = rec["ms"] / rec["launches"]
+    kt = g.profile_kernels(reps=20)
+    name, rec = max(kt.items(), key=lambda kv: kv[1]["us"] * kv[1]["per_step"])
+    per_launch_bytes = rec["bytes"]
+    per_launch_ms = rec["us"] / 1e3
     hbm, peak_kind = peaks()
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
     traffic = None
@@ -360,8 +358,11 @@ def main():
         "step_hbm_fraction": (step_bytes / (ms_max / args.steps / 1e3) / 1e9) / hbm,
         "roofline": {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_kind,
-                     "bytes_per_launch": per_launch_bytes, "ms_per_launch": per_launch_ms},
-        "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 4)} for k, v in prof.items()},
+                     "bytes_per_launch": per_launch_bytes, "us_per_launch": rec["us"],
+                     "timing": "graph of 20 back-to-back launches of the step's own launch, CUDA events"},
+        "kernels": {k: {"us_per_launch": round(v["us"], 3), "per_step": v["per_step"],
+                        "step_share": round(v["us"] * v["per_step"] / (ms_max / args.steps * 1e3), 4)}
+                    for k, v in kt.items()},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": n_local * 12,
                 "d2h_bytes_per_step": n_local * 4, "api": "gpt2q_decode (host tok/pos/slot in, next tokens out)"},
         "gpu_launches": int(launches),

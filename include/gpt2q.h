@@ -144,6 +144,15 @@ int gpt2q_sync(gpt2q_handle* h);
 int gpt2q_profile(gpt2q_handle* h, int enable);
 int gpt2q_profile_read(gpt2q_handle* h, char* json, size_t cap);
 
+/* Runs one decode step of the current sequences; the first launch of every kernel
+ * type (the argmax excepted) is replayed `reps` times back to back in a CUDA graph with
+ * the step's own arguments and timed with CUDA events. Writes JSON
+ * {"kernel": {"us": per-launch time, "bytes": algorithmic bytes per launch,
+ *  "per_step": launches per decode step}, ...}. The replays repeat residual
+ * additions, so decode results after this call are not meaningful until the next
+ * prefill. */
+int gpt2q_profile_kernels(gpt2q_handle* h, int reps, char* json, size_t cap);
+
 /* Greedy argmax (IEEE total order, ties -> last index) of n_rows rows of device fp32
  * logits (row stride ld >= vocab floats) into device d_next[n_rows], on `stream` (a
  * cudaStream_t; NULL = legacy default stream). Allocates nothing: its per-row scratch is

@@ -138,6 +138,11 @@ struct gpt2q_handle {
     uint64_t capture_kernels = 0;
     uint64_t launches = 0;
 
+    // kernel-timing pass (gpt2q_profile_kernels): name -> (us per launch, bytes per launch)
+    int ktime_reps = 0;
+    std::map<std::string, std::pair<double, double>> ktime_res;
+    std::map<std::string, int> ktime_count;
+
     bool prof = false;
     std::vector<ProfRec> prof_pending;
     std::vector<cudaEvent_t> ev_pool;
@@ -195,8 +200,45 @@ cudaEvent_t pooled_event(gpt2q_handle* H) {
     return e;
 }
 
+// Steady-state time of one kernel launch: `reps` back-to-back launches with the very same
+// arguments captured in one CUDA graph, timed with CUDA events on the handle's stream.
+// Only kernels that may run repeatedly without leaving the buffers out of bounds are
+// timed this way (not the argmax finaliser, which advances positions).
+template <class F>
+int time_kernel(gpt2q_handle* H, const char* name, double bytes, F&& f) {
+    cudaError_t e = f();
+    if (e != cudaSuccess) return H->fail(GPT2Q_ECUDA, std::string(name) + ": " + cudaGetErrorString(e));
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ex = nullptr;
+    CK(cudaStreamBeginCapture(H->stream, cudaStreamCaptureModeThreadLocal));
+    for (int r = 0; r < H->ktime_reps; ++r) f();
+    CK(cudaStreamEndCapture(H->stream, &g));
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return H->fail(GPT2Q_ECUDA, std::string("kernel timing graph: ") + cudaGetErrorString(e));
+    cudaEvent_t a = pooled_event(H), b = pooled_event(H);
+    e = cudaGraphLaunch(ex, H->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(a, H->stream);
+    if (e == cudaSuccess) e = cudaGraphLaunch(ex, H->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(b, H->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(H->stream);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+    H->ev_pool.push_back(a);
+    H->ev_pool.push_back(b);
+    cudaGraphExecDestroy(ex);
+    if (e != cudaSuccess) return H->fail(GPT2Q_ECUDA, std::string("kernel timing: ") + cudaGetErrorString(e));
+    H->ktime_res[name] = {ms * 1000.0 / H->ktime_reps, bytes};
+    H->launches += 1 + 2 * (uint64_t)H->ktime_reps;
+    return GPT2Q_OK;
+}
+
 template <class F>
 int run_kernel(gpt2q_handle* H, const char* name, double bytes, F&& f) {
+    if (H->ktime_reps > 0 && !H->capturing) {
+        H->ktime_count[name]++;
+        if (!H->ktime_res.count(name) && std::strcmp(name, "argmax") != 0) return time_kernel(H, name, bytes, f);
+    }
     cudaEvent_t a = nullptr, b = nullptr;
     if (H->prof && !H->capturing) {
         a = pooled_event(H);
@@ -1154,6 +1196,37 @@ int gpt2q_profile(gpt2q_handle* H, int enable) {
         }
     }
     return GPT2Q_OK;
+}
+
+int gpt2q_profile_kernels(gpt2q_handle* H, int reps, char* json, size_t cap) {
+    if (!H || !json || cap == 0 || reps <= 0) return GPT2Q_EARG;
+    if (H->cur_n <= 0) return H->fail(GPT2Q_EARG, "profile_kernels: no sequences (call prefill or decode first)");
+    CK(cudaSetDevice(H->device));
+    for (int b = 0; b < H->cur_n; ++b)
+        if (H->hpos[b] + 1 > H->cfg.n_ctx) return H->fail(GPT2Q_EARG, "profile_kernels: positions at n_ctx");
+    H->ktime_reps = reps;
+    H->ktime_res.clear();
+    H->ktime_count.clear();
+    int rc = enqueue_decode(H, H->cur_n);
+    H->ktime_reps = 0;
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(H->stream));
+    for (int b = 0; b < H->cur_n; ++b) H->hpos[b] += 1;
+    std::string s = "{";
+    bool first = true;
+    for (auto& kv : H->ktime_count) {
+        auto it = H->ktime_res.find(kv.first);
+        if (it == H->ktime_res.end()) continue;
+        char buf[256];
+        std::snprintf(buf, sizeof buf, "%s\"%s\": {\"us\": %.4f, \"bytes\": %.0f, \"per_step\": %d}",
+                      first ? "" : ", ", kv.first.c_str(), it->second.first, it->second.second, kv.second);
+        s += buf;
+        first = false;
+    }
+    s += "}";
+    if (s.size() + 1 > cap) return H->fail(GPT2Q_EARG, "profile_kernels: buffer too small");
+    std::memcpy(json, s.c_str(), s.size() + 1);
+    return check_device_error(H);
 }
 
 int gpt2q_profile_read(gpt2q_handle* H, char* json, size_t cap) {

@@ -163,6 +163,12 @@ class Gpu:
     def profile(self, enable: bool):
         self._check(self._lib.gpt2q_profile(self.h, 1 if enable else 0))
 
+    def profile_kernels(self, reps: int = 20) -> dict:
+        """Steady-state per-launch time of every kernel type of one decode step."""
+        buf = C.create_string_buffer(1 << 16)
+        self._check(self._lib.gpt2q_profile_kernels(self.h, int(reps), buf, len(buf)))
+        return json.loads(buf.value.decode())
+
     def profile_read(self) -> dict:
         buf = C.create_string_buffer(1 << 16)
         self._check(self._lib.gpt2q_profile_read(self.h, buf, len(buf)))
