@@ -42,10 +42,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 WORKLOADS = {
-    # name: (model, policy, batch per rank, prompt len, decode steps, scaling)
-    "small-int8-b32": ("small", "auto", 32, 128, 128, "weak"),
-    "small-int8-b1": ("small", "auto", 1, 64, 64, "weak"),
-    "small-int4-b256": ("small", "q4auto", 256, 264, 256, "strong"),
+    # name: (model, policy, batch, prompt len, decode steps, scaling)
+    "small-int8-b32": ("small", "auto", 32, 128, 128, "weak"),      # BASELINE configs[1] (per GPU)
+    "small-int8-b1": ("small", "auto", 1, 64, 64, "weak"),          # configs[0] shape, int8
+    "small-int4-b256": ("small", "q4auto", 256, 264, 256, "strong"),  # configs[2], ragged 16..512
+    "medium-int8-prefill": ("medium", "auto", 64, 1024, 1, "strong"),  # configs[3]
+    "xl-int8-tp": ("xl", "auto", 16, 256, 256, "strong"),           # configs[4], tensor parallel
 }
 
 
@@ -133,11 +135,46 @@ class ClockSampler:
 
 
 def build_pack(model: str, policy: str):
+    """Seeded synthetic pack, cached under $TMPDIR so ranks and repeated runs share it."""
+    import tempfile
+
     from smelt_b200 import pack as P
     from smelt_b200 import synth
 
     meta = P.CONFIGS[model]
-    return synth.synthetic_pack(meta, policy, seed=0)
+    path = os.path.join(tempfile.gettempdir(), f"smelt_b200_pack_{model}_{policy}_seed0.npz")
+    lock = path + ".lock"
+    for _ in range(3600):
+        if os.path.exists(path):
+            try:
+                z = np.load(path, allow_pickle=False)
+                pk = P.Pack(meta)
+                for name in z["names"]:
+                    shape = tuple(int(v) for v in z[f"shape::{name}"])
+                    pk.tensors[str(name)] = P.Tensor(shape, str(z[f"atom::{name}"]), z[f"data::{name}"])
+                return pk
+            except Exception:
+                pass
+        try:
+            fd = os.open(lock, os.O_CREAT | os.O_EXCL | os.O_WRONLY)
+        except FileExistsError:
+            time.sleep(1.0)  # another rank is writing the cache
+            continue
+        try:
+            pk = synth.synthetic_pack(meta, policy, seed=0)
+            arrays = {"names": np.array(list(pk.tensors))}
+            for name, t in pk.tensors.items():
+                arrays[f"shape::{name}"] = np.array(t.shape, np.int64)
+                arrays[f"atom::{name}"] = np.array(t.atom)
+                arrays[f"data::{name}"] = t.data
+            tmp = path + f".{os.getpid()}.npz"
+            np.savez(tmp, **arrays)
+            os.replace(tmp, path)
+            return pk
+        finally:
+            os.close(fd)
+            os.unlink(lock)
+    raise RuntimeError("timed out waiting for the pack cache")
 
 
 def prompts_for(rank: int, world: int, n: int, plen: int, vocab: int, ragged: bool):
@@ -208,11 +245,215 @@ def run_reference(args, wl):
     print(json.dumps(line), flush=True)
 
 
+def prefill_flops(meta, T: int) -> float:
+    """FLOPs of one prompt of T tokens: 2*T*P_lin + causal attention + last-position head."""
+    d, L = meta.n_embd, meta.n_layer
+    p_lin = 12 * d * d * L
+    return 2.0 * T * p_lin + 2.0 * L * d * T * (T + 1) + 2.0 * d * meta.vocab
+
+
+def dist_setup():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    return world, rank, local, dev
+
+
+def max_over_ranks(v: float, world: int, dev) -> float:
+    import torch
+
+    t = torch.tensor([v], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_prefill(args, wl):
+    """prompts of 1024 tokens, prefill plus one decode step per step, sequences
+    split across ranks (strong scaling); tensor-core bound."""
+    import torch
+
+    from smelt_b200 import shard, synth
+    from smelt_b200.gpu import Gpu
+
+    model, policy, batch, plen, _dec, scaling = wl
+    world, rank, local, dev = dist_setup()
+    pk = build_pack(model, policy)
+    meta = pk.meta
+    ids = synth.prompt_ids(batch * plen, meta.vocab, seed=1)
+    lo, hi = shard.shard_sequences(np.full(batch, plen), world)[rank]
+    prompts = [ids[i * plen:(i + 1) * plen] for i in range(lo, hi)]
+    g = Gpu(pk, device=local, max_seqs=max(1, len(prompts)), max_tokens=16384)
+    stream = torch.cuda.Stream(device=dev)
+    g.set_stream(stream.cuda_stream)
+
+    def step():
+        g.prefill(prompts)
+        g.decode_steps(1, len(prompts), want_tokens=False)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}") as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, world, dev)
+    wall_max = max_over_ranks(wall, world, dev)
+    tokens = batch * plen * args.steps
+    flops_rank = sum(prefill_flops(meta, p.size) for p in prompts)
+    peak = 1404.9
+    pj = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak_kind = "fallback (sustained)"
+    if os.path.exists(pj):
+        with open(pj) as f:
+            peak = float(json.load(f).get("bf16_tflops_sustained", peak))
+        peak_kind = "measured bf16 sustained"
+    achieved = flops_rank / (ms / args.steps / 1e3) / 1e12 if prompts else 0.0
+    line = {
+        "metric": "prefill tokens/s (GPT-2 medium int8)", "value": tokens / (ms_max / 1e3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "int8xfp32 (fp16x3 tensor)",
+        "data": "synthetic",
+        "config": {"workload": args.config, "model": f"gpt2-{model}", "weights": policy, "global_batch": batch,
+                   "prompt": plen, "step": "prefill all prompts + 1 decode step",
+                   "l2": f"inputs larger than L2: {batch * plen * meta.n_embd * 4 / 1e6:.0f} MB of activations per layer"},
+        "roofline": {"bound": "tensor", "kernel": "whole prefill step", "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                     "flops_per_step_rank": flops_rank,
+                     "note": "algorithmic FLOPs (2MNK); the fp16x3 split issues 3x the MMAs"},
+        "e2e": {"value": tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": sum(p.size for p in prompts) * 4,
+                "d2h_bytes_per_step": len(prompts) * 4, "api": "gpt2q_prefill + gpt2q_decode_steps"},
+        "gpu_launches": None, "clocks": clk.summary(),
+    }
+    g.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_tp(args, wl):
+    """GPT-2 XL int8, tensor parallel over the torchrun ranks (NCCL all-reduce
+    of the two c_proj partial sums per layer); 16 sequences, decode positions 256..511."""
+    import torch
+
+    from smelt_b200 import synth
+    from smelt_b200.gpu import Gpu
+
+    model, policy, batch, plen, dec, scaling = wl
+    world, rank, local, dev = dist_setup()
+    pk = build_pack(model, policy)
+    meta = pk.meta
+    ids = synth.prompt_ids(batch * plen, meta.vocab, seed=1)
+    prompts = [ids[i * plen:(i + 1) * plen] for i in range(batch)]
+    if world > 1:
+        uid = [torch.cuda.nccl.unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(uid, src=0)
+        g = Gpu(pk, device=local, max_seqs=batch, tp_size=world, tp_rank=rank, nccl_id=uid[0])
+    else:
+        g = Gpu(pk, device=local, max_seqs=batch)
+    stream = torch.cuda.Stream(device=dev)
+    g.set_stream(stream.cuda_stream)
+    g.prefill(prompts)
+    span = dec
+    done = 0
+
+    def run_steps(k):
+        nonlocal done
+        while k > 0:
+            if done >= span:
+                g.prefill(prompts)
+                done = 0
+            n = min(k, span - done)
+            g.decode_steps(n, batch, want_tokens=False)
+            done += n
+            k -= n
+
+    run_steps(max(args.warmup, 3))
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    l0 = g.launches
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}") as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        k = args.steps
+        # prefills that rewind the positions are not decode steps: keep them out of the timing
+        timed_ms = 0.0
+        while k > 0:
+            if done >= span:
+                ev1.record(stream)
+                torch.cuda.synchronize()
+                timed_ms += ev0.elapsed_time(ev1)
+                g.prefill(prompts)
+                done = 0
+                ev0.record(stream)
+            n = min(k, span - done)
+            g.decode_steps(n, batch, want_tokens=False)
+            done += n
+            k -= n
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        timed_ms += ev0.elapsed_time(ev1)
+    launches = g.launches - l0
+    ms_max = max_over_ranks(timed_ms, world, dev)
+    weights = sum(t.data.nbytes for t in pk.tensors.values() if len(t.shape) == 2)
+    line = {
+        "metric": "decode tokens/s (GPT-2 XL int8, tensor parallel)", "value": batch * args.steps / (ms_max / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "dtype": "int8xfp32", "data": "synthetic",
+        "config": {"workload": args.config, "model": f"gpt2-{model}", "weights": policy, "global_batch": batch,
+                   "prompt": plen, "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2: {weights / 1e6:.0f} MB of int8 weights per step"},
+        "step_hbm_fraction": None, "gpu_launches": int(launches), "clocks": clk.summary(),
+        "roofline": {"bound": "hbm", "kernel": "whole decode step",
+                     "achieved": (weights / world) / (ms_max / args.steps / 1e3) / 1e9, "peak": peaks()[0],
+                     "unit": "GB/s", "frac": (weights / world) / (ms_max / args.steps / 1e3) / 1e9 / peaks()[0],
+                     "traffic": None, "note": "weight bytes per rank only (KV excluded)"},
+        "e2e": None,
+    }
+    g.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def main():
     args = parse()
     wl = WORKLOADS[args.config]
     if args.impl == "reference":
         run_reference(args, wl)
+        return
+    if args.config == "medium-int8-prefill":
+        run_prefill(args, wl)
+        return
+    if args.config == "xl-int8-tp":
+        run_tp(args, wl)
         return
     import torch
 

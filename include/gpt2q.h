@@ -171,6 +171,10 @@ int gpt2q_argmax_noalloc(const float* d_logits, int vocab, int ld, int n_rows, u
  * (Rng::new(seed) = seed ^ 0x9E3779B97F4A7C15) with the Box-Muller normal of
  * perf-lab/src/bin/atoms.rs:78-83. `state` is advanced in place. */
 uint64_t gpt2q_rng_new(uint64_t seed);
+/* Converter group quantisers (host, multithreaded): n % 32 == 0 values -> SMT payload.
+ * q8: atoms.rs:65-78 (34 B per group); q4: perf-lab atoms.rs:89-99 math, 18 B per group. */
+int gpt2q_quantize_q8(const float* x, size_t n, uint8_t* out);
+int gpt2q_quantize_q4(const float* x, size_t n, uint8_t* out);
 void gpt2q_rng_normal_f32(uint64_t* state, float* out, size_t n, double stdv);
 void gpt2q_rng_below(uint64_t* state, uint32_t* out, size_t n, uint64_t bound);
 

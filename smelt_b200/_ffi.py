@@ -20,6 +20,7 @@ EXPORTS = [
     "gpt2q_step", "gpt2q_decode", "gpt2q_prefill", "gpt2q_decode_steps", "gpt2q_generate_greedy",
     "gpt2q_dequant", "gpt2q_launches", "gpt2q_set_stream", "gpt2q_sync", "gpt2q_profile",
     "gpt2q_profile_read", "gpt2q_profile_kernels", "gpt2q_argmax_noalloc", "gpt2q_rng_new", "gpt2q_rng_normal_f32", "gpt2q_rng_below",
+    "gpt2q_quantize_q8", "gpt2q_quantize_q4",
 ]
 
 
@@ -101,6 +102,9 @@ def load(path: str | None = None):
     lib.gpt2q_rng_normal_f32.restype = None
     lib.gpt2q_rng_below.argtypes = [_u64p, _u32p, C.c_size_t, C.c_uint64]
     lib.gpt2q_rng_below.restype = None
+    for fn in (lib.gpt2q_quantize_q8, lib.gpt2q_quantize_q4):
+        fn.argtypes = [_f32p, C.c_size_t, C.POINTER(C.c_uint8)]
+        fn.restype = C.c_int
     if path is None:
         _lib = lib
     return lib

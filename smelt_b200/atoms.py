@@ -95,6 +95,31 @@ def q4_encode(x: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
+def _native(fn_name: str, x: np.ndarray, block: int):
+    """Run the library's multithreaded quantiser (same bytes as the numpy version)."""
+    import ctypes as C
+
+    from . import _ffi
+
+    lib = _ffi.load()
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    if x.size % 32:
+        raise ValueError("payload must be a multiple of 32 values")
+    out = np.empty(x.size // 32 * block, dtype=np.uint8)
+    rc = getattr(lib, fn_name)(x.ctypes.data_as(C.POINTER(C.c_float)), x.size, out.ctypes.data_as(C.POINTER(C.c_uint8)))
+    if rc != 0:
+        raise ValueError(f"{fn_name} failed ({rc})")
+    return out
+
+
+def q8_encode_fast(x: np.ndarray) -> np.ndarray:
+    return _native("gpt2q_quantize_q8", x, Q8_BLOCK)
+
+
+def q4_encode_fast(x: np.ndarray) -> np.ndarray:
+    return _native("gpt2q_quantize_q4", x, Q4_BLOCK)
+
+
 def f16_encode(x: np.ndarray) -> np.ndarray:
     return f32_to_f16_bits(np.ascontiguousarray(x, dtype=np.float32).reshape(-1)).view(np.uint8)
 

@@ -48,21 +48,30 @@ namespace gpt2q {
 namespace {
 
 constexpr int BM = 128, BK = 64, THREADS = 224;
-constexpr int RAW_STAGES = 4;
 constexpr int MAX_SPLITS = 8;  // portable cluster size
 
 template <int BN, bool PRESPLIT>
 struct Cfg {
-    static constexpr int OS = BN >= 256 ? 2 : (BN >= 128 ? 3 : 4);  // operand stages
+    // decode tiles (BN <= 64) use ~105 KB so two CTAs share an SM
+    // operand stages: decode tiles (BN <= 64) keep two CTAs per SM so consecutive linears
+    // overlap under programmatic dependent launch
+    static constexpr int OS = 2;
+    static constexpr int RAW_STAGES = BN == 128 ? 4 : 2;  // raw int8/int4 weight tiles in flight
     static constexpr int A_BYTES = BM * 128;                          // one of hi/lo
     static constexpr int B_BYTES = BN * 128;                          // one of hi/lo
     static constexpr int RAW_BYTES = PRESPLIT ? 0 : BM * 64;          // int8 tile (int4 uses half)
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + OS * 2 * A_BYTES;
     static constexpr int OFF_RAW = OFF_B + OS * 2 * B_BYTES;
-    static constexpr int OFF_BAR = OFF_RAW + RAW_STAGES * RAW_BYTES;
+    // decode: the CTA's group scales, one padded row per weight row (conflict-free)
+    static constexpr int SC_KB = 8;                  // k-blocks of scales staged at a time
+    static constexpr int SC_STRIDE = 2 * SC_KB + 1;  // floats per row
+    static constexpr int OFF_SC = OFF_RAW + RAW_STAGES * RAW_BYTES;
+    static constexpr int SC_BYTES = PRESPLIT ? 0 : BM * SC_STRIDE * 4;
+    static constexpr int OFF_BAR = OFF_SC + SC_BYTES;
     static constexpr int N_BAR = 2 * RAW_STAGES + 2 * OS + 1;
     static constexpr int SMEM = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem slot, flag, alignment slack
+    static_assert(SMEM <= 232448, "shared memory per CTA");
     // the split-K partial tile [BN][128] fp32 reuses the operand rings once every MMA is done
     static_assert(BN * BM * 4 <= OFF_RAW, "partial tile must fit in the operand rings");
 };
@@ -76,22 +85,6 @@ struct TcParams {
     int* err;
 };
 
-__device__ __forceinline__ uint4 pack_hi_lo(const float* f, uint4& lo_out) {
-    uint4 hi, lo;
-    uint32_t* h = &hi.x;
-    uint32_t* l = &lo.x;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        __half2 hh = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-        float2 back = __half22float2(hh);
-        __half2 ll = __floats2half2_rn(f[2 * i] - back.x, f[2 * i + 1] - back.y);
-        h[i] = *reinterpret_cast<uint32_t*>(&hh);
-        l[i] = *reinterpret_cast<uint32_t*>(&ll);
-    }
-    lo_out = lo;
-    return hi;
-}
-
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, const uint4& v) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
@@ -103,17 +96,76 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
     return v;
 }
 
-// Write output chunk j (8 values) of row r into the swizzled hi/lo A tiles.
-__device__ __forceinline__ void put8(uint32_t a_hi, uint32_t a_lo, int r, int j, const float* f) {
-    uint4 lo;
-    uint4 hi = pack_hi_lo(f, lo);
-    const uint32_t off = (uint32_t)r * 128u + (uint32_t)((j ^ (r & 7)) * 16);
-    st_shared_v4(a_hi + off, hi);
-    st_shared_v4(a_lo + off, lo);
+// ---- exact fp16 dequantisation (two values per instruction) ----
+// int8 pair -> half2 exactly: bytes biased by +128 go into the mantissa of 1024 (0x64xx),
+// then 1152 is subtracted. int4 nibbles are biased by +8 and 1032 is subtracted.
+__device__ __forceinline__ __half2 bytes_to_h2(uint32_t biased, uint32_t sel) {
+    const uint32_t v = __byte_perm(biased, 0x64646464u, sel);
+    return *reinterpret_cast<const __half2*>(&v);
+}
+
+// q (exact fp16 integers) times the prescaled group scale s2 = f16(scale) * 2^P:
+// hi = f16(q*s), lo = fma(q, s, -hi) — the residual of the 18-bit product has at most 8
+// significant bits, so the fp16 FMA returns it exactly and hi + lo == q*s.
+__device__ __forceinline__ void qs_hi_lo(__half2 q, __half2 s2, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __hmul2(q, s2);
+    const __half2 l = __hfma2(q, s2, __hneg2(h));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// 16 int8 weights (one uint4) of row r, k-chunk c (elements 16c..16c+15), into the
+// swizzled hi/lo A tiles (output chunks 2c, 2c+1).
+__device__ __forceinline__ void put16_q8(uint32_t a_hi, uint32_t a_lo, int r, int c, const uint4& v, __half2 s2) {
+    const __half2 off = __float2half2_rn(1152.0f);
+    const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
+    uint4 hi[2], lo[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 q01 = __hsub2(bytes_to_h2(w[i], 0x5140u), off);
+        const __half2 q23 = __hsub2(bytes_to_h2(w[i], 0x5342u), off);
+        uint32_t* ph = &hi[i >> 1].x + (i & 1) * 2;
+        uint32_t* pl = &lo[i >> 1].x + (i & 1) * 2;
+        qs_hi_lo(q01, s2, ph[0], pl[0]);
+        qs_hi_lo(q23, s2, ph[1], pl[1]);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const uint32_t o = (uint32_t)r * 128u + (uint32_t)(((2 * c + j) ^ (r & 7)) * 16);
+        st_shared_v4(a_hi + o, hi[j]);
+        st_shared_v4(a_lo + o, lo[j]);
+    }
+}
+
+// One 32-group of int4 weights (16 packed bytes: byte j = elem j | elem j+16 << 4) of row r,
+// k-group c (elements 32c..32c+31) -> output chunks 4c..4c+3.
+__device__ __forceinline__ void put32_q4(uint32_t a_hi, uint32_t a_lo, int r, int c, const uint4& v, __half2 s2) {
+    const __half2 off = __float2half2_rn(1032.0f);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint4 hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // word i: bytes 4i..4i+3 -> elements 4i.. (low) and 16+4i.. (high)
+        const uint32_t ul = (w[i] & 0x0F0F0F0Fu) ^ 0x08080808u;
+        const uint32_t uh = ((w[i] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+        uint32_t* phl = &hi[i >> 1].x + (i & 1) * 2;
+        uint32_t* pll = &lo[i >> 1].x + (i & 1) * 2;
+        uint32_t* phh = &hi[2 + (i >> 1)].x + (i & 1) * 2;
+        uint32_t* plh = &lo[2 + (i >> 1)].x + (i & 1) * 2;
+        qs_hi_lo(__hsub2(bytes_to_h2(ul, 0x5140u), off), s2, phl[0], pll[0]);
+        qs_hi_lo(__hsub2(bytes_to_h2(ul, 0x5342u), off), s2, phl[1], pll[1]);
+        qs_hi_lo(__hsub2(bytes_to_h2(uh, 0x5140u), off), s2, phh[0], plh[0]);
+        qs_hi_lo(__hsub2(bytes_to_h2(uh, 0x5342u), off), s2, phh[1], plh[1]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t o = (uint32_t)r * 128u + (uint32_t)(((4 * c + j) ^ (r & 7)) * 16);
+        st_shared_v4(a_hi + o, hi[j]);
+        st_shared_v4(a_lo + o, lo[j]);
+    }
 }
 
 template <int ATOM, int BN, bool PRESPLIT>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
     k_linear_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wlo,
                 const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
                 TcParams p) {
@@ -122,8 +174,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* raw_full = bars;
-    uint64_t* raw_empty = bars + RAW_STAGES;
-    uint64_t* op_full = bars + 2 * RAW_STAGES;
+    uint64_t* raw_empty = bars + C::RAW_STAGES;
+    uint64_t* op_full = bars + 2 * C::RAW_STAGES;
     uint64_t* op_empty = op_full + C::OS;
     uint64_t* acc_full = op_empty + C::OS;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
@@ -137,7 +189,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     tc::pdl_trigger();
     if (threadIdx.x == 0) {
-        for (int i = 0; i < RAW_STAGES; ++i) {
+        for (int i = 0; i < C::RAW_STAGES; ++i) {
             tc::mbar_init(&raw_full[i], 1);
             tc::mbar_init(&raw_empty[i], 128);
         }
@@ -172,7 +224,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tc::tma_load_2d(a, &tm_w, (kb0 + i) * BK, n0, &op_full[s]);
                     tc::tma_load_2d(a + C::A_BYTES, &tm_wlo, (kb0 + i) * BK, n0, &op_full[s]);
                 } else {
-                    const int s = i % RAW_STAGES, use = i / RAW_STAGES;
+                    const int s = i % C::RAW_STAGES, use = i / C::RAW_STAGES;
                     if (!tc::mbar_wait(&raw_empty[s], (use & 1) ^ 1, p.err)) break;
                     tc::mbar_arrive_expect_tx(&raw_full[s], RAW_TX);
                     const int kx = (kb0 + i) * (ATOM == ATOM_Q8 ? 64 : 32);
@@ -185,8 +237,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int i = (issued > C::OS ? issued - C::OS : 0); i < issued; ++i)
                     tc::mbar_wait(&op_full[i % C::OS], (i / C::OS) & 1, p.err);
             } else {
-                for (int i = (issued > RAW_STAGES ? issued - RAW_STAGES : 0); i < issued; ++i)
-                    tc::mbar_wait(&raw_full[i % RAW_STAGES], (i / RAW_STAGES) & 1, p.err);
+                for (int i = (issued > C::RAW_STAGES ? issued - C::RAW_STAGES : 0); i < issued; ++i)
+                    tc::mbar_wait(&raw_full[i % C::RAW_STAGES], (i / C::RAW_STAGES) & 1, p.err);
             }
         }
     } else if (warp == 6) {
@@ -242,19 +294,27 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int n = n0 + t;
             const bool row_ok = n < p.w.rows;
             const __half* srow = p.w.s + (size_t)(row_ok ? n : 0) * p.w.sstride;
+            float* sc = reinterpret_cast<float*>(smem + C::OFF_SC) + t * C::SC_STRIDE;
             bool ok = true;
             for (int i = 0; i < nkb && ok; ++i) {
-                const int rs = i % RAW_STAGES, ruse = i / RAW_STAGES;
+                if (i % C::SC_KB == 0) {
+                    // this row's scales for k-blocks i..i+SC_KB-1, prescaled by 2^P; one burst of
+                    // independent loads instead of a dependent global load per k-block
+                    const int gbase = (kb0 + i) * 2;
+#pragma unroll
+                    for (int j = 0; j < 2 * C::SC_KB; ++j) {
+                        const int gi = gbase + j;
+                        sc[j] = (row_ok && gi < p.w.sstride) ? __half2float(srow[gi]) * p.pre : 0.f;
+                    }
+                }
+                const int rs = i % C::RAW_STAGES, ruse = i / C::RAW_STAGES;
                 const int os = i % C::OS, ouse = i / C::OS;
                 ok = tc::mbar_wait(&raw_full[rs], ruse & 1, p.err) &&
                      tc::mbar_wait(&op_empty[os], (ouse & 1) ^ 1, p.err);
                 if (!ok) break;
-                const int g0 = (kb0 + i) * 2;  // two 32-groups per 64-k stage
-                float s0 = 0.f, s1 = 0.f;
-                if (row_ok) {
-                    s0 = __half2float(srow[g0]) * p.pre;
-                    if (g0 + 1 < p.w.sstride) s1 = __half2float(srow[g0 + 1]) * p.pre;
-                }
+                const int jj = 2 * (i % C::SC_KB);
+                const __half2 s0 = __float2half2_rn(sc[jj]);
+                const __half2 s1 = __float2half2_rn(sc[jj + 1]);
                 const uint32_t raw = tc::smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES);
                 const uint32_t a_hi = tc::smem_u32(smem + C::OFF_A + os * 2 * C::A_BYTES);
                 const uint32_t a_lo = a_hi + C::A_BYTES;
@@ -263,37 +323,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         const uint4 v = ld_shared_v4(raw + t * 64 + ((c ^ ((t >> 1) & 3)) * 16));
-                        const float sc = (c < 2) ? s0 : s1;
-                        float f[16];
-                        i8x4_to_f32(v.x, f + 0);
-                        i8x4_to_f32(v.y, f + 4);
-                        i8x4_to_f32(v.z, f + 8);
-                        i8x4_to_f32(v.w, f + 12);
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) f[e] *= sc;
-                        put8(a_hi, a_lo, t, 2 * c, f);
-                        put8(a_hi, a_lo, t, 2 * c + 1, f + 8);
+                        put16_q8(a_hi, a_lo, t, c, v, (c < 2) ? s0 : s1);
                     }
                 } else {
                     // row t: 2 chunks of 16 packed bytes (one 32-group each), 32-byte swizzle
 #pragma unroll
                     for (int c = 0; c < 2; ++c) {
                         const uint4 v = ld_shared_v4(raw + t * 32 + ((c ^ ((t >> 2) & 1)) * 16));
-                        const float sc = (c == 0) ? s0 : s1;
-                        float lo[16], hi[16];
-                        i4x8_to_f32(v.x, lo + 0, hi + 0);
-                        i4x8_to_f32(v.y, lo + 4, hi + 4);
-                        i4x8_to_f32(v.z, lo + 8, hi + 8);
-                        i4x8_to_f32(v.w, lo + 12, hi + 12);
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            lo[e] *= sc;
-                            hi[e] *= sc;
-                        }
-                        put8(a_hi, a_lo, t, 4 * c, lo);
-                        put8(a_hi, a_lo, t, 4 * c + 1, lo + 8);
-                        put8(a_hi, a_lo, t, 4 * c + 2, hi);
-                        put8(a_hi, a_lo, t, 4 * c + 3, hi + 8);
+                        put32_q4(a_hi, a_lo, t, c, v, (c == 0) ? s0 : s1);
                     }
                 }
                 tc::fence_proxy_async_smem();

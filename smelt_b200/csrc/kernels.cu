@@ -365,21 +365,23 @@ cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, cons
 }
 
 // ------------------------------------------------------------------ decode attention
-// One block of 4 warps per (head, sequence). Each warp takes 32 keys at a time: lane j
+// One block of NW warps per (head, sequence). Each warp takes 32 keys at a time: lane j
 // scores key t0+j against q (q broadcast from shared memory); the V rows of the same 32
 // keys are loaded in the same burst (lane l owns dims 2l, 2l+1, coalesced 256-byte rows),
-// so one memory round trip serves the whole block. The warp does an online-softmax update
-// and the four warps are merged through shared memory.
+// so one memory round trip serves the whole block; the K/V burst of the first block is
+// issued before q is staged. The warp does an online-softmax update and the warps are
+// merged through shared memory. Four warps measured best on long contexts (many CTAs per SM).
 // Semantics: softmax(q.K^T * scale) V over positions 0..pos (gpt2.rs:261-291).
-__global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q, int ldq, KVGeom g,
-                                                     size_t layer_off, const int* __restrict__ slot,
-                                                     const int* __restrict__ pos, float* __restrict__ out,
-                                                     __half* __restrict__ ohi, __half* __restrict__ olo, int ldo,
-                                                     float scale) {
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* __restrict__ q, int ldq, KVGeom g,
+                                                         size_t layer_off, const int* __restrict__ slot,
+                                                         const int* __restrict__ pos, float* __restrict__ out,
+                                                         __half* __restrict__ ohi, __half* __restrict__ olo,
+                                                         int ldo, float scale) {
     constexpr int HD = 64;
     __shared__ float4 qs[HD / 4];
-    __shared__ float wm[4], wl[4];
-    __shared__ float wo[4][HD];
+    __shared__ float wm[NW], wl[NW];
+    __shared__ float wo[NW][HD];
     tc::pdl_trigger();
     tc::pdl_wait();
     const int head = blockIdx.x, b = blockIdx.y;
@@ -387,23 +389,31 @@ __global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q
     const int T = pos[b] + 1;
     const float* K = g.base + (size_t)slot[b] * g.slot_stride + layer_off + (size_t)head * g.head_stride;
     const float* V = K + g.sel_stride;
-    if (threadIdx.x < HD / 4)
-        qs[threadIdx.x] = *reinterpret_cast<const float4*>(q + (size_t)b * ldq + head * HD + threadIdx.x * 4);
-    __syncthreads();
 
     float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
-    for (int t0 = warp * 32; t0 < T; t0 += 128) {
+    bool first = true;
+    for (int t0 = warp * 32; t0 < T || first; t0 += 32 * NW) {
+        const bool active = t0 < T;
         const int t = t0 + lane;
-        const int nv = min(32, T - t0);
-        // one burst: this lane's K row and the V slice of all 32 rows
+        const int nv = active ? min(32, T - t0) : 1;
+        const int tl = active ? t0 : 0;
+        // one burst: this lane's K row and the V slice of all 32 rows (issued before q is needed)
         float4 kr[HD / 4];
-        const float4* kp = reinterpret_cast<const float4*>(K + (size_t)min(t, T - 1) * HD);
+        const float4* kp = reinterpret_cast<const float4*>(K + (size_t)min(tl + lane, T - 1) * HD);
 #pragma unroll
         for (int i = 0; i < HD / 4; ++i) kr[i] = __ldg(kp + i);
         float2 vv[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-            vv[j] = __ldg(reinterpret_cast<const float2*>(V + (size_t)(t0 + min(j, nv - 1)) * HD) + lane);
+            vv[j] = __ldg(reinterpret_cast<const float2*>(V + (size_t)(tl + min(j, nv - 1)) * HD) + lane);
+        if (first) {
+            if (threadIdx.x < HD / 4)
+                qs[threadIdx.x] =
+                    *reinterpret_cast<const float4*>(q + (size_t)b * ldq + head * HD + threadIdx.x * 4);
+            __syncthreads();
+            first = false;
+        }
+        if (!active) break;
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
         for (int i = 0; i < HD / 4; ++i) {
@@ -438,10 +448,10 @@ __global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q
     if (threadIdx.x < HD) {
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w]);
         float L = 0.f, O = 0.f;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
+        for (int w = 0; w < NW; ++w) {
             if (wm[w] != -INFINITY) {
                 const float f = expf(wm[w] - M);
                 L += wl[w] * f;
@@ -460,7 +470,7 @@ cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t 
                                float scale, cudaStream_t st) {
     if (B <= 0) return cudaSuccess;
     if (g.hd != 64) return cudaErrorInvalidValue;
-    return launch_pdl(k_attn_decode, dim3(n_head, B), dim3(128), 0, st, q, ldq, g, layer_off, slot, pos, out, ohi,
+    return launch_pdl(k_attn_decode<4>, dim3(n_head, B), dim3(128), 0, st, q, ldq, g, layer_off, slot, pos, out, ohi,
                       olo, ldo, scale);
 }
 

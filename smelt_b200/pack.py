@@ -107,9 +107,9 @@ def convert_tensor(name: str, hf: np.ndarray, policy: str) -> Tensor:
         f = np.ascontiguousarray(f.T)
     atom = choose_atom(f.shape, policy)
     if atom == atoms.ATOM_Q8:
-        data = atoms.q8_encode(f)
+        data = atoms.q8_encode_fast(f)
     elif atom == atoms.ATOM_Q4:
-        data = atoms.q4_encode(f)
+        data = atoms.q4_encode_fast(f)
     elif atom == atoms.ATOM_F32:
         data = f.reshape(-1).view(np.uint8).copy()
     else:

@@ -22,7 +22,8 @@ def edge_values(n_blocks=512, seed=3):
     return x
 
 
-@pytest.mark.parametrize("enc,oenc", [(atoms.q8_encode, O.q8_encode), (atoms.q4_encode, O.q4_encode)])
+@pytest.mark.parametrize("enc,oenc", [(atoms.q8_encode, O.q8_encode), (atoms.q4_encode, O.q4_encode),
+                                      (atoms.q8_encode_fast, O.q8_encode), (atoms.q4_encode_fast, O.q4_encode)])
 def test_encoders_bit_exact(enc, oenc):
     x = edge_values()
     assert np.array_equal(enc(x), oenc(x))
