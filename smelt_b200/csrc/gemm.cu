@@ -181,7 +181,8 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BN, n0 = blockIdx.y * BM;
+    // weight-row tiles vary fastest: CTAs running together share activation tiles in L2
+    const int n0 = blockIdx.x * BM, m0 = blockIdx.y * BN;
     const int split = blockIdx.z;
     const int kb0 = split * p.kb_per_split;
     const int nkb = min(p.kb_per_split, p.nkb_total - kb0);
@@ -627,7 +628,7 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
     tp.post = wt.post;
     tp.epi = e;
     tp.err = p.err;
-    dim3 grid(m_tiles, n_tiles, splits);
+    dim3 grid(n_tiles, m_tiles, splits);
     if (presplit) {
         if (w.atom == ATOM_Q8) return launch_bn<ATOM_Q8, true>(BN, wt.hi, wt.lo, *xh, *xl, tp, grid, st);
         return launch_bn<ATOM_Q4, true>(BN, wt.hi, wt.lo, *xh, *xl, tp, grid, st);

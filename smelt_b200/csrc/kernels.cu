@@ -201,11 +201,13 @@ cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y,
 }
 
 // ------------------------------------------------------------------ linear (CUDA cores)
-// One half-warp per output row n; its 16 lanes stride over the row in 16-byte chunks
-// (coalesced 256 B per half-warp load). Each chunk is dequantised in registers with
-// the byte-permute conversion, dotted with MT activation rows, and the partial dot
-// of a group is scaled once by the group's f16 scale. Partial sums are reduced with
-// half-warp shuffles; lane mi writes activation row m0+mi through the epilogue.
+// Decode GEMV / small-M GEMM. KS half-warps share one output row n and split its 16-byte
+// chunks (interleaved, so the KS*16 lanes of a row read KS*256 contiguous bytes); each
+// chunk is dequantised in registers with the byte-permute conversion, dotted with MT
+// activation rows, and the partial dot of a group is scaled once by the group's f16
+// scale. Half-warp shuffles reduce each part; parts are added in fixed order through
+// shared memory (deterministic); lane mi then writes activation row m0+mi through the
+// epilogue. The first batch of weight chunks is loaded before griddepcontrol.wait.
 template <int ATOM>
 struct ChunkTraits;
 template <>
@@ -268,43 +270,54 @@ __device__ __forceinline__ float dot_chunk(const float* f, const float* __restri
 }
 
 template <int ATOM, int MT, int U>
-__global__ void __launch_bounds__(256) k_linear_simt(QW w, const float* __restrict__ X, int ldx, int M,
+__global__ void __launch_bounds__(128) k_linear_simt(QW w, const float* __restrict__ X, int ldx, int M, int KS,
                                                      Epi epi) {
     constexpr int CE = ChunkTraits<ATOM>::CE;
+    __shared__ float red[8][MT];  // [half-warp][row of the activation batch]
     tc::pdl_trigger();
-    tc::pdl_wait();
     const int lane16 = threadIdx.x & 15;
-    const int n = blockIdx.x * (blockDim.x >> 4) + (threadIdx.x >> 4);
+    const int hw = threadIdx.x >> 4;            // half-warp 0..7
+    const int row_local = hw / KS, kpart = hw % KS;
+    const int n = blockIdx.x * (8 / KS) + row_local;
     const bool active = n < w.rows;
     const int nn = active ? n : (w.rows - 1);
     const int nch = w.cols / CE;
+    const int first = kpart * 16 + lane16, stride = 16 * KS;
     const uint8_t* wrow = w.q + (size_t)nn * w.qstride;
     const __half* srow = w.s + (size_t)nn * w.sstride;
+
+    uint4 wv[U];
+    float sc[U];
+    auto load_batch = [&](int c0) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = c0 + stride * u;
+            if (c < nch) {
+                wv[u] = __ldg(reinterpret_cast<const uint4*>(wrow + (size_t)c * 16));
+                if (ChunkTraits<ATOM>::SCALED)
+                    sc[u] = __half2float(srow[ATOM == ATOM_Q8 ? (c >> 1) : c]);
+                else
+                    sc[u] = 1.f;
+            } else {
+                wv[u] = make_uint4(0, 0, 0, 0);
+                sc[u] = 0.f;
+            }
+        }
+    };
+    // The weights do not depend on earlier kernels: start streaming them before waiting
+    // for the activations, so the load overlaps the previous kernel's tail.
+    load_batch(first);
+    tc::pdl_wait();
 
     for (int m0 = 0; m0 < M; m0 += MT) {
         float acc[MT];
 #pragma unroll
         for (int i = 0; i < MT; ++i) acc[i] = 0.f;
-        for (int c0 = lane16; c0 < nch; c0 += 16 * U) {
-            uint4 wv[U];
-            float sc[U];
+        for (int c0 = first; c0 < nch; c0 += stride * U) {
+            if (m0 != 0 || c0 != first) load_batch(c0);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int c = c0 + 16 * u;
-                if (c < nch) {
-                    wv[u] = __ldg(reinterpret_cast<const uint4*>(wrow + (size_t)c * 16));
-                    if (ChunkTraits<ATOM>::SCALED)
-                        sc[u] = __half2float(srow[ATOM == ATOM_Q8 ? (c >> 1) : c]);
-                    else
-                        sc[u] = 1.f;
-                } else {
-                    wv[u] = make_uint4(0, 0, 0, 0);
-                    sc[u] = 0.f;
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int c = c0 + 16 * u;
+                const int c = c0 + stride * u;
                 if (c < nch) {
                     float f[CE];
                     decode_chunk<ATOM>(wv[u], f);
@@ -312,13 +325,7 @@ __global__ void __launch_bounds__(256) k_linear_simt(QW w, const float* __restri
                     for (int mi = 0; mi < MT; ++mi) {
                         if (m0 + mi < M) {
                             const float* xr = X + (size_t)(m0 + mi) * ldx + (size_t)c * CE;
-                            float p;
-                            if (ATOM == ATOM_Q4) {
-                                // elements 0..15 pair with x[0..15], 16..31 with x[16..31]
-                                p = dot_chunk<32>(f, xr);
-                            } else {
-                                p = dot_chunk<CE>(f, xr);
-                            }
+                            const float p = dot_chunk<CE>(f, xr);
                             if (ChunkTraits<ATOM>::SCALED)
                                 acc[mi] = fmaf(sc[u], p, acc[mi]);
                             else
@@ -335,7 +342,23 @@ __global__ void __launch_bounds__(256) k_linear_simt(QW w, const float* __restri
             v += __shfl_xor_sync(0xffffffffu, v, 4);
             v += __shfl_xor_sync(0xffffffffu, v, 2);
             v += __shfl_xor_sync(0xffffffffu, v, 1);
-            if (active && lane16 == mi && m0 + mi < M) epi_apply(epi, m0 + mi, n, v);
+            acc[mi] = v;
+        }
+        if (KS == 1) {
+#pragma unroll
+            for (int mi = 0; mi < MT; ++mi)
+                if (active && lane16 == mi && m0 + mi < M) epi_apply(epi, m0 + mi, n, acc[mi]);
+        } else {
+            __syncthreads();  // red[] of the previous pass has been consumed
+#pragma unroll
+            for (int mi = 0; mi < MT; ++mi)
+                if (lane16 == mi) red[hw][mi] = acc[mi];
+            __syncthreads();
+            if (kpart == 0 && lane16 < MT && active && m0 + lane16 < M) {
+                float v = 0.f;
+                for (int k = 0; k < KS; ++k) v += red[hw + k][lane16];
+                epi_apply(epi, m0 + lane16, n, v);
+            }
         }
     }
 }
@@ -343,15 +366,20 @@ __global__ void __launch_bounds__(256) k_linear_simt(QW w, const float* __restri
 template <int ATOM>
 static cudaError_t linear_dispatch(const QW& w, const float* X, int ldx, int M, const Epi& e,
                                    cudaStream_t st) {
-    // Rows per block: keep at least ~2 blocks per SM on the small matrices.
-    int rpb = 8;
-    if (w.rows < 148 * 2 * 8) rpb = 4;
-    if (w.rows < 148 * 2 * 4) rpb = 2;
-    dim3 grid((w.rows + rpb - 1) / rpb), block(16 * rpb);
-    if (M == 1) return launch_pdl(k_linear_simt<ATOM, 1, 4>, grid, block, 0, st, w, X, ldx, M, e);
-    if (M <= 2) return launch_pdl(k_linear_simt<ATOM, 2, 4>, grid, block, 0, st, w, X, ldx, M, e);
-    if (M <= 4) return launch_pdl(k_linear_simt<ATOM, 4, 4>, grid, block, 0, st, w, X, ldx, M, e);
-    return launch_pdl(k_linear_simt<ATOM, 8, 2>, grid, block, 0, st, w, X, ldx, M, e);
+    constexpr int CE = ChunkTraits<ATOM>::CE;
+    // weight chunks in flight per lane: 8 x 16 B (int4 chunks hold 32 weights: 4)
+    constexpr int UW = (ATOM == ATOM_Q4) ? 4 : 8;
+    const int nch = w.cols / CE;
+    // half-warps per row: enough that one batch of UW chunks per lane covers the row, and
+    // enough rows-per-block splitting that the grid fills the GPU twice over
+    int KS = 1;
+    while (KS < 8 && nch > 16 * UW * KS) KS *= 2;
+    while (KS < 8 && (long long)(w.rows + 8 / KS - 1) / (8 / KS) < 2 * 148 * 4 && nch >= 16 * 2 * KS) KS *= 2;
+    const dim3 grid((w.rows + 8 / KS - 1) / (8 / KS)), block(128);
+    if (M == 1) return launch_pdl(k_linear_simt<ATOM, 1, UW>, grid, block, 0, st, w, X, ldx, M, KS, e);
+    if (M <= 2) return launch_pdl(k_linear_simt<ATOM, 2, UW>, grid, block, 0, st, w, X, ldx, M, KS, e);
+    if (M <= 4) return launch_pdl(k_linear_simt<ATOM, 4, 4>, grid, block, 0, st, w, X, ldx, M, KS, e);
+    return launch_pdl(k_linear_simt<ATOM, 8, 2>, grid, block, 0, st, w, X, ldx, M, KS, e);
 }
 
 cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, const Epi& e, cudaStream_t st) {
