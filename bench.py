@@ -43,11 +43,11 @@ sys.path.insert(0, ROOT)
 
 WORKLOADS = {
     # name: (model, policy, batch, prompt len, decode steps, scaling)
-    "small-int8-b32": ("small", "auto", 32, 128, 128, "weak"),      # BASELINE configs[1] (per GPU)
-    "small-int8-b1": ("small", "auto", 1, 64, 64, "weak"),          # configs[0] shape, int8
-    "small-int4-b256": ("small", "q4auto", 256, 264, 256, "strong"),  # configs[2], ragged 16..512
-    "medium-int8-prefill": ("medium", "auto", 64, 1024, 1, "strong"),  # configs[3]
-    "xl-int8-tp": ("xl", "auto", 16, 256, 256, "strong"),           # configs[4], tensor parallel
+    "small-int8-b32": ("small", "auto", 32, 128, 128, "weak"),      # 32 sequences per GPU, 128 + 128
+    "small-int8-b1": ("small", "auto", 1, 64, 64, "weak"),          # single-sequence latency, int8
+    "small-int4-b256": ("small", "q4auto", 256, 264, 256, "strong"),  # 256 ragged prompts 16..512, int4
+    "medium-int8-prefill": ("medium", "auto", 64, 1024, 1, "strong"),  # 64 x 1024-token prefill
+    "xl-int8-tp": ("xl", "auto", 16, 256, 256, "strong"),           # GPT-2 XL, tensor parallel
 }
 
 
@@ -209,7 +209,20 @@ def cpu_baseline(pk, plen: int, sample_steps: int, threads: int):
     return sample_steps / dt, dt
 
 
+METRICS = {
+    "small-int8-b32": "decode tokens/s (GPT-2 small int8)",
+    "small-int8-b1": "decode tokens/s (GPT-2 small int8)",
+    "small-int4-b256": "decode tokens/s (GPT-2 small int4)",
+    "medium-int8-prefill": "prefill tokens/s (GPT-2 medium int8)",
+    "xl-int8-tp": "decode tokens/s (GPT-2 XL int8, tensor parallel)",
+}
+
+
 def run_reference(args, wl):
+    """The reference's CPU path (one token per `Engine::step` call, gpt2.rs:227) on the host cores,
+    restated by the oracle, on a bounded sample of this workload: decode workloads time one
+    token for each of 2 sequences per step; the prefill workload times 8 consecutive prompt
+    tokens per step (the reference prefills by stepping token by token)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -219,28 +232,44 @@ def run_reference(args, wl):
     from oracle import oracle as O
 
     eng = O.Engine(pk.meta.as_dict(), {n: (t.shape, t.atom, t.data) for n, t in pk.tensors.items()}, threads)
-    # each step: one decode token for each of 2 sequences (sequential, as the reference runs batches)
-    per_step = 2
-    kvs = [eng.empty_kv() for _ in range(per_step)]
+    prefill = args.config == "medium-int8-prefill"
+    per_step = 8 if prefill else 2
+    kvs = [eng.empty_kv() for _ in range(1 if prefill else per_step)]
+    from smelt_b200 import synth
+
+    ids = np.asarray(synth.prompt_ids(4096, pk.meta.vocab, seed=1))
+    pos = 0
     for w in range(args.warmup):
-        for j in range(per_step):
-            eng.step(1, plen + w % dec, kvs[j])
+        if prefill:
+            for j in range(per_step):
+                eng.step(int(ids[pos % 4096]), pos % pk.meta.n_ctx, kvs[0])
+                pos += 1
+        else:
+            for j in range(per_step):
+                eng.step(1, plen + w % dec, kvs[j])
     t0 = time.perf_counter()
     for s in range(args.steps):
         for j in range(per_step):
-            eng.step((s * 31 + j) % pk.meta.vocab, plen + (args.warmup + s) % dec, kvs[j])
+            if prefill:
+                eng.step(int(ids[pos % 4096]), pos % pk.meta.n_ctx, kvs[0])
+                pos += 1
+            else:
+                eng.step((s * 31 + j) % pk.meta.vocab, plen + (args.warmup + s) % dec, kvs[j])
     dt = time.perf_counter() - t0
     tok_s = args.steps * per_step / dt
+    sample = (f"{args.steps} steps x {per_step} consecutive prompt tokens of one sequence"
+              if prefill else
+              f"{args.steps} steps x {per_step} sequences x 1 token at positions {plen}..{plen + dec - 1}")
     line = {
-        "impl": "reference", "metric": "decode tokens/s", "value": tok_s, "unit": "tokens/s",
+        "impl": "reference", "metric": METRICS[args.config], "value": tok_s, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": wl[5],
         "vs_baseline": None, "dtype": "int8xfp32" if policy == "auto" else "int4xfp32", "data": "synthetic",
-        "config": {"workload": args.config, "model": f"gpt2-{model}", "weights": policy, "prompt": plen},
+        "config": {"workload": args.config, "model": f"gpt2-{model}", "weights": policy, "global_batch": batch,
+                   "prompt": plen},
         "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} steps x {per_step} sequences x 1 token at positions "
-                                   f"{plen}..{plen + dec - 1}, oracle C++ restatement of gpt2.rs step, "
-                                   f"{threads}-thread row split per matmul"},
+                         "sample": sample + f", oracle C++ restatement of gpt2.rs step, "
+                                            f"{threads}-thread row split per matmul"},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -280,7 +309,7 @@ def max_over_ranks(v: float, world: int, dev) -> float:
 
 
 def run_prefill(args, wl):
-    """64 prompts of 1024 tokens; a step is their prefill and the greedy token
+    """GPT-2 medium int8 prefill, 64 prompts of 1024 tokens; a step is their prefill and the greedy token
     after each (generate_greedy with one step), sequences split across ranks (strong
     scaling); tensor-core bound."""
     import torch
@@ -333,7 +362,7 @@ def run_prefill(args, wl):
         peak_kind = "measured bf16 sustained"
     achieved = flops_rank / (ms / args.steps / 1e3) / 1e12 if prompts else 0.0
     line = {
-        "metric": "prefill tokens/s (GPT-2 medium int8)", "value": tokens / (ms_max / 1e3), "unit": "tokens/s",
+        "metric": METRICS[args.config], "value": tokens / (ms_max / 1e3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "int8xfp32 (fp16x3 tensor)",
         "data": "synthetic",
@@ -357,7 +386,7 @@ def run_prefill(args, wl):
 
 
 def run_tp(args, wl):
-    """configs[4]: GPT-2 XL int8, tensor parallel over the torchrun ranks (NCCL all-reduce
+    """GPT-2 XL int8, tensor parallel over the torchrun ranks (NCCL all-reduce
     of the two c_proj partial sums per layer); 16 sequences, decode positions 256..511."""
     import torch
 
@@ -424,7 +453,7 @@ def run_tp(args, wl):
     ms_max = max_over_ranks(timed_ms, world, dev)
     weights = sum(t.data.nbytes for t in pk.tensors.values() if len(t.shape) == 2)
     line = {
-        "metric": "decode tokens/s (GPT-2 XL int8, tensor parallel)", "value": batch * args.steps / (ms_max / 1e3),
+        "metric": METRICS[args.config], "value": batch * args.steps / (ms_max / 1e3),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "int8xfp32", "data": "synthetic",
@@ -592,7 +621,7 @@ def main():
     step_bytes = statistics.mean(algorithmic_step_bytes(pk, p) for p in positions_timed)
 
     line = {
-        "metric": "decode tokens/s (GPT-2 small int8)" if policy == "auto" else "decode tokens/s (GPT-2 small int4)",
+        "metric": METRICS[args.config],
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "int8xfp32" if policy == "auto" else "int4xfp32", "data": "synthetic",

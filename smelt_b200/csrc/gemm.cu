@@ -164,6 +164,87 @@ __device__ __forceinline__ void put32_q4(uint32_t a_hi, uint32_t a_lo, int r, in
     }
 }
 
+// Epilogue of output row nn for NJ tokens m_j = mbase + j * mstep (written where m_j < mend).
+// Every lane of the warp calls it (the KV-cache token offsets travel by shuffle). All global
+// loads of the chunk are issued before its first store, per-row terms are computed once, and
+// the operation order per element is that of epi_apply.
+template <int NJ>
+__device__ __forceinline__ void epi_chunk(const Epi& e, int nn, bool row_ok, const float (&acc)[NJ], int mbase,
+                                          int mstep, int mend, float post) {
+    const int lane = threadIdx.x & 31;
+    const bool has_b = e.bias != nullptr;
+    const float b = (has_b && row_ok) ? __ldg(e.bias + nn) : 0.f;
+    bool ok[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) ok[j] = row_ok && (mbase + j * mstep < mend);
+    switch (e.kind) {
+        case EPI_STORE: {
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                float v = acc[j] * post;
+                if (has_b) v += b;
+                if (ok[j]) e.out[(size_t)(mbase + j * mstep) * e.ldo + nn] = v;
+            }
+            break;
+        }
+        case EPI_RESID: {
+            float r[NJ];
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) r[j] = ok[j] ? e.out[(size_t)(mbase + j * mstep) * e.ldo + nn] : 0.f;
+#pragma unroll
+            for (int j = 0; j < NJ; ++j)
+                if (ok[j]) e.out[(size_t)(mbase + j * mstep) * e.ldo + nn] = r[j] + (acc[j] * post + b);
+            break;
+        }
+        case EPI_GELU: {
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                float v = acc[j] * post;
+                if (has_b) v += b;
+                const float gv = gelu_tanh(v);
+                const size_t o = (size_t)(mbase + j * mstep) * e.ldo + nn;
+                if (ok[j]) {
+                    e.out[o] = gv;
+                    if (e.out_hi) {
+                        const __half h = __float2half_rn(gv);
+                        e.out_hi[o] = h;
+                        e.out_lo[o] = __float2half_rn(gv - __half2float(h));
+                    }
+                }
+            }
+            break;
+        }
+        default: {  // EPI_QKV
+            // lane l holds the KV-cache offset of token mbase + l * mstep (shuffled in uniform flow)
+            const int ml = mbase + lane * mstep;
+            long long mine = 0;
+            if (lane < NJ && ml < mend)
+                mine = (long long)e.slot[ml] * (long long)e.slot_stride + (long long)e.pos[ml] * e.hd;
+            const bool isq = nn < e.d_local;
+            float* col = e.kv;
+            if (!isq && row_ok) {
+                const int sel = nn >= 2 * e.d_local ? 1 : 0;  // 0 = K, 1 = V
+                const int c = nn - (sel + 1) * e.d_local;
+                const int head = c / e.hd, i = c - head * e.hd;
+                col = e.kv + e.layer_off + (size_t)sel * e.sel_stride + (size_t)head * e.head_stride + i;
+            }
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                const long long off = __shfl_sync(0xffffffffu, mine, j);
+                float v = acc[j] * post;
+                if (has_b) v += b;
+                if (ok[j]) {
+                    if (isq)
+                        e.out[(size_t)(mbase + j * mstep) * e.ldo + nn] = v;
+                    else
+                        col[off] = v;
+                }
+            }
+            break;
+        }
+    }
+}
+
 template <int ATOM, int BN, bool PRESPLIT>
 __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
     k_linear_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wlo,
@@ -348,18 +429,14 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
         const int nn = n0 + row;
         const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
         float* part = reinterpret_cast<float*>(smem);  // [BN][128], operand rings are free now
+        const int mend = min(p.M, m0 + BN);
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
             float v[32];
             tc::tmem_ld32(taddr + c0, v);
             if (p.splits == 1) {
-                if (acc_ok && nn < p.w.rows) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int m = m0 + c0 + j;
-                        if (m < p.M) epi_apply(p.epi, m, nn, v[j] * p.post);
-                    }
-                }
+                if (m0 + c0 >= mend) break;  // warp-uniform
+                epi_chunk<32>(p.epi, nn, acc_ok && nn < p.w.rows, v, m0 + c0, 1, mend, p.post);
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) part[(c0 + j) * BM + row] = v[j];
@@ -374,22 +451,31 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
         if (warp >= 1 && warp <= 4) {
             const int row = (warp & 3) * 32 + lane;
             const int nn = n0 + row;
-            const uint32_t rank = tc::cluster_rank();
+            const int rank = (int)tc::cluster_rank();
             const uint32_t local = tc::smem_u32(smem);
-            for (int c = (int)rank; c < BN; c += p.splits) {
-                const int m = m0 + c;
-                if (m >= p.M) break;
-                float vals[MAX_SPLITS];
+            const int mend = min(p.M, m0 + BN);
+            constexpr int RJ = 8;  // columns per batch: RJ * splits remote loads in flight
+            // this CTA reduces and writes columns rank, rank + splits, rank + 2 * splits, ...
+            for (int q0 = 0; m0 + rank + q0 * p.splits < mend; q0 += RJ) {
+                float acc[RJ];
+                uint32_t addr[RJ];
 #pragma unroll
-                for (int sp = 0; sp < MAX_SPLITS; ++sp)
-                    vals[sp] = (sp < p.splits)
-                                   ? tc::ld_cluster_f32(tc::map_cluster(local + (uint32_t)((c * BM + row) * 4), sp))
-                                   : 0.f;
-                float acc = 0.f;
+                for (int j = 0; j < RJ; ++j) {
+                    const int c = min(rank + (q0 + j) * p.splits, BN - 1);
+                    addr[j] = local + (uint32_t)((c * BM + row) * 4);
+                    acc[j] = 0.f;
+                }
 #pragma unroll
-                for (int sp = 0; sp < MAX_SPLITS; ++sp)
-                    if (sp < p.splits) acc += vals[sp];
-                if (nn < p.w.rows) epi_apply(p.epi, m, nn, acc * p.post);
+                for (int sp = 0; sp < MAX_SPLITS; ++sp) {
+                    if (sp < p.splits) {
+                        float t[RJ];
+#pragma unroll
+                        for (int j = 0; j < RJ; ++j) t[j] = tc::ld_cluster_f32(tc::map_cluster(addr[j], sp));
+#pragma unroll
+                        for (int j = 0; j < RJ; ++j) acc[j] += t[j];
+                    }
+                }
+                epi_chunk<RJ>(p.epi, nn, nn < p.w.rows, acc, m0 + rank + q0 * p.splits, p.splits, mend, p.post);
             }
         }
         tc::cluster_sync();  // no CTA leaves while its partial may still be read
