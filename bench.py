@@ -568,12 +568,12 @@ def main():
             ev1.record(stream)
         barrier()
         ms = ev0.elapsed_time(ev1)
+        launches = g.launches - l0  # kernels launched inside the timed region
         # keep sampling clocks for at least ~1 s of the same work when the timed region was short
         t_extra = time.perf_counter()
         while time.perf_counter() - t_extra < max(0.0, 1.0 - ms / 1e3):
             run_steps(min(args.steps, 32))
             torch.cuda.synchronize()
-    launches = g.launches - l0
     ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
         torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
@@ -606,7 +606,26 @@ def main():
     # ---- roofline: every kernel type of one decode step timed in steady state (its first
     # launch replayed back to back in a CUDA graph, CUDA events on the launch stream) ----
     g.prefill(prompts)
-    kt = g.profile_kernels(reps=20)
+    persistent = n_local == 1 and g.info()["persistent_decode"]
+    if persistent:
+        # the whole step is one kernel; a launch runs S consecutive steps
+        S = max(1, min(32, span - 1))
+        g.decode_steps(S, 1, want_tokens=False)
+        g.prefill(prompts)
+        pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            pe0.record(stream)
+        g.set_stream(stream.cuda_stream)
+        g.decode_steps(S, 1, want_tokens=False)
+        with torch.cuda.stream(stream):
+            pe1.record(stream)
+        torch.cuda.synchronize()
+        g.set_stream(None)
+        pos_s = [start_pos + k for k in range(S)]
+        kt = {"k_decode_persistent": {"us": pe0.elapsed_time(pe1) * 1e3, "per_step": 1.0 / S,
+                                      "bytes": sum(algorithmic_step_bytes(pk, p) for p in pos_s)}}
+    else:
+        kt = g.profile_kernels(reps=20)
     name, rec = max(kt.items(), key=lambda kv: kv[1]["us"] * kv[1]["per_step"])
     per_launch_bytes = rec["bytes"]
     per_launch_ms = rec["us"] / 1e3
@@ -634,7 +653,8 @@ def main():
         "roofline": {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_kind,
                      "bytes_per_launch": per_launch_bytes, "us_per_launch": rec["us"],
-                     "timing": "graph of 20 back-to-back launches of the step's own launch, CUDA events"},
+                     "timing": ("one launch of %d consecutive steps, CUDA events" % round(1 / rec["per_step"]))
+                     if persistent else "graph of 20 back-to-back launches of the step's own launch, CUDA events"},
         "kernels": {k: {"us_per_launch": round(v["us"], 3), "per_step": v["per_step"],
                         "step_share": round(v["us"] * v["per_step"] / (ms_max / args.steps * 1e3), 4)}
                     for k, v in kt.items()},

@@ -153,6 +153,15 @@ int gpt2q_profile_read(gpt2q_handle* h, char* json, size_t cap);
  * prefill. */
 int gpt2q_profile_kernels(gpt2q_handle* h, int reps, char* json, size_t cap);
 
+/* Which execution paths this handle uses, as JSON:
+ * {"persistent_decode": bool, "persistent_why": reason when false,
+ *  "persistent_ctas": CTAs of the persistent launch, "tensor_core": bool}.
+ * The persistent decode serves every single-sequence decode step (gpt2q_step,
+ * gpt2q_decode with n_seq = 1, gpt2q_decode_steps with one sequence); the
+ * environment variable GPT2Q_NO_PERSISTENT at create time turns it off.
+ * No counterpart in the reference (gpu.rs has one kernel sequence). */
+int gpt2q_info(gpt2q_handle* h, char* json, size_t cap);
+
 /* Greedy argmax (IEEE total order, ties -> last index) of n_rows rows of device fp32
  * logits (row stride ld >= vocab floats) into device d_next[n_rows], on `stream` (a
  * cudaStream_t; NULL = legacy default stream). Allocates nothing: its per-row scratch is

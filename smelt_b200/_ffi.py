@@ -19,7 +19,7 @@ EXPORTS = [
     "gpt2q_create", "gpt2q_create_tp", "gpt2q_destroy", "gpt2q_last_error", "gpt2q_reset_kv",
     "gpt2q_step", "gpt2q_decode", "gpt2q_prefill", "gpt2q_decode_steps", "gpt2q_generate_greedy",
     "gpt2q_dequant", "gpt2q_launches", "gpt2q_set_stream", "gpt2q_sync", "gpt2q_profile",
-    "gpt2q_profile_read", "gpt2q_profile_kernels", "gpt2q_argmax_noalloc", "gpt2q_rng_new", "gpt2q_rng_normal_f32", "gpt2q_rng_below",
+    "gpt2q_profile_read", "gpt2q_profile_kernels", "gpt2q_info", "gpt2q_argmax_noalloc", "gpt2q_rng_new", "gpt2q_rng_normal_f32", "gpt2q_rng_below",
     "gpt2q_quantize_q8", "gpt2q_quantize_q4",
 ]
 
@@ -94,6 +94,8 @@ def load(path: str | None = None):
     lib.gpt2q_profile_read.restype = C.c_int
     lib.gpt2q_profile_kernels.argtypes = [_hp, C.c_int, C.c_char_p, C.c_size_t]
     lib.gpt2q_profile_kernels.restype = C.c_int
+    lib.gpt2q_info.argtypes = [_hp, C.c_char_p, C.c_size_t]
+    lib.gpt2q_info.restype = C.c_int
     lib.gpt2q_argmax_noalloc.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
     lib.gpt2q_argmax_noalloc.restype = C.c_int
     lib.gpt2q_rng_new.argtypes = [C.c_uint64]

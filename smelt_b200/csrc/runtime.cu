@@ -8,7 +8,9 @@
 //    layer for a single sequence, gpu.rs:128-134);
 //  - a decode step is a fixed kernel sequence captured once per batch size in a
 //    CUDA graph; greedy argmax runs on the device and feeds the next step, so a
-//    multi-step decode never returns to the host between tokens.
+//    multi-step decode never returns to the host between tokens;
+//  - a single sequence on an eligible int8 model decodes through one persistent
+//    launch (persistent.h) that runs any number of steps.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -25,6 +27,7 @@
 #include "gpt2q.h"
 #include "gemm.h"
 #include "kernels.h"
+#include "persistent.h"
 #include "tp.h"
 
 using namespace gpt2q;
@@ -149,6 +152,7 @@ struct gpt2q_handle {
     std::map<std::string, ProfAgg> prof_agg;
 
     GemmPlan gemm;  // tensor-core path for large M
+    MkPlan mk;      // persistent single-sequence decode
     TpComm* tp = nullptr;
 
     int fail(int code, const std::string& m) {
@@ -530,8 +534,59 @@ int flush_profile(gpt2q_handle* H) {
     return GPT2Q_OK;
 }
 
+// `steps` greedy steps of the single current sequence in one persistent launch.
+int run_persistent(gpt2q_handle* H, int steps) {
+    const gpt2q_config& c = H->cfg;
+    MkParams p{};
+    p.stream = H->mk.stream;
+    p.cta_bytes = H->mk.cta_bytes;
+    p.seg_bytes = H->mk.seg_bytes;
+    p.d = c.n_embd;
+    p.n_layer = c.n_layer;
+    p.n_head = c.n_head;
+    p.vocab = c.vocab;
+    p.n_ctx = c.n_ctx;
+    p.head_rows = H->mk.head_rows;
+    p.ln_eps = c.ln_eps;
+    p.attn_scale = 1.0f / std::sqrt((float)H->hd);
+    p.layers = H->mk.layers;
+    p.lnf_g = H->lnf_g;
+    p.lnf_b = H->lnf_b;
+    p.wte = H->wte.w;
+    p.wpe = H->wpe.w;
+    p.kv = H->kv.base;
+    p.kv_slot = H->kv.slot_stride;
+    p.kv_layer = H->kv.layer_stride;
+    p.kv_sel = H->kv.sel_stride;
+    p.kv_head = H->kv.head_stride;
+    p.slot = H->d_slot;
+    p.pos = H->d_pos;
+    p.tok = H->d_tok;
+    p.next = H->d_next;
+    p.genlog = H->d_genlog;
+    p.logits = H->logits;
+    p.p1 = H->mk.p1;
+    p.p2 = H->mk.p2;
+    p.best = H->mk.best;
+    p.epoch = H->mk.epoch;
+    p.err = H->mk.err;
+    p.abort_flag = H->mk.err + 1;
+    p.steps = steps;
+    p.trace = H->mk.trace;
+    int rc = run_kernel(H, "decode_persistent", (double)H->mk.cta_bytes * 8 * H->mk.clusters * steps,
+                        [&]() { return launch_decode_persistent(H->mk, p, H->stream); });
+    if (rc) return rc;
+    H->hpos[0] += steps;
+    return GPT2Q_OK;
+}
+
+bool use_persistent(const gpt2q_handle* H, int B) {
+    return B == 1 && H->mk.enabled && !H->capturing && H->ktime_reps == 0;
+}
+
 // Run one decode step for the current state (graph replay when possible).
 int run_decode_step(gpt2q_handle* H, int B) {
+    if (use_persistent(H, B)) return run_persistent(H, 1);
     const bool graph_ok = H->use_graphs && !H->prof && H->stream != nullptr;
     if (graph_ok) {
         auto it = H->dec_graphs.find(B);
@@ -731,7 +786,8 @@ int do_decode(gpt2q_handle* H, const uint32_t* tok, const int32_t* pos, const in
 }
 
 int check_device_error(gpt2q_handle* H) {
-    const int e = gemm_take_error(H->gemm, H->stream);
+    int e = gemm_take_error(H->gemm, H->stream);
+    if (e == 0) e = mk_take_error(H->mk, H->stream);
     if (e > 0) return H->fail(GPT2Q_ETIMEOUT, "a bounded device-side wait timed out (error word " + std::to_string(e) + ")");
     if (e < 0) return H->fail(GPT2Q_ECUDA, "reading the device error word failed");
     return GPT2Q_OK;
@@ -962,6 +1018,31 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
             }
         }
     }
+    if (tp_size == 1) {
+        MkWeights mw;
+        mw.wte = H->wte.w;
+        mw.wpe = H->wpe.w;
+        bool have_all = H->lnf_g && H->lnf_b;
+        for (auto& L : H->layers) {
+            mw.attn.push_back(L.attn.w);
+            mw.proj.push_back(L.proj.w);
+            mw.fc.push_back(L.fc.w);
+            mw.mproj.push_back(L.mproj.w);
+            mw.layers.push_back(MkLayer{L.ln1_g, L.ln1_b, L.ln2_g, L.ln2_b, L.attn.bias, L.proj.bias, L.fc.bias,
+                                        L.mproj.bias});
+            have_all = have_all && L.ln1_g && L.ln1_b && L.ln2_g && L.ln2_b && L.attn.bias && L.proj.bias &&
+                       L.fc.bias && L.mproj.bias;
+        }
+        if (have_all) {
+            const cudaError_t me = mk_setup(H->mk, mw, d, c.n_layer, c.n_head, c.vocab, c.n_ctx, device, H->stream);
+            if (me != cudaSuccess) {
+                H->err = std::string("persistent decode setup: ") + cudaGetErrorString(me);
+                return bail(GPT2Q_ECUDA);
+            }
+        } else {
+            H->mk.why = "a LayerNorm or bias vector is missing";
+        }
+    }
     if (tp_size > 1) {
         H->tp = tp_create(tp_size, tp_rank, nccl_id, device);
         if (!H->tp || tp_last_error(H->tp)[0]) {
@@ -1012,6 +1093,7 @@ void gpt2q_destroy(gpt2q_handle* H) {
     for (auto e : H->ev_pool) cudaEventDestroy(e);
     if (H->tp) tp_destroy(H->tp);
     gemm_destroy(H->gemm);
+    mk_destroy(H->mk);
     for (auto& a : H->allocs) cudaFree(a.p);
     if (H->h_stage) cudaFreeHost(H->h_stage);
     if (H->own_stream) cudaStreamDestroy(H->own_stream);
@@ -1072,9 +1154,14 @@ int gpt2q_decode_steps(gpt2q_handle* H, int steps, uint32_t* out_tokens) {
     for (int b = 0; b < B; ++b)
         if (H->hpos[b] + steps > H->cfg.n_ctx)
             return H->fail(GPT2Q_EARG, "decode_steps would run past n_ctx");
-    for (int s = 0; s < steps; ++s) {
-        int rc = run_decode_step(H, B);
+    if (steps > 0 && use_persistent(H, B)) {
+        int rc = run_persistent(H, steps);
         if (rc) return rc;
+    } else {
+        for (int s = 0; s < steps; ++s) {
+            int rc = run_decode_step(H, B);
+            if (rc) return rc;
+        }
     }
     if (out_tokens && steps > 0) {
         // genlog[b][p] holds the token predicted from position p
@@ -1227,6 +1314,39 @@ int gpt2q_profile_kernels(gpt2q_handle* H, int reps, char* json, size_t cap) {
     if (s.size() + 1 > cap) return H->fail(GPT2Q_EARG, "profile_kernels: buffer too small");
     std::memcpy(json, s.c_str(), s.size() + 1);
     return check_device_error(H);
+}
+
+int gpt2q_info(gpt2q_handle* H, char* json, size_t cap) {
+    if (!H || !json || cap == 0) return GPT2Q_EARG;
+    std::string why;
+    for (char ch : H->mk.why) why += (ch == '"' || ch == '\\') ? '\'' : ch;
+    const std::string head = std::string("{\"persistent_decode\": ") + (H->mk.enabled ? "true" : "false") +
+                          ", \"persistent_why\": \"" + why + "\", \"persistent_ctas\": " +
+                          std::to_string(H->mk.enabled ? MK_CS * H->mk.clusters : 0) +
+                          ", \"tensor_core\": " + (H->gemm.enabled ? "true" : "false");
+    std::string tr;
+    if (H->mk.trace) {
+        // phase stamps (ns since the first stamp of CTA 0) of the last persistent launch
+        const int G = MK_CS * H->mk.clusters;
+        std::vector<unsigned long long> t((size_t)G * MK_TRACE);
+        CK(cudaMemcpy(t.data(), H->mk.trace, t.size() * 8, cudaMemcpyDeviceToHost));
+        tr = ", \"persistent_trace\": [";
+        for (int g = 0; g < G; ++g) {
+            tr += g ? ", [" : "[";
+            for (int k = 0; k < MK_TRACE; ++k) {
+                const unsigned long long raw = t[(size_t)g * MK_TRACE + k];
+                const bool counter = mk_trace_counter(k);
+                const long long v = counter ? (long long)raw : raw ? (long long)(raw - t[0]) : -1;
+                tr += (k ? ", " : "") + std::to_string(v);
+            }
+            tr += "]";
+        }
+        tr += "]";
+    }
+    const std::string s = head + tr + "}";
+    if (s.size() + 1 > cap) return H->fail(GPT2Q_EARG, "info: buffer too small");
+    std::memcpy(json, s.c_str(), s.size() + 1);
+    return GPT2Q_OK;
 }
 
 int gpt2q_profile_read(gpt2q_handle* H, char* json, size_t cap) {

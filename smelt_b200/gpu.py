@@ -169,6 +169,12 @@ class Gpu:
         self._check(self._lib.gpt2q_profile_kernels(self.h, int(reps), buf, len(buf)))
         return json.loads(buf.value.decode())
 
+    def info(self) -> dict:
+        """Execution paths of this handle (persistent single-sequence decode, tensor cores)."""
+        buf = C.create_string_buffer(1 << 20)
+        self._check(self._lib.gpt2q_info(self.h, buf, len(buf)))
+        return json.loads(buf.value.decode())
+
     def profile_read(self) -> dict:
         buf = C.create_string_buffer(1 << 16)
         self._check(self._lib.gpt2q_profile_read(self.h, buf, len(buf)))

@@ -142,8 +142,10 @@ def test_errors_are_reported_and_handle_survives():
 
 
 def test_launch_counter_counts_graph_kernels():
-    pk = make_pack(TINY, "auto")
+    # fp32 weights take the per-kernel decode (the persistent decode needs int8)
+    pk = make_pack(TINY, "f32")
     with Gpu(pk) as g:
+        assert not g.info()["persistent_decode"]
         g.step(1, 0)
         n0 = g.launches
         g.step(2, 1)
