@@ -105,7 +105,6 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 
@@ -198,18 +197,6 @@ __device__ __forceinline__ void dot_q8_rows(const uint8_t* q, const __half* s, c
     for (int r = 0; r < R; ++r) out[r] = acc[r];
 }
 
-// Sum over the block; red holds 8 floats (one per warp).
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    v = warp_sum(v);
-    const int warp = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < NWC; ++w) t += red[w];
-    return t;
-}
-
 __device__ __forceinline__ void softmax_update(float s, float v0, float v1, float& m, float& l, float& o0,
                                                float& o1) {
     const float mn = fmaxf(m, s);
@@ -220,33 +207,21 @@ __device__ __forceinline__ void softmax_update(float s, float v0, float v1, floa
     m = mn;
 }
 
-// Start the asynchronous copy of layer l's vectors (this CTA's slices) into vb.
-__device__ __forceinline__ void fetch_layer_vectors(const MkParams& p, const MkLayer& lw, int h, int rank,
-                                                    float* vb) {
+// Bulk copies of layer l's vectors (this CTA's slices) into vb, completing on `bar`; one thread.
+__device__ __forceinline__ void fetch_layer_vectors(const MkParams& p, const MkLayer& lw, int h, int rank, float* vb,
+                                                    uint64_t* bar) {
     const int d = p.d, dsl = d / MK_CS;
     const VecLayout V(d);
-    for (int c = threadIdx.x * 4; c < d; c += NCT * 4) {
-        cp_async16(vb + V.ln1g + c, lw.ln1_g + c);
-        cp_async16(vb + V.ln1b + c, lw.ln1_b + c);
-        cp_async16(vb + V.ln2g + c, lw.ln2_g + c);
-        cp_async16(vb + V.ln2b + c, lw.ln2_b + c);
-    }
-    // bias slices: 6 + dsl/4 + 8 + dsl/4 chunks, one per thread (dsl <= 4 * (NCT - 14) / 2)
-    const int t = threadIdx.x, nb = dsl / 4;
-    if (t < 6) {
-        const int sel = t >> 1, c = (t & 1) * 4;
-        cp_async16(vb + V.bqkv + sel * 8 + c, lw.b_qkv + sel * d + h * HD + rank * 8 + c);
-    } else if (t < 6 + nb) {
-        const int c = (t - 6) * 4;
-        cp_async16(vb + V.bproj + c, lw.b_proj + rank * dsl + c);
-    } else if (t < 14 + nb) {
-        const int c = (t - 6 - nb) * 4;
-        cp_async16(vb + V.bfc + c, lw.b_fc + (h * MK_CS + rank) * 32 + c);
-    } else if (t < 14 + 2 * nb) {
-        const int c = (t - 14 - nb) * 4;
-        cp_async16(vb + V.bmproj + c, lw.b_mproj + rank * dsl + c);
-    }
-    cp_async_commit();
+    const uint32_t dv = (uint32_t)d * 4;
+    tc::mbar_arrive_expect_tx(bar, 4 * dv + 3 * 32 + 2 * (uint32_t)dsl * 4 + 128);
+    bulk_g2s(vb + V.ln1g, lw.ln1_g, dv, bar);
+    bulk_g2s(vb + V.ln1b, lw.ln1_b, dv, bar);
+    bulk_g2s(vb + V.ln2g, lw.ln2_g, dv, bar);
+    bulk_g2s(vb + V.ln2b, lw.ln2_b, dv, bar);
+    for (int sel = 0; sel < 3; ++sel) bulk_g2s(vb + V.bqkv + sel * 8, lw.b_qkv + sel * d + h * HD + rank * 8, 32, bar);
+    bulk_g2s(vb + V.bproj, lw.b_proj + rank * dsl, (uint32_t)dsl * 4, bar);
+    bulk_g2s(vb + V.bfc, lw.b_fc + (h * MK_CS + rank) * 32, 128, bar);
+    bulk_g2s(vb + V.bmproj, lw.b_mproj + rank * dsl, (uint32_t)dsl * 4, bar);
 }
 
 // Warm L2 with this CTA's block of cached K/V rows (positions < pos) of layer l.
@@ -280,13 +255,14 @@ __device__ __forceinline__ void wait_rx(uint64_t* bar, uint32_t parity, const Mk
     raise_error(p, 5);
 }
 
-// y = LN(x) * g + b over d features (population variance, two passes: gpt2.rs:178-185), g and
-// b in shared memory. x is read from `x`; with `xcopy` it is also stored there. Each thread
-// holds columns tid + 256 k, k < 4.
+// y = LN(x) * g + b over d features with the population variance (gpt2.rs:178-185), g and b
+// in shared memory; mean and E[x^2] come from one block reduction (var = E[x^2] - mean^2).
+// x is read from `x`; with `xcopy` it is also stored there. Each thread holds columns
+// tid + 256 k, k < 4.
 __device__ __forceinline__ void layernorm(const float* x, float* xcopy, float* y, const float* g, const float* b,
                                           int d, float eps, float* red) {
     float xv[4];
-    float s = 0.f;
+    float s = 0.f, q = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int c = threadIdx.x + k * NCT;
@@ -295,19 +271,28 @@ __device__ __forceinline__ void layernorm(const float* x, float* xcopy, float* y
             xv[k] = x[c];
             if (xcopy) xcopy[c] = xv[k];
             s += xv[k];
+            q = fmaf(xv[k], xv[k], q);
         }
     }
-    const float mean = block_sum(s, red) / (float)d;
-    float q = 0.f;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int c = threadIdx.x + k * NCT;
-        if (c < d) {
-            const float t = xv[k] - mean;
-            q += t * t;
-        }
+    for (int o = 16; o; o >>= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+        q += __shfl_xor_sync(0xffffffffu, q, o);
     }
-    const float var = block_sum(q, red + NWC) / (float)d;
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        red[2 * warp] = s;
+        red[2 * warp + 1] = q;
+    }
+    __syncthreads();
+    float ts = 0.f, tq = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWC; ++w) {
+        ts += red[2 * w];
+        tq += red[2 * w + 1];
+    }
+    const float mean = ts / (float)d;
+    const float var = fmaxf(tq / (float)d - mean * mean, 0.f);
     const float rstd = __frcp_rn(sqrtf(var + eps));
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -368,7 +353,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
     float* red = fs + 32;                  // [16]
     float* kst = red + 16;                 // [2][KV_STAGE][64]: this CTA's cached K | V rows
     uint64_t* kvbar = reinterpret_cast<uint64_t*>(kst + 2 * KV_STAGE * HD);
-    unsigned long long* bw = reinterpret_cast<unsigned long long*>(kvbar + 1);  // [8]
+    uint64_t* vbar = kvbar + 1;  // [2]: per-layer vectors, one per buffer
+    unsigned long long* bw = reinterpret_cast<unsigned long long*>(vbar + 2);  // [8]
     MkLayer* lws = reinterpret_cast<MkLayer*>(bw + 8);                         // [n_layer]
     const uint32_t rx_bytes[RX_N] = {(uint32_t)(MK_CS * 24 * 4), (uint32_t)(MK_CS * APP * 4), (uint32_t)(d * 4),
                                      (uint32_t)(d * 4), (uint32_t)(d * 4)};
@@ -419,6 +405,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
         for (int i = 0; i < NSLOT; ++i) tc::mbar_init(&full[i], 1);
         for (int i = 0; i < RX_N; ++i) tc::mbar_init(&rx[i], 1);
         tc::mbar_init(kvbar, 1);
+        tc::mbar_init(&vbar[0], 1);
+        tc::mbar_init(&vbar[1], 1);
         tc::fence_mbar_init();
         for (int i = 0; i < RX_N; ++i)
             if (n_layers_total > 0) tc::mbar_arrive_expect_tx(&rx[i], rx_bytes[i]);
@@ -430,7 +418,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
     }
     for (int l = tid; l < L; l += NCT) lws[l] = p.layers[l];
     __syncthreads();
-    fetch_layer_vectors(p, lws[0], h, rank, vbuf);
+    if (tid == 32) fetch_layer_vectors(p, lws[0], h, rank, vbuf, &vbar[0]);
+    cp_async_wait_all();  // ln_f vectors
     tc::cluster_sync();  // every CTA's receive barriers are armed before the first send
 
     // optional phase stamps: step 0, layer 1 in detail, layer ends, head
@@ -471,8 +460,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
         for (int l = 0; l < L; ++l, ++gl) {
             tlayer = l;
             float* vb = vbuf + (gl & 1) * VL.total;
-            cp_async_wait_all();
-            __syncthreads();  // this layer's vectors have landed; x (local) is complete
+            wait_rx(&vbar[gl & 1], (uint32_t)((gl >> 1) & 1), p);  // this layer's vectors
+            __syncthreads();  // x (local) is complete
             MK_TRL(29);
             float* kcache = p.kv + (size_t)slot * p.kv_slot + (size_t)l * p.kv_layer + (size_t)h * p.kv_head;
             float* vcache = kcache + p.kv_sel;
@@ -485,7 +474,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
             if (tid == 0) {
                 if (staged) {
                     const uint32_t bytes = (uint32_t)((t1c - t0) * HD * 4);
-                    asm volatile("fence.proxy.async;" ::: "memory");  // rows written by peers, read by TMA
                     tc::mbar_arrive_expect_tx(kvbar, 2 * bytes);
                     bulk_g2s(kst, kcache + (size_t)t0 * HD, bytes, kvbar);
                     bulk_g2s(kst + KV_STAGE * HD, vcache + (size_t)t0 * HD, bytes, kvbar);
@@ -497,10 +485,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
             {
                 // next layer's vectors (the other buffer is free)
                 const int nl = (l + 1 < L) ? l + 1 : 0;
-                const unsigned long long tB = tA ? globaltimer() : 0;
-                if (l + 1 < L || step + 1 < p.steps)
-                    fetch_layer_vectors(p, lws[nl], h, rank, vbuf + ((gl + 1) & 1) * VL.total);
-                if (tB) trace[34] = globaltimer() - tB;
+                if (tid == 32 && (l + 1 < L || step + 1 < p.steps))
+                    fetch_layer_vectors(p, lws[nl], h, rank, vbuf + ((gl + 1) & 1) * VL.total, &vbar[(gl + 1) & 1]);
             }
             MK_TRL(30);
             // ---- LN1 (residual from the previous layer's exchange, or the embedding) ----
@@ -877,8 +863,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
             }
         }
         tok = next;
-        // once per step: this step's K/V rows (plain stores) are released to the cluster
+        // once per step: this step's K/V rows (plain stores) are released to the cluster, and
+        // ordered before the bulk copies that stage them in later steps
         tc::cluster_sync();
+        if (tid == 0) asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     if (g == 0 && tid == 0) *p.epoch = epoch0 + (uint32_t)p.steps;
 #undef MK_TRL
@@ -886,7 +874,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
     // every bulk copy issued has been consumed unless the launch aborted; wait for stragglers
     if (tid == 0)
         for (int i = max(0, total - NSLOT); i < total; ++i) drain_wait(&full[i % NSLOT], (uint32_t)((i / NSLOT) & 1), p);
-    cp_async_wait_all();
     tc::cluster_sync();  // no CTA leaves while a peer may still touch its shared memory
 }
 
@@ -912,7 +899,7 @@ size_t smem_bytes(int d, int seg, int n_layer) {
     const int dsl = d / MK_CS;
     const size_t floats = (size_t)4 * d + 2 * V.total + MK_CS * 24 + MK_CS * APP + 3 * d + 32 + APP + dsl + d +
                           NWC * APS + HD + 32 + 16 + 2 * KV_STAGE * HD;
-    return (size_t)NSLOT * seg + 128 + floats * 4 + 8 + 8 * 8 + sizeof(MkLayer) * n_layer;
+    return (size_t)NSLOT * seg + 128 + floats * 4 + 3 * 8 + 8 * 8 + sizeof(MkLayer) * n_layer;
 }
 
 }  // namespace
