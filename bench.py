@@ -637,6 +637,8 @@ def main():
         with open(tfile) as f:
             tj = json.load(f)
         traffic = tj.get(args.config, {}).get(name)
+        if persistent and tj.get(args.config, {}).get("k_decode_persistent_per_step"):
+            traffic = tj[args.config]["k_decode_persistent_per_step"] * round(1 / rec["per_step"])
     step_bytes = statistics.mean(algorithmic_step_bytes(pk, p) for p in positions_timed)
 
     line = {
