@@ -1,0 +1,320 @@
+// Causal prefill attention on the tensor cores (tcgen05 / TMEM), one CTA per
+// (128-query tile, head).
+//
+// Per key block of 128 positions:
+//   S  = (Q * 2^-3) K^T          tcgen05.mma kind::f16, M = 128 queries, N = 128 keys, K = 64
+//   P  = exp(S - m_new)          one thread per query row (TMEM lane), online softmax in fp32
+//   PV = P V                     tcgen05.mma, M = 128, N = 64 (head dim), K = 128 keys
+//   O  = O * exp(m_old - m_new) + PV   (O in registers)
+// Both products use the fp16x3 split of gemm.cu: every fp32 operand x is held as
+// x_hi + x_lo (fp16 pair, ~22 bits) and A_hi B_hi + A_hi B_lo + A_lo B_hi accumulate in fp32
+// TMEM, so scores and outputs keep fp32-class accuracy (the dropped lo*lo term is ~2^-22
+// relative). The pair only keeps 22 bits while lo is a normal fp16, so every operand is first
+// scaled by a power of two that brings its largest magnitude to [2^13, 2^14): Q per query row,
+// K and V per key block, P by 2^14. The scales are undone exactly on S and PV, together with
+// the attention scale 1/sqrt(64) = 2^-3.
+//
+// Operands are K-major tiles with the 128-byte swizzle (rows of 64 fp16; 8-row groups 1024
+// bytes apart), as in gemm.cu: Q [128 q][64], K [128 keys][64], P [128 q][128 keys] as two
+// 64-key chunks, and V^T [64 dims][128 keys] as two 64-key chunks (V is transposed while it
+// is converted). Reference semantics: gpt2.rs:261-291 (softmax(q.K^T / sqrt(hd)) . V over
+// positions 0..t), per query position t of the prompt.
+#include <cuda_fp16.h>
+
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace gpt2q {
+namespace {
+
+constexpr int QT = 128;  // queries per CTA (TMEM lanes)
+constexpr int KB = 128;  // keys per block
+constexpr int HD = 64;
+constexpr int THREADS = 128;
+constexpr int TILE_Q = QT * 128;        // bytes of one [128][64] fp16 tile
+constexpr int TILE_VT = HD * 128;       // bytes of one [64][64] fp16 tile
+constexpr int OFF_QH = 0, OFF_QL = OFF_QH + TILE_Q;
+constexpr int OFF_KH = OFF_QL + TILE_Q, OFF_KL = OFF_KH + TILE_Q;
+constexpr int OFF_VH = OFF_KL + TILE_Q, OFF_VL = OFF_VH + 2 * TILE_VT;  // two 64-key chunks each
+constexpr int OFF_PH = OFF_VL + 2 * TILE_VT, OFF_PL = OFF_PH + 2 * TILE_Q;
+constexpr int OFF_BAR = OFF_PL + 2 * TILE_Q;
+constexpr int SMEM = OFF_BAR + 64 + 1024;  // barriers, TMEM slot, block-max scratch, alignment slack
+static_assert(SMEM <= 232448, "shared memory per CTA");
+constexpr uint32_t TMEM_COLS = 256;  // S: columns 0..127, PV: 128..191
+
+// Byte offset of 16-byte chunk c (8 fp16) of row r in a 128-byte-swizzled K-major tile.
+__device__ __forceinline__ uint32_t sw_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
+// Row r of a [rows][64] tile from 64 fp32 values (times `mul`, a power of two): hi and lo.
+__device__ __forceinline__ void put_row64(uint8_t* hi, uint8_t* lo, int r, const float* v, float mul) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half h0, l0, h1, l1;
+            split_hl(v[8 * c + 2 * j] * mul, h0, l0);
+            split_hl(v[8 * c + 2 * j + 1] * mul, h1, l1);
+            h[j] = pack_h2(h0, h1);
+            l[j] = pack_h2(l0, l1);
+        }
+        const uint32_t o = sw_off(r, c);
+        *reinterpret_cast<uint4*>(hi + o) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(lo + o) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+// 2^e as a float, e in [-126, 127].
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+
+// Exponent e with m * 2^e in [2^13, 2^14) for m > 0 (0 for m == 0 or subnormal), in [-60, 60].
+__device__ __forceinline__ int scale_exp(float m) {
+    const int b = (__float_as_int(m) >> 23) & 0xff;
+    if (b == 0) return 0;
+    return max(-60, min(60, 13 - (b - 127)));
+}
+
+__device__ __forceinline__ float row_absmax(const float* v) {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) m = fmaxf(m, fabsf(v[i]));
+    return m;
+}
+
+// Maximum over the 128 threads of the CTA (red: 4 floats of shared memory).
+__device__ __forceinline__ float block_max(float m, float* red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    const float r = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();  // red is reused by the next call
+    return r;
+}
+
+__device__ __forceinline__ void load_row64(const float* src, bool ok, float* v) {
+#pragma unroll
+    for (int i = 0; i < 64; i += 4) {
+        // coherent loads: q and K/V come from the preceding kernel, and a non-coherent (__ldg)
+        // load could be scheduled above griddepcontrol.wait
+        float4 x = ok ? __ldcg(reinterpret_cast<const float4*>(src + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[i] = x.x;
+        v[i + 1] = x.y;
+        v[i + 2] = x.z;
+        v[i + 3] = x.w;
+    }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    k_attn_prefill_tc(const float* q, int ldq, KVGeom g, size_t layer_off,
+                      const AttnTile* __restrict__ tiles, float* __restrict__ out, __half* __restrict__ ohi,
+                      __half* __restrict__ olo, int ldo, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw_[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
+    uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* bar_pv = bar_s + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
+    float* red = reinterpret_cast<float*>(bar_s + 4);  // [4]
+    const int tid = threadIdx.x, warp = tid >> 5;
+
+    if (tid == 0) {
+        tc::mbar_init(bar_s, 1);
+        tc::mbar_init(bar_pv, 1);
+        tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    tc::pdl_trigger();  // after the TMEM allocation: dependents never hold columns this CTA waits for
+    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lanes
+
+    tc::pdl_wait();  // q and the K/V rows were written by the preceding kernels
+    const AttnTile tile = tiles[blockIdx.y];
+    const int head = blockIdx.x;
+    const float* Kc = g.base + (size_t)tile.slot * g.slot_stride + layer_off + (size_t)head * g.head_stride;
+    const float* Vc = Kc + g.sel_stride;
+    const int qpos = tile.q0 + tid;  // this thread's query position (TMEM lane tid)
+    const bool qvalid = qpos < tile.T;
+
+    // ---- Q tile, row scaled by 2^eq ----
+    int eq;
+    {
+        float v[64];
+        load_row64(q + (size_t)(tile.row0 + (qvalid ? qpos : 0)) * ldq + head * HD, qvalid, v);
+        eq = scale_exp(row_absmax(v));
+        put_row64(smem + OFF_QH, smem + OFF_QL, tid, v, pow2f(eq));
+    }
+
+    constexpr uint32_t idesc_s = tc::idesc_f16_f32(QT, KB);
+    constexpr uint32_t idesc_pv = tc::idesc_f16_f32(QT, HD);
+    float o[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    const int kend = min(tile.T, tile.q0 + QT);  // keys past the last query of the tile are masked
+    const int nkb = (kend + KB - 1) / KB;
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+        const int k0 = kb * KB;
+        // ---- K tile and V^T tile (keys k0 + tid), each scaled by 2^ek / 2^ev of the block ----
+        int ek, ev;
+        {
+            const int kp = k0 + tid;
+            const bool kvalid = kp < tile.T;
+            float v[64];
+            load_row64(Kc + (size_t)(kvalid ? kp : 0) * HD, kvalid, v);
+            ek = scale_exp(block_max(row_absmax(v), red));
+            put_row64(smem + OFF_KH, smem + OFF_KL, tid, v, pow2f(ek));
+            load_row64(Vc + (size_t)(kvalid ? kp : 0) * HD, kvalid, v);
+            ev = scale_exp(block_max(row_absmax(v), red));
+            const float sv = pow2f(ev);
+            // V^T chunk tid / 64, column tid % 64: element (dim d, key) -> row d
+            uint8_t* vh = smem + OFF_VH + (tid >> 6) * TILE_VT;
+            uint8_t* vl = smem + OFF_VL + (tid >> 6) * TILE_VT;
+            const int col = tid & 63;
+#pragma unroll
+            for (int dd = 0; dd < 64; ++dd) {
+                __half h, lo;
+                split_hl(v[dd] * sv, h, lo);
+                const uint32_t off = sw_off(dd, col >> 3) + (uint32_t)((col & 7) * 2);
+                *reinterpret_cast<__half*>(vh + off) = h;
+                *reinterpret_cast<__half*>(vl + off) = lo;
+            }
+        }
+        tc::fence_proxy_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        // ---- S = Q K^T ----
+        if (tid == 0) {
+            tc::tc_fence_after();
+            const uint32_t qh = tc::smem_u32(smem + OFF_QH), ql = tc::smem_u32(smem + OFF_QL);
+            const uint32_t kh = tc::smem_u32(smem + OFF_KH), kl = tc::smem_u32(smem + OFF_KL);
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                const uint32_t ko = ks * 32;
+                tc::mma_f16(tmem, tc::desc_sw128(qh + ko), tc::desc_sw128(kh + ko), idesc_s, ks > 0 ? 1u : 0u);
+                tc::mma_f16(tmem, tc::desc_sw128(qh + ko), tc::desc_sw128(kl + ko), idesc_s, 1u);
+                tc::mma_f16(tmem, tc::desc_sw128(ql + ko), tc::desc_sw128(kh + ko), idesc_s, 1u);
+            }
+            tc::mma_commit(bar_s);
+        }
+        ok = tc::mbar_wait(bar_s, (uint32_t)(kb & 1), err) && ok;
+        tc::tc_fence_after();
+        // ---- online softmax of this thread's query row ----
+        float s[KB];
+#pragma unroll
+        for (int c = 0; c < KB; c += 32) tc::tmem_ld32(t_lane + c, s + c);
+        const float s_unscale = pow2f(-(eq + ek) - 3);  // operand scales and 1/sqrt(64)
+        float bmax = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < KB; ++j) {
+            const int kp = k0 + j;
+            s[j] = (kp > qpos || kp >= tile.T) ? -INFINITY : s[j] * s_unscale;
+            bmax = fmaxf(bmax, s[j]);
+        }
+        const float mnew = fmaxf(m, bmax);
+        const float alpha = (mnew == -INFINITY) ? 1.f : expf(m - mnew);
+        float psum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys; chunk c lives in P chunk c / 8
+            uint32_t h[4], lo[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p0 = (mnew == -INFINITY) ? 0.f : expf(s[8 * c + 2 * j] - mnew);
+                const float p1 = (mnew == -INFINITY) ? 0.f : expf(s[8 * c + 2 * j + 1] - mnew);
+                psum += p0 + p1;
+                __half h0, l0, h1, l1;
+                split_hl(p0 * 16384.0f, h0, l0);  // P * 2^14
+                split_hl(p1 * 16384.0f, h1, l1);
+                h[j] = pack_h2(h0, h1);
+                lo[j] = pack_h2(l0, l1);
+            }
+            const uint32_t off = (uint32_t)((c >> 3) * TILE_Q) + sw_off(tid, c & 7);
+            *reinterpret_cast<uint4*>(smem + OFF_PH + off) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4*>(smem + OFF_PL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        l = l * alpha + psum;
+        m = mnew;
+        tc::fence_proxy_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        // ---- PV = P V (columns 128..191) ----
+        if (tid == 0) {
+            tc::tc_fence_after();
+            const uint32_t ph = tc::smem_u32(smem + OFF_PH), pl = tc::smem_u32(smem + OFF_PL);
+            const uint32_t vh = tc::smem_u32(smem + OFF_VH), vl = tc::smem_u32(smem + OFF_VL);
+#pragma unroll
+            for (int ks = 0; ks < KB / 16; ++ks) {
+                const uint32_t ao = (uint32_t)((ks >> 2) * TILE_Q + (ks & 3) * 32);
+                const uint32_t bo = (uint32_t)((ks >> 2) * TILE_VT + (ks & 3) * 32);
+                tc::mma_f16(tmem + 128, tc::desc_sw128(ph + ao), tc::desc_sw128(vh + bo), idesc_pv, ks > 0 ? 1u : 0u);
+                tc::mma_f16(tmem + 128, tc::desc_sw128(ph + ao), tc::desc_sw128(vl + bo), idesc_pv, 1u);
+                tc::mma_f16(tmem + 128, tc::desc_sw128(pl + ao), tc::desc_sw128(vh + bo), idesc_pv, 1u);
+            }
+            tc::mma_commit(bar_pv);
+        }
+        ok = tc::mbar_wait(bar_pv, (uint32_t)(kb & 1), err) && ok;
+        tc::tc_fence_after();
+        float pv[HD];
+        tc::tmem_ld32(t_lane + 128, pv);
+        tc::tmem_ld32(t_lane + 160, pv + 32);
+        const float pv_unscale = pow2f(-14 - ev);
+#pragma unroll
+        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha, pv[i] * pv_unscale);
+        if (!ok) break;
+    }
+    // ---- out = O / l (fp32 and the fp16 hi/lo copy for the c_proj GEMM) ----
+    if (qvalid && ok) {
+        const size_t base = (size_t)(tile.row0 + qpos) * ldo + head * HD;
+        const float inv = 1.0f / l;
+#pragma unroll
+        for (int i = 0; i < HD; i += 4) {
+            float r[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) r[j] = o[i + j] * inv;
+            *reinterpret_cast<float4*>(out + base + i) = make_float4(r[0], r[1], r[2], r[3]);
+            if (ohi) {
+                __half h[4], lo[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) split_hl(r[j], h[j], lo[j]);
+                *reinterpret_cast<uint2*>(ohi + base + i) = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
+                *reinterpret_cast<uint2*>(olo + base + i) = make_uint2(pack_h2(lo[0], lo[1]), pack_h2(lo[2], lo[3]));
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace
+
+cudaError_t launch_attn_prefill_tc(const float* q, int ldq, const KVGeom& g, size_t layer_off, const AttnTile* tiles,
+                                   int n_tiles, float* out, __half* ohi, __half* olo, int ldo, int n_head, int* err,
+                                   cudaStream_t st) {
+    if (n_tiles <= 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_head, n_tiles);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_attn_prefill_tc, q, ldq, g, layer_off, tiles, out, ohi, olo, ldo, err);
+}
+
+}  // namespace gpt2q

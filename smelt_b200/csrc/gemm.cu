@@ -30,10 +30,13 @@
 // Programmatic dependent launch: weight loads and their conversion start before the
 // previous kernel has finished; activations are only touched after griddepcontrol.wait.
 // All mbarrier waits are bounded (tcgen05.cuh); a timeout sets the error word.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdio>
+#include <string>
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
@@ -50,30 +53,47 @@ namespace {
 constexpr int BM = 128, BK = 64, THREADS = 224;
 constexpr int MAX_SPLITS = 8;  // portable cluster size
 
-template <int BN, bool PRESPLIT>
+template <int BN, bool PRESPLIT, bool DEEP>
 struct Cfg {
-    // decode tiles (BN <= 64) use ~105 KB so two CTAs share an SM
-    // operand stages: decode tiles (BN <= 64) keep two CTAs per SM so consecutive linears
-    // overlap under programmatic dependent launch
-    static constexpr int OS = 2;
-    static constexpr int RAW_STAGES = BN == 128 ? 4 : 2;  // raw int8/int4 weight tiles in flight
+    // DEEP (decode tiles, small grids): one CTA per SM that, launched early under
+    // programmatic dependent launch, streams and dequantises as much of its split-K slice as
+    // shared memory holds while it waits for its activations, so mostly MMAs remain once X
+    // arrives. Otherwise two CTAs share an SM (BN <= 64) and the rings are short.
+    static constexpr int OS = DEEP ? (BN == 32 ? 5 : 4) : 2;  // weight operand (fp16 hi/lo) stages
+    // activation (X hi/lo) stages, a ring of their own: a CTA requests several X k-blocks at
+    // once when its inputs become ready, instead of one L2 round trip per k-block
+    static constexpr int XS = DEEP ? 4 : 2;
+    static constexpr int RAW_STAGES = DEEP ? 3 : (BN == 128 ? 4 : 2);  // raw int8/int4 tiles in flight
+    // BN <= 64: X_hi and X_lo tiles are adjacent, so one MMA with N = 2 BN multiplies a weight
+    // half by both; A_hi and A_lo each accumulate into their own TMEM block of 2 BN columns.
+    static constexpr bool DUAL = BN <= 64;
+    static constexpr int TMEM_COLS = DUAL ? 4 * BN : BN;
+    static constexpr int PS = BN + 4;  // split-K partial tile [128 rows][PS] fp32 (padded rows)
+    // Decode tiles exchange split-K partials by pushing them (bulk copies into the peers'
+    // shared memory); rank r receives the block of CW token columns it reduces. One area of
+    // [splits][128][CW] fp32 (splits * CW <= BN + 32) receives, another one sends.
+    static constexpr bool PUSH = BN <= 64;
+    static constexpr int XCH_FLOATS = 128 * (BN + 32);
     static constexpr int A_BYTES = BM * 128;                          // one of hi/lo
     static constexpr int B_BYTES = BN * 128;                          // one of hi/lo
     static constexpr int RAW_BYTES = PRESPLIT ? 0 : BM * 64;          // int8 tile (int4 uses half)
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + OS * 2 * A_BYTES;
-    static constexpr int OFF_RAW = OFF_B + OS * 2 * B_BYTES;
+    static constexpr int OFF_RAW = OFF_B + XS * 2 * B_BYTES;
     // decode: the CTA's group scales, one padded row per weight row (conflict-free)
     static constexpr int SC_KB = 8;                  // k-blocks of scales staged at a time
     static constexpr int SC_STRIDE = 2 * SC_KB + 1;  // floats per row
     static constexpr int OFF_SC = OFF_RAW + RAW_STAGES * RAW_BYTES;
     static constexpr int SC_BYTES = PRESPLIT ? 0 : BM * SC_STRIDE * 4;
     static constexpr int OFF_BAR = OFF_SC + SC_BYTES;
-    static constexpr int N_BAR = 2 * RAW_STAGES + 2 * OS + 1;
+    static constexpr int N_BAR = 2 * RAW_STAGES + 2 * OS + 2 * XS + 2;
     static constexpr int SMEM = OFF_BAR + N_BAR * 8 + 16 + 1024;  // + tmem slot, flag, alignment slack
     static_assert(SMEM <= 232448, "shared memory per CTA");
-    // the split-K partial tile [BN][128] fp32 reuses the operand rings once every MMA is done
-    static_assert(BN * BM * 4 <= OFF_RAW, "partial tile must fit in the operand rings");
+    // shallow decode tiles that fit twice in an SM's shared memory share it
+    static constexpr int MIN_BLOCKS = (!DEEP && BN <= 64 && SMEM <= 232448 / 2 - 1024) ? 2 : 1;
+    // the split-K partial tile reuses the operand rings once every MMA is done
+    static_assert(PS * BM * 4 <= OFF_RAW, "partial tile must fit in the operand rings");
+    static_assert(!PUSH || 2 * XCH_FLOATS * 4 <= OFF_RAW, "exchange areas must fit in the operand rings");
 };
 
 struct TcParams {
@@ -83,7 +103,19 @@ struct TcParams {
     float pre;   // 2^P
     Epi epi;
     int* err;
+    unsigned long long* trace;  // optional [grid][TC_TRACE] globaltimer stamps (one traced launch)
 };
+
+constexpr int TC_TRACE = 16;
+
+__device__ __forceinline__ void tc_stamp(const TcParams& p, int k) {
+    if (p.trace) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        const size_t cta = blockIdx.x + (size_t)gridDim.x * (blockIdx.y + (size_t)gridDim.y * blockIdx.z);
+        p.trace[cta * TC_TRACE + k] = t;
+    }
+}
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, const uint4& v) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
@@ -170,10 +202,11 @@ __device__ __forceinline__ void put32_q4(uint32_t a_hi, uint32_t a_lo, int r, in
 // the operation order per element is that of epi_apply.
 template <int NJ>
 __device__ __forceinline__ void epi_chunk(const Epi& e, int nn, bool row_ok, const float (&acc)[NJ], int mbase,
-                                          int mstep, int mend, float post) {
+                                          int mstep, int mend, float post, const float* resid_pre = nullptr,
+                                          const float* bias_pre = nullptr) {
     const int lane = threadIdx.x & 31;
     const bool has_b = e.bias != nullptr;
-    const float b = (has_b && row_ok) ? __ldg(e.bias + nn) : 0.f;
+    const float b = bias_pre ? *bias_pre : ((has_b && row_ok) ? __ldg(e.bias + nn) : 0.f);
     bool ok[NJ];
 #pragma unroll
     for (int j = 0; j < NJ; ++j) ok[j] = row_ok && (mbase + j * mstep < mend);
@@ -190,7 +223,8 @@ __device__ __forceinline__ void epi_chunk(const Epi& e, int nn, bool row_ok, con
         case EPI_RESID: {
             float r[NJ];
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) r[j] = ok[j] ? e.out[(size_t)(mbase + j * mstep) * e.ldo + nn] : 0.f;
+            for (int j = 0; j < NJ; ++j)
+                r[j] = resid_pre ? resid_pre[j] : (ok[j] ? e.out[(size_t)(mbase + j * mstep) * e.ldo + nn] : 0.f);
 #pragma unroll
             for (int j = 0; j < NJ; ++j)
                 if (ok[j]) e.out[(size_t)(mbase + j * mstep) * e.ldo + nn] = r[j] + (acc[j] * post + b);
@@ -245,12 +279,12 @@ __device__ __forceinline__ void epi_chunk(const Epi& e, int nn, bool row_ok, con
     }
 }
 
-template <int ATOM, int BN, bool PRESPLIT>
-__global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
+template <int ATOM, int BN, bool PRESPLIT, bool DEEP>
+__global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS))
     k_linear_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wlo,
                 const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
                 TcParams p) {
-    using C = Cfg<BN, PRESPLIT>;
+    using C = Cfg<BN, PRESPLIT, DEEP>;
     extern __shared__ __align__(1024) uint8_t smem_raw_[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -258,7 +292,10 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
     uint64_t* raw_empty = bars + C::RAW_STAGES;
     uint64_t* op_full = bars + 2 * C::RAW_STAGES;
     uint64_t* op_empty = op_full + C::OS;
-    uint64_t* acc_full = op_empty + C::OS;
+    uint64_t* x_full = op_empty + C::OS;
+    uint64_t* x_empty = x_full + C::XS;
+    uint64_t* acc_full = x_empty + C::XS;
+    uint64_t* recv_full = acc_full + 1;  // split-K peers' partials have landed
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + C::N_BAR * 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -269,28 +306,50 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
     const int nkb = min(p.kb_per_split, p.nkb_total - kb0);
     constexpr int RAW_TX = (ATOM == ATOM_Q8) ? BM * 64 : BM * 32;
 
-    tc::pdl_trigger();
+    if (threadIdx.x == 0) tc_stamp(p, 0);
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::RAW_STAGES; ++i) {
             tc::mbar_init(&raw_full[i], 1);
             tc::mbar_init(&raw_empty[i], 128);
         }
         for (int i = 0; i < C::OS; ++i) {
-            // decode: X producer (+tx) and 128 converter threads; prefill: both producers (+tx)
-            tc::mbar_init(&op_full[i], PRESPLIT ? 2 : 1 + 128);
+            // prefill: the weight producer (+tx); decode: the 128 converter threads
+            tc::mbar_init(&op_full[i], PRESPLIT ? 1 : 128);
             tc::mbar_init(&op_empty[i], 1);
         }
+        for (int i = 0; i < C::XS; ++i) {
+            tc::mbar_init(&x_full[i], 1);
+            tc::mbar_init(&x_empty[i], 1);
+        }
         tc::mbar_init(acc_full, 1);
+        tc::mbar_init(recv_full, 1);
+        if (C::PUSH && p.splits > 1) {
+            // this CTA reduces token columns [rank CW, rank CW + CW) of the tile: every other split
+            // sends it one [128][CW] fp32 block
+            const int rank = (int)tc::cluster_rank();
+            const int CW = ((BN + p.splits - 1) / p.splits + 3) & ~3;
+            if (min(BN, (rank + 1) * CW) > rank * CW)
+                tc::mbar_arrive_expect_tx(recv_full, (uint32_t)((p.splits - 1) * 128 * CW * 4));
+        }
         tc::fence_mbar_init();
     }
     if (warp == 0) {
-        tc::tmem_alloc(tmem_slot, BN);
+        tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // dependents may start only once this CTA holds its TMEM columns: a dependent CTA that
+    // took them first would wait for this grid while this grid waits for its columns
+    tc::pdl_trigger();
+    const bool push = C::PUSH && p.splits > 1;
+    // split-K exchange over three cluster-barrier phases: 0 = barriers initialised, 1 = every
+    // CTA's MMAs are done (its operand rings may be written) and its partials staged, 2 = all
+    // copies into every CTA have landed (none may exit before)
+    if (push) tc::cluster_arrive_relaxed();
+    if (threadIdx.x == 0) tc_stamp(p, 1);
 
     if (warp == 0) {
         // ---------------- weight tile producer (no dependency on earlier kernels) ----------------
@@ -307,13 +366,15 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
                     tc::tma_load_2d(a + C::A_BYTES, &tm_wlo, (kb0 + i) * BK, n0, &op_full[s]);
                 } else {
                     const int s = i % C::RAW_STAGES, use = i / C::RAW_STAGES;
-                    if (!tc::mbar_wait(&raw_empty[s], (use & 1) ^ 1, p.err)) break;
+                    if (!tc::mbar_wait_spin(&raw_empty[s], (use & 1) ^ 1, p.err)) break;
                     tc::mbar_arrive_expect_tx(&raw_full[s], RAW_TX);
                     const int kx = (kb0 + i) * (ATOM == ATOM_Q8 ? 64 : 32);
                     tc::tma_load_2d(smem + C::OFF_RAW + s * C::RAW_BYTES, &tm_w, kx, n0, &raw_full[s]);
                 }
+                if (i == 0) tc_stamp(p, 2);
                 issued = i + 1;
             }
+            tc_stamp(p, 3);
             // drain: every issued copy has landed before the CTA can exit
             if (PRESPLIT) {
                 for (int i = (issued > C::OS ? issued - C::OS : 0); i < issued; ++i)
@@ -329,44 +390,61 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
             tc::prefetch_tmap(&tm_xhi);
             tc::prefetch_tmap(&tm_xlo);
             tc::pdl_wait();  // X was written by the previous kernel
+            tc_stamp(p, 8);
             int issued = 0;
             for (int i = 0; i < nkb; ++i) {
-                const int s = i % C::OS, use = i / C::OS;
-                if (!tc::mbar_wait(&op_empty[s], (use & 1) ^ 1, p.err)) break;
-                tc::mbar_arrive_expect_tx(&op_full[s], 2 * C::B_BYTES);
+                const int s = i % C::XS, use = i / C::XS;
+                if (!tc::mbar_wait(&x_empty[s], (use & 1) ^ 1, p.err)) break;
+                tc::mbar_arrive_expect_tx(&x_full[s], 2 * C::B_BYTES);
                 const int kx = (kb0 + i) * BK;
                 uint8_t* b = smem + C::OFF_B + s * 2 * C::B_BYTES;
-                tc::tma_load_2d(b, &tm_xhi, kx, m0, &op_full[s]);
-                tc::tma_load_2d(b + C::B_BYTES, &tm_xlo, kx, m0, &op_full[s]);
+                tc::tma_load_2d(b, &tm_xhi, kx, m0, &x_full[s]);
+                tc::tma_load_2d(b + C::B_BYTES, &tm_xlo, kx, m0, &x_full[s]);
+                if (i == 0) tc_stamp(p, 9);
                 issued = i + 1;
             }
-            for (int i = (issued > C::OS ? issued - C::OS : 0); i < issued; ++i)
-                tc::mbar_wait(&op_full[i % C::OS], (i / C::OS) & 1, p.err);
+            for (int i = (issued > C::XS ? issued - C::XS : 0); i < issued; ++i)
+                tc::mbar_wait(&x_full[i % C::XS], (i / C::XS) & 1, p.err);
         }
     } else if (warp == 5) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_f16_f32(BM, BN);
+            constexpr uint32_t idesc = tc::idesc_f16_f32(BM, C::DUAL ? 2 * BN : BN);
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % C::OS, use = i / C::OS;
-                if (!tc::mbar_wait(&op_full[s], use & 1, p.err)) break;
+                const int xs = i % C::XS, xuse = i / C::XS;
+                if (!(PRESPLIT ? tc::mbar_wait(&op_full[s], use & 1, p.err)
+                               : tc::mbar_wait_spin(&op_full[s], use & 1, p.err)))
+                    break;
+                if (!tc::mbar_wait(&x_full[xs], xuse & 1, p.err)) break;
+                if (i == 0) tc_stamp(p, 6);
                 tc::tc_fence_after();
                 const uint32_t a_hi = tc::smem_u32(smem + C::OFF_A + s * 2 * C::A_BYTES);
                 const uint32_t a_lo = a_hi + C::A_BYTES;
-                const uint32_t b_hi = tc::smem_u32(smem + C::OFF_B + s * 2 * C::B_BYTES);
+                const uint32_t b_hi = tc::smem_u32(smem + C::OFF_B + xs * 2 * C::B_BYTES);
                 const uint32_t b_lo = b_hi + C::B_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk) {
                     const uint32_t ko = kk * 32;
                     const uint64_t dah = tc::desc_sw128(a_hi + ko), dal = tc::desc_sw128(a_lo + ko);
-                    const uint64_t dbh = tc::desc_sw128(b_hi + ko), dbl = tc::desc_sw128(b_lo + ko);
-                    tc::mma_f16(tmem, dah, dbh, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                    tc::mma_f16(tmem, dah, dbl, idesc, 1u);
-                    tc::mma_f16(tmem, dal, dbh, idesc, 1u);
+                    const uint64_t dbh = tc::desc_sw128(b_hi + ko);
+                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                    if constexpr (C::DUAL) {
+                        // [X_hi; X_lo] is one 2 BN-row operand: A_hi -> columns 0..2BN, A_lo -> 2BN..4BN
+                        tc::mma_f16(tmem, dah, dbh, idesc, acc);
+                        tc::mma_f16(tmem + 2 * BN, dal, dbh, idesc, acc);
+                    } else {
+                        const uint64_t dbl = tc::desc_sw128(b_lo + ko);
+                        tc::mma_f16(tmem, dah, dbh, idesc, acc);
+                        tc::mma_f16(tmem, dah, dbl, idesc, 1u);
+                        tc::mma_f16(tmem, dal, dbh, idesc, 1u);
+                    }
                 }
                 tc::mma_commit(&op_empty[s]);
+                tc::mma_commit(&x_empty[xs]);
             }
             tc::mma_commit(acc_full);
+            tc_stamp(p, 7);
             tc::mbar_wait(acc_full, 0, p.err);  // every MMA has completed before teardown
         }
     } else {
@@ -394,6 +472,7 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
                 ok = tc::mbar_wait(&raw_full[rs], ruse & 1, p.err) &&
                      tc::mbar_wait(&op_empty[os], (ouse & 1) ^ 1, p.err);
                 if (!ok) break;
+                if (i == 0 && t == 0) tc_stamp(p, 4);
                 const int jj = 2 * (i % C::SC_KB);
                 const __half2 s0 = __float2half2_rn(sc[jj]);
                 const __half2 s1 = __float2half2_rn(sc[jj + 1]);
@@ -420,67 +499,170 @@ __global__ void __launch_bounds__(THREADS, (BN <= 64 ? 2 : 1))
                 tc::mbar_arrive(&op_full[os]);
             }
         }
+        if (threadIdx.x == 32) tc_stamp(p, 5);
         // ---- epilogue part 1: TMEM -> (outputs | shared-memory partial) ----
+        // the bias is a weight: its load flies while the MMAs finish
+        const int n_epi = n0 + (warp & 3) * 32 + lane;
+        const float bias_v = (p.epi.bias && n_epi < p.w.rows) ? __ldg(p.epi.bias + n_epi) : 0.f;
         const bool acc_ok = tc::mbar_wait(acc_full, 0, p.err);
+        if (threadIdx.x == 32) tc_stamp(p, 10);
         tc::tc_fence_after();
         tc::pdl_wait();  // outputs / residual inputs belong to earlier kernels
+        if (threadIdx.x == 32) tc_stamp(p, 11);
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;  // TMEM lane owned by this thread
         const int nn = n0 + row;
         const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
-        float* part = reinterpret_cast<float*>(smem);  // [BN][128], operand rings are free now
+        float* part = reinterpret_cast<float*>(smem);  // [128][PS], operand rings are free now
         const int mend = min(p.M, m0 + BN);
+        // push exchange: rank r reduces token columns [r CW, r CW + CW) of the tile
+        const int rank = push ? (int)tc::cluster_rank() : 0;
+        const int CW = ((BN + p.splits - 1) / p.splits + 3) & ~3;
+        float* recv = reinterpret_cast<float*>(smem);  // [splits][128][CW]
+        float* send = recv + C::XCH_FLOATS;            // [splits][128][CW]
+        const int own_w = max(0, min(BN, (rank + 1) * CW) - rank * CW);
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
             float v[32];
-            tc::tmem_ld32(taddr + c0, v);
+            if constexpr (C::DUAL) {  // (A_hi X_hi + A_hi X_lo) + (A_lo X_hi + A_lo X_lo)
+                float t[32];
+                tc::tmem_ld32x2(taddr + c0, taddr + BN + c0, v, t);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += t[j];
+                float u[32];
+                tc::tmem_ld32x2(taddr + 2 * BN + c0, taddr + 3 * BN + c0, t, u);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += t[j] + u[j];
+            } else {
+                tc::tmem_ld32(taddr + c0, v);
+            }
             if (p.splits == 1) {
                 if (m0 + c0 >= mend) break;  // warp-uniform
-                epi_chunk<32>(p.epi, nn, acc_ok && nn < p.w.rows, v, m0 + c0, 1, mend, p.post);
+                epi_chunk<32>(p.epi, nn, acc_ok && nn < p.w.rows, v, m0 + c0, 1, mend, p.post, nullptr, &bias_v);
+            } else if (push) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const int c = c0 + j, r = c / CW, q = c - r * CW;
+                    float* dst = (r == rank ? recv : send) + ((size_t)r * 128 + row) * CW + q;
+                    *reinterpret_cast<float4*>(dst) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                }
             } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) part[(c0 + j) * BM + row] = v[j];
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(part + row * C::PS + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
+        }
+        if (push) {
+            tc::fence_proxy_async_smem();  // the partials are read by bulk copies
+            tc::named_bar_sync(1, 128);
+            if (threadIdx.x == 32) tc_stamp(p, 12);
+            // acc_full came first: this CTA's MMAs, and their shared-memory reads, are complete
+            tc::cluster_wait();            // phase 0
+            tc::cluster_arrive_relaxed();  // phase 1
+            tc::cluster_wait();
+            if (threadIdx.x == 32) {
+                for (int r = 0; r < p.splits; ++r) {
+                    if (r == rank || min(BN, (r + 1) * CW) <= r * CW) continue;
+                    tc::bulk_send((uint32_t)r, send + (size_t)r * 128 * CW, recv + (size_t)rank * 128 * CW,
+                                  (uint32_t)(128 * CW * 4), recv_full);
+                }
+                tc_stamp(p, 13);
+            }
+            __syncwarp();
+            const bool ok = acc_ok && (own_w == 0 || tc::mbar_wait_cluster(recv_full, 0, p.err));
+            if (threadIdx.x == 32) tc_stamp(p, 14);
+            __syncwarp();
+            tc::cluster_arrive_relaxed();  // phase 2: everything sent to this CTA has landed
+            // sum the splits in rank order, then the epilogue for this CTA's token columns
+            const bool resid = p.epi.kind == EPI_RESID;
+            for (int cb = 0; cb < own_w && m0 + rank * CW + cb < mend; cb += 4) {
+                const int m = m0 + rank * CW + cb;
+                float rp[4], acc[4] = {0.f, 0.f, 0.f, 0.f};
+                if (resid) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        rp[j] = (nn < p.w.rows && m + j < mend) ? p.epi.out[(size_t)(m + j) * p.epi.ldo + nn] : 0.f;
+                }
+#pragma unroll
+                for (int sp = 0; sp < MAX_SPLITS; ++sp) {
+                    if (sp < p.splits) {
+                        const float4 x = *reinterpret_cast<const float4*>(recv + ((size_t)sp * 128 + row) * CW + cb);
+                        acc[0] += x.x;
+                        acc[1] += x.y;
+                        acc[2] += x.z;
+                        acc[3] += x.w;
+                    }
+                }
+                epi_chunk<4>(p.epi, nn, ok && nn < p.w.rows, acc, m, 1, mend, p.post, resid ? rp : nullptr, &bias_v);
             }
         }
     }
+    if (push && (warp == 0 || warp >= 5)) {
+        __syncwarp();
+        tc::cluster_wait();            // phase 0
+        tc::cluster_arrive_relaxed();  // phase 1
+        tc::cluster_wait();
+        tc::cluster_arrive_relaxed();  // phase 2
+    }
     tc::tc_fence_before();
     __syncthreads();
-    if (p.splits > 1) {
+    if (!push && threadIdx.x == 32) tc_stamp(p, 12);
+    if (push) {
+        tc::cluster_wait();  // phase 2: no copy into or out of any CTA of the cluster is in flight
+    } else if (p.splits > 1) {
         // ---- epilogue part 2: cluster-wide split-K reduction over distributed shared memory ----
         tc::cluster_sync();  // every CTA's partial tile is in its shared memory
+        if (threadIdx.x == 32) tc_stamp(p, 13);
         if (warp >= 1 && warp <= 4) {
             const int row = (warp & 3) * 32 + lane;
             const int nn = n0 + row;
             const int rank = (int)tc::cluster_rank();
             const uint32_t local = tc::smem_u32(smem);
             const int mend = min(p.M, m0 + BN);
-            constexpr int RJ = 8;  // columns per batch: RJ * splits remote loads in flight
-            // this CTA reduces and writes columns rank, rank + splits, rank + 2 * splits, ...
-            for (int q0 = 0; m0 + rank + q0 * p.splits < mend; q0 += RJ) {
-                float acc[RJ];
-                uint32_t addr[RJ];
+            // rank r reduces and writes a contiguous block of CW columns (tokens): 16-byte
+            // remote loads, all splits of a batch in flight together, summed in rank order
+            const int CW = ((BN + p.splits - 1) / p.splits + 3) & ~3;
+            const int cend = min(BN, (rank + 1) * CW);
+            constexpr int RJ = 8;
+            for (int cb = rank * CW; cb < cend && m0 + cb < mend; cb += RJ) {
+                float acc[RJ], rp[RJ];
+                const bool resid = p.epi.kind == EPI_RESID;
+                if (resid) {  // residual loads in flight together with the remote partial loads
 #pragma unroll
-                for (int j = 0; j < RJ; ++j) {
-                    const int c = min(rank + (q0 + j) * p.splits, BN - 1);
-                    addr[j] = local + (uint32_t)((c * BM + row) * 4);
-                    acc[j] = 0.f;
+                    for (int j = 0; j < RJ; ++j) {
+                        const int m = m0 + cb + j;
+                        rp[j] = (nn < p.w.rows && m < mend && cb + j < cend) ? p.epi.out[(size_t)m * p.epi.ldo + nn] : 0.f;
+                    }
                 }
+#pragma unroll
+                for (int j = 0; j < RJ; ++j) acc[j] = 0.f;
+                const uint32_t a0 = local + (uint32_t)((row * C::PS + cb) * 4);
+                const bool second = cb + 4 < cend;  // columns cb+4..cb+7 belong to this block
 #pragma unroll
                 for (int sp = 0; sp < MAX_SPLITS; ++sp) {
                     if (sp < p.splits) {
-                        float t[RJ];
-#pragma unroll
-                        for (int j = 0; j < RJ; ++j) t[j] = tc::ld_cluster_f32(tc::map_cluster(addr[j], sp));
-#pragma unroll
-                        for (int j = 0; j < RJ; ++j) acc[j] += t[j];
+                        const float4 x = tc::ld_cluster_f32x4(tc::map_cluster(a0, sp));
+                        const float4 y = second ? tc::ld_cluster_f32x4(tc::map_cluster(a0 + 16, sp))
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                        acc[0] += x.x;
+                        acc[1] += x.y;
+                        acc[2] += x.z;
+                        acc[3] += x.w;
+                        acc[4] += y.x;
+                        acc[5] += y.y;
+                        acc[6] += y.z;
+                        acc[7] += y.w;
                     }
                 }
-                epi_chunk<RJ>(p.epi, nn, nn < p.w.rows, acc, m0 + rank + q0 * p.splits, p.splits, mend, p.post);
+                epi_chunk<RJ>(p.epi, nn, nn < p.w.rows, acc, m0 + cb, 1, min(mend, m0 + cend), p.post,
+                              resid ? rp : nullptr);
             }
         }
+        if (threadIdx.x == 32) tc_stamp(p, 14);
         tc::cluster_sync();  // no CTA leaves while its partial may still be read
     }
-    if (warp == 0) tc::tmem_dealloc(tmem, BN);
+    if (threadIdx.x == 0) tc_stamp(p, 15);
+    if (warp == 0) tc::tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 // One-time exact split of a quantised weight for the prefill path: w' = deq(w) * 2^P,
@@ -525,11 +707,11 @@ bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int ATOM, int BN, bool PRESPLIT>
+template <int ATOM, int BN, bool PRESPLIT, bool DEEP>
 cudaError_t launch_tc(const CUtensorMap& tw, const CUtensorMap& twlo, const CUtensorMap& txh, const CUtensorMap& txl,
                       const TcParams& tp, dim3 grid, cudaStream_t st) {
-    auto kern = k_linear_tc<ATOM, BN, PRESPLIT>;
-    const int smem = Cfg<BN, PRESPLIT>::SMEM;
+    auto kern = k_linear_tc<ATOM, BN, PRESPLIT, DEEP>;
+    const int smem = Cfg<BN, PRESPLIT, DEEP>::SMEM;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -556,14 +738,61 @@ cudaError_t launch_tc(const CUtensorMap& tw, const CUtensorMap& twlo, const CUte
     return cudaLaunchKernelEx(&cfg, kern, tw, twlo, txh, txl, tp);
 }
 
+// Clusters of `cs` CTAs of this kernel that the device holds at once (cached per size).
+template <int ATOM, int BN, bool PRESPLIT, bool DEEP>
+int resident_clusters(int cs) {
+    static std::atomic<int> cache[MAX_SPLITS + 1];
+    if (cs < 1 || cs > MAX_SPLITS) return 0;
+    int v = cache[cs].load(std::memory_order_relaxed);
+    if (v != 0) return v;
+    auto kern = k_linear_tc<ATOM, BN, PRESPLIT, DEEP>;
+    const int smem = Cfg<BN, PRESPLIT, DEEP>::SMEM;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1, 1, cs);
+        cfg.blockDim = dim3(THREADS, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = cs;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    v = n > 0 ? n : -1;
+    cache[cs].store(v, std::memory_order_relaxed);
+    return v;
+}
+
+// Decode tiles (BN <= 64) run the deep configuration (one CTA per SM) only when the whole
+// grid is resident at once in it; a second wave would start late and serialise.
+template <int ATOM, int BN, bool PRESPLIT>
+cudaError_t launch_small(const CUtensorMap& tw, const CUtensorMap& twlo, const CUtensorMap& txh,
+                         const CUtensorMap& txl, const TcParams& tp, dim3 grid, cudaStream_t st) {
+    // measured on GPT-2 small decode at 32 sequences: the shallow configuration is faster (the
+    // MMA issue rate, not the weight stream, bounds these tiles), so deep is opt-in
+    static const bool want_deep = [] {
+        const char* e = getenv("GPT2Q_TC_DEEP");
+        return e && e[0] == '1';
+    }();
+    const long clusters = (long)grid.x * grid.y;
+    const bool deep = want_deep && clusters <= resident_clusters<ATOM, BN, PRESPLIT, true>((int)grid.z);
+    if (deep) return launch_tc<ATOM, BN, PRESPLIT, true>(tw, twlo, txh, txl, tp, grid, st);
+    return launch_tc<ATOM, BN, PRESPLIT, false>(tw, twlo, txh, txl, tp, grid, st);
+}
+
 template <int ATOM, bool PRESPLIT>
 cudaError_t launch_bn(int BN, const CUtensorMap& tw, const CUtensorMap& twlo, const CUtensorMap& txh,
                       const CUtensorMap& txl, const TcParams& tp, dim3 grid, cudaStream_t st) {
     switch (BN) {
-        case 32: return launch_tc<ATOM, 32, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
-        case 64: return launch_tc<ATOM, 64, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
-        case 128: return launch_tc<ATOM, 128, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
-        default: return launch_tc<ATOM, 256, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
+        case 32: return launch_small<ATOM, 32, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
+        case 64: return launch_small<ATOM, 64, PRESPLIT>(tw, twlo, txh, txl, tp, grid, st);
+        case 128: return launch_tc<ATOM, 128, PRESPLIT, false>(tw, twlo, txh, txl, tp, grid, st);
+        default: return launch_tc<ATOM, 256, PRESPLIT, false>(tw, twlo, txh, txl, tp, grid, st);
     }
 }
 
@@ -591,6 +820,11 @@ struct GemmState {
     std::unordered_map<const void*, WeightTc> w;                 // weight payload -> maps
     std::unordered_map<XKey, CUtensorMap, XKeyHash> xmaps;       // activation buffer -> map
     std::vector<void*> owned;                                     // split weight copies
+    // phase trace of one launch (GPT2Q_TC_TRACE="rows x cols x M", e.g. 768x3072x32)
+    unsigned long long* trace = nullptr;
+    int trace_rows = 0, trace_cols = 0, trace_m = 0;
+    bool traced = false;
+    dim3 trace_grid;
 };
 
 bool GemmPlan::usable(const QW& w, int M) const {
@@ -617,12 +851,18 @@ int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax) {
     if (cudaMalloc(&p.err, 4) != cudaSuccess || cudaMemset(p.err, 0, 4) != cudaSuccess) return -1;
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     p.state = new GemmState();
+    if (const char* e = std::getenv("GPT2Q_TC_TRACE")) {
+        if (std::sscanf(e, "%dx%dx%d", &p.state->trace_rows, &p.state->trace_cols, &p.state->trace_m) == 3 &&
+            cudaMalloc(&p.state->trace, (size_t)4096 * TC_TRACE * 8) == cudaSuccess)
+            cudaMemset(p.state->trace, 0, (size_t)4096 * TC_TRACE * 8);
+    }
     p.enabled = true;
     return 0;
 }
 
 void gemm_destroy(GemmPlan& p) {
     if (p.err) cudaFree(p.err);
+    if (p.state && p.state->trace) cudaFree(p.state->trace);
     if (p.state)
         for (void* q : p.state->owned) cudaFree(q);
     delete p.state;
@@ -714,13 +954,43 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
     tp.post = wt.post;
     tp.epi = e;
     tp.err = p.err;
+    tp.trace = nullptr;
     dim3 grid(n_tiles, m_tiles, splits);
+    GemmState& gs = *p.state;
+    if (gs.trace && !gs.traced && w.rows == gs.trace_rows && w.cols == gs.trace_cols && M == gs.trace_m &&
+        (size_t)grid.x * grid.y * grid.z <= 4096) {
+        tp.trace = gs.trace;
+        gs.traced = true;
+        gs.trace_grid = grid;
+    }
     if (presplit) {
         if (w.atom == ATOM_Q8) return launch_bn<ATOM_Q8, true>(BN, wt.hi, wt.lo, *xh, *xl, tp, grid, st);
         return launch_bn<ATOM_Q4, true>(BN, wt.hi, wt.lo, *xh, *xl, tp, grid, st);
     }
     if (w.atom == ATOM_Q8) return launch_bn<ATOM_Q8, false>(BN, wt.raw, wt.raw, *xh, *xl, tp, grid, st);
     return launch_bn<ATOM_Q4, false>(BN, wt.raw, wt.raw, *xh, *xl, tp, grid, st);
+}
+
+std::string gemm_trace_json(const GemmPlan& p) {
+    if (!p.state || !p.state->trace || !p.state->traced) return "";
+    const dim3 g = p.state->trace_grid;
+    const size_t n = (size_t)g.x * g.y * g.z;
+    std::vector<unsigned long long> t(n * TC_TRACE);
+    if (cudaMemcpy(t.data(), p.state->trace, t.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return "";
+    unsigned long long t0 = ~0ull;
+    for (auto v : t)
+        if (v && v < t0) t0 = v;
+    std::string s = "{\"grid\": [" + std::to_string(g.x) + ", " + std::to_string(g.y) + ", " + std::to_string(g.z) +
+                    "], \"stamps\": [";
+    for (size_t c = 0; c < n; ++c) {
+        s += c ? ", [" : "[";
+        for (int k = 0; k < TC_TRACE; ++k) {
+            const unsigned long long v = t[c * TC_TRACE + k];
+            s += (k ? ", " : "") + std::to_string(v ? (long long)(v - t0) : -1);
+        }
+        s += "]";
+    }
+    return s + "]}";
 }
 
 int gemm_take_error(GemmPlan& p, cudaStream_t st) {

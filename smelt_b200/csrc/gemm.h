@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include <string>
+
 #include "common.cuh"
 
 namespace gpt2q {
@@ -37,6 +39,8 @@ void gemm_destroy(GemmPlan& p);
 int gemm_register_weight(GemmPlan& p, const QW& w, float max_abs_w, bool presplit, cudaStream_t st);
 cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, int M, const Epi& e,
                              cudaStream_t st);
+// Phase stamps of the launch selected by GPT2Q_TC_TRACE ("" when none), as JSON.
+std::string gemm_trace_json(const GemmPlan& p);
 // Reads and clears the device error word (0 = no error). Synchronises `st`.
 int gemm_take_error(GemmPlan& p, cudaStream_t st);
 

@@ -28,7 +28,10 @@ bool pdl_enabled() {
 
 // Every kernel here is launched as a programmatic dependent of the previous kernel in
 // the stream: it lets its own dependents start early (pdl_trigger) and waits for its
-// inputs (pdl_wait) before touching activations.
+// inputs (pdl_wait) before touching activations. Activations written by a preceding kernel
+// are read with coherent loads only (never __ldg or const __restrict__): the compiler may
+// treat non-coherent loads as invariant and schedule them above griddepcontrol.wait.
+// Weights, scales and biases, constant for the handle's lifetime, may use __ldg.
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                               Args... args) {
@@ -94,16 +97,25 @@ __device__ __forceinline__ void vec_get(const float2& v, float* f) { f[0] = v.x;
 __device__ __forceinline__ float4 vec_make4(const float* f) { return make_float4(f[0], f[1], f[2], f[3]); }
 
 template <int VEC, int NV>
-__global__ void __launch_bounds__(128) k_layernorm(const float* __restrict__ x, int ldx, const int* __restrict__ rows,
+__global__ void __launch_bounds__(128) k_layernorm(const float* x, int ldx, const int* __restrict__ rows,
                                                    float* __restrict__ y, int ldy, __half* __restrict__ yhi,
                                                    __half* __restrict__ ylo, const float* __restrict__ g,
                                                    const float* __restrict__ b, float eps, int M) {
     using V = typename VecT<VEC>::T;
     constexpr int D = 32 * VEC * NV;
     tc::pdl_trigger();
-    tc::pdl_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
+    // gain and bias are weights: loaded before the wait for the preceding kernel
+    const V* gv = reinterpret_cast<const V*>(g);
+    const V* bv = reinterpret_cast<const V*>(b);
+    float gg[NV][VEC], bb[NV][VEC];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        vec_get(gv[lane + 32 * j], gg[j]);
+        vec_get(bv[lane + 32 * j], bb[j]);
+    }
+    tc::pdl_wait();
     if (warp >= M) return;
     const int src = rows ? rows[warp] : warp;
     const V* xr = reinterpret_cast<const V*>(x + (size_t)src * ldx);
@@ -126,16 +138,12 @@ __global__ void __launch_bounds__(128) k_layernorm(const float* __restrict__ x, 
         }
     const float var = warp_sum(q) / (float)D;
     const float rstd = __frcp_rn(sqrtf(var + eps));
-    const V* gv = reinterpret_cast<const V*>(g);
-    const V* bv = reinterpret_cast<const V*>(b);
     float* yr = y + (size_t)warp * ldy;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-        float gg[VEC], bb[VEC], o[VEC];
-        vec_get(gv[lane + 32 * j], gg);
-        vec_get(bv[lane + 32 * j], bb);
+        float o[VEC];
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = (v[j][e] - mean) * rstd * gg[e] + bb[e];
+        for (int e = 0; e < VEC; ++e) o[e] = (v[j][e] - mean) * rstd * gg[j][e] + bb[j][e];
         const int i0 = (lane + 32 * j) * VEC;
         if (VEC == 4) {
             *reinterpret_cast<float4*>(yr + i0) = vec_make4(o);
@@ -158,7 +166,7 @@ __global__ void __launch_bounds__(128) k_layernorm(const float* __restrict__ x, 
 }
 
 // Any d (multiple of 2): strided scalar form of the same computation.
-__global__ void __launch_bounds__(128) k_layernorm_any(const float* __restrict__ x, int ldx,
+__global__ void __launch_bounds__(128) k_layernorm_any(const float* x, int ldx,
                                                        const int* __restrict__ rows, float* __restrict__ y, int ldy,
                                                        __half* __restrict__ yhi, __half* __restrict__ ylo,
                                                        const float* __restrict__ g, const float* __restrict__ b, int d,
@@ -256,11 +264,11 @@ __device__ __forceinline__ void decode_chunk<ATOM_F32>(const uint4& v, float* f)
 }
 
 template <int CE>
-__device__ __forceinline__ float dot_chunk(const float* f, const float* __restrict__ xr) {
+__device__ __forceinline__ float dot_chunk(const float* f, const float* xr) {
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
     for (int i = 0; i < CE; i += 4) {
-        float4 xv = __ldg(reinterpret_cast<const float4*>(xr + i));
+        float4 xv = __ldcg(reinterpret_cast<const float4*>(xr + i));
         a0 = fmaf(f[i], xv.x, a0);
         a1 = fmaf(f[i + 1], xv.y, a1);
         a2 = fmaf(f[i + 2], xv.z, a2);
@@ -270,7 +278,7 @@ __device__ __forceinline__ float dot_chunk(const float* f, const float* __restri
 }
 
 template <int ATOM, int MT, int U>
-__global__ void __launch_bounds__(128) k_linear_simt(QW w, const float* __restrict__ X, int ldx, int M, int KS,
+__global__ void __launch_bounds__(128) k_linear_simt(QW w, const float* X, int ldx, int M, int KS,
                                                      Epi epi) {
     constexpr int CE = ChunkTraits<ATOM>::CE;
     __shared__ float red[8][MT];  // [half-warp][row of the activation batch]
@@ -401,7 +409,7 @@ cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, cons
 // merged through shared memory. Four warps measured best on long contexts (many CTAs per SM).
 // Semantics: softmax(q.K^T * scale) V over positions 0..pos (gpt2.rs:261-291).
 template <int NW>
-__global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* __restrict__ q, int ldq, KVGeom g,
+__global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* q, int ldq, KVGeom g,
                                                          size_t layer_off, const int* __restrict__ slot,
                                                          const int* __restrict__ pos, float* __restrict__ out,
                                                          __half* __restrict__ ohi, __half* __restrict__ olo,
@@ -429,11 +437,11 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* __restrict
         float4 kr[HD / 4];
         const float4* kp = reinterpret_cast<const float4*>(K + (size_t)min(tl + lane, T - 1) * HD);
 #pragma unroll
-        for (int i = 0; i < HD / 4; ++i) kr[i] = __ldg(kp + i);
+        for (int i = 0; i < HD / 4; ++i) kr[i] = __ldcg(kp + i);
         float2 vv[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-            vv[j] = __ldg(reinterpret_cast<const float2*>(V + (size_t)(tl + min(j, nv - 1)) * HD) + lane);
+            vv[j] = __ldcg(reinterpret_cast<const float2*>(V + (size_t)(tl + min(j, nv - 1)) * HD) + lane);
         if (first) {
             if (threadIdx.x < HD / 4)
                 qs[threadIdx.x] =
@@ -507,7 +515,7 @@ cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t 
 // query row i; each half holds 32 of the 64 q/o dims in registers. Keys/values are
 // staged 32 at a time in shared memory with the two halves interleaved so a warp's
 // paired reads hit distinct banks. Causal mask: key t attends iff t <= query position.
-__global__ void __launch_bounds__(128) k_attn_prefill(const float* __restrict__ q, int ldq, KVGeom g,
+__global__ void __launch_bounds__(128) k_attn_prefill(const float* q, int ldq, KVGeom g,
                                                       size_t layer_off, const AttnTile* __restrict__ tiles,
                                                       float* __restrict__ out, __half* __restrict__ ohi,
                                                       __half* __restrict__ olo, int ldo, float scale) {
@@ -545,8 +553,8 @@ __global__ void __launch_bounds__(128) k_attn_prefill(const float* __restrict__ 
             const int r = e / (HD / 4), c4 = (e % (HD / 4)) * 4;
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
             if (k0 + r < tile.T) {
-                kv = __ldg(reinterpret_cast<const float4*>(K + (size_t)(k0 + r) * HD + c4));
-                vv = __ldg(reinterpret_cast<const float4*>(V + (size_t)(k0 + r) * HD + c4));
+                kv = __ldcg(reinterpret_cast<const float4*>(K + (size_t)(k0 + r) * HD + c4));
+                vv = __ldcg(reinterpret_cast<const float4*>(V + (size_t)(k0 + r) * HD + c4));
             }
             const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, vk[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
@@ -616,7 +624,7 @@ __device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsig
     return a > b ? a : b;
 }
 
-__global__ void __launch_bounds__(256) k_argmax_partial(const float* __restrict__ logits, int V, int ld,
+__global__ void __launch_bounds__(256) k_argmax_partial(const float* logits, int V, int ld,
                                                         unsigned long long* __restrict__ best) {
     __shared__ unsigned long long sm[8];
     tc::pdl_trigger();

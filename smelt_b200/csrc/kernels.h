@@ -36,6 +36,11 @@ cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t 
 cudaError_t launch_attn_prefill(const float* q, int ldq, const KVGeom& g, size_t layer_off,
                                 const AttnTile* tiles, int n_tiles, float* out, __half* ohi, __half* olo, int ldo,
                                 int n_head, float scale, cudaStream_t st);
+// Causal prefill attention on the tensor cores (attn_tc.cu): tiles of 128 queries, head dim 64,
+// scale 1/8. Bounded waits record a timeout in `err`.
+cudaError_t launch_attn_prefill_tc(const float* q, int ldq, const KVGeom& g, size_t layer_off, const AttnTile* tiles,
+                                   int n_tiles, float* out, __half* ohi, __half* olo, int ldo, int n_head, int* err,
+                                   cudaStream_t st);
 // Greedy argmax per row (total order, ties -> last index). `best` holds one zeroed u64 per
 // row; the finaliser consumes and re-zeroes it, writes next[], and optionally logs the
 // token at genlog[b][gpos[b]], feeds it back (tok_adv) and advances pos_adv.

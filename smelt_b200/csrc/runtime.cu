@@ -649,8 +649,11 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
     const int M = offs[s1] - base;
     const int ns = s1 - s0;
     // host staging: tok[M] pos[M] slot[M] lastrow[ns] lastpos[ns] tiles[4*nt]
+    // attention tiles: 128 queries on the tensor cores, 64 on the CUDA cores
+    const bool attn_tc = H->gemm.enabled && H->hd == 64 && !std::getenv("GPT2Q_ATTN_CORES");
+    const int qt = attn_tc ? 128 : 64;
     int nt = 0;
-    for (int s = s0; s < s1; ++s) nt += (offs[s + 1] - offs[s] + 63) / 64;
+    for (int s = s0; s < s1; ++s) nt += (offs[s + 1] - offs[s] + qt - 1) / qt;
     if (nt > H->max_tiles) return H->fail(GPT2Q_EARG, "too many attention tiles in one prefill chunk");
     int rc = ensure_stage(H, (size_t)3 * M + 2 * ns + 4 * (size_t)nt);
     if (rc) return rc;
@@ -672,7 +675,7 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
         }
         st_lrow[s - s0] = r0 + T - 1;
         st_lpos[s - s0] = T - 1;
-        for (int q0 = 0; q0 < T; q0 += 64) st_tiles[ti++] = AttnTile{r0, q0, T, slot};
+        for (int q0 = 0; q0 < T; q0 += qt) st_tiles[ti++] = AttnTile{r0, q0, T, slot};
     }
     CK(cudaMemcpyAsync(H->p_tok, st_tok, (size_t)M * 4, cudaMemcpyHostToDevice, H->stream));
     CK(cudaMemcpyAsync(H->p_pos, st_pos, (size_t)M * 4, cudaMemcpyHostToDevice, H->stream));
@@ -691,9 +694,15 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
     RUN("embed", (double)M * d * 6, launch_embed(H->wte.w, H->wpe.w, H->p_tok, H->p_pos, H->x, d, M, H->stream));
     for (int l = 0; l < H->cfg.n_layer; ++l) {
         rc = block(H, l, M, H->p_slot, H->p_pos, [&](int layer) {
-            RUN("attn_prefill", kv_bytes + (double)M * H->d_local * 8,
-                launch_attn_prefill(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->p_tiles, nt,
-                                    H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, scale, H->stream));
+            if (attn_tc)
+                RUN("attn_prefill_tc", kv_bytes + (double)M * H->d_local * 8,
+                    launch_attn_prefill_tc(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->p_tiles,
+                                           nt, H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, H->gemm.err,
+                                           H->stream));
+            else
+                RUN("attn_prefill", kv_bytes + (double)M * H->d_local * 8,
+                    launch_attn_prefill(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->p_tiles, nt,
+                                        H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, scale, H->stream));
             return GPT2Q_OK;
         });
         if (rc) return rc;
@@ -1343,6 +1352,8 @@ int gpt2q_info(gpt2q_handle* H, char* json, size_t cap) {
         }
         tr += "]";
     }
+    const std::string gt = gemm_trace_json(H->gemm);
+    if (!gt.empty()) tr += ", \"tc_trace\": " + gt;
     const std::string s = head + tr + "}";
     if (s.size() + 1 > cap) return H->fail(GPT2Q_EARG, "info: buffer too small");
     std::memcpy(json, s.c_str(), s.size() + 1);

@@ -7,6 +7,8 @@ when a handle is created.
 import numpy as np
 import pytest
 
+from oracle import oracle as O
+from smelt_b200 import pack as P
 from smelt_b200.gpu import Gpu
 
 from .helpers import MINI, TINY, make_pack, oracle_engine, oracle_prefix_logits
@@ -25,6 +27,7 @@ def _built():
 @pytest.mark.parametrize("meta", [TINY, MINI])
 def test_tc_step_matches_oracle(meta, policy, monkeypatch):
     monkeypatch.setenv("GPT2Q_TC_MIN_M", "1")
+    monkeypatch.setenv("GPT2Q_NO_PERSISTENT", "1")  # single-token steps through the tcgen05 linear
     pk = make_pack(meta, policy, 0, 0.02)
     eng = oracle_engine(pk)
     ids = ((np.arange(30) * 53 + 3) % meta.vocab).astype(np.uint32)
@@ -69,3 +72,28 @@ def test_tc_large_prefill_matches_oracle():
         ref = oracle_prefix_logits(eng, prompts[i])[-1]
         assert np.abs(lg[i] - ref).max() <= 1e-3
         assert nxt[i] == int(np.argmax(ref[::-1]) and (len(ref) - 1 - np.argmax(ref[::-1])))
+
+
+LONG = P.Meta(n_embd=256, n_layer=2, n_head=4, n_ctx=512, vocab=1031)
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+def test_tc_prefill_attention_matches_cuda_cores_and_oracle(policy, monkeypatch):
+    """Tensor-core prefill attention (128-query tiles, several 128-key blocks, ragged ends)
+    against the CUDA-core attention kernel and the oracle."""
+    pk = make_pack(LONG, policy, 0, 0.02)
+    eng = oracle_engine(pk)
+    rng = np.random.default_rng(7)
+    lens = [1, 127, 128, 129, 300, 450]
+    prompts = [rng.integers(0, LONG.vocab, n).astype(np.uint32) for n in lens]
+    with Gpu(pk, max_seqs=len(prompts), max_tokens=2048) as g:
+        nxt_tc, lg_tc = g.prefill(prompts, want_logits=True)
+    monkeypatch.setenv("GPT2Q_ATTN_CORES", "1")
+    with Gpu(pk, max_seqs=len(prompts), max_tokens=2048) as g:
+        nxt_cc, lg_cc = g.prefill(prompts, want_logits=True)
+    assert np.abs(lg_tc - lg_cc).max() <= 1e-3
+    assert np.array_equal(nxt_tc, nxt_cc)
+    for i, p in enumerate(prompts):
+        ref = oracle_prefix_logits(eng, p)[-1]
+        assert np.abs(lg_tc[i] - ref).max() <= 1e-3
+        assert nxt_tc[i] == O.argmax(ref)
