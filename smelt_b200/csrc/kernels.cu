@@ -401,12 +401,11 @@ cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, cons
 }
 
 // ------------------------------------------------------------------ decode attention
-// One block of NW warps per (head, sequence). Each warp takes 32 keys at a time: lane j
-// scores key t0+j against q (q broadcast from shared memory); the V rows of the same 32
-// keys are loaded in the same burst (lane l owns dims 2l, 2l+1, coalesced 256-byte rows),
-// so one memory round trip serves the whole block; the K/V burst of the first block is
-// issued before q is staged. The warp does an online-softmax update and the warps are
-// merged through shared memory. Four warps measured best on long contexts (many CTAs per SM).
+// One block of NW warps per (head, sequence); warp w takes keys w*32 + 128 i .. +31. Lane l
+// owns dims 2l, 2l+1 of q, K and V, so every K and V row is one coalesced 256-byte load; the
+// K and V rows of a warp's 32 keys are loaded in one burst. Scores: 2 FMAs per key and lane, then a 31-shuffle transpose-reduction leaves the
+// score of key t0 + l in lane l. The warp does an online-softmax update and the warps are
+// merged through shared memory.
 // Semantics: softmax(q.K^T * scale) V over positions 0..pos (gpt2.rs:261-291).
 template <int NW>
 __global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* q, int ldq, KVGeom g,
@@ -415,7 +414,6 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* q, int ldq
                                                          __half* __restrict__ ohi, __half* __restrict__ olo,
                                                          int ldo, float scale) {
     constexpr int HD = 64;
-    __shared__ float4 qs[HD / 4];
     __shared__ float wm[NW], wl[NW];
     __shared__ float wo[NW][HD];
     tc::pdl_trigger();
@@ -427,39 +425,34 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* q, int ldq
     const float* V = K + g.sel_stride;
 
     float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
-    bool first = true;
-    for (int t0 = warp * 32; t0 < T || first; t0 += 32 * NW) {
-        const bool active = t0 < T;
+    const float2 qv = __ldcg(reinterpret_cast<const float2*>(q + (size_t)b * ldq + head * HD) + lane);
+    for (int t0 = warp * 32; t0 < T; t0 += 32 * NW) {
+        const int nv = min(32, T - t0);
+        // one burst: dims 2l, 2l+1 of the 32 K rows and the 32 V rows (rows past T repeat the last)
+        float2 kk[32], vv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const size_t row = (size_t)(t0 + min(j, nv - 1)) * HD;
+            kk[j] = __ldcg(reinterpret_cast<const float2*>(K + row) + lane);
+            vv[j] = __ldcg(reinterpret_cast<const float2*>(V + row) + lane);
+        }
+        float sc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sc[j] = fmaf(qv.y, kk[j].y, qv.x * kk[j].x);
+        // transpose-reduction: after the step with offset o, sc[i] holds key (keys of this
+        // lane's half) + i summed over the lanes that differ in bits >= o
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < o; ++i) {
+                const float send = upper ? sc[i] : sc[i + o];
+                const float keep = upper ? sc[i + o] : sc[i];
+                sc[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
         const int t = t0 + lane;
-        const int nv = active ? min(32, T - t0) : 1;
-        const int tl = active ? t0 : 0;
-        // one burst: this lane's K row and the V slice of all 32 rows (issued before q is needed)
-        float4 kr[HD / 4];
-        const float4* kp = reinterpret_cast<const float4*>(K + (size_t)min(tl + lane, T - 1) * HD);
-#pragma unroll
-        for (int i = 0; i < HD / 4; ++i) kr[i] = __ldcg(kp + i);
-        float2 vv[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-            vv[j] = __ldcg(reinterpret_cast<const float2*>(V + (size_t)(tl + min(j, nv - 1)) * HD) + lane);
-        if (first) {
-            if (threadIdx.x < HD / 4)
-                qs[threadIdx.x] =
-                    *reinterpret_cast<const float4*>(q + (size_t)b * ldq + head * HD + threadIdx.x * 4);
-            __syncthreads();
-            first = false;
-        }
-        if (!active) break;
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-        for (int i = 0; i < HD / 4; ++i) {
-            const float4 qv = qs[i];
-            a0 = fmaf(qv.x, kr[i].x, a0);
-            a1 = fmaf(qv.y, kr[i].y, a1);
-            a2 = fmaf(qv.z, kr[i].z, a2);
-            a3 = fmaf(qv.w, kr[i].w, a3);
-        }
-        const float s = (t < T) ? ((a0 + a1) + (a2 + a3)) * scale : -INFINITY;
+        const float s = (t < T) ? sc[0] * scale : -INFINITY;
         const float mnew = fmaxf(m, warp_max(s));
         const float corr = expf(m - mnew);
         const float p = (t < T) ? expf(s - mnew) : 0.f;
