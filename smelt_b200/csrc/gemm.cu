@@ -51,7 +51,11 @@ namespace gpt2q {
 namespace {
 
 constexpr int BM = 128, BK = 64, THREADS = 224;
-constexpr int MAX_SPLITS = 8;  // portable cluster size
+constexpr int MAX_SPLITS = 16;      // decode tiles (pushed exchange): non-portable clusters up to 16
+constexpr int MAX_SPLITS_PULL = 8;  // wider tiles (pulled exchange): portable cluster size
+
+// Token columns per reducing CTA in the split-K exchange (a multiple of 4).
+__host__ __device__ constexpr int push_cw(int bn, int splits) { return ((bn + splits - 1) / splits + 3) & ~3; }
 
 template <int BN, bool PRESPLIT, bool DEEP>
 struct Cfg {
@@ -69,9 +73,9 @@ struct Cfg {
     static constexpr bool DUAL = BN <= 64;
     static constexpr int TMEM_COLS = DUAL ? 4 * BN : BN;
     static constexpr int PS = BN + 4;  // split-K partial tile [128 rows][PS] fp32 (padded rows)
-    // Decode tiles exchange split-K partials by pushing them (bulk copies into the peers'
-    // shared memory); rank r receives the block of CW token columns it reduces. One area of
-    // [splits][128][CW] fp32 (splits * CW <= BN + 32) receives, another one sends.
+    // Decode tiles exchange split-K partials by pushing them (16-byte remote stores into the
+    // peers' shared memory); rank r receives the block of CW token columns it reduces into an
+    // area of [splits][128][CW] fp32 (splits * CW <= BN + 32) over the free operand rings.
     static constexpr bool PUSH = BN <= 64;
     static constexpr int XCH_FLOATS = 128 * (BN + 32);
     static constexpr int A_BYTES = BM * 128;                          // one of hi/lo
@@ -93,7 +97,7 @@ struct Cfg {
     static constexpr int MIN_BLOCKS = (!DEEP && BN <= 64 && SMEM <= 232448 / 2 - 1024) ? 2 : 1;
     // the split-K partial tile reuses the operand rings once every MMA is done
     static_assert(PS * BM * 4 <= OFF_RAW, "partial tile must fit in the operand rings");
-    static_assert(!PUSH || 2 * XCH_FLOATS * 4 <= OFF_RAW, "exchange areas must fit in the operand rings");
+    static_assert(!PUSH || XCH_FLOATS * 4 <= OFF_RAW, "exchange area must fit in the operand rings");
 };
 
 struct TcParams {
@@ -324,12 +328,12 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
         tc::mbar_init(acc_full, 1);
         tc::mbar_init(recv_full, 1);
         if (C::PUSH && p.splits > 1) {
-            // this CTA reduces token columns [rank CW, rank CW + CW) of the tile: every other split
-            // sends it one [128][CW] fp32 block
+            // this CTA reduces token columns [rank CW, rank CW + w) of the tile (w <= CW: the last
+            // block may be narrower): every other split stores 128 rows x w fp32 into it
             const int rank = (int)tc::cluster_rank();
-            const int CW = ((BN + p.splits - 1) / p.splits + 3) & ~3;
-            if (min(BN, (rank + 1) * CW) > rank * CW)
-                tc::mbar_arrive_expect_tx(recv_full, (uint32_t)((p.splits - 1) * 128 * CW * 4));
+            const int CW = push_cw(BN, p.splits);
+            const int w = min(BN, (rank + 1) * CW) - rank * CW;
+            if (w > 0) tc::mbar_arrive_expect_tx(recv_full, (uint32_t)((p.splits - 1) * 128 * w * 4));
         }
         tc::fence_mbar_init();
     }
@@ -346,8 +350,8 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
     tc::pdl_trigger();
     const bool push = C::PUSH && p.splits > 1;
     // split-K exchange over three cluster-barrier phases: 0 = barriers initialised, 1 = every
-    // CTA's MMAs are done (its operand rings may be written) and its partials staged, 2 = all
-    // copies into every CTA have landed (none may exit before)
+    // CTA's MMAs are done (its operand rings may be written), 2 = all stores into every CTA
+    // have landed (none may exit before)
     if (push) tc::cluster_arrive_relaxed();
     if (threadIdx.x == 0) tc_stamp(p, 1);
 
@@ -507,6 +511,12 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
         const bool acc_ok = tc::mbar_wait(acc_full, 0, p.err);
         if (threadIdx.x == 32) tc_stamp(p, 10);
         tc::tc_fence_after();
+        if (push) {
+            // this CTA's MMAs, and their shared-memory reads, are complete: its operand rings
+            // may now receive the peers' partials (phase 1)
+            tc::cluster_wait();  // phase 0
+            tc::cluster_arrive_relaxed();
+        }
         tc::pdl_wait();  // outputs / residual inputs belong to earlier kernels
         if (threadIdx.x == 32) tc_stamp(p, 11);
         const int quarter = warp & 3;
@@ -517,10 +527,20 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
         const int mend = min(p.M, m0 + BN);
         // push exchange: rank r reduces token columns [r CW, r CW + CW) of the tile
         const int rank = push ? (int)tc::cluster_rank() : 0;
-        const int CW = ((BN + p.splits - 1) / p.splits + 3) & ~3;
-        float* recv = reinterpret_cast<float*>(smem);  // [splits][128][CW]
-        float* send = recv + C::XCH_FLOATS;            // [splits][128][CW]
+        const int CW = push_cw(BN, p.splits);
+        float* recv = reinterpret_cast<float*>(smem);  // [splits][128][CW]: slot s from split s
         const int own_w = max(0, min(BN, (rank + 1) * CW) - rank * CW);
+        // residual rows of this CTA's token columns, loaded while the partials travel
+        constexpr int RPRE = 8;
+        const bool resid = p.epi.kind == EPI_RESID;
+        float rpre[RPRE];
+        if (push && resid && own_w <= RPRE) {
+#pragma unroll
+            for (int j = 0; j < RPRE; ++j) {
+                const int m = m0 + rank * CW + j;
+                rpre[j] = (j < own_w && nn < p.w.rows && m < mend) ? p.epi.out[(size_t)m * p.epi.ldo + nn] : 0.f;
+            }
+        }
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
             float v[32];
@@ -540,11 +560,18 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
                 if (m0 + c0 >= mend) break;  // warp-uniform
                 epi_chunk<32>(p.epi, nn, acc_ok && nn < p.w.rows, v, m0 + c0, 1, mend, p.post, nullptr, &bias_v);
             } else if (push) {
+                if (c0 == 0) tc::cluster_wait();  // phase 1: every peer's rings may be written
+                // columns of rank r go to slot `rank` of CTA r: remote 16-byte stores that
+                // complete on r's recv_full, plain stores for this CTA's own columns
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
                     const int c = c0 + j, r = c / CW, q = c - r * CW;
-                    float* dst = (r == rank ? recv : send) + ((size_t)r * 128 + row) * CW + q;
-                    *reinterpret_cast<float4*>(dst) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    float* dst = recv + ((size_t)rank * 128 + row) * CW + q;
+                    const float4 val = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    if (r == rank)
+                        *reinterpret_cast<float4*>(dst) = val;
+                    else
+                        tc::st_async_f32x4((uint32_t)r, dst, val, recv_full);
                 }
             } else {
 #pragma unroll
@@ -553,35 +580,25 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
             }
         }
         if (push) {
-            tc::fence_proxy_async_smem();  // the partials are read by bulk copies
-            tc::named_bar_sync(1, 128);
-            if (threadIdx.x == 32) tc_stamp(p, 12);
-            // acc_full came first: this CTA's MMAs, and their shared-memory reads, are complete
-            tc::cluster_wait();            // phase 0
-            tc::cluster_arrive_relaxed();  // phase 1
-            tc::cluster_wait();
-            if (threadIdx.x == 32) {
-                for (int r = 0; r < p.splits; ++r) {
-                    if (r == rank || min(BN, (r + 1) * CW) <= r * CW) continue;
-                    tc::bulk_send((uint32_t)r, send + (size_t)r * 128 * CW, recv + (size_t)rank * 128 * CW,
-                                  (uint32_t)(128 * CW * 4), recv_full);
-                }
-                tc_stamp(p, 13);
-            }
-            __syncwarp();
+            if (threadIdx.x == 32) tc_stamp(p, 13);
             const bool ok = acc_ok && (own_w == 0 || tc::mbar_wait_cluster(recv_full, 0, p.err));
             if (threadIdx.x == 32) tc_stamp(p, 14);
             __syncwarp();
             tc::cluster_arrive_relaxed();  // phase 2: everything sent to this CTA has landed
-            // sum the splits in rank order, then the epilogue for this CTA's token columns
-            const bool resid = p.epi.kind == EPI_RESID;
+            // sum the splits in rank order (this thread's own row of each slot: its own slot was
+            // written by itself), then the epilogue for this CTA's token columns
             for (int cb = 0; cb < own_w && m0 + rank * CW + cb < mend; cb += 4) {
                 const int m = m0 + rank * CW + cb;
                 float rp[4], acc[4] = {0.f, 0.f, 0.f, 0.f};
                 if (resid) {
+                    if (own_w <= RPRE) {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        rp[j] = (nn < p.w.rows && m + j < mend) ? p.epi.out[(size_t)(m + j) * p.epi.ldo + nn] : 0.f;
+                        for (int j = 0; j < 4; ++j) rp[j] = (cb == 0) ? rpre[j] : rpre[4 + j];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            rp[j] = (nn < p.w.rows && m + j < mend) ? p.epi.out[(size_t)(m + j) * p.epi.ldo + nn] : 0.f;
+                    }
                 }
 #pragma unroll
                 for (int sp = 0; sp < MAX_SPLITS; ++sp) {
@@ -621,7 +638,7 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
             const int mend = min(p.M, m0 + BN);
             // rank r reduces and writes a contiguous block of CW columns (tokens): 16-byte
             // remote loads, all splits of a batch in flight together, summed in rank order
-            const int CW = ((BN + p.splits - 1) / p.splits + 3) & ~3;
+            const int CW = push_cw(BN, p.splits);
             const int cend = min(BN, (rank + 1) * CW);
             constexpr int RJ = 8;
             for (int cb = rank * CW; cb < cend && m0 + cb < mend; cb += RJ) {
@@ -639,7 +656,7 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
                 const uint32_t a0 = local + (uint32_t)((row * C::PS + cb) * 4);
                 const bool second = cb + 4 < cend;  // columns cb+4..cb+7 belong to this block
 #pragma unroll
-                for (int sp = 0; sp < MAX_SPLITS; ++sp) {
+                for (int sp = 0; sp < MAX_SPLITS_PULL; ++sp) {
                     if (sp < p.splits) {
                         const float4 x = tc::ld_cluster_f32x4(tc::map_cluster(a0, sp));
                         const float4 y = second ? tc::ld_cluster_f32x4(tc::map_cluster(a0 + 16, sp))
@@ -726,6 +743,10 @@ cudaError_t launch_tc(const CUtensorMap& tw, const CUtensorMap& twlo, const CUte
         attrs[na].val.programmaticStreamSerializationAllowed = 1;
         ++na;
     }
+    if (grid.z > 8) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
     if (grid.z > 1) {
         attrs[na].id = cudaLaunchAttributeClusterDimension;
         attrs[na].val.clusterDim.x = 1;
@@ -748,7 +769,8 @@ int resident_clusters(int cs) {
     auto kern = k_linear_tc<ATOM, BN, PRESPLIT, DEEP>;
     const int smem = Cfg<BN, PRESPLIT, DEEP>::SMEM;
     int n = 0;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess &&
+        (cs <= 8 || cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess)) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(1, 1, cs);
         cfg.blockDim = dim3(THREADS, 1, 1);
@@ -933,14 +955,19 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
     const int m_tiles = (M + BN - 1) / BN;
     const int n_tiles = (w.rows + BM - 1) / BM;
     const int nkb = (K + BK - 1) / BK;
-    int splits = 1;
+    int splits = 1, kb_per = nkb;
     const int tiles = m_tiles * n_tiles;
     if (tiles < 120) {
-        splits = std::min(std::min(nkb, MAX_SPLITS), (148 + tiles - 1) / tiles);
-        splits = std::max(splits, 1);
+        // about one wave of CTAs; decode tiles exchange partials in [splits][128][CW] areas
+        // that hold splits * CW <= BN + 32 columns
+        const int s0 = std::max(1, std::min(std::min(nkb, BN <= 64 ? MAX_SPLITS : MAX_SPLITS_PULL),
+                                            (148 + tiles - 1) / tiles));
+        for (int s = s0; s >= 1; --s) {
+            kb_per = (nkb + s - 1) / s;
+            splits = (nkb + kb_per - 1) / kb_per;
+            if (BN > 64 || splits * push_cw(BN, splits) <= BN + 32) break;
+        }
     }
-    int kb_per = (nkb + splits - 1) / splits;
-    splits = (nkb + kb_per - 1) / kb_per;
     const CUtensorMap* xh = xmap(p, x.hi, K, x.ld, BN);
     const CUtensorMap* xl = xmap(p, x.lo, K, x.ld, BN);
     if (!xh || !xl) return cudaErrorInvalidValue;

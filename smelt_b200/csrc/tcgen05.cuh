@@ -145,18 +145,15 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     atomicExch(err, ERR_WAIT_TIMEOUT);
     return false;
 }
-// 1-D bulk copy of `bytes` (a 16-byte multiple) from this CTA's shared memory to the same
-// offsets `dst_local` / `bar_local` in CTA `rank`, completing tx bytes on that CTA's mbarrier.
-__device__ __forceinline__ void bulk_send(uint32_t rank, const void* src, const void* dst_local, uint32_t bytes,
-                                          const uint64_t* bar_local) {
+// 16-byte store into CTA `rank`'s shared memory at the same offset as `dst_local`, completing
+// 16 tx bytes on that CTA's mbarrier at the offset of `bar_local`.
+__device__ __forceinline__ void st_async_f32x4(uint32_t rank, const void* dst_local, float4 v,
+                                               const uint64_t* bar_local) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
             map_cluster(smem_u32(dst_local), rank)),
-        "r"(smem_u32(src)), "r"(bytes), "r"(map_cluster(smem_u32(bar_local), rank))
+        "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(map_cluster(smem_u32(bar_local), rank))
         : "memory");
-}
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
     float v;

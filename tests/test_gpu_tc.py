@@ -97,3 +97,26 @@ def test_tc_prefill_attention_matches_cuda_cores_and_oracle(policy, monkeypatch)
         ref = oracle_prefix_logits(eng, p)[-1]
         assert np.abs(lg_tc[i] - ref).max() <= 1e-3
         assert nxt_tc[i] == O.argmax(ref)
+
+
+MID = P.Meta(n_embd=384, n_layer=2, n_head=6, n_ctx=128, vocab=1031)
+
+
+@pytest.mark.parametrize("batch", [17, 40, 64])
+def test_tc_split_k_exchange_shapes_match_cuda_core_path(batch, monkeypatch):
+    """d = 384 decode batches split K 3 to 16 ways; at 33-64 sequences some reducing CTAs own
+    a narrower last block of token columns than the others (e.g. 12, 12, 12, 12, 12, 4)."""
+    pk = make_pack(MID, "auto", 1, 0.02)
+    rng = np.random.default_rng(batch)
+    prompts = [rng.integers(0, MID.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 50, batch)]
+    res = {}
+    for mode in ("simt", "tc"):
+        monkeypatch.setenv("GPT2Q_TC_DISABLE", "1" if mode == "simt" else "0")
+        with Gpu(pk, max_seqs=batch) as g:
+            g.prefill(prompts)
+            toks = g.decode_steps(4, batch)
+            nxt, lg = g.decode(toks[-1], [p.size + 4 for p in prompts], want_logits=True)
+        res[mode] = (toks, nxt, lg)
+    a, b = res["simt"], res["tc"]
+    assert np.abs(a[2] - b[2]).max() <= 1e-3
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
