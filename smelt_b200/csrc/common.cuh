@@ -172,4 +172,11 @@ __device__ __forceinline__ void split_hl(float x, __half& hi, __half& lo) {
     lo = __float2half_rn(x - __half2float(hi));
 }
 
+// split_hl of two values with paired conversions (same roundings): hi = (hi(a), hi(b)).
+__device__ __forceinline__ void split_hl2(float a, float b, __half2& hi, __half2& lo) {
+    hi = __floats2half2_rn(a, b);
+    const float2 h = __half22float2(hi);
+    lo = __floats2half2_rn(a - h.x, b - h.y);
+}
+
 }  // namespace gpt2q

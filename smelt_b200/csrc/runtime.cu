@@ -121,7 +121,6 @@ struct gpt2q_handle {
     // fp16 hi/lo copies of the linear inputs (h: LayerNorm out, att: attention out, f: GELU out)
     __half *h_hi = nullptr, *h_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr, *f_hi = nullptr, *f_lo = nullptr;
     unsigned long long* best = nullptr;  // argmax slots, one per sequence
-    float* tp_red = nullptr;  // tensor-parallel partial sums [Mmax][d]
     // prefill scratch
     uint32_t* p_tok = nullptr;
     int *p_pos = nullptr, *p_slot = nullptr, *p_lastrow = nullptr, *p_lastpos = nullptr;
@@ -408,14 +407,16 @@ int linear(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int 
     return GPT2Q_OK;
 }
 
-// Residual update of row-split projections under tensor parallelism: y = partial (+bias on
-// rank 0), all-reduce(y), x += y.
-int tp_residual(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int M) {
+// Residual update of a row-split projection under tensor parallelism: this rank's partial
+// (+bias on rank 0) into its exchange buffer `parity`, then one kernel sums the ranks'
+// partials from peer memory into x and applies the LayerNorm (g, b) that follows, when given.
+int tp_residual(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int M, int parity, const float* g,
+                const float* b) {
     const int d = H->cfg.n_embd;
-    Epi e = epi_store(H->tp_red, d, H->tp_rank == 0 ? L.bias : nullptr);
+    Epi e = epi_store(tp_partial(H->tp, parity), d, H->tp_rank == 0 ? L.bias : nullptr);
     int rc = linear(H, name, L, X, M, e);
     if (rc) return rc;
-    rc = tp_allreduce_add(H->tp, H->tp_red, H->x, (size_t)M * d, H->stream);
+    rc = tp_reduce_ln(H->tp, parity, H->x, M, d, g, b, H->cfg.ln_eps, H->h, H->h_hi, H->h_lo, H->stream);
     if (rc) return H->fail(GPT2Q_ENCCL, tp_last_error(H->tp));
     if (H->capturing)
         H->capture_kernels++;
@@ -452,22 +453,27 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     const In hin{H->h, H->h_hi, H->h_lo, d};
     const In ain{H->att, H->att_hi, H->att_lo, H->d_local};
     const In fin{H->f, H->f_hi, H->f_lo, H->fc_local};
-    RUN("layernorm", (double)M * d * 8,
-        launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln1_g, Lw.ln1_b, d, eps, M, H->stream));
+    // under tensor parallelism every LayerNorm after the first is applied by the residual
+    // reduction before it
+    const bool tp = H->tp_size > 1;
+    if (!(tp && layer > 0))
+        RUN("layernorm", (double)M * d * 8,
+            launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln1_g, Lw.ln1_b, d, eps, M, H->stream));
     int rc = linear(H, "linear_qkv", Lw.attn, hin, M, epi_qkv(H, layer, slot, pos, Lw.attn.bias));
     if (rc) return rc;
     rc = attn_fn(layer);
     if (rc) return rc;
-    if (H->tp_size > 1) {
-        rc = tp_residual(H, "linear_attn_proj", Lw.proj, ain, M);
+    if (tp) {
+        rc = tp_residual(H, "linear_attn_proj", Lw.proj, ain, M, 0, Lw.ln2_g, Lw.ln2_b);
     } else {
         Epi e = epi_store(H->x, d, Lw.proj.bias);
         e.kind = EPI_RESID;
         rc = linear(H, "linear_attn_proj", Lw.proj, ain, M, e);
     }
     if (rc) return rc;
-    RUN("layernorm", (double)M * d * 8,
-        launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln2_g, Lw.ln2_b, d, eps, M, H->stream));
+    if (!tp)
+        RUN("layernorm", (double)M * d * 8,
+            launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln2_g, Lw.ln2_b, d, eps, M, H->stream));
     {
         Epi e = epi_store(H->f, H->fc_local, Lw.fc.bias);
         e.kind = EPI_GELU;
@@ -476,8 +482,12 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
         rc = linear(H, "linear_fc_gelu", Lw.fc, hin, M, e);
         if (rc) return rc;
     }
-    if (H->tp_size > 1) {
-        rc = tp_residual(H, "linear_mlp_proj", Lw.mproj, fin, M);
+    if (tp) {
+        // the next layer's first LayerNorm; after the last layer the final one runs on its own
+        // (prefill normalises only the last row of each sequence)
+        const bool last = layer + 1 == H->cfg.n_layer;
+        const LayerW* nx = last ? nullptr : &H->layers[layer + 1];
+        rc = tp_residual(H, "linear_mlp_proj", Lw.mproj, fin, M, 1, nx ? nx->ln1_g : nullptr, nx ? nx->ln1_b : nullptr);
     } else {
         Epi e = epi_store(H->x, d, Lw.mproj.bias);
         e.kind = EPI_RESID;
@@ -797,6 +807,7 @@ int do_decode(gpt2q_handle* H, const uint32_t* tok, const int32_t* pos, const in
 int check_device_error(gpt2q_handle* H) {
     int e = gemm_take_error(H->gemm, H->stream);
     if (e == 0) e = mk_take_error(H->mk, H->stream);
+    if (e == 0 && H->tp) e = tp_take_error(H->tp, H->stream);
     if (e > 0) return H->fail(GPT2Q_ETIMEOUT, "a bounded device-side wait timed out (error word " + std::to_string(e) + ")");
     if (e < 0) return H->fail(GPT2Q_ECUDA, "reading the device error word failed");
     return GPT2Q_OK;
@@ -999,10 +1010,9 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     H->d_pos = H->dalloc<int>((size_t)c.max_seqs * 4);
     H->d_slot = H->dalloc<int>((size_t)c.max_seqs * 4);
     H->d_genlog = H->dalloc<uint32_t>((size_t)c.max_seqs * c.n_ctx * 4);
-    if (tp_size > 1) H->tp_red = H->dalloc<float>(M * d * 4);
     if (!H->x || !H->h || !H->qb || !H->att || !H->f || !H->logits || !H->p_tok || !H->p_pos || !H->p_slot ||
         !H->p_lastrow || !H->p_lastpos || !H->p_tiles || !H->d_tok || !H->d_next || !H->d_pos || !H->d_slot ||
-        !H->d_genlog || (tp_size > 1 && !H->tp_red) || !H->h_hi || !H->h_lo || !H->att_hi || !H->att_lo ||
+        !H->d_genlog || !H->h_hi || !H->h_lo || !H->att_hi || !H->att_lo ||
         !H->f_hi || !H->f_lo || !H->best) {
         H->err = "cudaMalloc workspace";
         return bail(GPT2Q_EOOM);
@@ -1053,7 +1063,7 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
         }
     }
     if (tp_size > 1) {
-        H->tp = tp_create(tp_size, tp_rank, nccl_id, device);
+        H->tp = tp_create(tp_size, tp_rank, nccl_id, device, M * d);
         if (!H->tp || tp_last_error(H->tp)[0]) {
             H->err = std::string("NCCL init: ") + (H->tp ? tp_last_error(H->tp) : "failed");
             return bail(GPT2Q_ENCCL);
@@ -1332,7 +1342,9 @@ int gpt2q_info(gpt2q_handle* H, char* json, size_t cap) {
     const std::string head = std::string("{\"persistent_decode\": ") + (H->mk.enabled ? "true" : "false") +
                           ", \"persistent_why\": \"" + why + "\", \"persistent_ctas\": " +
                           std::to_string(H->mk.enabled ? MK_CS * H->mk.clusters : 0) +
-                          ", \"tensor_core\": " + (H->gemm.enabled ? "true" : "false");
+                          ", \"tensor_core\": " + (H->gemm.enabled ? "true" : "false") +
+                          ", \"tp_size\": " + std::to_string(H->tp_size) +
+                          ", \"tp_peer_mapped\": " + (tp_peer_mapped(H->tp) ? "true" : "false");
     std::string tr;
     if (H->mk.trace) {
         // phase stamps (ns since the first stamp of CTA 0) of the last persistent launch

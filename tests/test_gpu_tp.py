@@ -1,4 +1,4 @@
-"""Tensor-parallel handles (gpt2q_create_tp, NCCL all-reduce) on 2 GPUs vs one GPU.
+"""Tensor-parallel handles (gpt2q_create_tp, partial sums read from peer memory) on 2 GPUs vs one GPU.
 
 A 5-head model splits unevenly (3 + 2 heads), like GPT-2 XL's 25 heads over 2/4/8
 ranks. Ranks run as spawned processes, one per GPU; NVLS is off for the test.
@@ -34,9 +34,10 @@ def _rank(rank, world, uid, policy, q):
             nxt, lg = g.prefill(_prompts(), want_logits=True)
             toks = g.decode_steps(5, 2)
             nxt2, lg2 = g.decode(toks[-1], [p.size + 5 for p in _prompts()], want_logits=True)
-        q.put((rank, None, nxt, lg, toks, nxt2, lg2))
+            peer = g.info()["tp_peer_mapped"]
+        q.put((rank, None, nxt, lg, toks, nxt2, lg2, peer))
     except Exception as e:  # report instead of hanging the parent
-        q.put((rank, repr(e), None, None, None, None, None))
+        q.put((rank, repr(e), None, None, None, None, None, None))
 
 
 @pytest.mark.parametrize("policy", ["auto", "q4auto"])
@@ -70,7 +71,8 @@ def test_tp2_matches_single_gpu(policy):
         p.join(timeout=120)
     for r in (0, 1):
         assert res[r][1] is None, res[r][1]
-        _, _, n_r, lg_r, t_r, n2_r, lg2_r = res[r]
+        _, _, n_r, lg_r, t_r, n2_r, lg2_r, peer = res[r]
+        assert peer, "NVLink-connected GPUs: the partials are summed from peer memory"
         assert np.abs(lg_r - lg).max() <= 1e-3
         assert np.abs(lg2_r - lg2).max() <= 1e-3
         assert np.array_equal(n_r, nxt) and np.array_equal(t_r, toks) and np.array_equal(n2_r, nxt2)
