@@ -401,71 +401,100 @@ cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, cons
 }
 
 // ------------------------------------------------------------------ decode attention
-// One block of NW warps per (head, sequence); warp w takes keys w*32 + 128 i .. +31. Lane l
-// owns dims 2l, 2l+1 of q, K and V, so every K and V row is one coalesced 256-byte load; the
-// K and V rows of a warp's 32 keys are loaded in one burst. Scores: 2 FMAs per key and lane, then a 31-shuffle transpose-reduction leaves the
-// score of key t0 + l in lane l. The warp does an online-softmax update and the warps are
-// merged through shared memory.
+// One block of two warps per (head, sequence). The (sequence, head) K and V rows 0..pos are
+// contiguous, so thread 0 streams them with 1-D bulk copies, 64 keys (16 KB of K + 16 KB of V)
+// per shared-memory stage, two stages, each refilled as soon as both warps are done with it:
+// HBM stays busy for the whole kernel and the registers hold no loads in flight. Warp w
+// takes keys 32w..32w+31 of every chunk. Lane l owns dims 2l, 2l+1 of q, K and V (conflict-
+// free shared-memory reads); scores take 2 FMAs per key and lane, then a 31-shuffle
+// transpose-reduction leaves the score of key t0 + l in lane l. Each warp keeps an online
+// softmax; the two warps are merged through shared memory.
 // Semantics: softmax(q.K^T * scale) V over positions 0..pos (gpt2.rs:261-291).
-template <int NW>
-__global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* q, int ldq, KVGeom g,
-                                                         size_t layer_off, const int* __restrict__ slot,
-                                                         const int* __restrict__ pos, float* __restrict__ out,
-                                                         __half* __restrict__ ohi, __half* __restrict__ olo,
-                                                         int ldo, float scale) {
-    constexpr int HD = 64;
-    __shared__ float wm[NW], wl[NW];
-    __shared__ float wo[NW][HD];
-    tc::pdl_trigger();
-    tc::pdl_wait();
+constexpr int AD_HD = 64, AD_CH = 64, AD_NST = 2, AD_WARPS = 2;
+constexpr int AD_STAGE_FLOATS = 2 * AD_CH * AD_HD;  // K then V
+constexpr size_t AD_SMEM = (size_t)AD_NST * AD_STAGE_FLOATS * 4 + 64;
+
+__global__ void __launch_bounds__(AD_WARPS * 32) k_attn_decode(const float* q, int ldq, KVGeom g, size_t layer_off,
+                                                               const int* __restrict__ slot,
+                                                               const int* __restrict__ pos, float* __restrict__ out,
+                                                               __half* __restrict__ ohi, __half* __restrict__ olo,
+                                                               int ldo, float scale, int* err) {
+    extern __shared__ __align__(16) float ad_smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(ad_smem + AD_NST * AD_STAGE_FLOATS);
+    __shared__ float wm[AD_WARPS], wl[AD_WARPS];
+    __shared__ float wo[AD_WARPS][AD_HD];
     const int head = blockIdx.x, b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    tc::pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < AD_NST; ++s) tc::mbar_init(&full[s], 1);
+        tc::fence_mbar_init();
+    }
+    __syncthreads();
+    tc::pdl_wait();
     const int T = pos[b] + 1;
     const float* K = g.base + (size_t)slot[b] * g.slot_stride + layer_off + (size_t)head * g.head_stride;
     const float* V = K + g.sel_stride;
+    const int nch = (T + AD_CH - 1) / AD_CH;
+    auto issue = [&](int c) {  // thread 0: chunk c into stage c % AD_NST
+        float* st = ad_smem + (c % AD_NST) * AD_STAGE_FLOATS;
+        const int rows = min(AD_CH, T - c * AD_CH);
+        const uint32_t bytes = (uint32_t)rows * AD_HD * 4;
+        tc::mbar_arrive_expect_tx(&full[c % AD_NST], 2 * bytes);
+        tc::bulk_load_1d(st, K + (size_t)c * AD_CH * AD_HD, bytes, &full[c % AD_NST]);
+        tc::bulk_load_1d(st + AD_CH * AD_HD, V + (size_t)c * AD_CH * AD_HD, bytes, &full[c % AD_NST]);
+    };
+    if (threadIdx.x == 0)
+        for (int c = 0; c < nch && c < AD_NST; ++c) issue(c);
+    const float2 qv = __ldcg(reinterpret_cast<const float2*>(q + (size_t)b * ldq + head * AD_HD) + lane);
 
     float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
-    const float2 qv = __ldcg(reinterpret_cast<const float2*>(q + (size_t)b * ldq + head * HD) + lane);
-    for (int t0 = warp * 32; t0 < T; t0 += 32 * NW) {
-        const int nv = min(32, T - t0);
-        // one burst: dims 2l, 2l+1 of the 32 K rows and the 32 V rows (rows past T repeat the last)
-        float2 kk[32], vv[32];
+    bool ok = true;
+    for (int c = 0; c < nch; ++c) {
+        const int s = c % AD_NST;
+        ok = ok && tc::mbar_wait(&full[s], (uint32_t)((c / AD_NST) & 1), err);
+        const float* Ks = ad_smem + s * AD_STAGE_FLOATS + warp * 32 * AD_HD;
+        const float* Vs = Ks + AD_CH * AD_HD;
+        const int t0 = c * AD_CH + warp * 32;
+        const int nv = min(32, T - t0);  // may be <= 0 for the last chunk
+        if (nv > 0) {
+            float sc[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const size_t row = (size_t)(t0 + min(j, nv - 1)) * HD;
-            kk[j] = __ldcg(reinterpret_cast<const float2*>(K + row) + lane);
-            vv[j] = __ldcg(reinterpret_cast<const float2*>(V + row) + lane);
-        }
-        float sc[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sc[j] = fmaf(qv.y, kk[j].y, qv.x * kk[j].x);
-        // transpose-reduction: after the step with offset o, sc[i] holds key (keys of this
-        // lane's half) + i summed over the lanes that differ in bits >= o
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int i = 0; i < o; ++i) {
-                const float send = upper ? sc[i] : sc[i + o];
-                const float keep = upper ? sc[i + o] : sc[i];
-                sc[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            for (int j = 0; j < 32; ++j) {
+                const float2 kk = reinterpret_cast<const float2*>(Ks + min(j, nv - 1) * AD_HD)[lane];
+                sc[j] = fmaf(qv.y, kk.y, qv.x * kk.x);
             }
-        }
-        const int t = t0 + lane;
-        const float s = (t < T) ? sc[0] * scale : -INFINITY;
-        const float mnew = fmaxf(m, warp_max(s));
-        const float corr = expf(m - mnew);
-        const float p = (t < T) ? expf(s - mnew) : 0.f;
-        l = l * corr + warp_sum(p);
-        o0 *= corr;
-        o1 *= corr;
+            // transpose-reduction: after the step with offset o, sc[i] holds key (keys of this
+            // lane's half) + i summed over the lanes that differ in bits >= o
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const float pj = __shfl_sync(0xffffffffu, p, j);  // 0 for j >= nv
-            o0 = fmaf(pj, vv[j].x, o0);
-            o1 = fmaf(pj, vv[j].y, o1);
+            for (int o = 16; o >= 1; o >>= 1) {
+                const bool upper = (lane & o) != 0;
+#pragma unroll
+                for (int i = 0; i < o; ++i) {
+                    const float send = upper ? sc[i] : sc[i + o];
+                    const float keep = upper ? sc[i + o] : sc[i];
+                    sc[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            const bool valid = lane < nv;
+            const float sv = valid ? sc[0] * scale : -INFINITY;
+            const float mnew = fmaxf(m, warp_max(sv));
+            const float corr = expf(m - mnew);
+            const float p = valid ? expf(sv - mnew) : 0.f;
+            l = l * corr + warp_sum(p);
+            o0 *= corr;
+            o1 *= corr;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float pj = __shfl_sync(0xffffffffu, p, j);  // 0 for j >= nv
+                const float2 vv = reinterpret_cast<const float2*>(Vs + min(j, nv - 1) * AD_HD)[lane];
+                o0 = fmaf(pj, vv.x, o0);
+                o1 = fmaf(pj, vv.y, o1);
+            }
+            m = mnew;
         }
-        m = mnew;
+        __syncthreads();  // both warps are done with stage s
+        if (threadIdx.x == 0 && c + AD_NST < nch) issue(c + AD_NST);
     }
     if (lane == 0) {
         wm[warp] = m;
@@ -474,13 +503,13 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* q, int ldq
     wo[warp][2 * lane] = o0;
     wo[warp][2 * lane + 1] = o1;
     __syncthreads();
-    if (threadIdx.x < HD) {
+    if (threadIdx.x < AD_HD) {
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w]);
+        for (int w = 0; w < AD_WARPS; ++w) M = fmaxf(M, wm[w]);
         float L = 0.f, O = 0.f;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) {
+        for (int w = 0; w < AD_WARPS; ++w) {
             if (wm[w] != -INFINITY) {
                 const float f = expf(wm[w] - M);
                 L += wl[w] * f;
@@ -488,7 +517,7 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* q, int ldq
             }
         }
         const float r = O / L;
-        const size_t o = (size_t)b * ldo + head * HD + threadIdx.x;
+        const size_t o = (size_t)b * ldo + head * AD_HD + threadIdx.x;
         out[o] = r;
         if (ohi) split_hl(r, ohi[o], olo[o]);
     }
@@ -496,11 +525,16 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode(const float* q, int ldq
 
 cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t layer_off, const int* slot,
                                const int* pos, float* out, __half* ohi, __half* olo, int ldo, int n_head, int B,
-                               float scale, cudaStream_t st) {
+                               float scale, int* err, cudaStream_t st) {
     if (B <= 0) return cudaSuccess;
-    if (g.hd != 64) return cudaErrorInvalidValue;
-    return launch_pdl(k_attn_decode<4>, dim3(n_head, B), dim3(128), 0, st, q, ldq, g, layer_off, slot, pos, out, ohi,
-                      olo, ldo, scale);
+    if (g.hd != AD_HD) return cudaErrorInvalidValue;
+    static bool attr = [] {
+        return cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AD_SMEM) ==
+               cudaSuccess;
+    }();
+    if (!attr) return cudaErrorInvalidValue;
+    return launch_pdl(k_attn_decode, dim3(n_head, B), dim3(AD_WARPS * 32), AD_SMEM, st, q, ldq, g, layer_off, slot,
+                      pos, out, ohi, olo, ldo, scale, err);
 }
 
 // ------------------------------------------------------------------ prefill attention

@@ -30,9 +30,10 @@ cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y,
 // out = epilogue(X[M][K] . W^T) on CUDA cores (fp32 FMA, weights dequantised in registers).
 cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, const Epi& e,
                                cudaStream_t st);
+// err: device error word set when a bounded wait for the staged K/V rows gives up.
 cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t layer_off, const int* slot,
                                const int* pos, float* out, __half* ohi, __half* olo, int ldo, int n_head, int B,
-                               float scale, cudaStream_t st);
+                               float scale, int* err, cudaStream_t st);
 cudaError_t launch_attn_prefill(const float* q, int ldq, const KVGeom& g, size_t layer_off,
                                 const AttnTile* tiles, int n_tiles, float* out, __half* ohi, __half* olo, int ldo,
                                 int n_head, float scale, cudaStream_t st);

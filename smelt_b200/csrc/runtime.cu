@@ -121,6 +121,7 @@ struct gpt2q_handle {
     // fp16 hi/lo copies of the linear inputs (h: LayerNorm out, att: attention out, f: GELU out)
     __half *h_hi = nullptr, *h_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr, *f_hi = nullptr, *f_lo = nullptr;
     unsigned long long* best = nullptr;  // argmax slots, one per sequence
+    int* kerr = nullptr;  // device error word of the CUDA-core kernels' bounded waits
     // prefill scratch
     uint32_t* p_tok = nullptr;
     int *p_pos = nullptr, *p_slot = nullptr, *p_lastrow = nullptr, *p_lastpos = nullptr;
@@ -508,7 +509,7 @@ int enqueue_decode(gpt2q_handle* H, int B) {
             RUN("attn_decode", kv_bytes + (double)B * H->d_local * 8,
                 launch_attn_decode(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->d_slot,
                                    H->d_pos, H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, B, scale,
-                                   H->stream));
+                                   H->kerr, H->stream));
             return GPT2Q_OK;
         });
         if (rc) return rc;
@@ -808,6 +809,16 @@ int check_device_error(gpt2q_handle* H) {
     int e = gemm_take_error(H->gemm, H->stream);
     if (e == 0) e = mk_take_error(H->mk, H->stream);
     if (e == 0 && H->tp) e = tp_take_error(H->tp, H->stream);
+    if (e == 0 && H->kerr) {
+        int h = 0;
+        if (cudaMemcpyAsync(&h, H->kerr, 4, cudaMemcpyDeviceToHost, H->stream) != cudaSuccess ||
+            cudaStreamSynchronize(H->stream) != cudaSuccess)
+            e = -1;
+        else if (h != 0) {
+            cudaMemsetAsync(H->kerr, 0, 4, H->stream);
+            e = h;
+        }
+    }
     if (e > 0) return H->fail(GPT2Q_ETIMEOUT, "a bounded device-side wait timed out (error word " + std::to_string(e) + ")");
     if (e < 0) return H->fail(GPT2Q_ECUDA, "reading the device error word failed");
     return GPT2Q_OK;
@@ -999,6 +1010,7 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     H->f_hi = H->dalloc<__half>(M * H->fc_local * 2);
     H->f_lo = H->dalloc<__half>(M * H->fc_local * 2);
     H->best = H->dalloc<unsigned long long>((size_t)c.max_seqs * 8);
+    H->kerr = H->dalloc<int>(4);
     H->p_tok = H->dalloc<uint32_t>(M * 4);
     H->p_pos = H->dalloc<int>(M * 4);
     H->p_slot = H->dalloc<int>(M * 4);
@@ -1013,12 +1025,13 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     if (!H->x || !H->h || !H->qb || !H->att || !H->f || !H->logits || !H->p_tok || !H->p_pos || !H->p_slot ||
         !H->p_lastrow || !H->p_lastpos || !H->p_tiles || !H->d_tok || !H->d_next || !H->d_pos || !H->d_slot ||
         !H->d_genlog || !H->h_hi || !H->h_lo || !H->att_hi || !H->att_lo ||
-        !H->f_hi || !H->f_lo || !H->best) {
+        !H->f_hi || !H->f_lo || !H->best || !H->kerr) {
         H->err = "cudaMalloc workspace";
         return bail(GPT2Q_EOOM);
     }
     if (cudaMemsetAsync(H->d_genlog, 0xff, (size_t)c.max_seqs * c.n_ctx * 4, H->stream) != cudaSuccess ||
-        cudaMemsetAsync(H->best, 0, (size_t)c.max_seqs * 8, H->stream) != cudaSuccess)
+        cudaMemsetAsync(H->best, 0, (size_t)c.max_seqs * 8, H->stream) != cudaSuccess ||
+        cudaMemsetAsync(H->kerr, 0, 4, H->stream) != cudaSuccess)
         return bail(GPT2Q_ECUDA);
     {
         const int Kmax = std::max(std::max(d, H->fc_local), H->d_local);
