@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
             for (int i = 0; i < nkb; ++i) {
                 if (PRESPLIT) {
                     const int s = i % C::OS, use = i / C::OS;
-                    if (!tc::mbar_wait(&op_empty[s], (use & 1) ^ 1, p.err)) break;
+                    if (!tc::mbar_wait_spin(&op_empty[s], (use & 1) ^ 1, p.err)) break;
                     tc::mbar_arrive_expect_tx(&op_full[s], 2 * C::A_BYTES);
                     uint8_t* a = smem + C::OFF_A + s * 2 * C::A_BYTES;
                     tc::tma_load_2d(a, &tm_w, (kb0 + i) * BK, n0, &op_full[s]);
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
             int issued = 0;
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % C::XS, use = i / C::XS;
-                if (!tc::mbar_wait(&x_empty[s], (use & 1) ^ 1, p.err)) break;
+                if (!tc::mbar_wait_spin(&x_empty[s], (use & 1) ^ 1, p.err)) break;
                 tc::mbar_arrive_expect_tx(&x_full[s], 2 * C::B_BYTES);
                 const int kx = (kb0 + i) * BK;
                 uint8_t* b = smem + C::OFF_B + s * 2 * C::B_BYTES;
@@ -417,10 +417,10 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % C::OS, use = i / C::OS;
                 const int xs = i % C::XS, xuse = i / C::XS;
-                if (!(PRESPLIT ? tc::mbar_wait(&op_full[s], use & 1, p.err)
-                               : tc::mbar_wait_spin(&op_full[s], use & 1, p.err)))
-                    break;
-                if (!tc::mbar_wait(&x_full[xs], xuse & 1, p.err)) break;
+                // single-thread polls: a suspended try_wait may resume well after the phase
+                // completes, leaving the tensor pipe idle
+                if (!tc::mbar_wait_spin(&op_full[s], use & 1, p.err)) break;
+                if (!tc::mbar_wait_spin(&x_full[xs], xuse & 1, p.err)) break;
                 if (i == 0) tc_stamp(p, 6);
                 tc::tc_fence_after();
                 const uint32_t a_hi = tc::smem_u32(smem + C::OFF_A + s * 2 * C::A_BYTES);
