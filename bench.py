@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-steps", type=int, default=24)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's sequence count (profiling)")
+    ap.add_argument("--profile-one-step", action="store_true",
+                    help="after the warm-up, run exactly one decode step between cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off) and exit")
     return ap.parse_args()
 
 
@@ -547,6 +550,14 @@ def main():
 
     run_steps(max(args.warmup, 3))
     barrier()
+    if args.profile_one_step:
+        torch.cuda.profiler.start()
+        run_steps(1)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"profiled": "one decode step", "config": args.config, "batch": n_local}))
+        return
 
     # ---- timed region: K device-resident decode steps ----
     gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
