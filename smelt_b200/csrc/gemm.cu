@@ -682,6 +682,165 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
     if (warp == 0) tc::tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// ---------------------------------------------------------------- persistent prefill form
+// Compute-bound prefill tiles (BN = 256, exact fp16 hi/lo weight copies, no split-K): one CTA
+// per SM walks the tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... (weight-row tiles
+// fastest, so the CTAs running together share activation tiles in L2). The two operand rings
+// run on across tiles, and the fp32 accumulator is double-buffered in TMEM (2 x 256 columns):
+// the epilogue warps drain tile j while the MMAs of tile j + 1 run.
+constexpr int PB_BN = 256, PB_OS = 2, PB_XS = 2;
+constexpr int PB_A_BYTES = BM * 128, PB_B_BYTES = PB_BN * 128;
+constexpr int PB_OFF_B = PB_OS * 2 * PB_A_BYTES;
+constexpr int PB_OFF_BAR = PB_OFF_B + PB_XS * 2 * PB_B_BYTES;
+constexpr int PB_N_BAR = 2 * PB_OS + 2 * PB_XS + 4;
+constexpr int PB_SMEM = PB_OFF_BAR + PB_N_BAR * 8 + 16 + 1024;
+static_assert(PB_SMEM <= 232448, "shared memory per CTA");
+
+__global__ void __launch_bounds__(THREADS, 1)
+    k_linear_tc_persistent(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wlo,
+                           const __grid_constant__ CUtensorMap tm_xhi, const __grid_constant__ CUtensorMap tm_xlo,
+                           TcParams p, int n_row_tiles, int n_tiles) {
+    extern __shared__ __align__(1024) uint8_t smem_raw_[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PB_OFF_BAR);
+    uint64_t* op_full = bars;
+    uint64_t* op_empty = op_full + PB_OS;
+    uint64_t* x_full = op_empty + PB_OS;
+    uint64_t* x_empty = x_full + PB_XS;
+    uint64_t* acc_full = x_empty + PB_XS;  // [2]
+    uint64_t* acc_empty = acc_full + 2;    // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PB_OFF_BAR + PB_N_BAR * 8);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nkb = p.nkb_total;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < PB_OS; ++i) {
+            tc::mbar_init(&op_full[i], 1);
+            tc::mbar_init(&op_empty[i], 1);
+        }
+        for (int i = 0; i < PB_XS; ++i) {
+            tc::mbar_init(&x_full[i], 1);
+            tc::mbar_init(&x_empty[i], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&acc_full[b], 1);
+            tc::mbar_init(&acc_empty[b], 128);
+        }
+        tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, 2 * PB_BN);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    tc::pdl_trigger();  // after the TMEM allocation (see k_linear_tc)
+
+    if (warp == 0) {
+        // ---------------- weight tiles (exact fp16 hi/lo copies) ----------------
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_w);
+            tc::prefetch_tmap(&tm_wlo);
+            int it = 0;
+            for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+                const int n0 = (t % n_row_tiles) * BM;
+                for (int i = 0; i < nkb; ++i, ++it) {
+                    const int s = it % PB_OS, use = it / PB_OS;
+                    if (!tc::mbar_wait_spin(&op_empty[s], (use & 1) ^ 1, p.err)) break;
+                    tc::mbar_arrive_expect_tx(&op_full[s], 2 * PB_A_BYTES);
+                    uint8_t* a = smem + s * 2 * PB_A_BYTES;
+                    tc::tma_load_2d(a, &tm_w, i * BK, n0, &op_full[s]);
+                    tc::tma_load_2d(a + PB_A_BYTES, &tm_wlo, i * BK, n0, &op_full[s]);
+                }
+            }
+        }
+    } else if (warp == 6) {
+        // ---------------- activation tiles ----------------
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_xhi);
+            tc::prefetch_tmap(&tm_xlo);
+            tc::pdl_wait();  // X was written by the previous kernel
+            int it = 0;
+            for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+                const int m0 = (t / n_row_tiles) * PB_BN;
+                for (int i = 0; i < nkb; ++i, ++it) {
+                    const int s = it % PB_XS, use = it / PB_XS;
+                    if (!tc::mbar_wait_spin(&x_empty[s], (use & 1) ^ 1, p.err)) break;
+                    tc::mbar_arrive_expect_tx(&x_full[s], 2 * PB_B_BYTES);
+                    uint8_t* b = smem + PB_OFF_B + s * 2 * PB_B_BYTES;
+                    tc::tma_load_2d(b, &tm_xhi, i * BK, m0, &x_full[s]);
+                    tc::tma_load_2d(b + PB_B_BYTES, &tm_xlo, i * BK, m0, &x_full[s]);
+                }
+            }
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_f16_f32(BM, PB_BN);
+            int it = 0, j = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++j) {
+                const int buf = j & 1;
+                // the epilogue has drained this accumulator (tile j - 2)
+                ok = tc::mbar_wait_spin(&acc_empty[buf], ((j >> 1) & 1) ^ 1, p.err);
+                tc::tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * PB_BN);
+                for (int i = 0; i < nkb && ok; ++i, ++it) {
+                    const int s = it % PB_OS, use = it / PB_OS;
+                    const int xs = it % PB_XS, xuse = it / PB_XS;
+                    ok = tc::mbar_wait_spin(&op_full[s], use & 1, p.err) && tc::mbar_wait_spin(&x_full[xs], xuse & 1, p.err);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    const uint32_t a_hi = tc::smem_u32(smem + s * 2 * PB_A_BYTES), a_lo = a_hi + PB_A_BYTES;
+                    const uint32_t b_hi = tc::smem_u32(smem + PB_OFF_B + xs * 2 * PB_B_BYTES), b_lo = b_hi + PB_B_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint32_t ko = kk * 32;
+                        const uint64_t dah = tc::desc_sw128(a_hi + ko), dal = tc::desc_sw128(a_lo + ko);
+                        const uint64_t dbh = tc::desc_sw128(b_hi + ko), dbl = tc::desc_sw128(b_lo + ko);
+                        tc::mma_f16(d, dah, dbh, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                        tc::mma_f16(d, dah, dbl, idesc, 1u);
+                        tc::mma_f16(d, dal, dbh, idesc, 1u);
+                    }
+                    tc::mma_commit(&op_empty[s]);
+                    tc::mma_commit(&x_empty[xs]);
+                }
+                tc::mma_commit(&acc_full[buf]);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 1-4): TMEM -> fused epilogue, one tile at a time ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+        tc::pdl_wait();  // outputs / residual inputs belong to earlier kernels
+        int j = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++j) {
+            const int buf = j & 1;
+            const int n0 = (t % n_row_tiles) * BM, m0 = (t / n_row_tiles) * PB_BN;
+            const int nn = n0 + row;
+            const float bias_v = (p.epi.bias && nn < p.w.rows) ? __ldg(p.epi.bias + nn) : 0.f;
+            const bool ok = tc::mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), p.err);
+            tc::tc_fence_after();
+            const int mend = min(p.M, m0 + PB_BN);
+#pragma unroll 1
+            for (int c0 = 0; c0 < PB_BN; c0 += 32) {
+                if (m0 + c0 >= mend) break;  // warp-uniform
+                float v[32];
+                tc::tmem_ld32(taddr + (uint32_t)(buf * PB_BN + c0), v);
+                epi_chunk<32>(p.epi, nn, ok && nn < p.w.rows, v, m0 + c0, 1, mend, p.post, nullptr, &bias_v);
+            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&acc_empty[buf]);  // this accumulator may be overwritten
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, 2 * PB_BN);
+}
+
 // One-time exact split of a quantised weight for the prefill path: w' = deq(w) * 2^P,
 // hi = f16(w'), lo = f16(w' - hi), both [rows][cols].
 __global__ void k_presplit_weight(QW w, float pre, __half* __restrict__ hi, __half* __restrict__ lo) {
@@ -757,6 +916,28 @@ cudaError_t launch_tc(const CUtensorMap& tw, const CUtensorMap& twlo, const CUte
     cfg.attrs = attrs;
     cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, kern, tw, twlo, txh, txl, tp);
+}
+
+cudaError_t launch_persistent(const CUtensorMap& tw, const CUtensorMap& twlo, const CUtensorMap& txh,
+                              const CUtensorMap& txl, const TcParams& tp, int n_row_tiles, int n_tiles, cudaStream_t st) {
+    static int sms = [] {
+        int dev = 0, n = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        return n;
+    }();
+    cudaError_t e = cudaFuncSetAttribute(k_linear_tc_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_SMEM);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min(n_tiles, sms));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = PB_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_linear_tc_persistent, tw, twlo, txh, txl, tp, n_row_tiles, n_tiles);
 }
 
 // Clusters of `cs` CTAs of this kernel that the device holds at once (cached per size).
@@ -989,6 +1170,10 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
         tp.trace = gs.trace;
         gs.traced = true;
         gs.trace_grid = grid;
+    }
+    if (presplit && BN == PB_BN && splits == 1 && !tp.trace) {
+        static const bool off = std::getenv("GPT2Q_TC_NO_PERSISTENT") != nullptr;  // tuning
+        if (!off) return launch_persistent(wt.hi, wt.lo, *xh, *xl, tp, n_tiles, n_tiles * m_tiles, st);
     }
     if (presplit) {
         if (w.atom == ATOM_Q8) return launch_bn<ATOM_Q8, true>(BN, wt.hi, wt.lo, *xh, *xl, tp, grid, st);

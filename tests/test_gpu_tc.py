@@ -120,3 +120,25 @@ def test_tc_split_k_exchange_shapes_match_cuda_core_path(batch, monkeypatch):
     a, b = res["simt"], res["tc"]
     assert np.abs(a[2] - b[2]).max() <= 1e-3
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+def test_persistent_prefill_gemm_matches_per_tile_launch(monkeypatch):
+    """4096 prompt tokens: the 1024-row c_fc (8 x 16 = 128 tiles) runs in the persistent form
+    (one CTA per SM walking tiles, double-buffered TMEM accumulator). Same MMAs in the same
+    order as the one-tile-per-CTA launch, so the logits must be identical; and the oracle agrees."""
+    pk = make_pack(MINI, "auto", 0, 0.02)
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, MINI.vocab, 128).astype(np.uint32) for _ in range(32)]
+    res = {}
+    for mode in ("persistent", "per_tile"):
+        monkeypatch.setenv("GPT2Q_TC_NO_PERSISTENT", "1" if mode == "per_tile" else "")
+        if mode == "persistent":
+            monkeypatch.delenv("GPT2Q_TC_NO_PERSISTENT")
+        with Gpu(pk, max_seqs=len(prompts), max_tokens=4096) as g:
+            res[mode] = g.prefill(prompts, want_logits=True)
+    assert np.array_equal(res["persistent"][0], res["per_tile"][0])
+    assert np.array_equal(res["persistent"][1], res["per_tile"][1])
+    eng = oracle_engine(pk)
+    for i in (0, 31):
+        ref = oracle_prefix_logits(eng, prompts[i])[-1]
+        assert np.abs(res["persistent"][1][i] - ref).max() <= 1e-3
