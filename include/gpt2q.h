@@ -124,6 +124,15 @@ int gpt2q_decode_steps(gpt2q_handle* h, int steps, uint32_t* out_tokens);
 int gpt2q_generate_greedy(gpt2q_handle* h, const uint32_t* tokens, const int32_t* seq_offsets,
                           int n_seq, int steps, uint32_t* out);
 
+/* Teacher-forced negative log-likelihood per token of ids[0..n-1]
+ * (nll_per_token, gpt2.rs:347-364): the mean over positions p = 0..n-2 of
+ * -(logit[ids[p+1]] - max) + ln(sum exp(logit - max)), with the log-sum-exp in f64.
+ * One prefill over the sequence in cache slot `slot` (its KV cache is overwritten),
+ * the head on every position, and the per-position terms on the device: logits
+ * never leave the GPU; only the n-1 f64 terms are read back and summed in order.
+ * 2 <= n <= min(n_ctx, max_tokens). */
+int gpt2q_nll(gpt2q_handle* h, const uint32_t* ids, int n, int slot, double* out_nll);
+
 /* Dequantize a weight tensor exactly as Engine::vec_f32 (gpt2.rs:121-142)
  * into host `out` (n floats). Computed on the device from the uploaded bytes. */
 int gpt2q_dequant(gpt2q_handle* h, const char* name, float* out, uint64_t n);

@@ -20,7 +20,7 @@ EXPORTS = [
     "gpt2q_step", "gpt2q_decode", "gpt2q_prefill", "gpt2q_decode_steps", "gpt2q_generate_greedy",
     "gpt2q_dequant", "gpt2q_launches", "gpt2q_set_stream", "gpt2q_sync", "gpt2q_profile",
     "gpt2q_profile_read", "gpt2q_profile_kernels", "gpt2q_info", "gpt2q_argmax_noalloc", "gpt2q_rng_new", "gpt2q_rng_normal_f32", "gpt2q_rng_below",
-    "gpt2q_quantize_q8", "gpt2q_quantize_q4",
+    "gpt2q_quantize_q8", "gpt2q_quantize_q4", "gpt2q_nll",
 ]
 
 
@@ -88,6 +88,8 @@ def load(path: str | None = None):
     lib.gpt2q_set_stream.restype = C.c_int
     lib.gpt2q_sync.argtypes = [_hp]
     lib.gpt2q_sync.restype = C.c_int
+    lib.gpt2q_nll.argtypes = [_hp, _u32p, C.c_int, C.c_int, C.POINTER(C.c_double)]
+    lib.gpt2q_nll.restype = C.c_int
     lib.gpt2q_profile.argtypes = [_hp, C.c_int]
     lib.gpt2q_profile.restype = C.c_int
     lib.gpt2q_profile_read.argtypes = [_hp, C.c_char_p, C.c_size_t]

@@ -1,26 +1,27 @@
 // Causal prefill attention on the tensor cores (tcgen05 / TMEM), one CTA per
-// (128-query tile, head).
+// (128-query tile, head), two CTAs per SM (97 KB shared memory, 256 TMEM columns each), so
+// one CTA's softmax and operand conversion overlap the other's MMAs.
 //
-// Per key block of 128 positions:
-//   S  = (Q * 2^-3) K^T          tcgen05.mma kind::f16, M = 128 queries, N = 128 keys, K = 64
+// Per key block of 64 positions:
+//   S  = (Q * 2^-3) K^T          tcgen05.mma kind::f16, M = 128 queries, N = 64 keys, K = 64
 //   P  = exp(S - m_new)          one thread per query row (TMEM lane), online softmax in fp32
-//   PV = P V                     tcgen05.mma, M = 128, N = 64 (head dim), K = 128 keys
+//   PV = P V                     tcgen05.mma, M = 128, N = 64 (head dim), K = 64 keys
 //   O  = O * exp(m_old - m_new) + PV   (O in registers)
 // Both products use the fp16x3 split of gemm.cu: every fp32 operand x is held as
 // x_hi + x_lo (fp16 pair, ~22 bits) and A_hi B_hi + A_hi B_lo + A_lo B_hi accumulate in fp32
 // TMEM, so scores and outputs keep fp32-class accuracy (the dropped lo*lo term is ~2^-22
 // relative). B_hi and B_lo sit next to each other, so A_hi [B_hi; B_lo] is one MMA of twice
 // the width and each k-step issues two MMAs instead of three (the MMA issue rate, not its
-// width, bounds these tiles). The pair only keeps 22 bits while lo is a normal fp16, so every operand is first
-// scaled by a power of two that brings its largest magnitude to [2^13, 2^14): Q per query row,
-// K and V per key block, P by 2^14. The scales are undone exactly on S and PV, together with
-// the attention scale 1/sqrt(64) = 2^-3.
+// width, bounds these tiles). The pair only keeps 22 bits while lo is a normal fp16, so every
+// operand is first scaled by a power of two that brings its largest magnitude to
+// [2^13, 2^14): Q per query row, K and V per key block, P by 2^14. The scales are undone
+// exactly on S and PV, together with the attention scale 1/sqrt(64) = 2^-3.
 //
 // Operands are K-major tiles with the 128-byte swizzle (rows of 64 fp16; 8-row groups 1024
-// bytes apart), as in gemm.cu: Q [128 q][64], K [128 keys][64], P [128 q][128 keys] as two
-// 64-key chunks, and V^T [64 dims][128 keys] as two 64-key chunks (V is transposed while it
-// is converted). Reference semantics: gpt2.rs:261-291 (softmax(q.K^T / sqrt(hd)) . V over
-// positions 0..t), per query position t of the prompt.
+// bytes apart), as in gemm.cu: Q [128 q][64], K [64 keys][64], P [128 q][64 keys] and
+// V^T [64 dims][64 keys] (V is transposed while it is converted). Threads 0-63 convert the K
+// rows, threads 64-127 the V rows of a block. Reference semantics: gpt2.rs:261-291
+// (softmax(q.K^T / sqrt(hd)) . V over positions 0..t), per query position t of the prompt.
 #include <cuda_fp16.h>
 
 #include "kernels.h"
@@ -30,27 +31,22 @@ namespace gpt2q {
 namespace {
 
 constexpr int QT = 128;  // queries per CTA (TMEM lanes)
-constexpr int KB = 128;  // keys per block
+constexpr int KB = 64;   // keys per block
 constexpr int HD = 64;
 constexpr int THREADS = 128;
-constexpr int TILE_Q = QT * 128;        // bytes of one [128][64] fp16 tile
-constexpr int TILE_VT = HD * 128;       // bytes of one [64][64] fp16 tile
+constexpr int TILE_Q = QT * 128;   // bytes of one [128][64] fp16 tile
+constexpr int TILE_K = KB * 128;   // bytes of one [64][64] fp16 tile
 constexpr int OFF_QH = 0, OFF_QL = OFF_QH + TILE_Q;
-// K_hi and K_lo adjacent: [K_hi; K_lo] is one 256-row B operand
-constexpr int OFF_KH = OFF_QL + TILE_Q, OFF_KL = OFF_KH + TILE_Q;
-// V^T: per 64-key chunk c, V^T_hi then V^T_lo (adjacent: one 128-row B operand)
-constexpr int OFF_V = OFF_KL + TILE_Q;
-constexpr int OFF_PH = OFF_V + 4 * TILE_VT, OFF_PL = OFF_PH + 2 * TILE_Q;
-// raw fp32 K and V rows of the next key block, brought in by bulk copies while this block
-// is computed
-constexpr int RAW_BYTES = KB * HD * 4;
-constexpr int OFF_RK = OFF_PL + 2 * TILE_Q, OFF_RV = OFF_RK + RAW_BYTES;
-constexpr int OFF_BAR = OFF_RV + RAW_BYTES;
+// K_hi and K_lo adjacent: [K_hi; K_lo] is one 128-row B operand; same for V^T
+constexpr int OFF_KH = OFF_QL + TILE_Q, OFF_KL = OFF_KH + TILE_K;
+constexpr int OFF_VH = OFF_KL + TILE_K, OFF_VL = OFF_VH + TILE_K;
+constexpr int OFF_PH = OFF_VL + TILE_K, OFF_PL = OFF_PH + TILE_Q;
+constexpr int OFF_BAR = OFF_PL + TILE_Q;
 constexpr int SMEM = OFF_BAR + 64 + 1024;  // barriers, TMEM slot, block-max scratch, alignment slack
-static_assert(SMEM <= 232448, "shared memory per CTA");
-// S: columns 0..255 (Q_hi K_hi | Q_hi K_lo, Q_lo K_hi added to the first half);
-// PV: 256..383 (P_hi V_hi | P_hi V_lo, P_lo V_hi added to the first half)
-constexpr uint32_t TMEM_COLS = 512;
+static_assert(SMEM <= 232448 / 2 - 1024, "two CTAs per SM");
+// S: columns 0..127 (Q_hi K_hi | Q_hi K_lo, Q_lo K_hi added to the first half);
+// PV: 128..255 (P_hi V_hi | P_hi V_lo, P_lo V_hi added to the first half)
+constexpr uint32_t TMEM_COLS = 256;
 
 // Byte offset of 16-byte chunk c (8 fp16) of row r in a 128-byte-swizzled K-major tile.
 __device__ __forceinline__ uint32_t sw_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
@@ -95,13 +91,20 @@ __device__ __forceinline__ float row_absmax(const float* v) {
     return m;
 }
 
-// Maximum over the 128 threads of the CTA (red: 4 floats of shared memory).
-__device__ __forceinline__ float block_max(float m, float* red) {
+// Maxima over the 128 threads of the CTA of two values at once (red: 8 floats of shared memory).
+__device__ __forceinline__ float2 block_max2(float a, float b, float* red) {
 #pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    for (int o = 16; o; o >>= 1) {
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        red[threadIdx.x >> 5] = a;
+        red[4 + (threadIdx.x >> 5)] = b;
+    }
     __syncthreads();
-    const float r = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float2 r = make_float2(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])),
+                                 fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
     __syncthreads();  // red is reused by the next call
     return r;
 }
@@ -119,7 +122,7 @@ __device__ __forceinline__ void load_row64(const float* src, bool ok, float* v) 
     }
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, 2)
     k_attn_prefill_tc(const float* q, int ldq, KVGeom g, size_t layer_off,
                       const AttnTile* __restrict__ tiles, float* __restrict__ out, __half* __restrict__ ohi,
                       __half* __restrict__ olo, int ldo, int* err) {
@@ -127,15 +130,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
     uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* bar_pv = bar_s + 1;
-    uint64_t* bar_raw = bar_s + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 3);
-    float* red = reinterpret_cast<float*>(bar_s + 4);  // [4]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
+    float* red = reinterpret_cast<float*>(bar_s + 3);  // [8]
     const int tid = threadIdx.x, warp = tid >> 5;
 
     if (tid == 0) {
         tc::mbar_init(bar_s, 1);
         tc::mbar_init(bar_pv, 1);
-        tc::mbar_init(bar_raw, 1);
         tc::fence_mbar_init();
     }
     if (warp == 0) {
@@ -176,81 +177,38 @@ __global__ void __launch_bounds__(THREADS, 1)
     float m = -INFINITY, l = 0.f;
     const int kend = min(tile.T, tile.q0 + QT);  // keys past the last query of the tile are masked
     const int nkb = (kend + KB - 1) / KB;
-    // rows k0 .. min(k0 + KB, kend) - 1 of K and V (contiguous per sequence and head)
-    auto issue_raw = [&](int kb) {
-        const int k0 = kb * KB;
-        const uint32_t bytes = (uint32_t)(min(KB, kend - k0) * HD * 4);
-        tc::mbar_arrive_expect_tx(bar_raw, 2 * bytes);
-        tc::bulk_load_1d(smem + OFF_RK, Kc + (size_t)k0 * HD, bytes, bar_raw);
-        tc::bulk_load_1d(smem + OFF_RV, Vc + (size_t)k0 * HD, bytes, bar_raw);
-    };
-    if (tid == 0) issue_raw(0);
+    const bool is_k = tid < KB;        // threads 0-63: K row tid; 64-127: V row tid - 64
+    const int krow = tid & (KB - 1);
     bool ok = true;
     for (int kb = 0; kb < nkb; ++kb) {
         const int k0 = kb * KB;
-        ok = tc::mbar_wait_spin(bar_raw, (uint32_t)(kb & 1), err) && ok;
-        // ---- K tile and V^T tile (keys k0 + tid), each scaled by 2^ek / 2^ev of the block ----
+        // ---- K tile and V^T tile of keys k0..k0+63, each scaled by 2^ek / 2^ev of the block ----
         int ek, ev;
         {
-            const bool kvalid = k0 + tid < kend;
-            // row tid of raw K: float4 j of the row is read at index f(j) = (j & 8) | ((j ^ tid) & 7),
-            // so the 8 threads of a shared-memory phase hit 8 different bank groups
-            const float4* rk = reinterpret_cast<const float4*>(smem + OFF_RK) + tid * 16;
-            float4 k4[16];
-            float am = 0.f;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                k4[j] = kvalid ? rk[(j & 8) | ((j ^ tid) & 7)] : make_float4(0.f, 0.f, 0.f, 0.f);
-                am = fmaxf(am, fmaxf(fmaxf(fabsf(k4[j].x), fabsf(k4[j].y)), fmaxf(fabsf(k4[j].z), fabsf(k4[j].w))));
-            }
-            ek = scale_exp(block_max(am, red));
-            const float sk = pow2f(ek);
-            const bool swap = (tid & 1) != 0;
-#pragma unroll
-            for (int mm = 0; mm < 8; ++mm) {
-                // k4[2mm], k4[2mm+1] hold float4s 2c and 2c+1 (in swapped order for odd tid)
-                const float4 a = swap ? k4[2 * mm + 1] : k4[2 * mm];
-                const float4 b = swap ? k4[2 * mm] : k4[2 * mm + 1];
-                const int c = (((2 * mm) & 8) | (((2 * mm) ^ tid) & 7)) >> 1;
-                __half2 h0, h1, h2, h3, l0, l1, l2, l3;
-                split_hl2(a.x * sk, a.y * sk, h0, l0);
-                split_hl2(a.z * sk, a.w * sk, h1, l1);
-                split_hl2(b.x * sk, b.y * sk, h2, l2);
-                split_hl2(b.z * sk, b.w * sk, h3, l3);
-                const uint32_t o = sw_off(tid, c);
-                *reinterpret_cast<uint4*>(smem + OFF_KH + o) =
-                    make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
-                               *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
-                *reinterpret_cast<uint4*>(smem + OFF_KL + o) =
-                    make_uint4(*reinterpret_cast<uint32_t*>(&l0), *reinterpret_cast<uint32_t*>(&l1),
-                               *reinterpret_cast<uint32_t*>(&l2), *reinterpret_cast<uint32_t*>(&l3));
-            }
+            const int kp = k0 + krow;
+            const bool kvalid = kp < kend;
             float v[64];
-            const float4* rv = reinterpret_cast<const float4*>(smem + OFF_RV) + tid * 16;
+            load_row64((is_k ? Kc : Vc) + (size_t)(kvalid ? kp : 0) * HD, kvalid, v);
+            const float am = row_absmax(v);
+            const float2 mx = block_max2(is_k ? am : 0.f, is_k ? 0.f : am, red);
+            ek = scale_exp(mx.x);
+            ev = scale_exp(mx.y);
+            if (is_k) {
+                put_row64(smem + OFF_KH, smem + OFF_KL, krow, v, pow2f(ek));
+            } else {
+                // V^T column krow: element (dim d, key) -> row d
+                const float sv = pow2f(ev);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const float4 x = kvalid ? rv[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-                v[4 * j] = x.x;
-                v[4 * j + 1] = x.y;
-                v[4 * j + 2] = x.z;
-                v[4 * j + 3] = x.w;
-            }
-            ev = scale_exp(block_max(row_absmax(v), red));
-            const float sv = pow2f(ev);
-            // V^T chunk tid / 64, column tid % 64: element (dim d, key) -> row d
-            uint8_t* vh = smem + OFF_V + (tid >> 6) * 2 * TILE_VT;
-            uint8_t* vl = vh + TILE_VT;
-            const int col = tid & 63;
-#pragma unroll
-            for (int dd = 0; dd < 64; dd += 2) {
-                __half2 h, lo;
-                split_hl2(v[dd] * sv, v[dd + 1] * sv, h, lo);
-                const uint32_t off0 = sw_off(dd, col >> 3) + (uint32_t)((col & 7) * 2);
-                const uint32_t off1 = sw_off(dd + 1, col >> 3) + (uint32_t)((col & 7) * 2);
-                *reinterpret_cast<__half*>(vh + off0) = __low2half(h);
-                *reinterpret_cast<__half*>(vl + off0) = __low2half(lo);
-                *reinterpret_cast<__half*>(vh + off1) = __high2half(h);
-                *reinterpret_cast<__half*>(vl + off1) = __high2half(lo);
+                for (int dd = 0; dd < 64; dd += 2) {
+                    __half2 h, lo;
+                    split_hl2(v[dd] * sv, v[dd + 1] * sv, h, lo);
+                    const uint32_t off0 = sw_off(dd, krow >> 3) + (uint32_t)((krow & 7) * 2);
+                    const uint32_t off1 = sw_off(dd + 1, krow >> 3) + (uint32_t)((krow & 7) * 2);
+                    *reinterpret_cast<__half*>(smem + OFF_VH + off0) = __low2half(h);
+                    *reinterpret_cast<__half*>(smem + OFF_VL + off0) = __low2half(lo);
+                    *reinterpret_cast<__half*>(smem + OFF_VH + off1) = __high2half(h);
+                    *reinterpret_cast<__half*>(smem + OFF_VL + off1) = __high2half(lo);
+                }
             }
         }
         tc::fence_proxy_async_smem();
@@ -258,11 +216,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncthreads();
         // ---- S = Q K^T ----
         if (tid == 0) {
-            if (kb + 1 < nkb) issue_raw(kb + 1);  // every thread is done with the raw rows
             tc::tc_fence_after();
             const uint32_t qh = tc::smem_u32(smem + OFF_QH), ql = tc::smem_u32(smem + OFF_QL);
-            const uint32_t kh = tc::smem_u32(smem + OFF_KH), kl = tc::smem_u32(smem + OFF_KL);
-            (void)kl;
+            const uint32_t kh = tc::smem_u32(smem + OFF_KH);
 #pragma unroll
             for (int ks = 0; ks < HD / 16; ++ks) {
                 const uint32_t ko = ks * 32;
@@ -275,12 +231,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::tc_fence_after();
         // ---- online softmax of this thread's query row ----
         float s[KB];
-#pragma unroll
-        for (int c = 0; c < KB; c += 32) {
+        {
             float u[32];
-            tc::tmem_ld32x2(t_lane + c, t_lane + KB + c, *reinterpret_cast<float(*)[32]>(s + c), u);
+            tc::tmem_ld32x2(t_lane, t_lane + KB, *reinterpret_cast<float(*)[32]>(s), u);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) s[c + j] += u[j];
+            for (int j = 0; j < 32; ++j) s[j] += u[j];
+            tc::tmem_ld32x2(t_lane + 32, t_lane + KB + 32, *reinterpret_cast<float(*)[32]>(s + 32), u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) s[32 + j] += u[j];
         }
         const float s_unscale = pow2f(-(eq + ek) - 3);  // operand scales and 1/sqrt(64)
         float bmax = -INFINITY;
@@ -294,7 +252,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const float alpha = (mnew == -INFINITY) ? 1.f : __expf(m - mnew);
         float psum = 0.f;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys; chunk c lives in P chunk c / 8
+        for (int c = 0; c < KB / 8; ++c) {  // 8 chunks of 8 keys
             uint32_t h[4], lo[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -306,7 +264,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 h[j] = *reinterpret_cast<uint32_t*>(&h2);
                 lo[j] = *reinterpret_cast<uint32_t*>(&l2);
             }
-            const uint32_t off = (uint32_t)((c >> 3) * TILE_Q) + sw_off(tid, c & 7);
+            const uint32_t off = sw_off(tid, c);
             *reinterpret_cast<uint4*>(smem + OFF_PH + off) = make_uint4(h[0], h[1], h[2], h[3]);
             *reinterpret_cast<uint4*>(smem + OFF_PL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
@@ -315,17 +273,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::fence_proxy_async_smem();
         tc::tc_fence_before();
         __syncthreads();
-        // ---- PV = P V (columns 128..191) ----
+        // ---- PV = P V (columns 128..255) ----
         if (tid == 0) {
             tc::tc_fence_after();
             const uint32_t ph = tc::smem_u32(smem + OFF_PH), pl = tc::smem_u32(smem + OFF_PL);
-            const uint32_t v0 = tc::smem_u32(smem + OFF_V);
+            const uint32_t vh = tc::smem_u32(smem + OFF_VH);
 #pragma unroll
             for (int ks = 0; ks < KB / 16; ++ks) {
-                const uint32_t ao = (uint32_t)((ks >> 2) * TILE_Q + (ks & 3) * 32);
-                const uint32_t vh = v0 + (uint32_t)((ks >> 2) * 2 * TILE_VT + (ks & 3) * 32);
-                tc::mma_f16(tmem + 256, tc::desc_sw128(ph + ao), tc::desc_sw128(vh), idesc_pv2, ks > 0 ? 1u : 0u);
-                tc::mma_f16(tmem + 256, tc::desc_sw128(pl + ao), tc::desc_sw128(vh), idesc_pv, 1u);
+                const uint32_t ko = ks * 32;
+                tc::mma_f16(tmem + 128, tc::desc_sw128(ph + ko), tc::desc_sw128(vh + ko), idesc_pv2, ks > 0 ? 1u : 0u);
+                tc::mma_f16(tmem + 128, tc::desc_sw128(pl + ko), tc::desc_sw128(vh + ko), idesc_pv, 1u);
             }
             tc::mma_commit(bar_pv);
         }
@@ -334,18 +291,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         float pv[HD];
         {
             float u[32];
-            tc::tmem_ld32x2(t_lane + 256, t_lane + 256 + HD, *reinterpret_cast<float(*)[32]>(pv), u);
+            tc::tmem_ld32x2(t_lane + 128, t_lane + 128 + HD, *reinterpret_cast<float(*)[32]>(pv), u);
 #pragma unroll
             for (int j = 0; j < 32; ++j) pv[j] += u[j];
-            tc::tmem_ld32x2(t_lane + 288, t_lane + 288 + HD, *reinterpret_cast<float(*)[32]>(pv + 32), u);
+            tc::tmem_ld32x2(t_lane + 160, t_lane + 160 + HD, *reinterpret_cast<float(*)[32]>(pv + 32), u);
 #pragma unroll
             for (int j = 0; j < 32; ++j) pv[32 + j] += u[j];
         }
         const float pv_unscale = pow2f(-14 - ev);
 #pragma unroll
         for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha, pv[i] * pv_unscale);
-        // no early exit after a failed wait: the raw copy of the next block is in flight and
-        // is waited for (bounded) by the next iteration
     }
     // ---- out = O / l (fp32 and the fp16 hi/lo copy for the c_proj GEMM) ----
     if (qvalid && ok) {

@@ -8,6 +8,7 @@
 // tanh GELU, exact softmax) but not the launch structure: bias, GELU, residual
 // and the K/V scatter are fused into the linear epilogues, LayerNorm is one warp
 // per row, and attention is tiled with online softmax instead of thread-0 loops.
+#include <cfloat>
 #include <float.h>
 
 #include <cstdlib>
@@ -398,6 +399,45 @@ cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, cons
         case ATOM_F16: return linear_dispatch<ATOM_F16>(w, X, ldx, M, e, st);
         default: return linear_dispatch<ATOM_F32>(w, X, ldx, M, e, st);
     }
+}
+
+// ------------------------------------------------------------------ teacher-forced NLL
+// One block per row (gpt2.rs:353-361): max in fp32, then the f64 sum of exp((l - max) as f64)
+// and the target term (l[target] - max) as f64 - ln(sum). Reductions run in a fixed order.
+__global__ void __launch_bounds__(256) k_nll_rows(const float* logits, int vocab, int ld, const int* targets,
+                                                  double* terms) {
+    __shared__ float redf[8];
+    __shared__ double redd[8];
+    tc::pdl_trigger();
+    tc::pdl_wait();
+    const float* l = logits + (size_t)blockIdx.x * ld;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float m = -FLT_MAX;
+    for (int i = threadIdx.x; i < vocab; i += 256) m = fmaxf(m, __ldcg(l + i));
+    m = warp_max(m);
+    if (lane == 0) redf[warp] = m;
+    __syncthreads();
+    m = redf[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, redf[w]);
+    double s = 0.0;
+    for (int i = threadIdx.x; i < vocab; i += 256) s += exp((double)(__ldcg(l + i) - m));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) redd[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < 8; ++w) t += redd[w];
+        const int tgt = targets[blockIdx.x];
+        terms[blockIdx.x] = (double)(__ldcg(l + tgt) - m) - log(t);
+    }
+}
+
+cudaError_t launch_nll_rows(const float* logits, int vocab, int ld, int rows, const int* targets, double* terms,
+                            cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    return launch_pdl(k_nll_rows, dim3(rows), dim3(256), 0, st, logits, vocab, ld, targets, terms);
 }
 
 // ------------------------------------------------------------------ decode attention

@@ -30,6 +30,10 @@ cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y,
 // out = epilogue(X[M][K] . W^T) on CUDA cores (fp32 FMA, weights dequantised in registers).
 cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, const Epi& e,
                                cudaStream_t st);
+// terms[i] = (l[i][target[i]] - max_i) - ln(sum_j exp(l[i][j] - max_i)) in f64, rows i < rows
+// of logits l [rows][ld] (one block per row, fixed-order reductions).
+cudaError_t launch_nll_rows(const float* logits, int vocab, int ld, int rows, const int* targets, double* terms,
+                            cudaStream_t st);
 // err: device error word set when a bounded wait for the staged K/V rows gives up.
 cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t layer_off, const int* slot,
                                const int* pos, float* out, __half* ohi, __half* olo, int ldo, int n_head, int B,

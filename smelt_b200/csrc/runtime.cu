@@ -121,6 +121,11 @@ struct gpt2q_handle {
     // fp16 hi/lo copies of the linear inputs (h: LayerNorm out, att: attention out, f: GELU out)
     __half *h_hi = nullptr, *h_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr, *f_hi = nullptr, *f_lo = nullptr;
     unsigned long long* best = nullptr;  // argmax slots, one per sequence
+    // teacher-forced NLL (allocated on first use): head logits of up to NLL_ROWS positions,
+    // the target ids and the per-position f64 terms
+    float* nll_logits = nullptr;
+    int* nll_tgt = nullptr;
+    double* nll_terms = nullptr;
     int* kerr = nullptr;  // device error word of the CUDA-core kernels' bounded waits
     // prefill scratch
     uint32_t* p_tok = nullptr;
@@ -653,8 +658,10 @@ int ensure_stage(gpt2q_handle* H, size_t ints) {
 }
 
 // Prefill of one chunk of sequences [s0, s1) whose tokens fit the workspace.
+// layers_only: stop after the last transformer block (x holds the residual stream of every
+// prompt row), for callers that need more than the last position's logits.
 int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, const int32_t* slots, int s0,
-                  int s1) {
+                  int s1, bool layers_only = false) {
     const int d = H->cfg.n_embd;
     const int base = offs[s0];
     const int M = offs[s1] - base;
@@ -718,6 +725,7 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
         });
         if (rc) return rc;
     }
+    if (layers_only) return GPT2Q_OK;
     // ln_f + tied head for the last position of each sequence only.
     RUN("layernorm", (double)ns * d * 8,
         launch_layernorm(H->x, d, H->p_lastrow, H->h, d, H->h_hi, H->h_lo, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, ns,
@@ -1255,6 +1263,55 @@ int gpt2q_generate_greedy(gpt2q_handle* H, const uint32_t* tokens, const int32_t
         if (rc) return rc;
         for (size_t i = 0; i < who.size(); ++i) out[(size_t)who[i] * steps + 1 + k] = nx[i];
     }
+    return GPT2Q_OK;
+}
+
+int gpt2q_nll(gpt2q_handle* H, const uint32_t* ids, int n, int slot, double* out) {
+    if (!H) return GPT2Q_EARG;
+    if (!ids || !out) return H->fail(GPT2Q_EARG, "null ids/out");
+    if (n < 2 || n > H->cfg.n_ctx || n > H->Mmax) return H->fail(GPT2Q_EARG, "n out of range [2, min(n_ctx, max_tokens)]");
+    if (slot < 0 || slot >= H->cfg.max_seqs) return H->fail(GPT2Q_EARG, "slot out of range");
+    CK(cudaSetDevice(H->device));
+    int rc = check_tokens(H, ids, (size_t)n);
+    if (rc) return rc;
+    constexpr int NLL_ROWS = 256;
+    const int d = H->cfg.n_embd, V = H->cfg.vocab, R = n - 1;
+    if (!H->nll_logits) {
+        H->nll_logits = H->dalloc<float>((size_t)NLL_ROWS * V * 4);
+        H->nll_tgt = H->dalloc<int>((size_t)H->cfg.n_ctx * 4);
+        H->nll_terms = H->dalloc<double>((size_t)H->cfg.n_ctx * 8);
+        if (!H->nll_logits || !H->nll_tgt || !H->nll_terms) return H->fail(GPT2Q_EOOM, "NLL buffers");
+    }
+    const int32_t offs[2] = {0, n};
+    const int32_t slots[1] = {slot};
+    rc = prefill_chunk(H, ids, offs, slots, 0, 1, true);
+    if (rc) return rc;
+    // positions 0..n-2 predict ids[1..n-1]: ln_f over their rows, the head in chunks, the terms
+    std::vector<int> tgt(R);
+    for (int p = 0; p < R; ++p) tgt[p] = (int)ids[p + 1];
+    CK(cudaMemcpyAsync(H->nll_tgt, tgt.data(), (size_t)R * 4, cudaMemcpyHostToDevice, H->stream));
+    RUN("layernorm", (double)R * d * 8,
+        launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, R,
+                         H->stream));
+    for (int r0 = 0; r0 < R; r0 += NLL_ROWS) {
+        const int rows = std::min(NLL_ROWS, R - r0);
+        const size_t o = (size_t)r0 * d;
+        rc = linear(H, "linear_head", H->wte, In{H->h + o, H->h_hi + o, H->h_lo + o, d}, rows,
+                    epi_store(H->nll_logits, V, nullptr));
+        if (rc) return rc;
+        RUN("nll", (double)rows * V * 4,
+            launch_nll_rows(H->nll_logits, V, V, rows, H->nll_tgt + r0, H->nll_terms + r0, H->stream));
+    }
+    std::vector<double> terms(R);
+    CK(cudaMemcpyAsync(terms.data(), H->nll_terms, (size_t)R * 8, cudaMemcpyDeviceToHost, H->stream));
+    CK(cudaStreamSynchronize(H->stream));
+    rc = check_device_error(H);
+    if (rc) return rc;
+    // the reference's accumulation: total -= term in position order, then the mean
+    double total = 0.0;
+    for (int p = 0; p < R; ++p) total -= terms[p];
+    *out = total / (double)R;
+    // the slot's cache now holds this sequence; its decode state is not advanced
     return GPT2Q_OK;
 }
 

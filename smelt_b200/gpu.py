@@ -148,6 +148,15 @@ class Gpu:
             out.ctypes.data_as(_ffi._u32p)))
         return out
 
+    def nll(self, ids, slot: int = 0) -> float:
+        """Teacher-forced NLL per token (nll_per_token, gpt2.rs:347-364), computed on the
+        device; overwrites the KV cache of `slot`."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        out = C.c_double(0.0)
+        self._check(self._lib.gpt2q_nll(self.h, ids.ctypes.data_as(_ffi._u32p), int(ids.size), int(slot),
+                                        C.byref(out)))
+        return float(out.value)
+
     def dequant(self, name: str, numel: int) -> np.ndarray:
         out = np.empty(numel, dtype=np.float32)
         self._check(self._lib.gpt2q_dequant(self.h, name.encode(), out.ctypes.data_as(_ffi._f32p), numel))
