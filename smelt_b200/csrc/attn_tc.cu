@@ -24,6 +24,10 @@
 // (softmax(q.K^T / sqrt(hd)) . V over positions 0..t), per query position t of the prompt.
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+#include <string>
+#include <vector>
+
 #include "kernels.h"
 #include "tcgen05.cuh"
 
@@ -48,6 +52,21 @@ static_assert(SMEM <= 232448 / 2 - 1024, "two CTAs per SM");
 // PV: 128..255 (P_hi V_hi | P_hi V_lo, P_lo V_hi added to the first half)
 constexpr uint32_t TMEM_COLS = 256;
 
+// Phase trace of one launch (GPT2Q_ATTN_TRACE set at the first launch): globaltimer stamps of
+// thread 0 of the first ATR_CTAS CTAs: start, Q staged, then per key block kb < 8: K/V staged,
+// S ready, P staged, PV ready.
+constexpr int ATR_CTAS = 128, ATR_N = 2 + 4 * 8;
+__device__ unsigned long long g_attn_trace[ATR_CTAS * ATR_N];
+
+__device__ __forceinline__ void atr_stamp(bool on, int k) {
+    const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+    if (on && threadIdx.x == 0 && cta < ATR_CTAS && k < ATR_N) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        g_attn_trace[cta * ATR_N + k] = t;
+    }
+}
+
 // Byte offset of 16-byte chunk c (8 fp16) of row r in a 128-byte-swizzled K-major tile.
 __device__ __forceinline__ uint32_t sw_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
@@ -62,11 +81,10 @@ __device__ __forceinline__ void put_row64(uint8_t* hi, uint8_t* lo, int r, const
         uint32_t h[4], l[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            __half h0, l0, h1, l1;
-            split_hl(v[8 * c + 2 * j] * mul, h0, l0);
-            split_hl(v[8 * c + 2 * j + 1] * mul, h1, l1);
-            h[j] = pack_h2(h0, h1);
-            l[j] = pack_h2(l0, l1);
+            __half2 h2, l2;
+            split_hl2(v[8 * c + 2 * j] * mul, v[8 * c + 2 * j + 1] * mul, h2, l2);
+            h[j] = *reinterpret_cast<uint32_t*>(&h2);
+            l[j] = *reinterpret_cast<uint32_t*>(&l2);
         }
         const uint32_t o = sw_off(r, c);
         *reinterpret_cast<uint4*>(hi + o) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -125,7 +143,7 @@ __device__ __forceinline__ void load_row64(const float* src, bool ok, float* v) 
 __global__ void __launch_bounds__(THREADS, 2)
     k_attn_prefill_tc(const float* q, int ldq, KVGeom g, size_t layer_off,
                       const AttnTile* __restrict__ tiles, float* __restrict__ out, __half* __restrict__ ohi,
-                      __half* __restrict__ olo, int ldo, int* err) {
+                      __half* __restrict__ olo, int ldo, int* err, bool trace) {
     extern __shared__ __align__(1024) uint8_t smem_raw_[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
     uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -151,6 +169,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lanes
 
     tc::pdl_wait();  // q and the K/V rows were written by the preceding kernels
+    atr_stamp(trace, 0);
     const AttnTile tile = tiles[blockIdx.y];
     const int head = blockIdx.x;
     const float* Kc = g.base + (size_t)tile.slot * g.slot_stride + layer_off + (size_t)head * g.head_stride;
@@ -166,6 +185,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         eq = scale_exp(row_absmax(v));
         put_row64(smem + OFF_QH, smem + OFF_QL, tid, v, pow2f(eq));
     }
+    atr_stamp(trace, 1);
 
     constexpr uint32_t idesc_s2 = tc::idesc_f16_f32(QT, 2 * KB);  // Q_hi [K_hi; K_lo]
     constexpr uint32_t idesc_s = tc::idesc_f16_f32(QT, KB);
@@ -214,6 +234,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         tc::fence_proxy_async_smem();
         tc::tc_fence_before();
         __syncthreads();
+        atr_stamp(trace, 2 + 4 * kb);
         // ---- S = Q K^T ----
         if (tid == 0) {
             tc::tc_fence_after();
@@ -229,6 +250,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
         ok = tc::mbar_wait_spin(bar_s, (uint32_t)(kb & 1), err) && ok;
         tc::tc_fence_after();
+        atr_stamp(trace, 3 + 4 * kb);
         // ---- online softmax of this thread's query row ----
         float s[KB];
         {
@@ -273,6 +295,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         tc::fence_proxy_async_smem();
         tc::tc_fence_before();
         __syncthreads();
+        atr_stamp(trace, 4 + 4 * kb);
         // ---- PV = P V (columns 128..255) ----
         if (tid == 0) {
             tc::tc_fence_after();
@@ -288,6 +311,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
         ok = tc::mbar_wait_spin(bar_pv, (uint32_t)(kb & 1), err) && ok;
         tc::tc_fence_after();
+        atr_stamp(trace, 5 + 4 * kb);
         float pv[HD];
         {
             float u[32];
@@ -344,7 +368,29 @@ cudaError_t launch_attn_prefill_tc(const float* q, int ldq, const KVGeom& g, siz
     at.val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = &at;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_attn_prefill_tc, q, ldq, g, layer_off, tiles, out, ohi, olo, ldo, err);
+    static bool trace_pending = std::getenv("GPT2Q_ATTN_TRACE") != nullptr;
+    const bool trace = trace_pending;
+    trace_pending = false;
+    return cudaLaunchKernelEx(&cfg, k_attn_prefill_tc, q, ldq, g, layer_off, tiles, out, ohi, olo, ldo, err, trace);
+}
+
+std::string attn_tc_trace_json() {
+    if (!std::getenv("GPT2Q_ATTN_TRACE")) return "";
+    std::vector<unsigned long long> t(ATR_CTAS * ATR_N);
+    if (cudaMemcpyFromSymbol(t.data(), g_attn_trace, t.size() * 8) != cudaSuccess) return "";
+    unsigned long long t0 = ~0ull;
+    for (auto v : t)
+        if (v && v < t0) t0 = v;
+    std::string s = "[";
+    for (int c = 0; c < ATR_CTAS; ++c) {
+        s += c ? ", [" : "[";
+        for (int k = 0; k < ATR_N; ++k) {
+            const unsigned long long v = t[c * ATR_N + k];
+            s += (k ? ", " : "") + std::to_string(v ? (long long)(v - t0) : -1);
+        }
+        s += "]";
+    }
+    return s + "]";
 }
 
 }  // namespace gpt2q

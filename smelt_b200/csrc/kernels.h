@@ -1,5 +1,6 @@
 // Host-side launchers of the gpt2q CUDA kernels (definitions in kernels.cu).
 #pragma once
+#include <string>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -43,6 +44,8 @@ cudaError_t launch_attn_prefill(const float* q, int ldq, const KVGeom& g, size_t
                                 int n_head, float scale, cudaStream_t st);
 // Causal prefill attention on the tensor cores (attn_tc.cu): tiles of 128 queries, head dim 64,
 // scale 1/8. Bounded waits record a timeout in `err`.
+// Phase stamps of the traced tensor-core attention launch (GPT2Q_ATTN_TRACE), JSON; "" if none.
+std::string attn_tc_trace_json();
 cudaError_t launch_attn_prefill_tc(const float* q, int ldq, const KVGeom& g, size_t layer_off, const AttnTile* tiles,
                                    int n_tiles, float* out, __half* ohi, __half* olo, int ldo, int n_head, int* err,
                                    cudaStream_t st);

@@ -1436,6 +1436,8 @@ int gpt2q_info(gpt2q_handle* H, char* json, size_t cap) {
     }
     const std::string gt = gemm_trace_json(H->gemm);
     if (!gt.empty()) tr += ", \"tc_trace\": " + gt;
+    const std::string at = attn_tc_trace_json();
+    if (!at.empty()) tr += ", \"attn_trace\": " + at;
     const std::string s = head + tr + "}";
     if (s.size() + 1 > cap) return H->fail(GPT2Q_EARG, "info: buffer too small");
     std::memcpy(json, s.c_str(), s.size() + 1);
