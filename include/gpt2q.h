@@ -124,6 +124,15 @@ int gpt2q_decode_steps(gpt2q_handle* h, int steps, uint32_t* out_tokens);
 int gpt2q_generate_greedy(gpt2q_handle* h, const uint32_t* tokens, const int32_t* seq_offsets,
                           int n_seq, int steps, uint32_t* out);
 
+/* Publish a plastic adapter applied to the post-ln_f hidden state of every later step and
+ * prefill: h += B (A h), A [r][d] and B [d][r] fp32 row-major, 1 <= r <= 256
+ * (Gpu::set_adapter gpu.rs:188-194, k_adapter_apply cu/gpt2.cu:196-215). The copy is made
+ * on the handle's stream: work enqueued before the call sees the previous generation, work
+ * after it the new one (RCU-style). Host buffers may be reused when the call returns. */
+int gpt2q_set_adapter(gpt2q_handle* h, const float* A, const float* B, int r);
+/* Remove the adapter (Gpu::clear_adapter, gpu.rs:195). */
+int gpt2q_clear_adapter(gpt2q_handle* h);
+
 /* Teacher-forced negative log-likelihood per token of ids[0..n-1]
  * (nll_per_token, gpt2.rs:347-364): the mean over positions p = 0..n-2 of
  * -(logit[ids[p+1]] - max) + ln(sum exp(logit - max)), with the log-sum-exp in f64.

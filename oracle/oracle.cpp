@@ -483,6 +483,9 @@ struct orc_engine {
     float ln_eps;
     int threads;
     std::map<std::string, Tensor> t;
+    // plastic adapter on the post-ln_f state (gpu.rs:188-194, 364-367): h += B (A h)
+    int ad_r = 0;
+    std::vector<float> ad_a, ad_b;  // A [r][d], B [d][r]
     const Tensor& get(const std::string& n) const { return t.at(n); }
 };
 
@@ -695,7 +698,35 @@ extern "C" int orc_engine_step(const orc_engine* e, uint32_t tok, int pos, float
     std::vector<float> wf = vec_f32(e, "ln_f.weight");
     std::vector<float> bf = vec_f32(e, "ln_f.bias");
     layernorm(x.data(), d, wf.data(), bf.data(), e->ln_eps);
+    if (e->ad_r > 0) {
+        // k_adapter_apply (cu/gpt2.cu:196-215): ah[j] = sum_i A[j][i] h[i], then
+        // h[i] += sum_j B[i][j] ah[j], both sums sequential fused multiply-adds
+        const int r = e->ad_r;
+        std::vector<float> ah(r);
+        for (int j = 0; j < r; ++j) {
+            float acc = 0.f;
+            const float* ar = e->ad_a.data() + (size_t)j * d;
+            for (size_t i = 0; i < d; ++i) acc = std::fma(ar[i], x[i], acc);
+            ah[j] = acc;
+        }
+        for (size_t i = 0; i < d; ++i) {
+            float acc = 0.f;
+            const float* br = e->ad_b.data() + i * r;
+            for (int j = 0; j < r; ++j) acc = std::fma(br[j], ah[j], acc);
+            x[i] += acc;
+        }
+    }
     matmul(e, "wte.weight", x.data(), logits);
+    return 0;
+}
+
+// Gpu::set_adapter / clear_adapter (gpu.rs:188-194): r = 0 clears.
+extern "C" int orc_set_adapter(orc_engine* e, const float* a, const float* b, int r) {
+    if (r < 0) return -1;
+    e->ad_r = r;
+    e->ad_a.assign(a ? a : nullptr, a ? a + (size_t)r * e->n_embd : nullptr);
+    e->ad_b.assign(b ? b : nullptr, b ? b + (size_t)r * e->n_embd : nullptr);
+    if (r > 0 && (!a || !b)) e->ad_r = 0;
     return 0;
 }
 

@@ -87,6 +87,9 @@ int orc_vec_row(const orc_engine* e, const char* name, uint32_t row, float* out,
 int orc_generate_greedy(const orc_engine* e, const uint32_t* prompt, int n_prompt, int steps,
                         uint32_t* out);
 double orc_nll_per_token(const orc_engine* e, const uint32_t* ids, int n);
+/* Post-ln_f adapter h += B (A h) applied by every later step (gpu.rs:188-194,
+ * cu/gpt2.cu:196-215); A [r][d], B [d][r]; r = 0 clears. */
+int orc_set_adapter(orc_engine* e, const float* a, const float* b, int r);
 uint32_t orc_argmax(const float* v, size_t n);
 /* Independent float64 forward over T positions (bwparity.rs:215-305) on the
  * dequantised weights; logits_out is [T][vocab] f64. */

@@ -78,6 +78,8 @@ def _sig(lib):
     lib.orc_vec_row.restype = C.c_int
     lib.orc_generate_greedy.argtypes = [C.c_void_p, _u32p, C.c_int, C.c_int, _u32p]
     lib.orc_generate_greedy.restype = C.c_int
+    lib.orc_set_adapter.argtypes = [C.c_void_p, _f32p, _f32p, C.c_int]
+    lib.orc_set_adapter.restype = C.c_int
     lib.orc_nll_per_token.argtypes = [C.c_void_p, _u32p, C.c_int]
     lib.orc_nll_per_token.restype = C.c_double
     lib.orc_argmax.argtypes = [_f32p, C.c_size_t]
@@ -219,6 +221,17 @@ class Engine:
         out = np.zeros(steps, dtype=np.uint32)
         n = self._l.orc_generate_greedy(self.h, _p(p, _u32p), p.size, steps, _p(out, _u32p))
         return out[:n]
+
+    def set_adapter(self, a=None, b=None):
+        """Post-ln_f adapter h += B (A h) (gpu.rs:188-194, cu/gpt2.cu:196-215); None clears."""
+        if a is None:
+            self._l.orc_set_adapter(self.h, None, None, 0)
+            return
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        r = a.shape[0]
+        assert a.shape == (r, self.meta["n_embd"]) and b.shape == (self.meta["n_embd"], r)
+        self._l.orc_set_adapter(self.h, _p(a, _f32p), _p(b, _f32p), r)
 
     def nll_per_token(self, ids) -> float:
         p = np.ascontiguousarray(ids, dtype=np.uint32)

@@ -21,6 +21,7 @@ EXPORTS = [
     "gpt2q_dequant", "gpt2q_launches", "gpt2q_set_stream", "gpt2q_sync", "gpt2q_profile",
     "gpt2q_profile_read", "gpt2q_profile_kernels", "gpt2q_info", "gpt2q_argmax_noalloc", "gpt2q_rng_new", "gpt2q_rng_normal_f32", "gpt2q_rng_below",
     "gpt2q_quantize_q8", "gpt2q_quantize_q4", "gpt2q_nll",
+    "gpt2q_set_adapter", "gpt2q_clear_adapter",
 ]
 
 
@@ -88,6 +89,10 @@ def load(path: str | None = None):
     lib.gpt2q_set_stream.restype = C.c_int
     lib.gpt2q_sync.argtypes = [_hp]
     lib.gpt2q_sync.restype = C.c_int
+    lib.gpt2q_set_adapter.argtypes = [_hp, _f32p, _f32p, C.c_int]
+    lib.gpt2q_set_adapter.restype = C.c_int
+    lib.gpt2q_clear_adapter.argtypes = [_hp]
+    lib.gpt2q_clear_adapter.restype = C.c_int
     lib.gpt2q_nll.argtypes = [_hp, _u32p, C.c_int, C.c_int, C.POINTER(C.c_double)]
     lib.gpt2q_nll.restype = C.c_int
     lib.gpt2q_profile.argtypes = [_hp, C.c_int]

@@ -401,6 +401,54 @@ cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, cons
     }
 }
 
+// ------------------------------------------------------------------ plastic adapter
+// One block per row (cu/gpt2.cu:196-215): ah[j] = sum_i A[j][i] h[i], then
+// h[i] += sum_j B[i][j] ah[j], both sums sequential fused multiply-adds as in the reference
+// kernel; the row is staged in shared memory, and the hi/lo copy for the tensor-core head is
+// rewritten with the result.
+__global__ void __launch_bounds__(256) k_adapter_apply(const AdapterDesc* __restrict__ desc, float* h, __half* hhi,
+                                                       __half* hlo, int ld, int d) {
+    extern __shared__ float ad_sm[];  // [d] row, then [r] A h
+    tc::pdl_trigger();
+    const AdapterDesc D = *desc;  // published before the step was enqueued
+    tc::pdl_wait();
+    if (D.r <= 0) return;
+    float* hs = ad_sm;
+    float* ah = ad_sm + d;
+    float* hr = h + (size_t)blockIdx.x * ld;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) hs[i] = __ldcg(hr + i);
+    __syncthreads();
+    for (int j = threadIdx.x; j < D.r; j += blockDim.x) {
+        const float* ar = D.a + (size_t)j * d;
+        float s = 0.f;
+        for (int i = 0; i < d; ++i) s = fmaf(__ldg(ar + i), hs[i], s);
+        ah[j] = s;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float* br = D.b + (size_t)i * D.r;
+        float s = 0.f;
+        for (int j = 0; j < D.r; ++j) s = fmaf(__ldg(br + j), ah[j], s);
+        const float v = hs[i] + s;
+        hr[i] = v;
+        if (hhi) split_hl(v, hhi[(size_t)blockIdx.x * ld + i], hlo[(size_t)blockIdx.x * ld + i]);
+    }
+}
+
+cudaError_t launch_adapter(const AdapterDesc* desc, float* h, __half* hhi, __half* hlo, int ld, int d, int rows,
+                           int max_r, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    const size_t smem = (size_t)(d + max_r) * 4;
+    if (smem > 48 * 1024) {
+        static bool attr = [smem] {
+            return cudaFuncSetAttribute(k_adapter_apply, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+                   cudaSuccess;
+        }();
+        if (!attr) return cudaErrorInvalidValue;
+    }
+    return launch_pdl(k_adapter_apply, dim3(rows), dim3(256), smem, st, desc, h, hhi, hlo, ld, d);
+}
+
 // ------------------------------------------------------------------ teacher-forced NLL
 // One block per row (gpt2.rs:353-361): max in fp32, then the f64 sum of exp((l - max) as f64)
 // and the target term (l[target] - max) as f64 - ln(sum). Reductions run in a fixed order.

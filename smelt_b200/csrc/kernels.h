@@ -31,6 +31,17 @@ cudaError_t launch_layernorm(const float* x, int ldx, const int* rows, float* y,
 // out = epilogue(X[M][K] . W^T) on CUDA cores (fp32 FMA, weights dequantised in registers).
 cudaError_t launch_linear_simt(const QW& w, const float* X, int ldx, int M, const Epi& e,
                                cudaStream_t st);
+// Post-ln_f plastic adapter of the reference's GPU path (cu/gpt2.cu:196-215): the published
+// generation (A [r][d], B [d][r], r; r = 0 means none) lives in device memory, so a captured
+// step reads whichever generation is current when it runs.
+struct AdapterDesc {
+    const float* a;
+    const float* b;
+    int r;
+};
+// rows of h (ld floats apart): h += B (A h), and the fp16 hi/lo copy rewritten.
+cudaError_t launch_adapter(const AdapterDesc* desc, float* h, __half* hhi, __half* hlo, int ld, int d, int rows,
+                           int max_r, cudaStream_t st);
 // terms[i] = (l[i][target[i]] - max_i) - ln(sum_j exp(l[i][j] - max_i)) in f64, rows i < rows
 // of logits l [rows][ld] (one block per row, fixed-order reductions).
 cudaError_t launch_nll_rows(const float* logits, int vocab, int ld, int rows, const int* targets, double* terms,

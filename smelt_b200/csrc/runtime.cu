@@ -121,6 +121,14 @@ struct gpt2q_handle {
     // fp16 hi/lo copies of the linear inputs (h: LayerNorm out, att: attention out, f: GELU out)
     __half *h_hi = nullptr, *h_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr, *f_hi = nullptr, *f_lo = nullptr;
     unsigned long long* best = nullptr;  // argmax slots, one per sequence
+    // plastic adapter (allocated on first use): two generations of A/B buffers, alternating,
+    // and the device descriptor a step reads
+    static constexpr int AD_MAX_R = 256;
+    bool adapter_on = false;
+    int ad_gen = 0;
+    float* ad_a[2] = {nullptr, nullptr};
+    float* ad_b[2] = {nullptr, nullptr};
+    AdapterDesc* d_adapter = nullptr;
     // teacher-forced NLL (allocated on first use): head logits of up to NLL_ROWS positions,
     // the target ids and the per-position f64 terms
     float* nll_logits = nullptr;
@@ -141,7 +149,7 @@ struct gpt2q_handle {
     int* h_stage = nullptr;
     size_t h_stage_ints = 0;
 
-    std::map<int, std::pair<cudaGraphExec_t, uint64_t>> dec_graphs;  // B -> (graph, kernels)
+    std::map<int, std::pair<cudaGraphExec_t, uint64_t>> dec_graphs;  // 2 B + adapter -> (graph, kernels)
     bool capturing = false;
     uint64_t capture_kernels = 0;
     uint64_t launches = 0;
@@ -502,6 +510,15 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     return rc;
 }
 
+// The published adapter, applied to `rows` rows of h after ln_f (gpu.rs:364-367).
+int apply_adapter(gpt2q_handle* H, int rows) {
+    if (!H->adapter_on) return GPT2Q_OK;
+    const int d = H->cfg.n_embd;
+    RUN("adapter", (double)rows * d * 8,
+        launch_adapter(H->d_adapter, H->h, H->h_hi, H->h_lo, d, d, rows, gpt2q_handle::AD_MAX_R, H->stream));
+    return GPT2Q_OK;
+}
+
 // Decode step for B sequences reading d_tok/d_pos/d_slot; argmax advances the state.
 int enqueue_decode(gpt2q_handle* H, int B) {
     const int d = H->cfg.n_embd;
@@ -522,7 +539,9 @@ int enqueue_decode(gpt2q_handle* H, int B) {
     RUN("layernorm", (double)B * d * 8,
         launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, B,
                          H->stream));
-    int rc = linear(H, "linear_head", H->wte, In{H->h, H->h_hi, H->h_lo, d}, B,
+    int rc = apply_adapter(H, B);
+    if (rc) return rc;
+    rc = linear(H, "linear_head", H->wte, In{H->h, H->h_hi, H->h_lo, d}, B,
                     epi_store(H->logits, H->cfg.vocab, nullptr));
     if (rc) return rc;
     RUN("argmax", (double)B * H->cfg.vocab * 4,
@@ -597,15 +616,18 @@ int run_persistent(gpt2q_handle* H, int steps) {
 }
 
 bool use_persistent(const gpt2q_handle* H, int B) {
-    return B == 1 && H->mk.enabled && !H->capturing && H->ktime_reps == 0;
+    // the persistent kernel computes ln_f itself and has no adapter stage
+    return B == 1 && H->mk.enabled && !H->capturing && H->ktime_reps == 0 && !H->adapter_on;
 }
+
 
 // Run one decode step for the current state (graph replay when possible).
 int run_decode_step(gpt2q_handle* H, int B) {
     if (use_persistent(H, B)) return run_persistent(H, 1);
     const bool graph_ok = H->use_graphs && !H->prof && H->stream != nullptr;
     if (graph_ok) {
-        auto it = H->dec_graphs.find(B);
+        const int key = 2 * B + (H->adapter_on ? 1 : 0);  // the adapter stage is captured only when on
+        auto it = H->dec_graphs.find(key);
         if (it == H->dec_graphs.end()) {
             cudaGraph_t g = nullptr;
             CK(cudaStreamBeginCapture(H->stream, cudaStreamCaptureModeThreadLocal));
@@ -623,7 +645,7 @@ int run_decode_step(gpt2q_handle* H, int B) {
             ce = cudaGraphInstantiate(&ex, g, 0);
             cudaGraphDestroy(g);
             if (ce != cudaSuccess) return H->fail(GPT2Q_ECUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
-            it = H->dec_graphs.emplace(B, std::make_pair(ex, H->capture_kernels)).first;
+            it = H->dec_graphs.emplace(key, std::make_pair(ex, H->capture_kernels)).first;
         }
         CK(cudaGraphLaunch(it->second.first, H->stream));
         H->launches += it->second.second;
@@ -730,6 +752,8 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
     RUN("layernorm", (double)ns * d * 8,
         launch_layernorm(H->x, d, H->p_lastrow, H->h, d, H->h_hi, H->h_lo, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, ns,
                          H->stream));
+    rc = apply_adapter(H, ns);
+    if (rc) return rc;
     float* lg = H->logits + (size_t)s0 * H->cfg.vocab;
     rc = linear(H, "linear_head", H->wte, In{H->h, H->h_hi, H->h_lo, d}, ns, epi_store(lg, H->cfg.vocab, nullptr));
     if (rc) return rc;
@@ -1266,6 +1290,45 @@ int gpt2q_generate_greedy(gpt2q_handle* H, const uint32_t* tokens, const int32_t
     return GPT2Q_OK;
 }
 
+int gpt2q_set_adapter(gpt2q_handle* H, const float* A, const float* B, int r) {
+    if (!H) return GPT2Q_EARG;
+    if (!A || !B || r < 1 || r > gpt2q_handle::AD_MAX_R)
+        return H->fail(GPT2Q_EARG, "adapter: A and B required, 1 <= r <= 256");
+    CK(cudaSetDevice(H->device));
+    const int d = H->cfg.n_embd;
+    if (!H->d_adapter) {
+        for (int k = 0; k < 2; ++k) {
+            H->ad_a[k] = H->dalloc<float>((size_t)gpt2q_handle::AD_MAX_R * d * 4);
+            H->ad_b[k] = H->dalloc<float>((size_t)gpt2q_handle::AD_MAX_R * d * 4);
+        }
+        H->d_adapter = H->dalloc<AdapterDesc>(sizeof(AdapterDesc));
+        if (!H->ad_a[0] || !H->ad_a[1] || !H->ad_b[0] || !H->ad_b[1] || !H->d_adapter)
+            return H->fail(GPT2Q_EOOM, "adapter buffers");
+    }
+    // RCU publish on the handle's stream: the other generation's buffers are free once every
+    // step enqueued before the previous publish has run, which stream order guarantees
+    const int g = H->ad_gen ^ 1;
+    CK(cudaMemcpyAsync(H->ad_a[g], A, (size_t)r * d * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(H->ad_b[g], B, (size_t)r * d * 4, cudaMemcpyHostToDevice, H->stream));
+    const AdapterDesc desc{H->ad_a[g], H->ad_b[g], r};
+    CK(cudaMemcpyAsync(H->d_adapter, &desc, sizeof(desc), cudaMemcpyHostToDevice, H->stream));
+    CK(cudaStreamSynchronize(H->stream));  // the host descriptor goes out of scope
+    H->ad_gen = g;
+    H->adapter_on = true;
+    return GPT2Q_OK;
+}
+
+int gpt2q_clear_adapter(gpt2q_handle* H) {
+    if (!H) return GPT2Q_EARG;
+    if (!H->d_adapter) return GPT2Q_OK;
+    CK(cudaSetDevice(H->device));
+    const AdapterDesc desc{nullptr, nullptr, 0};
+    CK(cudaMemcpyAsync(H->d_adapter, &desc, sizeof(desc), cudaMemcpyHostToDevice, H->stream));
+    CK(cudaStreamSynchronize(H->stream));
+    H->adapter_on = false;
+    return GPT2Q_OK;
+}
+
 int gpt2q_nll(gpt2q_handle* H, const uint32_t* ids, int n, int slot, double* out) {
     if (!H) return GPT2Q_EARG;
     if (!ids || !out) return H->fail(GPT2Q_EARG, "null ids/out");
@@ -1293,6 +1356,8 @@ int gpt2q_nll(gpt2q_handle* H, const uint32_t* ids, int n, int slot, double* out
     RUN("layernorm", (double)R * d * 8,
         launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, H->lnf_g, H->lnf_b, d, H->cfg.ln_eps, R,
                          H->stream));
+    rc = apply_adapter(H, R);
+    if (rc) return rc;
     for (int r0 = 0; r0 < R; r0 += NLL_ROWS) {
         const int rows = std::min(NLL_ROWS, R - r0);
         const size_t o = (size_t)r0 * d;

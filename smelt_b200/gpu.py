@@ -148,6 +148,20 @@ class Gpu:
             out.ctypes.data_as(_ffi._u32p)))
         return out
 
+    def set_adapter(self, a, b):
+        """Publish a post-ln_f adapter h += B (A h) (Gpu::set_adapter, gpu.rs:188-194):
+        a [r, d], b [d, r] float32; later steps use it."""
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        r = a.shape[0]
+        if a.shape != (r, self.meta.n_embd) or b.shape != (self.meta.n_embd, r):
+            raise ValueError("adapter shapes must be a [r, d] and b [d, r]")
+        self._check(self._lib.gpt2q_set_adapter(self.h, a.ctypes.data_as(_ffi._f32p), b.ctypes.data_as(_ffi._f32p),
+                                                int(r)))
+
+    def clear_adapter(self):
+        self._check(self._lib.gpt2q_clear_adapter(self.h))
+
     def nll(self, ids, slot: int = 0) -> float:
         """Teacher-forced NLL per token (nll_per_token, gpt2.rs:347-364), computed on the
         device; overwrites the KV cache of `slot`."""
