@@ -102,10 +102,11 @@ def test_tc_prefill_attention_matches_cuda_cores_and_oracle(policy, monkeypatch)
 MID = P.Meta(n_embd=384, n_layer=2, n_head=6, n_ctx=128, vocab=1031)
 
 
-@pytest.mark.parametrize("batch", [17, 40, 64])
+@pytest.mark.parametrize("batch", [17, 40, 64, 100, 200])
 def test_tc_split_k_exchange_shapes_match_cuda_core_path(batch, monkeypatch):
     """d = 384 decode batches split K 3 to 16 ways; at 33-64 sequences some reducing CTAs own
-    a narrower last block of token columns than the others (e.g. 12, 12, 12, 12, 12, 4)."""
+    a narrower last block of token columns than the others (e.g. 12, 12, 12, 12, 12, 4); at 100
+    and 200 sequences the 128- and 256-token tiles exchange their partials the same way."""
     pk = make_pack(MID, "auto", 1, 0.02)
     rng = np.random.default_rng(batch)
     prompts = [rng.integers(0, MID.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 50, batch)]
