@@ -205,6 +205,24 @@ int gpt2q_quantize_q4(const float* x, size_t n, uint8_t* out);
 void gpt2q_rng_normal_f32(uint64_t* state, float* out, size_t n, double stdv);
 void gpt2q_rng_below(uint64_t* state, uint32_t* out, size_t n, uint64_t bound);
 
+/* SMT container loading (Engine::load, gpt2.rs:43-89, over PackReader, format.rs:94-175).
+ * The file is memory-mapped; with verify != 0 the merkle content_id (format.rs:121-145: blake3
+ * over the sorted BLAKE3 digests of every section) and every tensor digest (first 16 bytes of
+ * blake3 of its payload, gpt2.rs:91-110) are checked on all host threads, and a mismatch fails
+ * with GPT2Q_EARG and a message naming the section or tensor. META.arch supplies n_embd,
+ * n_layer, n_head, n_ctx, vocab_size and ln_eps; the TENSORS records become the tensor list of
+ * gpt2q_create. Errors are reported by gpt2q_last_error(NULL). */
+int gpt2q_create_from_smt(const char* path, int device, int max_seqs, int max_tokens, int verify,
+                          gpt2q_handle** out);
+
+/* Parses (and with verify != 0 verifies) an SMT container without touching a GPU; writes JSON
+ * {"content_id": hex, "verified": bool, "arch": {...}, "tensors": [{name, atom, len, shape}]}. */
+int gpt2q_smt_inspect(const char* path, int verify, char* json, size_t cap);
+
+/* BLAKE3 (32-byte output, unkeyed) of len bytes, the hash the SMT digests use; host threads
+ * hash the subtrees of large inputs. */
+int gpt2q_blake3(const void* data, uint64_t len, uint8_t* out32);
+
 #ifdef __cplusplus
 }
 #endif

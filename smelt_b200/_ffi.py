@@ -22,6 +22,7 @@ EXPORTS = [
     "gpt2q_profile_read", "gpt2q_profile_kernels", "gpt2q_info", "gpt2q_argmax_noalloc", "gpt2q_rng_new", "gpt2q_rng_normal_f32", "gpt2q_rng_below",
     "gpt2q_quantize_q8", "gpt2q_quantize_q4", "gpt2q_nll",
     "gpt2q_set_adapter", "gpt2q_clear_adapter",
+    "gpt2q_create_from_smt", "gpt2q_smt_inspect", "gpt2q_blake3",
 ]
 
 
@@ -111,6 +112,12 @@ def load(path: str | None = None):
     lib.gpt2q_rng_normal_f32.restype = None
     lib.gpt2q_rng_below.argtypes = [_u64p, _u32p, C.c_size_t, C.c_uint64]
     lib.gpt2q_rng_below.restype = None
+    lib.gpt2q_create_from_smt.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_hp)]
+    lib.gpt2q_create_from_smt.restype = C.c_int
+    lib.gpt2q_smt_inspect.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_size_t]
+    lib.gpt2q_smt_inspect.restype = C.c_int
+    lib.gpt2q_blake3.argtypes = [C.c_void_p, C.c_uint64, C.POINTER(C.c_uint8)]
+    lib.gpt2q_blake3.restype = C.c_int
     for fn in (lib.gpt2q_quantize_q8, lib.gpt2q_quantize_q4):
         fn.argtypes = [_f32p, C.c_size_t, C.POINTER(C.c_uint8)]
         fn.restype = C.c_int

@@ -15,7 +15,7 @@ import json
 import numpy as np
 
 from . import _ffi
-from .pack import Pack
+from .pack import Meta, Pack
 
 
 def _descs(pack: Pack):
@@ -58,6 +58,26 @@ class Gpu:
         self.h = h
         self.max_seqs = max_seqs
         self.device = device
+
+    @classmethod
+    def from_smt(cls, path: str, device: int = 0, max_seqs: int = 1, max_tokens: int = 0,
+                 verify: bool = True) -> "Gpu":
+        """Engine::load + Gpu::new (gpt2.rs:43-89, gpu.rs:75-157) straight from an SMT file:
+        the library maps the file, verifies the merkle content_id and every tensor digest
+        (unless verify=False) and uploads the tensors; any mismatch raises Gpt2qError."""
+        from .smt import inspect
+        arch = inspect(path, verify=False)["arch"]
+        self = cls.__new__(cls)
+        self._lib = _ffi.load()
+        self.meta = Meta(arch["n_embd"], arch["n_layer"], arch["n_head"], arch["n_ctx"], arch["vocab_size"])
+        h = C.c_void_p()
+        rc = self._lib.gpt2q_create_from_smt(str(path).encode(), device, max_seqs, max_tokens, 1 if verify else 0,
+                                             C.byref(h))
+        _ffi.check(self._lib, None, rc)
+        self.h = h
+        self.max_seqs = max_seqs
+        self.device = device
+        return self
 
     # ---- lifetime ----
     def close(self):

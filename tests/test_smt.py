@@ -1,0 +1,194 @@
+"""SMT container (format.rs, gpt2.rs:43-110) and BLAKE3: the library's C++ reader and hash
+against the committed BLAKE3 vectors and the oracle's Python restatement (oracle/smt_oracle.py),
+round trips through write_smt, and refusal of any corrupted section or tensor. CPU only."""
+import json
+import os
+import re
+import struct
+
+import numpy as np
+import pytest
+
+from oracle import smt_oracle
+from smelt_b200 import _ffi, smt
+from smelt_b200._ffi import Gpt2qError
+
+from .golden.make_blake3 import data as golden_data
+from .helpers import MINI, TINY, make_pack
+
+HERE = os.path.dirname(__file__)
+HEADER = os.path.join(HERE, "..", "include", "gpt2q.h")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    from smelt_b200 import build
+    build.build()
+
+
+def _vectors():
+    with open(os.path.join(HERE, "golden", "blake3_vectors.json")) as f:
+        return json.load(f)["vectors"]
+
+
+def test_library_exports_every_declared_symbol():
+    """Every function include/gpt2q.h declares is exported by libgpt2q.so and bound in _ffi."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    declared = set(re.findall(r"\b(gpt2q_\w+)\s*\(", text))
+    assert declared == set(_ffi.EXPORTS)
+    lib = _ffi.load()
+    for name in sorted(declared):
+        assert hasattr(lib, name), name
+
+
+def test_blake3_native_matches_vectors():
+    for v in _vectors():
+        assert smt.blake3(golden_data(v["seed"], v["len"])).hex() == v["digest"], v["len"]
+
+
+def test_blake3_restatement_matches_vectors():
+    """The pure-Python restatement (small inputs only: it is slow)."""
+    for v in _vectors():
+        if v["len"] <= 70000:
+            assert smt_oracle.blake3(golden_data(v["seed"], v["len"])).hex() == v["digest"], v["len"]
+
+
+def test_blake3_matches_installed_binding_on_random_lengths():
+    b3 = pytest.importorskip("blake3")
+    rng = np.random.default_rng(11)
+    for n in rng.integers(0, 40000, 40).tolist() + [int(x) for x in rng.integers(1 << 20, 5 << 20, 3)]:
+        d = rng.integers(0, 256, n, dtype=np.uint8).tobytes()
+        assert smt.blake3(d) == b3.blake3(d).digest(), n
+
+
+def _sections(buf: bytes):
+    off, out = 128, []
+    while off < len(buf):
+        ty, fl, ln = struct.unpack_from("<IIQ", buf, off)
+        out.append((ty, fl, off + 16, ln))
+        off += 16 + ln
+    return out
+
+
+def _remerkle(buf: bytearray) -> bytearray:
+    """Recompute INDEX and the content_id after an edit, so only the tensor digests disagree."""
+    secs = _sections(bytes(buf))
+    digests = {}
+    for ty, _, p, ln in secs:
+        if ty != smt.SEC_INDEX:
+            digests[ty] = smt.blake3(bytes(buf[p:p + ln]))
+    for ty, _, p, ln in secs:
+        if ty == smt.SEC_INDEX:
+            index = b"".join(struct.pack("<I", t) + digests[t] for t, _, _, _ in secs if t != smt.SEC_INDEX)
+            assert len(index) == ln
+            buf[p:p + ln] = index
+            digests[ty] = smt.blake3(index)
+    buf[16:48] = smt.blake3(b"".join(sorted(digests.values())))
+    return buf
+
+
+@pytest.mark.parametrize("meta,policy", [(TINY, "auto"), (TINY, "q4auto"), (MINI, "core.f16"), (TINY, "f32")])
+def test_write_then_inspect_and_read_round_trip(tmp_path, meta, policy):
+    pk = make_pack(meta, policy)
+    path = str(tmp_path / "m.smt")
+    cid = smt.write_smt(path, pk)
+    info = smt.inspect(path, verify=True)
+    assert info["content_id"] == cid.hex() and info["verified"]
+    a = info["arch"]
+    assert (a["n_embd"], a["n_layer"], a["n_head"], a["n_ctx"], a["vocab_size"]) == (
+        meta.n_embd, meta.n_layer, meta.n_head, meta.n_ctx, meta.vocab)
+    assert [t["name"] for t in info["tensors"]] == list(pk.tensors)
+    for t in info["tensors"]:
+        ref = pk.tensors[t["name"]]
+        assert t["atom"] == ref.atom and tuple(t["shape"]) == tuple(ref.shape) and t["len"] == ref.data.nbytes
+    back = smt_oracle.read_smt(path)
+    assert back.meta == pk.meta
+    for name, t in pk.tensors.items():
+        assert np.array_equal(back.tensors[name].data, np.ascontiguousarray(t.data).view(np.uint8).ravel())
+    buf = open(path, "rb").read()
+    assert struct.unpack_from("<H", buf, 4)[0] == smt.VERSION
+    assert struct.unpack_from("<Q", buf, 48)[0] == len(buf)
+    assert [s[0] for s in _sections(buf)] == [smt.SEC_META, smt.SEC_GRAPH, smt.SEC_TOKENIZER, smt.SEC_TENSORS,
+                                              smt.SEC_INDEX]
+
+
+def test_content_id_matches_installed_binding(tmp_path):
+    """content_id = blake3 over the sorted section digests (format.rs:74-82), by the crate."""
+    b3 = pytest.importorskip("blake3")
+    path = str(tmp_path / "m.smt")
+    cid = smt.write_smt(path, make_pack(TINY, "auto"))
+    buf = open(path, "rb").read()
+    digests = sorted(b3.blake3(buf[p:p + ln]).digest() for _, _, p, ln in _sections(buf))
+    assert b3.blake3(b"".join(digests)).digest() == cid
+
+
+def test_corruption_is_refused(tmp_path):
+    pk = make_pack(TINY, "auto")
+    path = str(tmp_path / "m.smt")
+    smt.write_smt(path, pk)
+    good = bytearray(open(path, "rb").read())
+    secs = {ty: (p, ln) for ty, _, p, ln in _sections(bytes(good))}
+    p_t, _ = secs[smt.SEC_TENSORS]
+    json_len = struct.unpack_from("<I", good, p_t + 4)[0]
+    recs = json.loads(good[p_t + 8:p_t + 8 + json_len])
+    victim = recs[3]
+    at = p_t + 8 + json_len + victim["offset"] + victim["len"] // 2
+
+    def write(b, name):
+        q = str(tmp_path / name)
+        open(q, "wb").write(bytes(b))
+        return q
+
+    # a flipped payload byte breaks the merkle content_id
+    bad = bytearray(good)
+    bad[at] ^= 0x01
+    q = write(bad, "flip.smt")
+    with pytest.raises(Gpt2qError, match="merkle content_id mismatch"):
+        smt.inspect(q, verify=True)
+    smt.inspect(q, verify=False)  # without verification it parses
+    with pytest.raises(ValueError, match="merkle"):
+        smt_oracle.read_smt(q)
+    # the same flip with INDEX and content_id recomputed: the tensor digest catches it
+    q = write(_remerkle(bytearray(bad)), "flip_remerkle.smt")
+    with pytest.raises(Gpt2qError, match="digest mismatch: " + re.escape(victim["name"])):
+        smt.inspect(q, verify=True)
+    with pytest.raises(ValueError, match="digest mismatch"):
+        smt_oracle.read_smt(q)
+    # a flipped META byte (inside the JSON) is a merkle mismatch too
+    bad = bytearray(good)
+    bad[secs[smt.SEC_META][0] + 3] ^= 0x20
+    with pytest.raises(Gpt2qError, match="merkle"):
+        smt.inspect(write(bad, "meta.smt"), verify=True)
+    # bad magic, truncation, section length past the end
+    bad = bytearray(good)
+    bad[0:4] = b"SMT\x02"
+    with pytest.raises(Gpt2qError, match="bad magic"):
+        smt.inspect(write(bad, "magic.smt"), verify=False)
+    with pytest.raises(Gpt2qError, match="past the end|truncated"):
+        smt.inspect(write(good[:len(good) - 5], "trunc.smt"), verify=False)
+    with pytest.raises(Gpt2qError, match="too short"):
+        smt.inspect(write(good[:100], "short.smt"), verify=False)
+    with pytest.raises(Gpt2qError, match="cannot open"):
+        smt.inspect(str(tmp_path / "missing.smt"), verify=False)
+
+
+def test_record_past_section_is_refused(tmp_path):
+    """A tensor record whose offset+len leaves the TENSORS payload is refused even unverified."""
+    pk = make_pack(TINY, "auto")
+    path = str(tmp_path / "m.smt")
+    smt.write_smt(path, pk)
+    buf = bytearray(open(path, "rb").read())
+    p_t, ln_t = {ty: (p, ln) for ty, _, p, ln in _sections(bytes(buf))}[smt.SEC_TENSORS]
+    json_len = struct.unpack_from("<I", buf, p_t + 4)[0]
+    text = buf[p_t + 8:p_t + 8 + json_len].decode()
+    recs = json.loads(text)
+    last = recs[-1]
+    old = f'"offset": {last["offset"]}'
+    new = f'"offset": {last["offset"] + 1}'.ljust(len(old))  # same JSON length: layout unchanged
+    assert len(new) == len(old) and text.count(old) == 1
+    buf[p_t + 8:p_t + 8 + json_len] = text.replace(old, new).encode()
+    q = str(tmp_path / "past.smt")
+    open(q, "wb").write(bytes(buf))
+    with pytest.raises(Gpt2qError, match="runs past the section"):
+        smt.inspect(q, verify=False)
