@@ -223,6 +223,34 @@ int gpt2q_smt_inspect(const char* path, int verify, char* json, size_t cap);
  * hash the subtrees of large inputs. */
 int gpt2q_blake3(const void* data, uint64_t len, uint8_t* out32);
 
+/* ---- Backward of the trunk (the reference's plasticity path: cu/backward.cu, gpu_backward.rs) ----
+ *
+ * Input gradient of the whole trunk for one sequence (trunk_input_grad, gpu_backward.rs:651-790,
+ * over the activations of bwparity.rs forward_stash:448-580): the forward over ids[0..n-1]
+ * (positions 0..n-1) keeps every activation the backward needs on the device, then
+ * dlogits [n][vocab] (host) is propagated through the tied head, ln_f and every layer, all
+ * positions at once. Writes dx [n][n_embd] (host): the gradient with respect to the embedding
+ * output wte[ids[p]] + wpe[p] at each position. lnf_out (host, may be NULL) receives the ln_f
+ * output [n][n_embd], which the tied head's weight gradient needs (dlogits[p][v] * lnf_out[p]).
+ * The plastic adapter is not part of the trunk. 1 <= n <= n_ctx; single-GPU handles only. */
+int gpt2q_trunk_input_grad(gpt2q_handle* h, const uint32_t* ids, int n, const float* dlogits, float* dx,
+                           float* lnf_out);
+
+/* Per-op backward kernels with the BwdOps signatures (gpu_backward.rs:69-93): host buffers,
+ * uploaded and downloaded per call on `device`, like GpuBackward's methods (gpu_backward.rs:
+ * 307-377). Errors are reported by gpt2q_last_error(NULL).
+ * lin_input_grad: dx[i] = sum_r w[r*cols+i] * dy[r] (k_lin_input_grad); cols % 4 == 0. */
+int gpt2q_bwd_lin_input_grad(int device, const float* w, const float* dy, int rows, int cols, float* dx);
+/* LayerNorm backward of one n-vector (k_ln_backward); dg and db accumulate. */
+int gpt2q_bwd_ln_backward(int device, const float* dy, const float* x, const float* g, const float* b, float eps,
+                          int n, float* dx, float* dg, float* db);
+/* dx[i] = dy[i] * gelu'(x_pre[i]) for the tanh GELU (k_gelu_bwd). */
+int gpt2q_bwd_gelu(int device, const float* x_pre, const float* dy, int n, float* dx);
+/* Causal training-form attention backward (k_attn_bwd_train): q/k/v/dy [t][stride], head h
+ * at column h*hd, stride/hd heads; dq overwritten, dk and dv accumulate. t <= 1024, hd <= 128. */
+int gpt2q_bwd_attn_train(int device, const float* q, const float* k, const float* v, const float* dy, int t, int hd,
+                         int stride, float* dq, float* dk, float* dv);
+
 #ifdef __cplusplus
 }
 #endif

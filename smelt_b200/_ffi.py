@@ -23,6 +23,8 @@ EXPORTS = [
     "gpt2q_quantize_q8", "gpt2q_quantize_q4", "gpt2q_nll",
     "gpt2q_set_adapter", "gpt2q_clear_adapter",
     "gpt2q_create_from_smt", "gpt2q_smt_inspect", "gpt2q_blake3",
+    "gpt2q_trunk_input_grad", "gpt2q_bwd_lin_input_grad", "gpt2q_bwd_ln_backward", "gpt2q_bwd_gelu",
+    "gpt2q_bwd_attn_train",
 ]
 
 
@@ -118,6 +120,18 @@ def load(path: str | None = None):
     lib.gpt2q_smt_inspect.restype = C.c_int
     lib.gpt2q_blake3.argtypes = [C.c_void_p, C.c_uint64, C.POINTER(C.c_uint8)]
     lib.gpt2q_blake3.restype = C.c_int
+    lib.gpt2q_trunk_input_grad.argtypes = [_hp, _u32p, C.c_int, _f32p, _f32p, _f32p]
+    lib.gpt2q_trunk_input_grad.restype = C.c_int
+    lib.gpt2q_bwd_lin_input_grad.argtypes = [C.c_int, _f32p, _f32p, C.c_int, C.c_int, _f32p]
+    lib.gpt2q_bwd_lin_input_grad.restype = C.c_int
+    lib.gpt2q_bwd_ln_backward.argtypes = [C.c_int, _f32p, _f32p, _f32p, _f32p, C.c_float, C.c_int, _f32p, _f32p,
+                                          _f32p]
+    lib.gpt2q_bwd_ln_backward.restype = C.c_int
+    lib.gpt2q_bwd_gelu.argtypes = [C.c_int, _f32p, _f32p, C.c_int, _f32p]
+    lib.gpt2q_bwd_gelu.restype = C.c_int
+    lib.gpt2q_bwd_attn_train.argtypes = [C.c_int, _f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, _f32p,
+                                         _f32p, _f32p]
+    lib.gpt2q_bwd_attn_train.restype = C.c_int
     for fn in (lib.gpt2q_quantize_q8, lib.gpt2q_quantize_q4):
         fn.argtypes = [_f32p, C.c_size_t, C.POINTER(C.c_uint8)]
         fn.restype = C.c_int

@@ -1,0 +1,628 @@
+// Backward kernels of the GPT-2 trunk, batched over positions (fp32, sm_100a).
+//
+// The reference runs one GEMV-shaped launch per position and per op (gpu_backward.rs:651-790
+// over cu/backward.cu); here every op takes all T positions of a sequence at once:
+// * k_bwd_linear: the transposed product dX = dY . W as an outer-product accumulation. A CTA
+//   owns 128 columns x 16 positions and a contiguous range of W's rows; each warp walks rows
+//   (coalesced 128-byte row segments of the quantised payload, dequantised exactly in
+//   registers) and broadcasts the staged dY values from shared memory. Row ranges are split
+//   across CTAs so the grid fills the 148 SMs; k_bwd_reduce sums the splits in fixed order and
+//   applies the epilogue (store, add, or GELU backward), so results are deterministic.
+// * k_bwd_ln: one CTA per row, fixed-order block reductions.
+// * attention: one CTA per (query row, head) recomputes the probability row, the row's dP and
+//   dq; one CTA per (key row, head) recomputes the column of P and dS from the saved row
+//   statistics and sums dk and dv over the later queries in increasing order, as the reference
+//   kernel's accumulation does. No atomics anywhere.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "backward.h"
+#include "gpt2q.h"
+
+namespace gpt2q {
+
+void set_global_error(const std::string& msg);
+
+namespace {
+
+constexpr int BL_COLS = 128;  // columns per CTA (4 per lane)
+constexpr int BL_TT = 16;     // positions per CTA
+constexpr int BL_RCH = 128;   // rows of dY staged per chunk
+constexpr int BL_WARPS = 8;
+constexpr int BL_PAD = 20;    // row stride of the staged dY tile (floats; 16-byte aligned rows)
+constexpr int ATT_MAX_T = 1024;
+constexpr int ATT_MAX_HD = 128;
+
+struct BwdSplit {
+    int splits, rows_per_split, col_tiles, t_tiles;
+};
+
+BwdSplit bwd_split(int T, int rows, int cols) {
+    BwdSplit s;
+    s.col_tiles = (cols + BL_COLS - 1) / BL_COLS;
+    s.t_tiles = (T + BL_TT - 1) / BL_TT;
+    const int chunks = (rows + BL_RCH - 1) / BL_RCH;
+    int want = (2 * 148 + s.col_tiles * s.t_tiles - 1) / (s.col_tiles * s.t_tiles);
+    want = want < 1 ? 1 : (want > 64 ? 64 : want);
+    if (want > chunks) want = chunks;
+    const int ch_per = (chunks + want - 1) / want;
+    s.rows_per_split = ch_per * BL_RCH;
+    s.splits = (rows + s.rows_per_split - 1) / s.rows_per_split;
+    if (s.splits < 1) s.splits = 1;
+    return s;
+}
+
+// Four consecutive dequantised weights W[r][c..c+3] (c % 4 == 0), each exactly (float)q * scale.
+template <int ATOM>
+__device__ __forceinline__ void load_w4(const QW& w, int r, int c, float f[4]) {
+    const uint8_t* row = w.q + (size_t)r * w.qstride;
+    if (ATOM == ATOM_F32) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(row) + (c >> 2));
+        f[0] = v.x, f[1] = v.y, f[2] = v.z, f[3] = v.w;
+    } else if (ATOM == ATOM_F16) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(row) + (c >> 2));
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
+    } else if (ATOM == ATOM_Q8) {
+        const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(row) + (c >> 2));
+        i8x4_to_f32(u, f);
+        const float s = __half2float(w.s[(size_t)r * w.sstride + (c >> 5)]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] *= s;
+    } else {  // Q4: per 32-group byte j = elem j (low nibble) | elem j+16 (high nibble)
+        const int g = c >> 5, e = c & 31;
+        const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(row + g * 16 + (e & 15)));
+        float lo[4], hi[4];
+        i4x8_to_f32(u, lo, hi);
+        const float s = __half2float(w.s[(size_t)r * w.sstride + g]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = (e < 16 ? lo[j] : hi[j]) * s;
+    }
+}
+
+template <int ATOM>
+__global__ void __launch_bounds__(256) k_bwd_linear(QW w, const float* __restrict__ dY, int ldy, int T,
+                                                    int rows_per_split, float* __restrict__ part) {
+    __shared__ __align__(16) float dys[BL_RCH * BL_PAD];
+    __shared__ __align__(16) float red[BL_WARPS * 8 * BL_COLS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = blockIdx.x * BL_COLS, t0 = blockIdx.y * BL_TT;
+    const int r_begin = blockIdx.z * rows_per_split;
+    const int r_end = min(w.rows, r_begin + rows_per_split);
+    const int c = c0 + 4 * lane;
+    const bool cok = c < w.cols;
+    float acc[BL_TT][4];
+#pragma unroll
+    for (int t = 0; t < BL_TT; ++t)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[t][j] = 0.f;
+
+    for (int rc = r_begin; rc < r_end; rc += BL_RCH) {
+        const int nr = min(BL_RCH, r_end - rc);
+        __syncthreads();
+        for (int i = threadIdx.x; i < BL_RCH * BL_TT; i += blockDim.x) {
+            const int t = i / BL_RCH, r = i - t * BL_RCH;
+            dys[r * BL_PAD + t] = (t0 + t < T && r < nr) ? dY[(size_t)(t0 + t) * ldy + rc + r] : 0.f;
+        }
+        __syncthreads();
+        if (cok) {
+            for (int rb = 0; rb < nr; rb += 4 * BL_WARPS) {
+                float f[4][4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int r = rb + warp + k * BL_WARPS;
+                    if (r < nr) {
+                        load_w4<ATOM>(w, rc + r, c, f[k]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) f[k][j] = 0.f;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int r = rb + warp + k * BL_WARPS;
+                    if (r < nr) {
+                        const float4* dv = reinterpret_cast<const float4*>(dys + r * BL_PAD);
+#pragma unroll
+                        for (int q = 0; q < BL_TT / 4; ++q) {
+                            const float4 y = dv[q];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                acc[4 * q + 0][j] = fmaf(y.x, f[k][j], acc[4 * q + 0][j]);
+                                acc[4 * q + 1][j] = fmaf(y.y, f[k][j], acc[4 * q + 1][j]);
+                                acc[4 * q + 2][j] = fmaf(y.z, f[k][j], acc[4 * q + 2][j]);
+                                acc[4 * q + 3][j] = fmaf(y.w, f[k][j], acc[4 * q + 3][j]);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    // sum the warps' partials in warp order, 8 positions per pass
+    float* out = part + (size_t)blockIdx.z * T * w.cols;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+            *reinterpret_cast<float4*>(red + (warp * 8 + t) * BL_COLS + 4 * lane) =
+                make_float4(acc[half * 8 + t][0], acc[half * 8 + t][1], acc[half * 8 + t][2], acc[half * 8 + t][3]);
+        __syncthreads();
+        for (int i = threadIdx.x; i < 8 * BL_COLS; i += blockDim.x) {
+            const int t = i / BL_COLS, cc = i - t * BL_COLS;
+            const int tg = t0 + half * 8 + t, cg = c0 + cc;
+            if (tg < T && cg < w.cols) {
+                float s = 0.f;
+#pragma unroll
+                for (int wp = 0; wp < BL_WARPS; ++wp) s += red[(wp * 8 + t) * BL_COLS + cc];
+                out[(size_t)tg * w.cols + cg] = s;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ float gelu_grad(float v) {
+    // d/dv of 0.5 v (1 + tanh(u)), u = c (v + 0.044715 v^3), in cu/backward.cu:124-130's order
+    const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+    const float th = tanhf(u);
+    const float sech2 = 1.f - th * th;
+    return 0.5f * (1.f + th) + 0.5f * v * sech2 * 0.7978845608028654f * (1.f + 3.f * 0.044715f * v * v);
+}
+
+__global__ void k_bwd_reduce(const float* __restrict__ part, int splits, int T, int cols, int epi,
+                             float* __restrict__ out, int ldo, const float* __restrict__ xpre, int ldx) {
+    const size_t n = (size_t)T * cols;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / cols), c = (int)(i - (size_t)t * cols);
+        float s = 0.f;
+        for (int z = 0; z < splits; ++z) s += part[(size_t)z * n + i];
+        float* o = out + (size_t)t * ldo + c;
+        if (epi == BWD_ADD)
+            *o += s;
+        else if (epi == BWD_GELU_BWD)
+            *o = s * gelu_grad(xpre[(size_t)t * ldx + c]);
+        else
+            *o = s;
+    }
+}
+
+// Sum over the block in fixed order (warp shuffles, then warp 0 over the warps' sums).
+__device__ float block_sum(float v, float* red) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.f;
+    for (int i = 0; i < nw; ++i) s += red[i];
+    return s;
+}
+
+__device__ float block_max(float v, float* red) {
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    float m = -1e30f;
+    for (int i = 0; i < nw; ++i) m = fmaxf(m, red[i]);
+    return m;
+}
+
+// LayerNorm backward of one row per CTA (cu/backward.cu:38-115): mean and population variance
+// recomputed from the saved input, then
+// dx = rstd * (dy*g - mean(dy*g) - xhat * mean(dy*g*xhat)).
+__global__ void __launch_bounds__(256) k_bwd_ln(const float* __restrict__ dY, int ldy, const float* __restrict__ X,
+                                                int ldx, const float* __restrict__ g, float eps, int n, int epi,
+                                                float* __restrict__ out, int ldo, float* dg, float* db) {
+    __shared__ float red[32];
+    const int t = blockIdx.x;
+    const float* x = X + (size_t)t * ldx;
+    const float* dy = dY + (size_t)t * ldy;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+    const float mean = block_sum(s, red) / (float)n;
+    float sq = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i] - mean;
+        sq = fmaf(v, v, sq);
+    }
+    const float rstd = 1.0f / sqrtf(block_sum(sq, red) / (float)n + eps);
+    float a = 0.f, cc = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float dh = dy[i] * g[i];
+        a += dh;
+        cc = fmaf(dh, (x[i] - mean) * rstd, cc);
+    }
+    const float mdxh = block_sum(a, red) / (float)n;
+    const float mdxh_xh = block_sum(cc, red) / (float)n;
+    float* o = out + (size_t)t * ldo;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float xh = (x[i] - mean) * rstd;
+        const float dh = dy[i] * g[i];
+        const float v = rstd * (dh - mdxh - xh * mdxh_xh);
+        if (epi == BWD_ADD)
+            o[i] += v;
+        else
+            o[i] = v;
+        if (dg) dg[i] += dy[i] * xh;
+        if (db) db[i] += dy[i];
+    }
+}
+
+__global__ void k_gelu_fwd(const float* __restrict__ x, float* __restrict__ out, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = gelu_tanh(x[i]);
+}
+
+__global__ void k_gelu_bwd(const float* __restrict__ x, const float* __restrict__ dy, float* __restrict__ dx,
+                           size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dx[i] = dy[i] * gelu_grad(x[i]);
+}
+
+// Scaled score and dot products shared by the attention kernels (same operands, same order,
+// so the probability recomputed by the key-row kernel equals the query-row kernel's).
+__device__ __forceinline__ float dot_hd(const float* a, const float* b, int hd) {
+    float d = 0.f;
+    for (int t = 0; t < hd; ++t) d = fmaf(a[t], b[t], d);
+    return d;
+}
+
+// Query row i of head h: P row (causal, j <= i), out_i = sum_j P_ij v_j.
+__global__ void __launch_bounds__(128) k_attn_fwd_train(const float* __restrict__ q, int ldq,
+                                                        const float* __restrict__ k, int ldk,
+                                                        const float* __restrict__ v, int ldv, int hd, float scale,
+                                                        float* __restrict__ out, int ldo) {
+    __shared__ float qs[ATT_MAX_HD];
+    __shared__ float sc[ATT_MAX_T];
+    __shared__ float red[32];
+    const int i = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const size_t base = (size_t)h * hd;
+    for (int t = tid; t < hd; t += blockDim.x) qs[t] = q[(size_t)i * ldq + base + t];
+    __syncthreads();
+    float mx = -1e30f;
+    for (int j = tid; j <= i; j += blockDim.x) {
+        const float s = dot_hd(qs, k + (size_t)j * ldk + base, hd) * scale;
+        sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    const float m = block_max(mx, red);
+    float ls = 0.f;
+    for (int j = tid; j <= i; j += blockDim.x) {
+        const float e = expf(sc[j] - m);
+        sc[j] = e;
+        ls += e;
+    }
+    const float L = block_sum(ls, red);
+    for (int j = tid; j <= i; j += blockDim.x) sc[j] = sc[j] / L;
+    __syncthreads();
+    for (int t = tid; t < hd; t += blockDim.x) {
+        float o = 0.f;
+        for (int j = 0; j <= i; ++j) o = fmaf(sc[j], v[(size_t)j * ldv + base + t], o);
+        out[(size_t)i * ldo + base + t] = o;
+    }
+}
+
+// Query row i of head h: P row, dP_j = dy_i . v_j, rs = sum_j dP_j P_j,
+// dS_j = (dP_j - rs) P_j scale, dq_i = sum_j dS_j k_j. Saves (m, L, rs) for the key-row pass.
+__global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__ q, int ldq,
+                                                       const float* __restrict__ k, int ldk,
+                                                       const float* __restrict__ v, int ldv,
+                                                       const float* __restrict__ dy, int lddy, int T, int hd,
+                                                       float scale, float* __restrict__ dq, int lddq,
+                                                       float* __restrict__ stats) {
+    __shared__ float qs[ATT_MAX_HD], dys[ATT_MAX_HD];
+    __shared__ float sc[ATT_MAX_T], dp[ATT_MAX_T];
+    __shared__ float red[32];
+    const int i = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const size_t base = (size_t)h * hd;
+    for (int t = tid; t < hd; t += blockDim.x) {
+        qs[t] = q[(size_t)i * ldq + base + t];
+        dys[t] = dy[(size_t)i * lddy + base + t];
+    }
+    __syncthreads();
+    float mx = -1e30f;
+    for (int j = tid; j <= i; j += blockDim.x) {
+        const float s = dot_hd(qs, k + (size_t)j * ldk + base, hd) * scale;
+        sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    const float m = block_max(mx, red);
+    float ls = 0.f;
+    for (int j = tid; j <= i; j += blockDim.x) {
+        const float e = expf(sc[j] - m);
+        sc[j] = e;
+        ls += e;
+    }
+    const float L = block_sum(ls, red);
+    float rsp = 0.f;
+    for (int j = tid; j <= i; j += blockDim.x) {
+        const float p = sc[j] / L;
+        sc[j] = p;
+        const float d = dot_hd(dys, v + (size_t)j * ldv + base, hd);
+        dp[j] = d;
+        rsp = fmaf(d, p, rsp);
+    }
+    const float rs = block_sum(rsp, red);
+    for (int j = tid; j <= i; j += blockDim.x) dp[j] = (dp[j] - rs) * sc[j] * scale;
+    __syncthreads();
+    for (int t = tid; t < hd; t += blockDim.x) {
+        float a = 0.f;
+        for (int j = 0; j <= i; ++j) a = fmaf(dp[j], k[(size_t)j * ldk + base + t], a);
+        dq[(size_t)i * lddq + base + t] = a;
+    }
+    if (tid == 0) {
+        float* st = stats + ((size_t)h * T + i) * 3;
+        st[0] = m;
+        st[1] = L;
+        st[2] = rs;
+    }
+}
+
+// Key row j of head h: P_ij and dS_ij for i >= j from the saved row statistics, then
+// dk_j = sum_i dS_ij q_i and dv_j = sum_i P_ij dy_i, i increasing.
+__global__ void __launch_bounds__(128) k_attn_bwd_keys(const float* __restrict__ q, int ldq,
+                                                       const float* __restrict__ k, int ldk,
+                                                       const float* __restrict__ v, int ldv,
+                                                       const float* __restrict__ dy, int lddy, int T, int hd,
+                                                       float scale, const float* __restrict__ stats, float* dk,
+                                                       int lddk, float* dv, int lddv, int accumulate) {
+    __shared__ float ks[ATT_MAX_HD], vs[ATT_MAX_HD];
+    __shared__ float pv[ATT_MAX_T], dsv[ATT_MAX_T];
+    const int j = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const size_t base = (size_t)h * hd;
+    for (int t = tid; t < hd; t += blockDim.x) {
+        ks[t] = k[(size_t)j * ldk + base + t];
+        vs[t] = v[(size_t)j * ldv + base + t];
+    }
+    __syncthreads();
+    for (int i = j + tid; i < T; i += blockDim.x) {
+        const float* st = stats + ((size_t)h * T + i) * 3;
+        const float s = dot_hd(q + (size_t)i * ldq + base, ks, hd) * scale;
+        const float p = expf(s - st[0]) / st[1];
+        const float d = dot_hd(dy + (size_t)i * lddy + base, vs, hd);
+        pv[i] = p;
+        dsv[i] = (d - st[2]) * p * scale;
+    }
+    __syncthreads();
+    for (int t = tid; t < hd; t += blockDim.x) {
+        float* dkp = dk + (size_t)j * lddk + base + t;
+        float* dvp = dv + (size_t)j * lddv + base + t;
+        float a = accumulate ? *dkp : 0.f, b = accumulate ? *dvp : 0.f;
+        for (int i = j; i < T; ++i) {
+            a = fmaf(dsv[i], q[(size_t)i * ldq + base + t], a);
+            b = fmaf(pv[i], dy[(size_t)i * lddy + base + t], b);
+        }
+        *dkp = a;
+        *dvp = b;
+    }
+}
+
+int grid_1d(size_t n, int block) {
+    size_t g = (n + block - 1) / block;
+    if (g > 148 * 16) g = 148 * 16;
+    return g < 1 ? 1 : (int)g;
+}
+
+}  // namespace
+
+size_t bwd_linear_part_floats(int T, int rows, int cols) {
+    const BwdSplit s = bwd_split(T, rows, cols);
+    return (size_t)s.splits * T * cols;
+}
+
+cudaError_t launch_bwd_linear(const QW& w, const float* dY, int ldy, int T, float* part, int epi, float* out,
+                              int ldo, const float* xpre, int ldx, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (w.cols % 4 != 0) return cudaErrorInvalidValue;
+    const BwdSplit s = bwd_split(T, w.rows, w.cols);
+    const dim3 grid(s.col_tiles, s.t_tiles, s.splits), block(256);
+    switch (w.atom) {
+        case ATOM_Q8: k_bwd_linear<ATOM_Q8><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part); break;
+        case ATOM_Q4: k_bwd_linear<ATOM_Q4><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part); break;
+        case ATOM_F16: k_bwd_linear<ATOM_F16><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part); break;
+        default: k_bwd_linear<ATOM_F32><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part); break;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t n = (size_t)T * w.cols;
+    k_bwd_reduce<<<grid_1d(n, 256), 256, 0, st>>>(part, s.splits, T, w.cols, epi, out, ldo, xpre, ldx);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_ln(const float* dY, int ldy, const float* x, int ldx, const float* g, float eps, int n, int T,
+                          int epi, float* out, int ldo, float* dg, float* db, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if ((dg || db) && T != 1) return cudaErrorInvalidValue;
+    k_bwd_ln<<<T, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, epi, out, ldo, dg, db);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gelu_fwd(const float* x, float* out, size_t n, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    k_gelu_fwd<<<grid_1d(n, 256), 256, 0, st>>>(x, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gelu_bwd(const float* x, const float* dy, float* dx, size_t n, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    k_gelu_bwd<<<grid_1d(n, 256), 256, 0, st>>>(x, dy, dx, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attn_fwd_train(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, int T,
+                                  int n_head, int hd, float* out, int ldo, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (T > ATT_MAX_T || hd > ATT_MAX_HD || hd <= 0 || n_head <= 0) return cudaErrorInvalidValue;
+    const float scale = 1.0f / sqrtf((float)hd);
+    k_attn_fwd_train<<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, hd, scale, out, ldo);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attn_bwd_train(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv,
+                                  const float* dy, int lddy, int T, int n_head, int hd, float* dq, int lddq, float* dk,
+                                  int lddk, float* dv, int lddv, int accumulate, float* stats, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (T > ATT_MAX_T || hd > ATT_MAX_HD || hd <= 0 || n_head <= 0) return cudaErrorInvalidValue;
+    const float scale = 1.0f / sqrtf((float)hd);
+    k_attn_bwd_rows<<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, dq, lddq, stats);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    k_attn_bwd_keys<<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, stats, dk, lddk,
+                                                     dv, lddv, accumulate);
+    return cudaGetLastError();
+}
+
+}  // namespace gpt2q
+
+// =================================================================== per-op C-ABI
+// Host-slice operations with the BwdOps signatures (gpu_backward.rs:69-93): every call uploads
+// its inputs, runs the kernel on `device` and downloads the outputs, like GpuBackward's
+// trait methods (gpu_backward.rs:307-377).
+using namespace gpt2q;
+
+namespace {
+
+struct Scratch {
+    std::vector<void*> ptrs;
+    cudaStream_t st = nullptr;
+    cudaError_t err = cudaSuccess;
+    ~Scratch() {
+        if (st) cudaStreamSynchronize(st);
+        for (void* p : ptrs) cudaFree(p);
+        if (st) cudaStreamDestroy(st);
+    }
+    float* up(const float* h, size_t n) {
+        float* d = alloc(n);
+        if (d && h && n) err = cudaMemcpyAsync(d, h, n * 4, cudaMemcpyHostToDevice, st);
+        return err == cudaSuccess ? d : nullptr;
+    }
+    float* alloc(size_t n) {
+        if (err != cudaSuccess) return nullptr;
+        void* p = nullptr;
+        err = cudaMalloc(&p, n ? n * 4 : 16);
+        if (err != cudaSuccess) return nullptr;
+        ptrs.push_back(p);
+        return static_cast<float*>(p);
+    }
+    int down(float* h, const float* d, size_t n) {
+        if (err == cudaSuccess && n) err = cudaMemcpyAsync(h, d, n * 4, cudaMemcpyDeviceToHost, st);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+        return err == cudaSuccess ? GPT2Q_OK : GPT2Q_ECUDA;
+    }
+};
+
+int open_scratch(int device, Scratch& s, const char* fn) {
+    if ((s.err = cudaSetDevice(device)) != cudaSuccess ||
+        (s.err = cudaStreamCreateWithFlags(&s.st, cudaStreamNonBlocking)) != cudaSuccess) {
+        set_global_error(std::string(fn) + ": " + cudaGetErrorString(s.err));
+        return GPT2Q_ECUDA;
+    }
+    return GPT2Q_OK;
+}
+
+int finish(Scratch& s, int rc, const char* fn) {
+    if (rc != GPT2Q_OK || s.err != cudaSuccess) {
+        set_global_error(std::string(fn) + ": " + cudaGetErrorString(s.err));
+        return GPT2Q_ECUDA;
+    }
+    return GPT2Q_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gpt2q_bwd_lin_input_grad(int device, const float* w, const float* dy, int rows, int cols, float* dx) {
+    if (!w || !dy || !dx || rows <= 0 || cols <= 0 || cols % 4 != 0) {
+        set_global_error("gpt2q_bwd_lin_input_grad: null pointer, or rows/cols not positive, or cols % 4 != 0");
+        return GPT2Q_EARG;
+    }
+    Scratch s;
+    if (open_scratch(device, s, "gpt2q_bwd_lin_input_grad") != GPT2Q_OK) return GPT2Q_ECUDA;
+    QW q{};
+    q.q = reinterpret_cast<const uint8_t*>(s.up(w, (size_t)rows * cols));
+    q.rows = rows;
+    q.cols = cols;
+    q.atom = ATOM_F32;
+    q.qstride = (size_t)cols * 4;
+    const float* ddy = s.up(dy, rows);
+    float* part = s.alloc(bwd_linear_part_floats(1, rows, cols));
+    float* ddx = s.alloc(cols);
+    if (s.err == cudaSuccess) s.err = launch_bwd_linear(q, ddy, rows, 1, part, BWD_STORE, ddx, cols, nullptr, 0, s.st);
+    return finish(s, s.down(dx, ddx, cols), "gpt2q_bwd_lin_input_grad");
+}
+
+int gpt2q_bwd_ln_backward(int device, const float* dy, const float* x, const float* g, const float* b, float eps,
+                          int n, float* dx, float* dg, float* db) {
+    (void)b;  // the bias does not enter the Jacobian (cu/backward.cu:114)
+    if (!dy || !x || !g || !dx || !dg || !db || n <= 0) {
+        set_global_error("gpt2q_bwd_ln_backward: null pointer or n <= 0");
+        return GPT2Q_EARG;
+    }
+    Scratch s;
+    if (open_scratch(device, s, "gpt2q_bwd_ln_backward") != GPT2Q_OK) return GPT2Q_ECUDA;
+    const float* ddy = s.up(dy, n);
+    const float* dxs = s.up(x, n);
+    const float* dgm = s.up(g, n);
+    float* ddx = s.alloc(n);
+    float* ddg = s.up(dg, n);
+    float* ddb = s.up(db, n);
+    if (s.err == cudaSuccess)
+        s.err = launch_bwd_ln(ddy, n, dxs, n, dgm, eps, n, 1, BWD_STORE, ddx, n, ddg, ddb, s.st);
+    int rc = s.down(dx, ddx, n);
+    if (rc == GPT2Q_OK) rc = s.down(dg, ddg, n);
+    if (rc == GPT2Q_OK) rc = s.down(db, ddb, n);
+    return finish(s, rc, "gpt2q_bwd_ln_backward");
+}
+
+int gpt2q_bwd_gelu(int device, const float* x_pre, const float* dy, int n, float* dx) {
+    if (!x_pre || !dy || !dx || n <= 0) {
+        set_global_error("gpt2q_bwd_gelu: null pointer or n <= 0");
+        return GPT2Q_EARG;
+    }
+    Scratch s;
+    if (open_scratch(device, s, "gpt2q_bwd_gelu") != GPT2Q_OK) return GPT2Q_ECUDA;
+    const float* dxp = s.up(x_pre, n);
+    const float* ddy = s.up(dy, n);
+    float* ddx = s.alloc(n);
+    if (s.err == cudaSuccess) s.err = launch_gelu_bwd(dxp, ddy, ddx, (size_t)n, s.st);
+    return finish(s, s.down(dx, ddx, n), "gpt2q_bwd_gelu");
+}
+
+int gpt2q_bwd_attn_train(int device, const float* q, const float* k, const float* v, const float* dy, int t, int hd,
+                         int stride, float* dq, float* dk, float* dv) {
+    if (!q || !k || !v || !dy || !dq || !dk || !dv || t <= 0 || hd <= 0 || stride <= 0 || stride % hd != 0 ||
+        t > ATT_MAX_T || hd > ATT_MAX_HD) {
+        set_global_error("gpt2q_bwd_attn_train: null pointer, or t/hd/stride out of range (t <= 1024, hd <= 128, "
+                         "stride a multiple of hd)");
+        return GPT2Q_EARG;
+    }
+    Scratch s;
+    if (open_scratch(device, s, "gpt2q_bwd_attn_train") != GPT2Q_OK) return GPT2Q_ECUDA;
+    const size_t total = (size_t)t * stride;
+    const int heads = stride / hd;
+    const float* d_q = s.up(q, total);
+    const float* d_k = s.up(k, total);
+    const float* d_v = s.up(v, total);
+    const float* d_dy = s.up(dy, total);
+    float* d_dq = s.alloc(total);
+    float* d_dk = s.up(dk, total);
+    float* d_dv = s.up(dv, total);
+    float* stats = s.alloc((size_t)3 * heads * t);
+    if (s.err == cudaSuccess)
+        s.err = launch_attn_bwd_train(d_q, stride, d_k, stride, d_v, stride, d_dy, stride, t, heads, hd, d_dq, stride,
+                                      d_dk, stride, d_dv, stride, 1, stats, s.st);
+    int rc = s.down(dq, d_dq, total);
+    if (rc == GPT2Q_OK) rc = s.down(dk, d_dk, total);
+    if (rc == GPT2Q_OK) rc = s.down(dv, d_dv, total);
+    return finish(s, rc, "gpt2q_bwd_attn_train");
+}
+
+}  // extern "C"

@@ -26,6 +26,7 @@
 
 #include "gpt2q.h"
 #include "gemm.h"
+#include "backward.h"
 #include "kernels.h"
 #include "persistent.h"
 #include "tp.h"
@@ -135,6 +136,9 @@ struct gpt2q_handle {
     int* nll_tgt = nullptr;
     double* nll_terms = nullptr;
     int* kerr = nullptr;  // device error word of the CUDA-core kernels' bounded waits
+    // trunk backward workspace (grown on demand, freed by destroy)
+    float* bwd_ws = nullptr;
+    size_t bwd_ws_floats = 0;
     // prefill scratch
     uint32_t* p_tok = nullptr;
     int *p_pos = nullptr, *p_slot = nullptr, *p_lastrow = nullptr, *p_lastpos = nullptr;
@@ -1122,6 +1126,154 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     return GPT2Q_OK;
 }
 
+
+// ------------------------------------------------------------------ trunk input gradient
+// Forward over one sequence with the activations the backward needs (the stash of the
+// reference's bwparity.rs forward_stash:448-580: per layer the residual entering the layer,
+// the residual after the attention branch, q|k|v with bias and the pre-GELU c_fc output; the
+// input of ln_f and its output), then trunk_input_grad (gpu_backward.rs:651-790) with every op
+// batched over the T positions. Weights are read in their uploaded atoms; the dequantised
+// values are exactly Engine::vec_f32's, the f32 weights the reference's backward uses.
+int trunk_grad(gpt2q_handle* H, const uint32_t* ids, int T, const float* dlogits, float* dx_out, float* lnf_out) {
+    const int d = H->cfg.n_embd, L = H->cfg.n_layer, V = H->cfg.vocab, NH = H->cfg.n_head, hd = H->hd;
+    const int F = H->fc_local, d3 = 3 * d;
+    const float eps = H->cfg.ln_eps;
+    auto up64 = [](size_t n) { return (n + 63) / 64 * 64; };
+    size_t part_n = bwd_linear_part_floats(T, V, d);
+    for (const LayerW& lw : H->layers) {
+        part_n = std::max(part_n, bwd_linear_part_floats(T, lw.attn.rows, lw.attn.cols));
+        part_n = std::max(part_n, bwd_linear_part_floats(T, lw.proj.rows, lw.proj.cols));
+        part_n = std::max(part_n, bwd_linear_part_floats(T, lw.fc.rows, lw.fc.cols));
+        part_n = std::max(part_n, bwd_linear_part_floats(T, lw.mproj.rows, lw.mproj.cols));
+    }
+    const size_t Td = up64((size_t)T * d), TF = up64((size_t)T * F), T3 = up64((size_t)T * d3);
+    const size_t need = (size_t)(L + 1) * Td + (size_t)L * (Td + T3 + TF)  // stash
+                        + Td                                               // ln_f output
+                        + 2 * Td + TF                                      // h, att, gelu(fc)
+                        + up64((size_t)T * V)                              // dlogits
+                        + 3 * Td + TF + T3                                 // G, DH, DATT, DFC, DQKV
+                        + up64(part_n) + up64((size_t)3 * NH * T) + up64((size_t)2 * T);
+    if (H->bwd_ws_floats < need) {
+        if (H->bwd_ws) {
+            CK(cudaStreamSynchronize(H->stream));
+            cudaFree(H->bwd_ws);
+            H->bwd_ws = nullptr;
+            H->bwd_ws_floats = 0;
+        }
+        if (cudaMalloc(&H->bwd_ws, need * 4) != cudaSuccess) {
+            H->bwd_ws = nullptr;
+            return H->fail(GPT2Q_EOOM, "trunk backward workspace (" + std::to_string(need * 4) + " bytes)");
+        }
+        H->bwd_ws_floats = need;
+    }
+    float* w = H->bwd_ws;
+    auto take = [&](size_t n) {
+        float* p = w;
+        w += n;
+        return p;
+    };
+    float* xs = take((size_t)(L + 1) * Td);  // x_in of layer l at l*Td; x_L is ln_f's input
+    float* xmid = take((size_t)L * Td);
+    float* qkv = take((size_t)L * T3);
+    float* fcpre = take((size_t)L * TF);
+    float* lnf = take(Td);
+    float* hb = take(Td);
+    float* att = take(Td);
+    float* fb = take(TF);
+    float* DL = take(up64((size_t)T * V));
+    float* G = take(Td);
+    float* DH = take(Td);
+    float* DATT = take(Td);
+    float* DFC = take(TF);
+    float* DQKV = take(T3);
+    float* part = take(up64(part_n));
+    float* stats = take(up64((size_t)3 * NH * T));
+    int* d_ids = reinterpret_cast<int*>(take(up64((size_t)2 * T)));
+    int* d_pos = d_ids + T;
+
+    std::vector<int> hi(2 * (size_t)T);
+    for (int p = 0; p < T; ++p) {
+        hi[p] = (int)ids[p];
+        hi[T + p] = p;
+    }
+    CK(cudaMemcpyAsync(d_ids, hi.data(), hi.size() * 4, cudaMemcpyHostToDevice, H->stream));
+    CK(cudaMemcpyAsync(DL, dlogits, (size_t)T * V * 4, cudaMemcpyHostToDevice, H->stream));
+
+    // ---- forward with the stash ----
+    RUN("embed", (double)T * d * 8,
+        launch_embed(H->wte.w, H->wpe.w, reinterpret_cast<const uint32_t*>(d_ids), d_pos, xs, d, T, H->stream));
+    for (int l = 0; l < L; ++l) {
+        const LayerW& lw = H->layers[l];
+        float* xin = xs + (size_t)l * Td;
+        float* xm = xmid + (size_t)l * Td;
+        float* qk = qkv + (size_t)l * T3;
+        float* fp = fcpre + (size_t)l * TF;
+        float* xo = xs + (size_t)(l + 1) * Td;
+        RUN("layernorm", (double)T * d * 8,
+            launch_layernorm(xin, d, nullptr, hb, d, nullptr, nullptr, lw.ln1_g, lw.ln1_b, d, eps, T, H->stream));
+        RUN("linear_qkv", linear_bytes(lw.attn, T, 1),
+            launch_linear_simt(lw.attn.w, hb, d, T, epi_store(qk, d3, lw.attn.bias), H->stream));
+        RUN("attn_train", (double)T * d3 * 4,
+            launch_attn_fwd_train(qk, d3, qk + d, d3, qk + 2 * d, d3, T, NH, hd, att, d, H->stream));
+        CK(cudaMemcpyAsync(xm, xin, (size_t)T * d * 4, cudaMemcpyDeviceToDevice, H->stream));
+        Epi er = epi_store(xm, d, lw.proj.bias);
+        er.kind = EPI_RESID;
+        RUN("linear_proj", linear_bytes(lw.proj, T, 2), launch_linear_simt(lw.proj.w, att, d, T, er, H->stream));
+        RUN("layernorm", (double)T * d * 8,
+            launch_layernorm(xm, d, nullptr, hb, d, nullptr, nullptr, lw.ln2_g, lw.ln2_b, d, eps, T, H->stream));
+        RUN("linear_fc", linear_bytes(lw.fc, T, 1),
+            launch_linear_simt(lw.fc.w, hb, d, T, epi_store(fp, F, lw.fc.bias), H->stream));
+        RUN("gelu", (double)T * F * 8, launch_gelu_fwd(fp, fb, (size_t)T * F, H->stream));
+        CK(cudaMemcpyAsync(xo, xm, (size_t)T * d * 4, cudaMemcpyDeviceToDevice, H->stream));
+        Epi em = epi_store(xo, d, lw.mproj.bias);
+        em.kind = EPI_RESID;
+        RUN("linear_mproj", linear_bytes(lw.mproj, T, 2), launch_linear_simt(lw.mproj.w, fb, F, T, em, H->stream));
+    }
+    const float* xL = xs + (size_t)L * Td;
+    RUN("layernorm", (double)T * d * 8,
+        launch_layernorm(xL, d, nullptr, lnf, d, nullptr, nullptr, H->lnf_g, H->lnf_b, d, eps, T, H->stream));
+
+    // ---- backward: head, ln_f, then the layers in reverse ----
+    auto bwd_lin = [&](const char* name, const Linear& Lw, const float* dY, int ldy, int epi, float* out, int ldo,
+                       const float* xpre, int ldx) {
+        const double bytes = (double)Lw.weight_bytes * ((T + 15) / 16) + (double)T * (Lw.rows + 2 * Lw.cols) * 4;
+        return run_kernel(H, name, bytes, [&]() {
+            return launch_bwd_linear(Lw.w, dY, ldy, T, part, epi, out, ldo, xpre, ldx, H->stream);
+        });
+    };
+    int rc = bwd_lin("bwd_linear_head", H->wte, DL, V, BWD_STORE, DH, d, nullptr, 0);
+    if (rc) return rc;
+    RUN("bwd_ln", (double)T * d * 16,
+        launch_bwd_ln(DH, d, xL, d, H->lnf_g, eps, d, T, BWD_STORE, G, d, nullptr, nullptr, H->stream));
+    for (int l = L - 1; l >= 0; --l) {
+        const LayerW& lw = H->layers[l];
+        const float* xin = xs + (size_t)l * Td;
+        const float* xm = xmid + (size_t)l * Td;
+        const float* qk = qkv + (size_t)l * T3;
+        const float* fp = fcpre + (size_t)l * TF;
+        // MLP branch: d_fc = gelu'(fc_pre) * (W_mproj^T g), dh2 = W_fc^T d_fc, g += LN2^T(dh2)
+        rc = bwd_lin("bwd_linear_mproj", lw.mproj, G, d, BWD_GELU_BWD, DFC, F, fp, F);
+        if (rc) return rc;
+        rc = bwd_lin("bwd_linear_fc", lw.fc, DFC, F, BWD_STORE, DH, d, nullptr, 0);
+        if (rc) return rc;
+        RUN("bwd_ln", (double)T * d * 16,
+            launch_bwd_ln(DH, d, xm, d, lw.ln2_g, eps, d, T, BWD_ADD, G, d, nullptr, nullptr, H->stream));
+        // attention branch on g = d(x_mid): c_proj^T, attention backward, c_attn^T, LN1^T
+        rc = bwd_lin("bwd_linear_proj", lw.proj, G, d, BWD_STORE, DATT, d, nullptr, 0);
+        if (rc) return rc;
+        RUN("bwd_attn", (double)T * d3 * 8,
+            launch_attn_bwd_train(qk, d3, qk + d, d3, qk + 2 * d, d3, DATT, d, T, NH, hd, DQKV, d3, DQKV + d, d3,
+                                  DQKV + 2 * d, d3, 0, stats, H->stream));
+        rc = bwd_lin("bwd_linear_qkv", lw.attn, DQKV, d3, BWD_STORE, DH, d, nullptr, 0);
+        if (rc) return rc;
+        RUN("bwd_ln", (double)T * d * 16,
+            launch_bwd_ln(DH, d, xin, d, lw.ln1_g, eps, d, T, BWD_ADD, G, d, nullptr, nullptr, H->stream));
+    }
+    CK(cudaMemcpyAsync(dx_out, G, (size_t)T * d * 4, cudaMemcpyDeviceToHost, H->stream));
+    if (lnf_out) CK(cudaMemcpyAsync(lnf_out, lnf, (size_t)T * d * 4, cudaMemcpyDeviceToHost, H->stream));
+    CK(cudaStreamSynchronize(H->stream));
+    return check_device_error(H);
+}
 }  // namespace
 
 // Message for gpt2q_last_error(NULL), used by calls that have no handle.
@@ -1159,6 +1311,7 @@ void gpt2q_destroy(gpt2q_handle* H) {
     gemm_destroy(H->gemm);
     mk_destroy(H->mk);
     for (auto& a : H->allocs) cudaFree(a.p);
+    if (H->bwd_ws) cudaFree(H->bwd_ws);
     if (H->h_stage) cudaFreeHost(H->h_stage);
     if (H->own_stream) cudaStreamDestroy(H->own_stream);
     delete H;
@@ -1378,6 +1531,19 @@ int gpt2q_nll(gpt2q_handle* H, const uint32_t* ids, int n, int slot, double* out
     *out = total / (double)R;
     // the slot's cache now holds this sequence; its decode state is not advanced
     return GPT2Q_OK;
+}
+
+int gpt2q_trunk_input_grad(gpt2q_handle* H, const uint32_t* ids, int n, const float* dlogits, float* dx,
+                           float* lnf_out) {
+    if (!H) return GPT2Q_EARG;
+    if (!ids || !dlogits || !dx) return H->fail(GPT2Q_EARG, "null ids/dlogits/dx");
+    if (n < 1 || n > H->cfg.n_ctx) return H->fail(GPT2Q_EARG, "n out of range [1, n_ctx]");
+    if (H->tp_size > 1) return H->fail(GPT2Q_EUNSUP, "trunk backward needs a single-GPU handle");
+    if (H->hd > 128) return H->fail(GPT2Q_EUNSUP, "trunk backward needs head dim <= 128");
+    CK(cudaSetDevice(H->device));
+    const int rc = check_tokens(H, ids, (size_t)n);
+    if (rc) return rc;
+    return trunk_grad(H, ids, n, dlogits, dx, lnf_out);
 }
 
 int gpt2q_dequant(gpt2q_handle* H, const char* name, float* out, uint64_t n) {

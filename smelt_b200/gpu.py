@@ -191,6 +191,21 @@ class Gpu:
                                         C.byref(out)))
         return float(out.value)
 
+    def trunk_input_grad(self, ids, dlogits):
+        """(dx [n][n_embd], lnf_out [n][n_embd]): the trunk input gradient of trunk_input_grad
+        (gpu_backward.rs:651-790) for dlogits [n][vocab], forward and backward on the device."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        n = ids.size
+        dl = np.ascontiguousarray(dlogits, dtype=np.float32)
+        if dl.shape != (n, self.meta.vocab):
+            raise ValueError(f"dlogits must be [{n}][{self.meta.vocab}]")
+        dx = np.empty((n, self.meta.n_embd), np.float32)
+        lnf = np.empty((n, self.meta.n_embd), np.float32)
+        self._check(self._lib.gpt2q_trunk_input_grad(self.h, ids.ctypes.data_as(_ffi._u32p), n,
+                                                     dl.ctypes.data_as(_ffi._f32p), dx.ctypes.data_as(_ffi._f32p),
+                                                     lnf.ctypes.data_as(_ffi._f32p)))
+        return dx, lnf
+
     def dequant(self, name: str, numel: int) -> np.ndarray:
         out = np.empty(numel, dtype=np.float32)
         self._check(self._lib.gpt2q_dequant(self.h, name.encode(), out.ctypes.data_as(_ffi._f32p), numel))

@@ -1,0 +1,43 @@
+"""The oracle's restatement of the trunk backward (oracle/backward_oracle.py) on its own: its four
+ops pass the reference's finite-difference self-checks (gpu_backward.rs:915-1090), and the
+composed trunk_input_grad (gpu_backward.rs:651-790) agrees with central differences of the f64
+forward (bwparity.rs:690-735) on small models. CPU only."""
+import numpy as np
+import pytest
+
+from oracle import backward_oracle as B
+
+from .helpers import MINI, TINY, make_pack
+
+
+@pytest.mark.parametrize("kernel", B.KERNELS)
+def test_mirror_ops_pass_reference_self_checks(kernel):
+    mr, tol = B.selfcheck(B.MirrorOps(), kernel)
+    assert mr < tol, (kernel, mr, tol)
+
+
+def test_rng_matches_reference_definition():
+    """xorshift64* with seed ^ 0x9E3779B97F4A7C15 (gpu_backward.rs:838-856): first outputs by hand."""
+    r = B.Rng(0)
+    x = 0x9E3779B97F4A7C15
+    x ^= x >> 12
+    x ^= (x << 25) & B.M64
+    x ^= x >> 27
+    assert r.next_u64() == (x * 0x2545F4914F6CDD1D) & B.M64
+    r = B.Rng(7)
+    vals = [r.f32() for _ in range(1000)]
+    assert all(-1.0 <= v < 1.0 for v in vals) and all(v.dtype == np.float32 for v in vals)
+
+
+@pytest.mark.parametrize("meta,policy", [(TINY, "f32"), (TINY, "auto"), (MINI, "q4auto")])
+def test_trunk_composition_matches_finite_differences(meta, policy):
+    pk = make_pack(meta, policy, 0, 0.02)
+    W = B.weights64(pk)
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, meta.vocab, 6).astype(np.uint32)
+    ids[3] = ids[0]  # a repeated token: the input path sums over its positions
+    dl = B.sparse_dlogits(len(ids), meta.vocab)
+    _, acts = B.forward_stash(W, meta, ids)
+    dx = B.trunk_input_grad(W, meta, acts, dl.astype(np.float64))
+    rows = B.fd_embedding_check(W, meta, ids, dl, dx, acts["lnf_out"], n_coords=16)
+    assert B.rel_max(rows[:, 0], rows[:, 1]) < 1e-3
