@@ -48,6 +48,7 @@ WORKLOADS = {
     "small-int4-b256": ("small", "q4auto", 256, 264, 256, "strong"),  # 256 ragged prompts 16..512, int4
     "medium-int8-prefill": ("medium", "auto", 64, 1024, 1, "strong"),  # 64 x 1024-token prefill
     "xl-int8-tp": ("xl", "auto", 16, 256, 256, "strong"),           # GPT-2 XL, tensor parallel
+    "small-int8-trunk-bwd": ("small", "auto", 1, 64, 0, "weak"),    # trunk input gradient of 64 positions
 }
 
 
@@ -218,7 +219,133 @@ METRICS = {
     "small-int4-b256": "decode tokens/s (GPT-2 small int4)",
     "medium-int8-prefill": "prefill tokens/s (GPT-2 medium int8)",
     "xl-int8-tp": "decode tokens/s (GPT-2 XL int8, tensor parallel)",
+    "small-int8-trunk-bwd": "trunk input-gradient positions/s (GPT-2 small int8, forward stash + backward)",
 }
+
+
+def bwd_sample(pk, T: int, seed: int = 1):
+    """Token ids and the sparse dlogits of the reference's bwparity gate (8 entries per position)."""
+    from oracle import backward_oracle as B
+    from smelt_b200 import synth
+
+    ids = np.asarray(synth.prompt_ids(T, pk.meta.vocab, seed=seed), np.uint32)
+    return ids, B.sparse_dlogits(T, pk.meta.vocab)
+
+
+def cpu_trunk_baseline(pk, T: int, reps: int):
+    """The oracle's trunk backward (f64 numpy, BLAS threads) on T positions, positions/s."""
+    from oracle import backward_oracle as B
+
+    W = B.weights64(pk)
+    ids, dl = bwd_sample(pk, T)
+    dl64 = dl.astype(np.float64)
+    _, acts = B.forward_stash(W, pk.meta, ids)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        _, acts = B.forward_stash(W, pk.meta, ids)
+        B.trunk_input_grad(W, pk.meta, acts, dl64)
+    dt = time.perf_counter() - t0
+    return reps * T / dt, dt
+
+
+def run_trunk_bwd(args, wl):
+    """Trunk input gradient of one 64-position sequence of GPT-2 small int8 (the reference's
+    plasticity backward, gpu_backward.rs:651-790): a step is one gpt2q_trunk_input_grad call,
+    i.e. the forward with its activation stash plus the backward through the head, ln_f and the
+    12 layers, all positions batched. Ranks run independent sequences (weak scaling)."""
+    import torch
+
+    from smelt_b200.gpu import Gpu
+
+    model, policy, _batch, T, _dec, scaling = wl
+    world, rank, local, dev = dist_setup()
+    pk = build_pack(model, policy)
+    meta = pk.meta
+    ids, dl = bwd_sample(pk, T, seed=1 + rank)
+    g = Gpu(pk, device=local, max_seqs=1)
+    stream = torch.cuda.Stream(device=dev)
+    g.set_stream(stream.cuda_stream)
+    for _ in range(max(args.warmup, 3)):
+        g.trunk_input_grad(ids, dl)
+    # per-kernel times of one call (CUDA events around every launch)
+    g.profile(True)
+    g.trunk_input_grad(ids, dl)
+    prof = g.profile_read()
+    g.profile(False)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    l0 = g.launches
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}") as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            g.trunk_input_grad(ids, dl)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        ms = ev0.elapsed_time(ev1)
+    launches = (g.launches - l0) / args.steps
+    ms_max = max_over_ranks(ms, world, dev)
+    wall_max = max_over_ranks(wall, world, dev)
+    hbm, peak_src = peaks()
+    top = max(prof.items(), key=lambda kv: kv[1]["ms"])
+    kname, kv = top
+    per_launch_ms = kv["ms"] / kv["launches"]
+    achieved = kv["bytes"] / kv["launches"] / (per_launch_ms / 1e3) / 1e9
+    total_ms = sum(v["ms"] for v in prof.values())
+    line = {
+        "metric": METRICS[args.config], "value": world * T * args.steps / (ms_max / 1e3), "unit": "positions/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "int8xfp32", "data": "synthetic",
+        "config": {"workload": args.config, "model": f"gpt2-{model}", "weights": policy, "positions": T,
+                   "dlogits": "8 random entries per position (bwparity gate)",
+                   "step": "gpt2q_trunk_input_grad: forward stash + backward, host dlogits in, host dx out",
+                   "l2": "no flush; the head backward streams the 41 MB int8 wte and 12.9 MB of dlogits"},
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": None, "peak_source": peak_src,
+                     "share_of_step": kv["ms"] / total_ms if total_ms else None,
+                     "note": "per-launch CUDA events in profiling mode; algorithmic bytes = weights once + dY + dX"},
+        "kernels": {k: {"launches": v["launches"], "us_per_launch": 1e3 * v["ms"] / v["launches"]}
+                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])[:8]},
+        "e2e": {"value": world * T * args.steps / wall_max, "unit": "positions/s",
+                "h2d_bytes_per_step": T * meta.vocab * 4 + T * 8, "d2h_bytes_per_step": 2 * T * meta.n_embd * 4,
+                "api": "gpt2q_trunk_input_grad"},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+    }
+    g.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, dt = cpu_trunk_baseline(pk, T, 12)
+        line["cpu_baseline"] = {"value": v, "unit": "positions/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"12 calls x {T} positions in {dt:.1f} s: oracle f64 numpy restatement "
+                                          "of forward_stash + trunk_input_grad, BLAS threads"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_reference_trunk(args, wl):
+    """The reference arm of the trunk-backward workload: the oracle's restatement on the host
+    cores, each step one call on the workload's 64 positions."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    pk = build_pack(wl[0], wl[1])
+    cpu_trunk_baseline(pk, wl[3], 1)
+    v, dt = cpu_trunk_baseline(pk, wl[3], args.steps)
+    line = {
+        "impl": "reference", "metric": METRICS[args.config], "value": v, "unit": "positions/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": wl[5], "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": args.config, "model": f"gpt2-{wl[0]}", "weights": wl[1], "positions": wl[3]},
+        "cpu_baseline": {"value": v, "unit": "positions/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{args.steps} calls x {wl[3]} positions, oracle f64 numpy restatement"},
+        "e2e": {"value": v, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
 
 
 def run_reference(args, wl):
@@ -484,13 +611,19 @@ def main():
     if args.batch > 0:
         wl = (wl[0], wl[1], args.batch) + tuple(wl[3:])
     if args.impl == "reference":
-        run_reference(args, wl)
+        if args.config == "small-int8-trunk-bwd":
+            run_reference_trunk(args, wl)
+        else:
+            run_reference(args, wl)
         return
     if args.config == "medium-int8-prefill":
         run_prefill(args, wl)
         return
     if args.config == "xl-int8-tp":
         run_tp(args, wl)
+        return
+    if args.config == "small-int8-trunk-bwd":
+        run_trunk_bwd(args, wl)
         return
     import torch
 

@@ -6,13 +6,13 @@
 //   owns 128 columns x 16 positions and a contiguous range of W's rows; each warp walks rows
 //   (coalesced 128-byte row segments of the quantised payload, dequantised exactly in
 //   registers) and broadcasts the staged dY values from shared memory. Row ranges are split
-//   across CTAs so the grid fills the 148 SMs; k_bwd_reduce sums the splits in fixed order and
-//   applies the epilogue (store, add, or GELU backward), so results are deterministic.
+//   across CTAs so the grid fills the 148 SMs; the last CTA of each tile sums the splits in
+//   fixed order and applies the epilogue (store, add, or GELU backward): deterministic.
 // * k_bwd_ln: one CTA per row, fixed-order block reductions.
 // * attention: one CTA per (query row, head) recomputes the probability row, the row's dP and
 //   dq; one CTA per (key row, head) recomputes the column of P and dS from the saved row
 //   statistics and sums dk and dv over the later queries in increasing order, as the reference
-//   kernel's accumulation does. No atomics anywhere.
+//   kernel's accumulation does. No floating-point atomics anywhere.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -30,9 +30,11 @@ namespace {
 
 constexpr int BL_COLS = 128;  // columns per CTA (4 per lane)
 constexpr int BL_TT = 16;     // positions per CTA
-constexpr int BL_RCH = 128;   // rows of dY staged per chunk
+constexpr int BL_RCH = 256;   // rows of dY staged per chunk (double-buffered)
 constexpr int BL_WARPS = 8;
 constexpr int BL_PAD = 20;    // row stride of the staged dY tile (floats; 16-byte aligned rows)
+constexpr int BL_RB = 8;      // weight rows in flight per warp
+constexpr int BL_PRE = BL_RCH * BL_TT / 256;  // dY values each thread prefetches per chunk
 constexpr int ATT_MAX_T = 1024;
 constexpr int ATT_MAX_HD = 128;
 
@@ -84,12 +86,38 @@ __device__ __forceinline__ void load_w4(const QW& w, int r, int c, float f[4]) {
     }
 }
 
+__device__ __forceinline__ float gelu_grad(float v) {
+    // d/dv of 0.5 v (1 + tanh(u)), u = c (v + 0.044715 v^3), in cu/backward.cu:124-130's order
+    const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+    const float th = tanhf(u);
+    const float sech2 = 1.f - th * th;
+    return 0.5f * (1.f + th) + 0.5f * v * sech2 * 0.7978845608028654f * (1.f + 3.f * 0.044715f * v * v);
+}
+
+__device__ __forceinline__ void bwd_epi(int epi, float s, float* out, int ldo, const float* xpre, int ldx, int t,
+                                        int c) {
+    float* o = out + (size_t)t * ldo + c;
+    if (epi == BWD_ADD)
+        *o += s;
+    else if (epi == BWD_GELU_BWD)
+        *o = s * gelu_grad(xpre[(size_t)t * ldx + c]);
+    else
+        *o = s;
+}
+
+// dX = dY . W for 128 columns x 16 positions over this CTA's row range. dY is staged chunk by
+// chunk into shared memory, the next chunk prefetched into registers while the current one is
+// consumed; each warp keeps 8 weight rows in flight. The warps' partials are summed in warp
+// order. With several row splits every CTA stores its partial and the last CTA of the tile
+// (atomic ticket after a fence) sums the splits in split order and applies the epilogue, so the
+// result does not depend on which CTA finishes last.
 template <int ATOM>
-__global__ void __launch_bounds__(256) k_bwd_linear(QW w, const float* __restrict__ dY, int ldy, int T,
-                                                    int rows_per_split, float* __restrict__ part) {
-    __shared__ __align__(16) float dys[BL_RCH * BL_PAD];
-    __shared__ __align__(16) float red[BL_WARPS * 8 * BL_COLS];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(256, 2) k_bwd_linear(QW w, const float* __restrict__ dY, int ldy, int T,
+                                                       int rows_per_split, float* part, unsigned* counters,
+                                                       int epi, float* out, int ldo, const float* xpre, int ldx) {
+    __shared__ __align__(16) float sm[2 * BL_RCH * BL_PAD];  // dY double buffer, then the warp partials
+    __shared__ bool is_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c0 = blockIdx.x * BL_COLS, t0 = blockIdx.y * BL_TT;
     const int r_begin = blockIdx.z * rows_per_split;
     const int r_end = min(w.rows, r_begin + rows_per_split);
@@ -101,19 +129,38 @@ __global__ void __launch_bounds__(256) k_bwd_linear(QW w, const float* __restric
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[t][j] = 0.f;
 
-    for (int rc = r_begin; rc < r_end; rc += BL_RCH) {
-        const int nr = min(BL_RCH, r_end - rc);
-        __syncthreads();
-        for (int i = threadIdx.x; i < BL_RCH * BL_TT; i += blockDim.x) {
-            const int t = i / BL_RCH, r = i - t * BL_RCH;
-            dys[r * BL_PAD + t] = (t0 + t < T && r < nr) ? dY[(size_t)(t0 + t) * ldy + rc + r] : 0.f;
-        }
-        __syncthreads();
-        if (cok) {
-            for (int rb = 0; rb < nr; rb += 4 * BL_WARPS) {
-                float f[4][4];
+    float pre[BL_PRE];
+    auto load_chunk = [&](int rc, int nr) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < BL_PRE; ++k) {
+            const int i = tid + k * 256, t = i / BL_RCH, r = i - t * BL_RCH;
+            pre[k] = (t0 + t < T && r < nr) ? dY[(size_t)(t0 + t) * ldy + rc + r] : 0.f;
+        }
+    };
+    auto store_chunk = [&](float* buf) {
+#pragma unroll
+        for (int k = 0; k < BL_PRE; ++k) {
+            const int i = tid + k * 256, t = i / BL_RCH, r = i - t * BL_RCH;
+            buf[r * BL_PAD + t] = pre[k];
+        }
+    };
+    const int nchunks = r_end > r_begin ? (r_end - r_begin + BL_RCH - 1) / BL_RCH : 0;
+    if (nchunks > 0) {
+        load_chunk(r_begin, min(BL_RCH, r_end - r_begin));
+        store_chunk(sm);
+    }
+    __syncthreads();
+    for (int ci = 0; ci < nchunks; ++ci) {
+        const int rc = r_begin + ci * BL_RCH;
+        const int nr = min(BL_RCH, r_end - rc);
+        const float* cur = sm + (ci & 1) * BL_RCH * BL_PAD;
+        const bool more = ci + 1 < nchunks;
+        if (more) load_chunk(rc + BL_RCH, min(BL_RCH, r_end - rc - BL_RCH));
+        if (cok) {
+            for (int rb = 0; rb < nr; rb += BL_RB * BL_WARPS) {
+                float f[BL_RB][4];
+#pragma unroll
+                for (int k = 0; k < BL_RB; ++k) {
                     const int r = rb + warp + k * BL_WARPS;
                     if (r < nr) {
                         load_w4<ATOM>(w, rc + r, c, f[k]);
@@ -123,28 +170,31 @@ __global__ void __launch_bounds__(256) k_bwd_linear(QW w, const float* __restric
                     }
                 }
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int r = rb + warp + k * BL_WARPS;
-                    if (r < nr) {
-                        const float4* dv = reinterpret_cast<const float4*>(dys + r * BL_PAD);
+                for (int k = 0; k < BL_RB; ++k) {
+                    // rows past nr carry zero weights; their staged dY row is any row in bounds
+                    const int r = min(rb + warp + k * BL_WARPS, BL_RCH - 1);
+                    const float4* dv = reinterpret_cast<const float4*>(cur + r * BL_PAD);
 #pragma unroll
-                        for (int q = 0; q < BL_TT / 4; ++q) {
-                            const float4 y = dv[q];
+                    for (int q = 0; q < BL_TT / 4; ++q) {
+                        const float4 y = dv[q];
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                acc[4 * q + 0][j] = fmaf(y.x, f[k][j], acc[4 * q + 0][j]);
-                                acc[4 * q + 1][j] = fmaf(y.y, f[k][j], acc[4 * q + 1][j]);
-                                acc[4 * q + 2][j] = fmaf(y.z, f[k][j], acc[4 * q + 2][j]);
-                                acc[4 * q + 3][j] = fmaf(y.w, f[k][j], acc[4 * q + 3][j]);
-                            }
+                        for (int j = 0; j < 4; ++j) {
+                            acc[4 * q + 0][j] = fmaf(y.x, f[k][j], acc[4 * q + 0][j]);
+                            acc[4 * q + 1][j] = fmaf(y.y, f[k][j], acc[4 * q + 1][j]);
+                            acc[4 * q + 2][j] = fmaf(y.z, f[k][j], acc[4 * q + 2][j]);
+                            acc[4 * q + 3][j] = fmaf(y.w, f[k][j], acc[4 * q + 3][j]);
                         }
                     }
                 }
             }
         }
+        if (more) store_chunk(sm + ((ci + 1) & 1) * BL_RCH * BL_PAD);
+        __syncthreads();
     }
-    // sum the warps' partials in warp order, 8 positions per pass
-    float* out = part + (size_t)blockIdx.z * T * w.cols;
+    // warp partials summed in warp order, 8 positions per pass
+    const bool split = gridDim.z > 1;
+    float* mine = part + (size_t)blockIdx.z * T * w.cols;
+    float* red = sm;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
         __syncthreads();
@@ -153,42 +203,39 @@ __global__ void __launch_bounds__(256) k_bwd_linear(QW w, const float* __restric
             *reinterpret_cast<float4*>(red + (warp * 8 + t) * BL_COLS + 4 * lane) =
                 make_float4(acc[half * 8 + t][0], acc[half * 8 + t][1], acc[half * 8 + t][2], acc[half * 8 + t][3]);
         __syncthreads();
-        for (int i = threadIdx.x; i < 8 * BL_COLS; i += blockDim.x) {
+        for (int i = tid; i < 8 * BL_COLS; i += blockDim.x) {
             const int t = i / BL_COLS, cc = i - t * BL_COLS;
             const int tg = t0 + half * 8 + t, cg = c0 + cc;
             if (tg < T && cg < w.cols) {
-                float s = 0.f;
+                float v = 0.f;
 #pragma unroll
-                for (int wp = 0; wp < BL_WARPS; ++wp) s += red[(wp * 8 + t) * BL_COLS + cc];
-                out[(size_t)tg * w.cols + cg] = s;
+                for (int wp = 0; wp < BL_WARPS; ++wp) v += red[(wp * 8 + t) * BL_COLS + cc];
+                if (split)
+                    mine[(size_t)tg * w.cols + cg] = v;
+                else
+                    bwd_epi(epi, v, out, ldo, xpre, ldx, tg, cg);
             }
         }
     }
-}
-
-__device__ __forceinline__ float gelu_grad(float v) {
-    // d/dv of 0.5 v (1 + tanh(u)), u = c (v + 0.044715 v^3), in cu/backward.cu:124-130's order
-    const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-    const float th = tanhf(u);
-    const float sech2 = 1.f - th * th;
-    return 0.5f * (1.f + th) + 0.5f * v * sech2 * 0.7978845608028654f * (1.f + 3.f * 0.044715f * v * v);
-}
-
-__global__ void k_bwd_reduce(const float* __restrict__ part, int splits, int T, int cols, int epi,
-                             float* __restrict__ out, int ldo, const float* __restrict__ xpre, int ldx) {
-    const size_t n = (size_t)T * cols;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int t = (int)(i / cols), c = (int)(i - (size_t)t * cols);
-        float s = 0.f;
-        for (int z = 0; z < splits; ++z) s += part[(size_t)z * n + i];
-        float* o = out + (size_t)t * ldo + c;
-        if (epi == BWD_ADD)
-            *o += s;
-        else if (epi == BWD_GELU_BWD)
-            *o = s * gelu_grad(xpre[(size_t)t * ldx + c]);
-        else
-            *o = s;
+    if (!split) return;
+    __threadfence();
+    __syncthreads();
+    unsigned* ticket = counters + blockIdx.y * gridDim.x + blockIdx.x;
+    if (tid == 0) is_last = atomicAdd(ticket, 1u) == gridDim.z - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const int tn = min(BL_TT, T - t0);
+    for (int i = tid; i < tn * BL_COLS; i += blockDim.x) {
+        const int t = i / BL_COLS, cc = i - t * BL_COLS;
+        const int tg = t0 + t, cg = c0 + cc;
+        if (cg < w.cols) {
+            float v = 0.f;
+            for (int z = 0; z < (int)gridDim.z; ++z) v += __ldcg(part + ((size_t)z * T + tg) * w.cols + cg);
+            bwd_epi(epi, v, out, ldo, xpre, ldx, tg, cg);
+        }
     }
+    if (tid == 0) *ticket = 0u;  // ready for the next launch
 }
 
 // Sum over the block in fixed order (warp shuffles, then warp 0 over the warps' sums).
@@ -255,9 +302,12 @@ __global__ void __launch_bounds__(256) k_bwd_ln(const float* __restrict__ dY, in
     }
 }
 
-__global__ void k_gelu_fwd(const float* __restrict__ x, float* __restrict__ out, size_t n) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        out[i] = gelu_tanh(x[i]);
+__global__ void k_gelu_fwd(const float* __restrict__ x, float* __restrict__ out, __half* ohi, __half* olo, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float g = gelu_tanh(x[i]);
+        out[i] = g;
+        if (ohi) split_hl(g, ohi[i], olo[i]);
+    }
 }
 
 __global__ void k_gelu_bwd(const float* __restrict__ x, const float* __restrict__ dy, float* __restrict__ dx,
@@ -268,17 +318,25 @@ __global__ void k_gelu_bwd(const float* __restrict__ x, const float* __restrict_
 
 // Scaled score and dot products shared by the attention kernels (same operands, same order,
 // so the probability recomputed by the key-row kernel equals the query-row kernel's).
+// HD > 0 fixes the head dim at compile time (loads batched by full unrolling); HD == 0 reads hd.
+template <int HD>
 __device__ __forceinline__ float dot_hd(const float* a, const float* b, int hd) {
     float d = 0.f;
-    for (int t = 0; t < hd; ++t) d = fmaf(a[t], b[t], d);
+    if (HD > 0) {
+#pragma unroll
+        for (int t = 0; t < HD; ++t) d = fmaf(a[t], b[t], d);
+    } else {
+        for (int t = 0; t < hd; ++t) d = fmaf(a[t], b[t], d);
+    }
     return d;
 }
 
 // Query row i of head h: P row (causal, j <= i), out_i = sum_j P_ij v_j.
+template <int HD>
 __global__ void __launch_bounds__(128) k_attn_fwd_train(const float* __restrict__ q, int ldq,
                                                         const float* __restrict__ k, int ldk,
                                                         const float* __restrict__ v, int ldv, int hd, float scale,
-                                                        float* __restrict__ out, int ldo) {
+                                                        float* __restrict__ out, int ldo, __half* ohi, __half* olo) {
     __shared__ float qs[ATT_MAX_HD];
     __shared__ float sc[ATT_MAX_T];
     __shared__ float red[32];
@@ -288,7 +346,7 @@ __global__ void __launch_bounds__(128) k_attn_fwd_train(const float* __restrict_
     __syncthreads();
     float mx = -1e30f;
     for (int j = tid; j <= i; j += blockDim.x) {
-        const float s = dot_hd(qs, k + (size_t)j * ldk + base, hd) * scale;
+        const float s = dot_hd<HD>(qs, k + (size_t)j * ldk + base, hd) * scale;
         sc[j] = s;
         mx = fmaxf(mx, s);
     }
@@ -304,13 +362,16 @@ __global__ void __launch_bounds__(128) k_attn_fwd_train(const float* __restrict_
     __syncthreads();
     for (int t = tid; t < hd; t += blockDim.x) {
         float o = 0.f;
+#pragma unroll 8
         for (int j = 0; j <= i; ++j) o = fmaf(sc[j], v[(size_t)j * ldv + base + t], o);
         out[(size_t)i * ldo + base + t] = o;
+        if (ohi) split_hl(o, ohi[(size_t)i * ldo + base + t], olo[(size_t)i * ldo + base + t]);
     }
 }
 
 // Query row i of head h: P row, dP_j = dy_i . v_j, rs = sum_j dP_j P_j,
 // dS_j = (dP_j - rs) P_j scale, dq_i = sum_j dS_j k_j. Saves (m, L, rs) for the key-row pass.
+template <int HD>
 __global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__ q, int ldq,
                                                        const float* __restrict__ k, int ldk,
                                                        const float* __restrict__ v, int ldv,
@@ -329,7 +390,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__
     __syncthreads();
     float mx = -1e30f;
     for (int j = tid; j <= i; j += blockDim.x) {
-        const float s = dot_hd(qs, k + (size_t)j * ldk + base, hd) * scale;
+        const float s = dot_hd<HD>(qs, k + (size_t)j * ldk + base, hd) * scale;
         sc[j] = s;
         mx = fmaxf(mx, s);
     }
@@ -345,7 +406,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__
     for (int j = tid; j <= i; j += blockDim.x) {
         const float p = sc[j] / L;
         sc[j] = p;
-        const float d = dot_hd(dys, v + (size_t)j * ldv + base, hd);
+        const float d = dot_hd<HD>(dys, v + (size_t)j * ldv + base, hd);
         dp[j] = d;
         rsp = fmaf(d, p, rsp);
     }
@@ -354,6 +415,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__
     __syncthreads();
     for (int t = tid; t < hd; t += blockDim.x) {
         float a = 0.f;
+#pragma unroll 8
         for (int j = 0; j <= i; ++j) a = fmaf(dp[j], k[(size_t)j * ldk + base + t], a);
         dq[(size_t)i * lddq + base + t] = a;
     }
@@ -367,6 +429,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__
 
 // Key row j of head h: P_ij and dS_ij for i >= j from the saved row statistics, then
 // dk_j = sum_i dS_ij q_i and dv_j = sum_i P_ij dy_i, i increasing.
+template <int HD>
 __global__ void __launch_bounds__(128) k_attn_bwd_keys(const float* __restrict__ q, int ldq,
                                                        const float* __restrict__ k, int ldk,
                                                        const float* __restrict__ v, int ldv,
@@ -384,9 +447,9 @@ __global__ void __launch_bounds__(128) k_attn_bwd_keys(const float* __restrict__
     __syncthreads();
     for (int i = j + tid; i < T; i += blockDim.x) {
         const float* st = stats + ((size_t)h * T + i) * 3;
-        const float s = dot_hd(q + (size_t)i * ldq + base, ks, hd) * scale;
+        const float s = dot_hd<HD>(q + (size_t)i * ldq + base, ks, hd) * scale;
         const float p = expf(s - st[0]) / st[1];
-        const float d = dot_hd(dy + (size_t)i * lddy + base, vs, hd);
+        const float d = dot_hd<HD>(dy + (size_t)i * lddy + base, vs, hd);
         pv[i] = p;
         dsv[i] = (d - st[2]) * p * scale;
     }
@@ -395,6 +458,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_keys(const float* __restrict__
         float* dkp = dk + (size_t)j * lddk + base + t;
         float* dvp = dv + (size_t)j * lddv + base + t;
         float a = accumulate ? *dkp : 0.f, b = accumulate ? *dvp : 0.f;
+#pragma unroll 8
         for (int i = j; i < T; ++i) {
             a = fmaf(dsv[i], q[(size_t)i * ldq + base + t], a);
             b = fmaf(pv[i], dy[(size_t)i * lddy + base + t], b);
@@ -414,25 +478,37 @@ int grid_1d(size_t n, int block) {
 
 size_t bwd_linear_part_floats(int T, int rows, int cols) {
     const BwdSplit s = bwd_split(T, rows, cols);
-    return (size_t)s.splits * T * cols;
+    return s.splits > 1 ? (size_t)s.splits * T * cols : 1;
 }
 
-cudaError_t launch_bwd_linear(const QW& w, const float* dY, int ldy, int T, float* part, int epi, float* out,
-                              int ldo, const float* xpre, int ldx, cudaStream_t st) {
+size_t bwd_linear_counters(int T, int cols) {
+    return (size_t)((cols + BL_COLS - 1) / BL_COLS) * ((T + BL_TT - 1) / BL_TT);
+}
+
+cudaError_t launch_bwd_linear(const QW& w, const float* dY, int ldy, int T, float* part, unsigned* counters, int epi,
+                              float* out, int ldo, const float* xpre, int ldx, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (w.cols % 4 != 0) return cudaErrorInvalidValue;
     const BwdSplit s = bwd_split(T, w.rows, w.cols);
     const dim3 grid(s.col_tiles, s.t_tiles, s.splits), block(256);
     switch (w.atom) {
-        case ATOM_Q8: k_bwd_linear<ATOM_Q8><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part); break;
-        case ATOM_Q4: k_bwd_linear<ATOM_Q4><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part); break;
-        case ATOM_F16: k_bwd_linear<ATOM_F16><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part); break;
-        default: k_bwd_linear<ATOM_F32><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part); break;
+        case ATOM_Q8:
+            k_bwd_linear<ATOM_Q8><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part, counters, epi, out,
+                                                          ldo, xpre, ldx);
+            break;
+        case ATOM_Q4:
+            k_bwd_linear<ATOM_Q4><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part, counters, epi, out,
+                                                          ldo, xpre, ldx);
+            break;
+        case ATOM_F16:
+            k_bwd_linear<ATOM_F16><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part, counters, epi, out,
+                                                           ldo, xpre, ldx);
+            break;
+        default:
+            k_bwd_linear<ATOM_F32><<<grid, block, 0, st>>>(w, dY, ldy, T, s.rows_per_split, part, counters, epi, out,
+                                                           ldo, xpre, ldx);
+            break;
     }
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    const size_t n = (size_t)T * w.cols;
-    k_bwd_reduce<<<grid_1d(n, 256), 256, 0, st>>>(part, s.splits, T, w.cols, epi, out, ldo, xpre, ldx);
     return cudaGetLastError();
 }
 
@@ -444,9 +520,9 @@ cudaError_t launch_bwd_ln(const float* dY, int ldy, const float* x, int ldx, con
     return cudaGetLastError();
 }
 
-cudaError_t launch_gelu_fwd(const float* x, float* out, size_t n, cudaStream_t st) {
+cudaError_t launch_gelu_fwd(const float* x, float* out, __half* ohi, __half* olo, size_t n, cudaStream_t st) {
     if (n == 0) return cudaSuccess;
-    k_gelu_fwd<<<grid_1d(n, 256), 256, 0, st>>>(x, out, n);
+    k_gelu_fwd<<<grid_1d(n, 256), 256, 0, st>>>(x, out, ohi, olo, n);
     return cudaGetLastError();
 }
 
@@ -457,11 +533,14 @@ cudaError_t launch_gelu_bwd(const float* x, const float* dy, float* dx, size_t n
 }
 
 cudaError_t launch_attn_fwd_train(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, int T,
-                                  int n_head, int hd, float* out, int ldo, cudaStream_t st) {
+                                  int n_head, int hd, float* out, int ldo, __half* ohi, __half* olo, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (T > ATT_MAX_T || hd > ATT_MAX_HD || hd <= 0 || n_head <= 0) return cudaErrorInvalidValue;
     const float scale = 1.0f / sqrtf((float)hd);
-    k_attn_fwd_train<<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, hd, scale, out, ldo);
+    if (hd == 64)
+        k_attn_fwd_train<64><<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, hd, scale, out, ldo, ohi, olo);
+    else
+        k_attn_fwd_train<0><<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, hd, scale, out, ldo, ohi, olo);
     return cudaGetLastError();
 }
 
@@ -471,11 +550,19 @@ cudaError_t launch_attn_bwd_train(const float* q, int ldq, const float* k, int l
     if (T <= 0) return cudaSuccess;
     if (T > ATT_MAX_T || hd > ATT_MAX_HD || hd <= 0 || n_head <= 0) return cudaErrorInvalidValue;
     const float scale = 1.0f / sqrtf((float)hd);
-    k_attn_bwd_rows<<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, dq, lddq, stats);
+    const dim3 grid(T, n_head);
+    if (hd == 64)
+        k_attn_bwd_rows<64><<<grid, 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, dq, lddq, stats);
+    else
+        k_attn_bwd_rows<0><<<grid, 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, dq, lddq, stats);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    k_attn_bwd_keys<<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, stats, dk, lddk,
-                                                     dv, lddv, accumulate);
+    if (hd == 64)
+        k_attn_bwd_keys<64><<<grid, 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, stats, dk, lddk, dv,
+                                                  lddv, accumulate);
+    else
+        k_attn_bwd_keys<0><<<grid, 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, stats, dk, lddk, dv,
+                                                 lddv, accumulate);
     return cudaGetLastError();
 }
 
@@ -554,8 +641,11 @@ int gpt2q_bwd_lin_input_grad(int device, const float* w, const float* dy, int ro
     q.qstride = (size_t)cols * 4;
     const float* ddy = s.up(dy, rows);
     float* part = s.alloc(bwd_linear_part_floats(1, rows, cols));
+    unsigned* counters = reinterpret_cast<unsigned*>(s.alloc(bwd_linear_counters(1, cols)));
+    if (s.err == cudaSuccess) s.err = cudaMemsetAsync(counters, 0, bwd_linear_counters(1, cols) * 4, s.st);
     float* ddx = s.alloc(cols);
-    if (s.err == cudaSuccess) s.err = launch_bwd_linear(q, ddy, rows, 1, part, BWD_STORE, ddx, cols, nullptr, 0, s.st);
+    if (s.err == cudaSuccess)
+        s.err = launch_bwd_linear(q, ddy, rows, 1, part, counters, BWD_STORE, ddx, cols, nullptr, 0, s.st);
     return finish(s, s.down(dx, ddx, cols), "gpt2q_bwd_lin_input_grad");
 }
 

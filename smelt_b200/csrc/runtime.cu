@@ -1147,12 +1147,14 @@ int trunk_grad(gpt2q_handle* H, const uint32_t* ids, int T, const float* dlogits
         part_n = std::max(part_n, bwd_linear_part_floats(T, lw.mproj.rows, lw.mproj.cols));
     }
     const size_t Td = up64((size_t)T * d), TF = up64((size_t)T * F), T3 = up64((size_t)T * d3);
+    const size_t n_ctr = up64(bwd_linear_counters(T, std::max(F, d3)));
     const size_t need = (size_t)(L + 1) * Td + (size_t)L * (Td + T3 + TF)  // stash
                         + Td                                               // ln_f output
                         + 2 * Td + TF                                      // h, att, gelu(fc)
+                        + 2 * Td + TF                                      // their fp16 hi/lo splits
                         + up64((size_t)T * V)                              // dlogits
                         + 3 * Td + TF + T3                                 // G, DH, DATT, DFC, DQKV
-                        + up64(part_n) + up64((size_t)3 * NH * T) + up64((size_t)2 * T);
+                        + up64(part_n) + up64((size_t)3 * NH * T) + up64((size_t)2 * T) + n_ctr;
     if (H->bwd_ws_floats < need) {
         if (H->bwd_ws) {
             CK(cudaStreamSynchronize(H->stream));
@@ -1165,6 +1167,8 @@ int trunk_grad(gpt2q_handle* H, const uint32_t* ids, int T, const float* dlogits
             return H->fail(GPT2Q_EOOM, "trunk backward workspace (" + std::to_string(need * 4) + " bytes)");
         }
         H->bwd_ws_floats = need;
+        // the split-reduction tickets sit at the end; every launch leaves them at zero
+        CK(cudaMemsetAsync(H->bwd_ws + need - n_ctr, 0, n_ctr * 4, H->stream));
     }
     float* w = H->bwd_ws;
     auto take = [&](size_t n) {
@@ -1180,6 +1184,12 @@ int trunk_grad(gpt2q_handle* H, const uint32_t* ids, int T, const float* dlogits
     float* hb = take(Td);
     float* att = take(Td);
     float* fb = take(TF);
+    __half* hb_hi = reinterpret_cast<__half*>(take(Td / 2));
+    __half* hb_lo = reinterpret_cast<__half*>(take(Td / 2));
+    __half* att_hi = reinterpret_cast<__half*>(take(Td / 2));
+    __half* att_lo = reinterpret_cast<__half*>(take(Td / 2));
+    __half* fb_hi = reinterpret_cast<__half*>(take(TF / 2));
+    __half* fb_lo = reinterpret_cast<__half*>(take(TF / 2));
     float* DL = take(up64((size_t)T * V));
     float* G = take(Td);
     float* DH = take(Td);
@@ -1190,6 +1200,7 @@ int trunk_grad(gpt2q_handle* H, const uint32_t* ids, int T, const float* dlogits
     float* stats = take(up64((size_t)3 * NH * T));
     int* d_ids = reinterpret_cast<int*>(take(up64((size_t)2 * T)));
     int* d_pos = d_ids + T;
+    unsigned* ctr = reinterpret_cast<unsigned*>(H->bwd_ws + H->bwd_ws_floats - n_ctr);
 
     std::vector<int> hi(2 * (size_t)T);
     for (int p = 0; p < T; ++p) {
@@ -1209,36 +1220,40 @@ int trunk_grad(gpt2q_handle* H, const uint32_t* ids, int T, const float* dlogits
         float* qk = qkv + (size_t)l * T3;
         float* fp = fcpre + (size_t)l * TF;
         float* xo = xs + (size_t)(l + 1) * Td;
+        // the linears take the tensor-core path for T >= 16 (fp16 hi/lo split inputs), as prefill does
         RUN("layernorm", (double)T * d * 8,
-            launch_layernorm(xin, d, nullptr, hb, d, nullptr, nullptr, lw.ln1_g, lw.ln1_b, d, eps, T, H->stream));
-        RUN("linear_qkv", linear_bytes(lw.attn, T, 1),
-            launch_linear_simt(lw.attn.w, hb, d, T, epi_store(qk, d3, lw.attn.bias), H->stream));
+            launch_layernorm(xin, d, nullptr, hb, d, hb_hi, hb_lo, lw.ln1_g, lw.ln1_b, d, eps, T, H->stream));
+        int rc = linear(H, "linear_qkv", lw.attn, In{hb, hb_hi, hb_lo, d}, T, epi_store(qk, d3, lw.attn.bias));
+        if (rc) return rc;
         RUN("attn_train", (double)T * d3 * 4,
-            launch_attn_fwd_train(qk, d3, qk + d, d3, qk + 2 * d, d3, T, NH, hd, att, d, H->stream));
+            launch_attn_fwd_train(qk, d3, qk + d, d3, qk + 2 * d, d3, T, NH, hd, att, d, att_hi, att_lo, H->stream));
         CK(cudaMemcpyAsync(xm, xin, (size_t)T * d * 4, cudaMemcpyDeviceToDevice, H->stream));
         Epi er = epi_store(xm, d, lw.proj.bias);
         er.kind = EPI_RESID;
-        RUN("linear_proj", linear_bytes(lw.proj, T, 2), launch_linear_simt(lw.proj.w, att, d, T, er, H->stream));
+        rc = linear(H, "linear_proj", lw.proj, In{att, att_hi, att_lo, d}, T, er);
+        if (rc) return rc;
         RUN("layernorm", (double)T * d * 8,
-            launch_layernorm(xm, d, nullptr, hb, d, nullptr, nullptr, lw.ln2_g, lw.ln2_b, d, eps, T, H->stream));
-        RUN("linear_fc", linear_bytes(lw.fc, T, 1),
-            launch_linear_simt(lw.fc.w, hb, d, T, epi_store(fp, F, lw.fc.bias), H->stream));
-        RUN("gelu", (double)T * F * 8, launch_gelu_fwd(fp, fb, (size_t)T * F, H->stream));
+            launch_layernorm(xm, d, nullptr, hb, d, hb_hi, hb_lo, lw.ln2_g, lw.ln2_b, d, eps, T, H->stream));
+        rc = linear(H, "linear_fc", lw.fc, In{hb, hb_hi, hb_lo, d}, T, epi_store(fp, F, lw.fc.bias));
+        if (rc) return rc;
+        RUN("gelu", (double)T * F * 8, launch_gelu_fwd(fp, fb, fb_hi, fb_lo, (size_t)T * F, H->stream));
         CK(cudaMemcpyAsync(xo, xm, (size_t)T * d * 4, cudaMemcpyDeviceToDevice, H->stream));
         Epi em = epi_store(xo, d, lw.mproj.bias);
         em.kind = EPI_RESID;
-        RUN("linear_mproj", linear_bytes(lw.mproj, T, 2), launch_linear_simt(lw.mproj.w, fb, F, T, em, H->stream));
+        rc = linear(H, "linear_mproj", lw.mproj, In{fb, fb_hi, fb_lo, F}, T, em);
+        if (rc) return rc;
     }
     const float* xL = xs + (size_t)L * Td;
     RUN("layernorm", (double)T * d * 8,
         launch_layernorm(xL, d, nullptr, lnf, d, nullptr, nullptr, H->lnf_g, H->lnf_b, d, eps, T, H->stream));
 
     // ---- backward: head, ln_f, then the layers in reverse ----
+    // algorithmic bytes: the weights once, dY, the output (and the GELU input or the added-to output)
     auto bwd_lin = [&](const char* name, const Linear& Lw, const float* dY, int ldy, int epi, float* out, int ldo,
                        const float* xpre, int ldx) {
-        const double bytes = (double)Lw.weight_bytes * ((T + 15) / 16) + (double)T * (Lw.rows + 2 * Lw.cols) * 4;
+        const double bytes = (double)Lw.weight_bytes + (double)T * (Lw.rows + (epi == BWD_STORE ? 1 : 2) * Lw.cols) * 4;
         return run_kernel(H, name, bytes, [&]() {
-            return launch_bwd_linear(Lw.w, dY, ldy, T, part, epi, out, ldo, xpre, ldx, H->stream);
+            return launch_bwd_linear(Lw.w, dY, ldy, T, part, ctr, epi, out, ldo, xpre, ldx, H->stream);
         });
     };
     int rc = bwd_lin("bwd_linear_head", H->wte, DL, V, BWD_STORE, DH, d, nullptr, 0);
@@ -1264,6 +1279,7 @@ int trunk_grad(gpt2q_handle* H, const uint32_t* ids, int T, const float* dlogits
         RUN("bwd_attn", (double)T * d3 * 8,
             launch_attn_bwd_train(qk, d3, qk + d, d3, qk + 2 * d, d3, DATT, d, T, NH, hd, DQKV, d3, DQKV + d, d3,
                                   DQKV + 2 * d, d3, 0, stats, H->stream));
+        H->launches++;  // query-row and key-row kernels
         rc = bwd_lin("bwd_linear_qkv", lw.attn, DQKV, d3, BWD_STORE, DH, d, nullptr, 0);
         if (rc) return rc;
         RUN("bwd_ln", (double)T * d * 16,
