@@ -197,6 +197,116 @@ __device__ __forceinline__ void dot_q8_rows(const uint8_t* q, const __half* s, c
     for (int r = 0; r < R; ++r) out[r] = acc[r];
 }
 
+// ---- int8 tensor-core dot products (mma.sync m16n8k32, s8 x s8 -> s32) ----
+// An fp32 vector x is written exactly enough as four int8 "pieces" per 32-wide group g:
+// x = 2^-S_g (p0 + p1 2^-7 + p2 2^-14 + p3 2^-21) + r with |r| <= 2^(E_g - 28), E_g the
+// exponent of max |x| over the group (|p0| <= 64, |p1..p3| <= 64). The pieces are the columns
+// 0..3 of the mma's B operand, so one instruction gives the exact integer dot products of 16
+// weight rows with all four pieces; the int32 results are combined in fp32 and scaled by the
+// weight group's f16 scale and 2^-S_g.
+__device__ __forceinline__ void mma_s8_16x8x32(int (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// Warp-wide: the four pieces of x[32*ks + lane] into pc[p][32*ks + lane] (pc rows d bytes
+// apart); returns 2^-S for the group.
+__device__ __forceinline__ float split_pieces(const float* x, int ks, int lane, int8_t* pc, int d) {
+    const float v0 = x[32 * ks + lane];
+    // max |x| of the group by its bit pattern (non-negative floats order as unsigned integers);
+    // S = 5 - floor(log2 max) so that |x| 2^S < 64, capped at 126 (tiny or zero groups)
+    const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(v0) & 0x7FFFFFFFu);
+    const int S = min(126, 132 - (int)(mb >> 23));
+    float v = v0 * __uint_as_float((uint32_t)(127 + S) << 23);  // exact power-of-two scaling
+    const float p0 = rintf(v);
+    v = (v - p0) * 128.f;
+    const float p1 = rintf(v);
+    v = (v - p1) * 128.f;
+    const float p2 = rintf(v);
+    v = (v - p2) * 128.f;
+    const float p3 = rintf(v);
+    int8_t* o = pc + 32 * ks + lane;
+    o[0] = (int8_t)(int)p0;
+    o[d] = (int8_t)(int)p1;
+    o[2 * d] = (int8_t)(int)p2;
+    o[3 * d] = (int8_t)(int)p3;
+    return __uint_as_float((uint32_t)(127 - S) << 23);  // 2^-S, S in [-122, 126]
+}
+
+// B fragments of x for this warp's groups ks = warp + 8 i (i < 4, ks < gsn): pieces go through
+// pc ([4][d] bytes; each warp writes and reads only its own groups), f[i] = 2^-S of group ks.
+__device__ __forceinline__ void vec_fragments(const float* x, int d, int8_t* pc, int warp, int lane, float (&f)[4],
+                                              uint32_t (&b0)[4], uint32_t (&b1)[4]) {
+    const int gsn = d >> 5;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int ks = warp + NWC * i;
+        f[i] = ks < gsn ? split_pieces(x, ks, lane, pc, d) : 0.f;
+    }
+    __syncwarp();
+    const int n = lane >> 2, t4 = 4 * (lane & 3);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int ks = warp + NWC * i;
+        const bool ok = ks < gsn && n < 4;
+        b0[i] = ok ? *reinterpret_cast<const uint32_t*>(pc + n * d + 32 * ks + t4) : 0u;
+        b1[i] = ok ? *reinterpret_cast<const uint32_t*>(pc + n * d + 32 * ks + 16 + t4) : 0u;
+    }
+}
+
+// Weights of the result columns lane (g, t) holds: pieces 2t and 2t+1 (columns 4..7 are zero).
+__device__ __forceinline__ float piece_w_lo(int lane) {
+    return (lane & 3) == 0 ? 1.f : ((lane & 3) == 1 ? 0x1p-14f : 0.f);
+}
+__device__ __forceinline__ float piece_w_hi(int lane) {
+    return (lane & 3) == 0 ? 0x1p-7f : ((lane & 3) == 1 ? 0x1p-21f : 0.f);
+}
+
+// 32 weight rows of a fragment-ordered segment (block 2 ks + mt of 512 bytes: lane's 16 bytes
+// are its A registers; scales Ss [32][gsn]) against x's fragments: this warp's k-groups summed
+// in group order; per-warp row sums to red32[warp][32] (the caller syncs and adds the warps).
+__device__ __forceinline__ void rows32_mma(const uint8_t* S, const __half* Ss, int gsn, const float (&f)[4],
+                                           const uint32_t (&b0)[4], const uint32_t (&b1)[4], int warp, int lane,
+                                           float* red32) {
+    const float wlo = piece_w_lo(lane), whi = piece_w_hi(lane);
+    const int gr = lane >> 2;
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int ks = warp + NWC * i;
+        if (ks < gsn) {
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const uint4 a = *reinterpret_cast<const uint4*>(S + ((size_t)(2 * ks + mt) * 32 + lane) * 16);
+                int c[4];
+                mma_s8_16x8x32(c, a, b0[i], b1[i]);
+                const float sa = __half2float(Ss[(mt * 16 + gr) * gsn + ks]) * f[i];
+                const float sb = __half2float(Ss[(mt * 16 + gr + 8) * gsn + ks]) * f[i];
+                const float va = fmaf((float)c[1], whi, (float)c[0] * wlo);
+                const float vb = fmaf((float)c[3], whi, (float)c[2] * wlo);
+                acc[mt][0] = fmaf(va, sa, acc[mt][0]);
+                acc[mt][1] = fmaf(vb, sb, acc[mt][1]);
+            }
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            acc[mt][u] += __shfl_xor_sync(0xffffffffu, acc[mt][u], 1);
+            acc[mt][u] += __shfl_xor_sync(0xffffffffu, acc[mt][u], 2);
+        }
+    if ((lane & 3) == 0) {
+        red32[warp * 32 + gr] = acc[0][0];
+        red32[warp * 32 + gr + 8] = acc[0][1];
+        red32[warp * 32 + 16 + gr] = acc[1][0];
+        red32[warp * 32 + 24 + gr] = acc[1][1];
+    }
+}
+
 __device__ __forceinline__ void softmax_update(float s, float v0, float v1, float& m, float& l, float& o0,
                                                float& o1) {
     const float mn = fmaxf(m, s);
@@ -782,6 +892,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
         const bool want_logits = p.logits != nullptr && step == p.steps - 1;
         unsigned long long best = 0ull;
         unsigned long long t_wait = 0, t_rel = 0, t_dot0 = 0, t_last = trace ? globaltimer() : 0;
+        // fragments of the ln_f output (B operands) for this warp's groups, kept in registers for
+        // the whole head; mpart is free once the last layer's x'' arrived
+        const int gsn = d >> 5;
+        float fk[4];
+        uint32_t hb0[4], hb1[4];
+        vec_fragments(ln, d, reinterpret_cast<int8_t*>(mpart), warp, lane, fk, hb0, hb1);
+        // per-warp row sums, double-buffered (2 x [8 warps][32 rows] in wred): one barrier per
+        // segment, after which the segment is released while warp 0 reduces its rows
         for (int k = 0; k < nseg_head; ++k) {
             const uint8_t* S = seg_wait();
             if (trace && tid == 0) {
@@ -790,21 +908,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
                 t_last = now;
                 if (k == 0) t_dot0 = now;
             }
-            const __half* Ss = reinterpret_cast<const __half*>(S + (size_t)32 * d);
-            if (k * 32 + 4 * warp < rows_head) {  // rows past the end are zero padding in the stream
-                float out[4];
-                dot_q8_rows<4, D>(S + (size_t)(4 * warp) * d, Ss + (size_t)(4 * warp) * (d / 32), ln, d, lane, out);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int r = 4 * warp + u;
-                    const int row = row0_head + k * 32 + r;
-                    if (k * 32 + r < rows_head) {
-                        const unsigned long long key = argmax_pack(out[u], row);
-                        best = key > best ? key : best;
-                        if (want_logits && lane == u) p.logits[row] = out[u];
-                    }
-                }
-            }
+            float* hred = wred + (k & 1) * (NWC * 32);
+            rows32_mma(S, reinterpret_cast<const __half*>(S + (size_t)32 * d), gsn, fk, hb0, hb1, warp, lane, hred);
             __syncthreads();
             const unsigned long long tR = (trace && tid == 0) ? globaltimer() : 0;
             seg_release();
@@ -813,7 +918,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
                 t_rel += t_last - tR;
                 if (k == 0) trace[35] = tR - t_dot0;
             }
+            if (tid < 32 && k * 32 + tid < rows_head) {  // rows past the end are zero padding
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < NWC; ++w) v += hred[w * 32 + tid];
+                const int row = row0_head + k * 32 + tid;
+                const unsigned long long key = argmax_pack(v, row);
+                best = key > best ? key : best;
+                if (want_logits) p.logits[row] = v;
+            }
         }
+        best = warp_max_u64(best);
         MK_TR(22);
         if (trace && tstep == 0 && tid == 0) {
             trace[24] = t_wait;
@@ -894,6 +1009,31 @@ __global__ void k_gather_rows(const GatherOp* __restrict__ ops) {
     }
 }
 
+// A block of R = 16 MT rows x K int8 columns in mma fragment order: 32-bit word w holds rows
+// (mt * 16 + g, + 8 for odd registers) and columns 32 ks + 4 t (+ 16 for registers 2, 3) of source
+// rows 0 .. n - 1 (zero past n), with block = w / 128 = ks * MT + mt, lane = (w % 128) / 4 =
+// 4 g + t and register w % 4: a lane's four A registers are 16 contiguous bytes.
+struct FragPackOp {
+    const uint8_t* src;
+    size_t src_stride;
+    uint8_t* dst;
+    int n, MT, K;
+};
+
+__global__ void k_pack_frag(const FragPackOp* __restrict__ ops) {
+    const FragPackOp o = ops[blockIdx.x];
+    const int words = 16 * o.MT * o.K / 4;
+    for (int w = threadIdx.x; w < words; w += blockDim.x) {
+        const int blk = w >> 7, lanew = (w >> 2) & 31, reg = w & 3;
+        const int ks = blk / o.MT, mt = blk - ks * o.MT, gq = lanew >> 2, t = lanew & 3;
+        const int row = mt * 16 + gq + ((reg & 1) ? 8 : 0);
+        const int col = 32 * ks + ((reg & 2) ? 16 : 0) + 4 * t;
+        uint32_t v = 0u;
+        if (row < o.n) v = *reinterpret_cast<const uint32_t*>(o.src + (size_t)row * o.src_stride + col);
+        reinterpret_cast<uint32_t*>(o.dst)[w] = v;
+    }
+}
+
 size_t smem_bytes(int d, int seg, int n_layer) {
     const VecLayout V(d);
     const int dsl = d / MK_CS;
@@ -962,6 +1102,7 @@ cudaError_t mk_setup(MkPlan& plan, const MkWeights& w, int d, int L, int H, int 
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(stream, 0, cta_bytes * G, st);
     std::vector<GatherOp> ops;
+    std::vector<FragPackOp> hops;  // lm head segments, in mma fragment order
     auto add = [&](const void* src, size_t stride, uint8_t* dst, int rows, int bytes) {
         if (rows > 0 && bytes > 0) ops.push_back({reinterpret_cast<const uint8_t*>(src), dst, stride, rows, bytes});
     };
@@ -998,7 +1139,7 @@ cudaError_t mk_setup(MkPlan& plan, const MkWeights& w, int d, int L, int H, int 
         for (int k = 0; k * 32 < rows; ++k) {
             uint8_t* S = base + (size_t)(3 * L + k) * seg;
             const int r0 = row0 + k * 32, n = std::min(32, rows - k * 32);
-            add(w.wte.q + (size_t)r0 * w.wte.qstride, w.wte.qstride, S, n, d);
+            hops.push_back({w.wte.q + (size_t)r0 * w.wte.qstride, w.wte.qstride, S, n, 2, d});
             add(reinterpret_cast<const uint8_t*>(w.wte.s) + (size_t)r0 * w.wte.sstride * 2,
                 (size_t)w.wte.sstride * 2, S + (size_t)32 * d, n, gs * 2);
         }
@@ -1011,8 +1152,17 @@ cudaError_t mk_setup(MkPlan& plan, const MkWeights& w, int d, int L, int H, int 
         k_gather_rows<<<(unsigned)ops.size(), 256, 0, st>>>(dops);
         e = cudaGetLastError();
     }
+    FragPackOp* dh = nullptr;
+    if (e == cudaSuccess && !hops.empty()) e = cudaMalloc(&dh, hops.size() * sizeof(FragPackOp));
+    if (e == cudaSuccess && dh)
+        e = cudaMemcpyAsync(dh, hops.data(), hops.size() * sizeof(FragPackOp), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && dh) {
+        k_pack_frag<<<(unsigned)hops.size(), 256, 0, st>>>(dh);
+        e = cudaGetLastError();
+    }
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (dops) cudaFree(dops);
+    if (dh) cudaFree(dh);
     plan.stream = stream;
     if (e != cudaSuccess) {
         mk_destroy(plan);
