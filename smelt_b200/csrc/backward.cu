@@ -11,8 +11,8 @@
 // * k_bwd_ln: one CTA per row, fixed-order block reductions.
 // * attention: one CTA per (query row, head) recomputes the probability row, the row's dP and
 //   dq; one CTA per (key row, head) recomputes the column of P and dS from the saved row
-//   statistics and sums dk and dv over the later queries in increasing order, as the reference
-//   kernel's accumulation does. No floating-point atomics anywhere.
+//   statistics and sums dk and dv over the later queries (strided over the CTA's thread groups,
+//   parts added in fixed order). No floating-point atomics anywhere.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -30,7 +30,7 @@ namespace {
 
 constexpr int BL_COLS = 128;  // columns per CTA (4 per lane)
 constexpr int BL_TT = 16;     // positions per CTA
-constexpr int BL_RCH = 256;   // rows of dY staged per chunk (double-buffered)
+constexpr int BL_RCH = 128;   // rows of dY staged per chunk (double-buffered)
 constexpr int BL_WARPS = 8;
 constexpr int BL_PAD = 20;    // row stride of the staged dY tile (floats; 16-byte aligned rows)
 constexpr int BL_RB = 8;      // weight rows in flight per warp
@@ -86,6 +86,73 @@ __device__ __forceinline__ void load_w4(const QW& w, int r, int c, float f[4]) {
     }
 }
 
+// Raw weight words of W[r][c..c+3] as loaded (dequantised later, so the next batch's loads can
+// be in flight while the current batch is consumed).
+template <int ATOM>
+struct WRaw {
+    uint32_t q;
+    float s;
+};
+template <>
+struct WRaw<ATOM_F16> {
+    uint2 v;
+};
+template <>
+struct WRaw<ATOM_F32> {
+    float4 v;
+};
+
+template <int ATOM>
+__device__ __forceinline__ void raw_load(const QW& w, int r, int c, WRaw<ATOM>& o) {
+    const uint8_t* row = w.q + (size_t)r * w.qstride;
+    if constexpr (ATOM == ATOM_F32) {
+        o.v = __ldg(reinterpret_cast<const float4*>(row) + (c >> 2));
+    } else if constexpr (ATOM == ATOM_F16) {
+        o.v = __ldg(reinterpret_cast<const uint2*>(row) + (c >> 2));
+    } else if constexpr (ATOM == ATOM_Q8) {
+        o.q = __ldg(reinterpret_cast<const uint32_t*>(row) + (c >> 2));
+        o.s = __half2float(w.s[(size_t)r * w.sstride + (c >> 5)]);
+    } else {
+        const int g = c >> 5, e = c & 31;
+        o.q = __ldg(reinterpret_cast<const uint32_t*>(row + g * 16 + (e & 15)));
+        o.s = __half2float(w.s[(size_t)r * w.sstride + g]);
+    }
+}
+
+template <int ATOM>
+__device__ __forceinline__ void raw_zero(WRaw<ATOM>& o) {
+    if constexpr (ATOM == ATOM_F32) {
+        o.v = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else if constexpr (ATOM == ATOM_F16) {
+        o.v = make_uint2(0u, 0u);
+    } else {
+        o.q = 0u;
+        o.s = 0.f;
+    }
+}
+
+// Exactly (float)q * scale for the quantised atoms (as Engine::vec_f32).
+template <int ATOM>
+__device__ __forceinline__ void raw_deq(const WRaw<ATOM>& o, int c, float f[4]) {
+    if constexpr (ATOM == ATOM_F32) {
+        f[0] = o.v.x, f[1] = o.v.y, f[2] = o.v.z, f[3] = o.v.w;
+    } else if constexpr (ATOM == ATOM_F16) {
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&o.v.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&o.v.y));
+        f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
+    } else if constexpr (ATOM == ATOM_Q8) {
+        i8x4_to_f32(o.q, f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] *= o.s;
+    } else {
+        float lo[4], hi[4];
+        i4x8_to_f32(o.q, lo, hi);
+        const bool low = (c & 31) < 16;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = (low ? lo[j] : hi[j]) * o.s;
+    }
+}
+
 __device__ __forceinline__ float gelu_grad(float v) {
     // d/dv of 0.5 v (1 + tanh(u)), u = c (v + 0.044715 v^3), in cu/backward.cu:124-130's order
     const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
@@ -115,7 +182,9 @@ template <int ATOM>
 __global__ void __launch_bounds__(256, 2) k_bwd_linear(QW w, const float* __restrict__ dY, int ldy, int T,
                                                        int rows_per_split, float* part, unsigned* counters,
                                                        int epi, float* out, int ldo, const float* xpre, int ldx) {
-    __shared__ __align__(16) float sm[2 * BL_RCH * BL_PAD];  // dY double buffer, then the warp partials
+    // dY double buffer, then (after the main loop) the warp partials
+    constexpr int SM_FLOATS = 2 * BL_RCH * BL_PAD > BL_WARPS * 8 * BL_COLS ? 2 * BL_RCH * BL_PAD : BL_WARPS * 8 * BL_COLS;
+    __shared__ __align__(16) float sm[SM_FLOATS];
     __shared__ bool is_last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c0 = blockIdx.x * BL_COLS, t0 = blockIdx.y * BL_TT;
@@ -150,40 +219,47 @@ __global__ void __launch_bounds__(256, 2) k_bwd_linear(QW w, const float* __rest
         store_chunk(sm);
     }
     __syncthreads();
+    // weights of the next batch (8 rows per warp, possibly in the next chunk) are loaded while
+    // the current batch is consumed
+    WRaw<ATOM> nxt[BL_RB];
+    auto load_batch = [&](int rbase) {
+#pragma unroll
+        for (int k = 0; k < BL_RB; ++k) {
+            const int r = rbase + warp + k * BL_WARPS;
+            if (cok && r < r_end)
+                raw_load<ATOM>(w, r, c, nxt[k]);
+            else
+                raw_zero<ATOM>(nxt[k]);
+        }
+    };
+    load_batch(r_begin);
     for (int ci = 0; ci < nchunks; ++ci) {
         const int rc = r_begin + ci * BL_RCH;
         const int nr = min(BL_RCH, r_end - rc);
         const float* cur = sm + (ci & 1) * BL_RCH * BL_PAD;
         const bool more = ci + 1 < nchunks;
         if (more) load_chunk(rc + BL_RCH, min(BL_RCH, r_end - rc - BL_RCH));
-        if (cok) {
-            for (int rb = 0; rb < nr; rb += BL_RB * BL_WARPS) {
-                float f[BL_RB][4];
+        for (int rb = 0; rb < nr; rb += BL_RB * BL_WARPS) {
+            WRaw<ATOM> wr[BL_RB];
 #pragma unroll
-                for (int k = 0; k < BL_RB; ++k) {
-                    const int r = rb + warp + k * BL_WARPS;
-                    if (r < nr) {
-                        load_w4<ATOM>(w, rc + r, c, f[k]);
-                    } else {
+            for (int k = 0; k < BL_RB; ++k) wr[k] = nxt[k];
+            load_batch(rc + rb + BL_RB * BL_WARPS);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) f[k][j] = 0.f;
-                    }
-                }
+            for (int k = 0; k < BL_RB; ++k) {
+                // rows past the range carry zero weights; their staged dY row is any row in bounds
+                const int r = min(rb + warp + k * BL_WARPS, BL_RCH - 1);
+                float f[4];
+                raw_deq<ATOM>(wr[k], c, f);
+                const float4* dv = reinterpret_cast<const float4*>(cur + r * BL_PAD);
 #pragma unroll
-                for (int k = 0; k < BL_RB; ++k) {
-                    // rows past nr carry zero weights; their staged dY row is any row in bounds
-                    const int r = min(rb + warp + k * BL_WARPS, BL_RCH - 1);
-                    const float4* dv = reinterpret_cast<const float4*>(cur + r * BL_PAD);
+                for (int q = 0; q < BL_TT / 4; ++q) {
+                    const float4 y = dv[q];
 #pragma unroll
-                    for (int q = 0; q < BL_TT / 4; ++q) {
-                        const float4 y = dv[q];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            acc[4 * q + 0][j] = fmaf(y.x, f[k][j], acc[4 * q + 0][j]);
-                            acc[4 * q + 1][j] = fmaf(y.y, f[k][j], acc[4 * q + 1][j]);
-                            acc[4 * q + 2][j] = fmaf(y.z, f[k][j], acc[4 * q + 2][j]);
-                            acc[4 * q + 3][j] = fmaf(y.w, f[k][j], acc[4 * q + 3][j]);
-                        }
+                    for (int j = 0; j < 4; ++j) {
+                        acc[4 * q + 0][j] = fmaf(y.x, f[j], acc[4 * q + 0][j]);
+                        acc[4 * q + 1][j] = fmaf(y.y, f[j], acc[4 * q + 1][j]);
+                        acc[4 * q + 2][j] = fmaf(y.z, f[j], acc[4 * q + 2][j]);
+                        acc[4 * q + 3][j] = fmaf(y.w, f[j], acc[4 * q + 3][j]);
                     }
                 }
             }
@@ -340,6 +416,7 @@ __global__ void __launch_bounds__(128) k_attn_fwd_train(const float* __restrict_
     __shared__ float qs[ATT_MAX_HD];
     __shared__ float sc[ATT_MAX_T];
     __shared__ float red[32];
+    __shared__ float pp[128];  // per-part partial sums (blockDim floats)
     const int i = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
     const size_t base = (size_t)h * hd;
     for (int t = tid; t < hd; t += blockDim.x) qs[t] = q[(size_t)i * ldq + base + t];
@@ -360,12 +437,21 @@ __global__ void __launch_bounds__(128) k_attn_fwd_train(const float* __restrict_
     const float L = block_sum(ls, red);
     for (int j = tid; j <= i; j += blockDim.x) sc[j] = sc[j] / L;
     __syncthreads();
-    for (int t = tid; t < hd; t += blockDim.x) {
+    // out_t = sum_j P_j v_j[t]: the blockDim / hd thread groups take j = part, part + parts, ...
+    // (more loads in flight), then the parts are added in part order
+    const int parts = blockDim.x / hd, t = tid % hd, part = tid / hd;
+    if (part < parts) {
         float o = 0.f;
 #pragma unroll 8
-        for (int j = 0; j <= i; ++j) o = fmaf(sc[j], v[(size_t)j * ldv + base + t], o);
-        out[(size_t)i * ldo + base + t] = o;
-        if (ohi) split_hl(o, ohi[(size_t)i * ldo + base + t], olo[(size_t)i * ldo + base + t]);
+        for (int j = part; j <= i; j += parts) o = fmaf(sc[j], v[(size_t)j * ldv + base + t], o);
+        pp[part * hd + t] = o;
+    }
+    __syncthreads();
+    if (tid < hd) {
+        float o = 0.f;
+        for (int q = 0; q < parts; ++q) o += pp[q * hd + tid];
+        out[(size_t)i * ldo + base + tid] = o;
+        if (ohi) split_hl(o, ohi[(size_t)i * ldo + base + tid], olo[(size_t)i * ldo + base + tid]);
     }
 }
 
@@ -381,6 +467,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__
     __shared__ float qs[ATT_MAX_HD], dys[ATT_MAX_HD];
     __shared__ float sc[ATT_MAX_T], dp[ATT_MAX_T];
     __shared__ float red[32];
+    __shared__ float pp[128];  // per-part partial sums (blockDim floats)
     const int i = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
     const size_t base = (size_t)h * hd;
     for (int t = tid; t < hd; t += blockDim.x) {
@@ -413,11 +500,18 @@ __global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__
     const float rs = block_sum(rsp, red);
     for (int j = tid; j <= i; j += blockDim.x) dp[j] = (dp[j] - rs) * sc[j] * scale;
     __syncthreads();
-    for (int t = tid; t < hd; t += blockDim.x) {
+    const int parts = blockDim.x / hd, t = tid % hd, part = tid / hd;
+    if (part < parts) {
         float a = 0.f;
 #pragma unroll 8
-        for (int j = 0; j <= i; ++j) a = fmaf(dp[j], k[(size_t)j * ldk + base + t], a);
-        dq[(size_t)i * lddq + base + t] = a;
+        for (int j = part; j <= i; j += parts) a = fmaf(dp[j], k[(size_t)j * ldk + base + t], a);
+        pp[part * hd + t] = a;
+    }
+    __syncthreads();
+    if (tid < hd) {
+        float a = 0.f;
+        for (int q = 0; q < parts; ++q) a += pp[q * hd + tid];
+        dq[(size_t)i * lddq + base + tid] = a;
     }
     if (tid == 0) {
         float* st = stats + ((size_t)h * T + i) * 3;
@@ -428,7 +522,8 @@ __global__ void __launch_bounds__(128) k_attn_bwd_rows(const float* __restrict__
 }
 
 // Key row j of head h: P_ij and dS_ij for i >= j from the saved row statistics, then
-// dk_j = sum_i dS_ij q_i and dv_j = sum_i P_ij dy_i, i increasing.
+// dk_j = sum_i dS_ij q_i and dv_j = sum_i P_ij dy_i (thread groups take interleaved i; their
+// partial sums are added in group order).
 template <int HD>
 __global__ void __launch_bounds__(128) k_attn_bwd_keys(const float* __restrict__ q, int ldq,
                                                        const float* __restrict__ k, int ldk,
@@ -438,6 +533,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_keys(const float* __restrict__
                                                        int lddk, float* dv, int lddv, int accumulate) {
     __shared__ float ks[ATT_MAX_HD], vs[ATT_MAX_HD];
     __shared__ float pv[ATT_MAX_T], dsv[ATT_MAX_T];
+    __shared__ float pp[128], pb[128];  // per-part partial sums of dk and dv
     const int j = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
     const size_t base = (size_t)h * hd;
     for (int t = tid; t < hd; t += blockDim.x) {
@@ -454,17 +550,28 @@ __global__ void __launch_bounds__(128) k_attn_bwd_keys(const float* __restrict__
         dsv[i] = (d - st[2]) * p * scale;
     }
     __syncthreads();
-    for (int t = tid; t < hd; t += blockDim.x) {
-        float* dkp = dk + (size_t)j * lddk + base + t;
-        float* dvp = dv + (size_t)j * lddv + base + t;
-        float a = accumulate ? *dkp : 0.f, b = accumulate ? *dvp : 0.f;
+    const int parts = blockDim.x / hd, t = tid % hd, part = tid / hd;
+    if (part < parts) {
+        float a = 0.f, b = 0.f;
 #pragma unroll 8
-        for (int i = j; i < T; ++i) {
+        for (int i = j + part; i < T; i += parts) {
             a = fmaf(dsv[i], q[(size_t)i * ldq + base + t], a);
             b = fmaf(pv[i], dy[(size_t)i * lddy + base + t], b);
         }
-        *dkp = a;
-        *dvp = b;
+        pp[part * hd + t] = a;
+        pb[part * hd + t] = b;
+    }
+    __syncthreads();
+    if (tid < hd) {
+        float* dkp = dk + (size_t)j * lddk + base + tid;
+        float* dvp = dv + (size_t)j * lddv + base + tid;
+        float a = 0.f, b = 0.f;
+        for (int q2 = 0; q2 < parts; ++q2) {
+            a += pp[q2 * hd + tid];
+            b += pb[q2 * hd + tid];
+        }
+        *dkp = accumulate ? *dkp + a : a;
+        *dvp = accumulate ? *dvp + b : b;
     }
 }
 
