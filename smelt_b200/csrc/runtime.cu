@@ -152,6 +152,7 @@ struct gpt2q_handle {
     // host staging (pinned)
     int* h_stage = nullptr;
     size_t h_stage_ints = 0;
+    int* h_err = nullptr;  // pinned: the device error words, read with the step's outputs
 
     std::map<int, std::pair<cudaGraphExec_t, uint64_t>> dec_graphs;  // 2 B + adapter -> (graph, kernels)
     bool capturing = false;
@@ -799,16 +800,17 @@ int do_prefill(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, con
     H->cur_n = n_seq;
     H->hpos.assign(n_seq, 0);
     H->hslot.assign(n_seq, 0);
-    rc = ensure_stage(H, (size_t)2 * n_seq);
+    const int M = H->cfg.max_seqs;
+    rc = ensure_stage(H, (size_t)2 * M);
     if (rc) return rc;
     for (int s = 0; s < n_seq; ++s) {
         H->hpos[s] = offs[s + 1] - offs[s];
         H->hslot[s] = slots ? slots[s] : s;
         H->h_stage[s] = H->hpos[s];
-        H->h_stage[n_seq + s] = H->hslot[s];
+        H->h_stage[M + s] = H->hslot[s];
     }
-    CK(cudaMemcpyAsync(H->d_pos, H->h_stage, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
-    CK(cudaMemcpyAsync(H->d_slot, H->h_stage + n_seq, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
+    // pos | slot are adjacent on the device: one copy
+    CK(cudaMemcpyAsync(H->d_pos, H->h_stage, (size_t)2 * M * 4, cudaMemcpyHostToDevice, H->stream));
     CK(cudaStreamSynchronize(H->stream));
     return GPT2Q_OK;
 }
@@ -818,7 +820,8 @@ int do_decode(gpt2q_handle* H, const uint32_t* tok, const int32_t* pos, const in
     if (!tok || !pos) return H->fail(GPT2Q_EARG, "null tok/pos");
     int rc = check_tokens(H, tok, (size_t)n_seq);
     if (rc) return rc;
-    rc = ensure_stage(H, (size_t)3 * n_seq);
+    const int M = H->cfg.max_seqs;
+    rc = ensure_stage(H, (size_t)3 * M);
     if (rc) return rc;
     std::vector<char> used(H->cfg.max_seqs, 0);
     H->hpos.assign(n_seq, 0);
@@ -829,14 +832,13 @@ int do_decode(gpt2q_handle* H, const uint32_t* tok, const int32_t* pos, const in
         if (slot < 0 || slot >= H->cfg.max_seqs || used[slot]) return H->fail(GPT2Q_EARG, "bad or repeated slot");
         used[slot] = 1;
         H->h_stage[i] = (int)tok[i];
-        H->h_stage[n_seq + i] = pos[i];
-        H->h_stage[2 * n_seq + i] = slot;
+        H->h_stage[M + i] = pos[i];
+        H->h_stage[2 * M + i] = slot;
         H->hpos[i] = pos[i];
         H->hslot[i] = slot;
     }
-    CK(cudaMemcpyAsync(H->d_tok, H->h_stage, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
-    CK(cudaMemcpyAsync(H->d_pos, H->h_stage + n_seq, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
-    CK(cudaMemcpyAsync(H->d_slot, H->h_stage + 2 * n_seq, (size_t)n_seq * 4, cudaMemcpyHostToDevice, H->stream));
+    // one copy of the tok | pos | slot block (entries past n_seq are not read by this step)
+    CK(cudaMemcpyAsync(H->d_tok, H->h_stage, (size_t)3 * M * 4, cudaMemcpyHostToDevice, H->stream));
     H->cur_n = n_seq;
     return run_decode_step(H, n_seq);
 }
@@ -860,12 +862,37 @@ int check_device_error(gpt2q_handle* H) {
     return GPT2Q_OK;
 }
 
+// The outputs and every device error word in one round trip: the words are copied to pinned
+// memory behind the outputs and inspected after a single synchronisation; only a non-zero word
+// takes the slow path that clears it and reports the error.
 int read_outputs(gpt2q_handle* H, int n, const float* dlogits, float* logits, uint32_t* next) {
     if (logits)
         CK(cudaMemcpyAsync(logits, dlogits, (size_t)n * H->cfg.vocab * 4, cudaMemcpyDeviceToHost, H->stream));
-    if (next) CK(cudaMemcpyAsync(next, H->d_next, (size_t)n * 4, cudaMemcpyDeviceToHost, H->stream));
+    if (!H->h_err) {
+        if (next) CK(cudaMemcpyAsync(next, H->d_next, (size_t)n * 4, cudaMemcpyDeviceToHost, H->stream));
+        CK(cudaStreamSynchronize(H->stream));
+        return check_device_error(H);
+    }
+    // the next tokens land in pinned memory (a direct copy to pageable memory is staged by the
+    // driver) and are copied out after the synchronisation
+    int* h_next = H->h_err + 16;
+    if (next) CK(cudaMemcpyAsync(h_next, H->d_next, (size_t)n * 4, cudaMemcpyDeviceToHost, H->stream));
+    int nw = 0;
+    auto word = [&](const int* d, int count) -> cudaError_t {
+        if (!d) return cudaSuccess;
+        const cudaError_t e = cudaMemcpyAsync(H->h_err + nw, d, (size_t)count * 4, cudaMemcpyDeviceToHost, H->stream);
+        nw += count;
+        return e;
+    };
+    CK(word(H->gemm.enabled ? H->gemm.err : nullptr, 1));
+    CK(word(H->mk.err, 2));
+    CK(word(tp_err_word(H->tp), 1));
+    CK(word(H->kerr, 1));
     CK(cudaStreamSynchronize(H->stream));
-    return check_device_error(H);
+    if (next) std::memcpy(next, h_next, (size_t)n * 4);
+    for (int i = 0; i < nw; ++i)
+        if (H->h_err[i] != 0) return check_device_error(H);
+    return GPT2Q_OK;
 }
 
 const gpt2q_tensor_desc* find(const std::map<std::string, const gpt2q_tensor_desc*>& m, const std::string& n) {
@@ -1053,10 +1080,14 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     H->p_lastrow = H->dalloc<int>((size_t)c.max_seqs * 4);
     H->p_lastpos = H->dalloc<int>((size_t)c.max_seqs * 4);
     H->p_tiles = H->dalloc<AttnTile>((size_t)H->max_tiles * sizeof(AttnTile));
-    H->d_tok = H->dalloc<uint32_t>((size_t)c.max_seqs * 4);
+    // tok | pos | slot in one block (max_seqs each), so a step's inputs are one host copy
+    int* dstate = H->dalloc<int>((size_t)3 * c.max_seqs * 4);
+    H->d_tok = reinterpret_cast<uint32_t*>(dstate);
+    H->d_pos = dstate ? dstate + c.max_seqs : nullptr;
+    H->d_slot = dstate ? dstate + 2 * c.max_seqs : nullptr;
     H->d_next = H->dalloc<uint32_t>((size_t)c.max_seqs * 4);
-    H->d_pos = H->dalloc<int>((size_t)c.max_seqs * 4);
-    H->d_slot = H->dalloc<int>((size_t)c.max_seqs * 4);
+    // pinned: 16 error-word slots, then the next tokens of up to max_seqs sequences
+    if (cudaMallocHost(&H->h_err, (16 + (size_t)c.max_seqs) * sizeof(int)) != cudaSuccess) H->h_err = nullptr;
     H->d_genlog = H->dalloc<uint32_t>((size_t)c.max_seqs * c.n_ctx * 4);
     if (!H->x || !H->h || !H->qb || !H->att || !H->f || !H->logits || !H->p_tok || !H->p_pos || !H->p_slot ||
         !H->p_lastrow || !H->p_lastpos || !H->p_tiles || !H->d_tok || !H->d_next || !H->d_pos || !H->d_slot ||
@@ -1329,6 +1360,7 @@ void gpt2q_destroy(gpt2q_handle* H) {
     for (auto& a : H->allocs) cudaFree(a.p);
     if (H->bwd_ws) cudaFree(H->bwd_ws);
     if (H->h_stage) cudaFreeHost(H->h_stage);
+    if (H->h_err) cudaFreeHost(H->h_err);
     if (H->own_stream) cudaStreamDestroy(H->own_stream);
     delete H;
 }

@@ -372,6 +372,8 @@ int tp_take_error(TpComm* c, cudaStream_t st) {
     return h;
 }
 
+const int* tp_err_word(const TpComm* c) { return c ? c->d_err : nullptr; }
+
 const char* tp_last_error(const TpComm* c) { return c ? c->err.c_str() : "no communicator"; }
 
 void tp_destroy(TpComm* c) {

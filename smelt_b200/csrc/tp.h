@@ -29,6 +29,8 @@ int tp_reduce_ln(TpComm* c, int parity, float* x, int M, int d, const float* g, 
                  __half* hhi, __half* hlo, cudaStream_t st);
 // Reads and clears the device error word (0 = fine, > 0 a bounded wait for a peer gave up).
 int tp_take_error(TpComm* c, cudaStream_t st);
+// Device address of the communicator's error word (null without a communicator).
+const int* tp_err_word(const TpComm* c);
 bool tp_peer_mapped(const TpComm* c);
 const char* tp_last_error(const TpComm* c);
 void tp_destroy(TpComm* c);
