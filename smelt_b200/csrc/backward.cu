@@ -8,7 +8,8 @@
 //   registers) and broadcasts the staged dY values from shared memory. Row ranges are split
 //   across CTAs so the grid fills the 148 SMs; the last CTA of each tile sums the splits in
 //   fixed order and applies the epilogue (store, add, or GELU backward): deterministic.
-// * k_bwd_ln: one CTA per row, fixed-order block reductions.
+// * k_bwd_ln_warp: one warp per row held in registers, shuffle reductions (k_bwd_ln, one CTA
+//   per row, for rows wider than 1600).
 // * attention: one CTA per (query row, head) recomputes the probability row, the row's dP and
 //   dq; one CTA per (key row, head) recomputes the column of P and dS from the saved row
 //   statistics and sums dk and dv over the later queries (strided over the CTA's thread groups,
@@ -378,6 +379,66 @@ __global__ void __launch_bounds__(256) k_bwd_ln(const float* __restrict__ dY, in
     }
 }
 
+// The same LayerNorm backward with one warp per row (rows of up to 32 * NPL features held in
+// registers, reductions by shuffles only): T rows in T / 8 CTAs.
+template <int NPL>
+__global__ void __launch_bounds__(256) k_bwd_ln_warp(const float* __restrict__ dY, int ldy,
+                                                     const float* __restrict__ X, int ldx,
+                                                     const float* __restrict__ g, float eps, int n, int T, int epi,
+                                                     float* __restrict__ out, int ldo, float* dg, float* db) {
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= T) return;
+    const float* x = X + (size_t)t * ldx;
+    const float* dy = dY + (size_t)t * ldy;
+    auto wsum = [](float v) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        return v;
+    };
+    float xv[NPL], dh[NPL];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+        const int i = lane + 32 * k;
+        xv[k] = i < n ? x[i] : 0.f;
+        dh[k] = i < n ? dy[i] * g[i] : 0.f;
+        s += xv[k];
+    }
+    const float mean = wsum(s) / (float)n;
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+        const float v = lane + 32 * k < n ? xv[k] - mean : 0.f;
+        sq = fmaf(v, v, sq);
+    }
+    const float rstd = 1.0f / sqrtf(wsum(sq) / (float)n + eps);
+    float a = 0.f, cc = 0.f;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+        if (lane + 32 * k < n) {
+            a += dh[k];
+            cc = fmaf(dh[k], (xv[k] - mean) * rstd, cc);
+        }
+    }
+    const float mdxh = wsum(a) / (float)n;
+    const float mdxh_xh = wsum(cc) / (float)n;
+    float* o = out + (size_t)t * ldo;
+#pragma unroll
+    for (int k = 0; k < NPL; ++k) {
+        const int i = lane + 32 * k;
+        if (i < n) {
+            const float xh = (xv[k] - mean) * rstd;
+            const float v = rstd * (dh[k] - mdxh - xh * mdxh_xh);
+            if (epi == BWD_ADD)
+                o[i] += v;
+            else
+                o[i] = v;
+            if (dg) dg[i] += dy[i] * xh;
+            if (db) db[i] += dy[i];
+        }
+    }
+}
+
 __global__ void k_gelu_fwd(const float* __restrict__ x, float* __restrict__ out, __half* ohi, __half* olo, size_t n) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const float g = gelu_tanh(x[i]);
@@ -575,6 +636,191 @@ __global__ void __launch_bounds__(128) k_attn_bwd_keys(const float* __restrict__
     }
 }
 
+// ---- head dim 64: a warp takes a whole row (lane l: dimensions 2l, 2l+1), so a row is one
+// coalesced 256-byte load; dot products reduce by an xor shuffle tree whose result every lane
+// holds. The query-row and key-row kernels call wdot64 with the same operands in the same
+// order, so the probabilities and dS the key-row kernel recomputes are the query-row kernel's.
+__device__ __forceinline__ float wdot64(float2 a, float2 b) {
+    float s = fmaf(a.y, b.y, a.x * b.x);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+}
+
+__device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+
+__global__ void __launch_bounds__(128) k_attn_fwd_w64(const float* __restrict__ q, int ldq,
+                                                      const float* __restrict__ k, int ldk,
+                                                      const float* __restrict__ v, int ldv, float scale,
+                                                      float* __restrict__ out, int ldo, __half* ohi, __half* olo) {
+    __shared__ float sc[ATT_MAX_T];
+    __shared__ float red[32];
+    __shared__ float2 part[4][32];
+    const int i = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t base = (size_t)blockIdx.y * 64 + 2 * lane;
+    const float2 qv = ld2(q + (size_t)i * ldq + base);
+    float mx = -1e30f;
+#pragma unroll 4
+    for (int j = warp; j <= i; j += 4) {
+        const float s = wdot64(qv, ld2(k + (size_t)j * ldk + base)) * scale;
+        if (lane == 0) sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    const float m = block_max(mx, red);
+    float ls = 0.f;
+    for (int j = tid; j <= i; j += blockDim.x) {
+        const float e = expf(sc[j] - m);
+        sc[j] = e;
+        ls += e;
+    }
+    const float L = block_sum(ls, red);
+    for (int j = tid; j <= i; j += blockDim.x) sc[j] = sc[j] / L;
+    __syncthreads();
+    float2 o = make_float2(0.f, 0.f);
+#pragma unroll 4
+    for (int j = warp; j <= i; j += 4) {
+        const float2 vv = ld2(v + (size_t)j * ldv + base);
+        const float p = sc[j];
+        o.x = fmaf(p, vv.x, o.x);
+        o.y = fmaf(p, vv.y, o.y);
+    }
+    part[warp][lane] = o;
+    __syncthreads();
+    if (warp == 0) {
+        float2 r = part[0][lane];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+            r.x += part[w][lane].x;
+            r.y += part[w][lane].y;
+        }
+        const size_t oi = (size_t)i * ldo + base;
+        *reinterpret_cast<float2*>(out + oi) = r;
+        if (ohi) {
+            split_hl(r.x, ohi[oi], olo[oi]);
+            split_hl(r.y, ohi[oi + 1], olo[oi + 1]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128) k_attn_bwd_rows_w64(const float* __restrict__ q, int ldq,
+                                                           const float* __restrict__ k, int ldk,
+                                                           const float* __restrict__ v, int ldv,
+                                                           const float* __restrict__ dy, int lddy, int T, float scale,
+                                                           float* __restrict__ dq, int lddq,
+                                                           float* __restrict__ stats) {
+    __shared__ float sc[ATT_MAX_T], dp[ATT_MAX_T];
+    __shared__ float red[32];
+    __shared__ float2 part[4][32];
+    const int i = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t base = (size_t)h * 64 + 2 * lane;
+    const float2 qv = ld2(q + (size_t)i * ldq + base);
+    const float2 dyv = ld2(dy + (size_t)i * lddy + base);
+    float mx = -1e30f;
+#pragma unroll 4
+    for (int j = warp; j <= i; j += 4) {
+        const float s = wdot64(qv, ld2(k + (size_t)j * ldk + base)) * scale;
+        if (lane == 0) sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    const float m = block_max(mx, red);
+    float ls = 0.f;
+    for (int j = tid; j <= i; j += blockDim.x) {
+        const float e = expf(sc[j] - m);
+        sc[j] = e;
+        ls += e;
+    }
+    const float L = block_sum(ls, red);
+    for (int j = tid; j <= i; j += blockDim.x) sc[j] = sc[j] / L;
+    __syncthreads();
+    float rsp = 0.f;
+#pragma unroll 4
+    for (int j = warp; j <= i; j += 4) {
+        const float d = wdot64(dyv, ld2(v + (size_t)j * ldv + base));
+        if (lane == 0) dp[j] = d;
+        rsp = fmaf(d, sc[j], rsp);
+    }
+    const float rs = block_sum(lane == 0 ? rsp : 0.f, red);
+    for (int j = tid; j <= i; j += blockDim.x) dp[j] = (dp[j] - rs) * sc[j] * scale;
+    __syncthreads();
+    float2 a = make_float2(0.f, 0.f);
+#pragma unroll 4
+    for (int j = warp; j <= i; j += 4) {
+        const float2 kv = ld2(k + (size_t)j * ldk + base);
+        const float ds = dp[j];
+        a.x = fmaf(ds, kv.x, a.x);
+        a.y = fmaf(ds, kv.y, a.y);
+    }
+    part[warp][lane] = a;
+    __syncthreads();
+    if (warp == 0) {
+        float2 r = part[0][lane];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+            r.x += part[w][lane].x;
+            r.y += part[w][lane].y;
+        }
+        *reinterpret_cast<float2*>(dq + (size_t)i * lddq + base) = r;
+    }
+    if (tid == 0) {
+        float* st = stats + ((size_t)h * T + i) * 3;
+        st[0] = m;
+        st[1] = L;
+        st[2] = rs;
+    }
+}
+
+__global__ void __launch_bounds__(128) k_attn_bwd_keys_w64(const float* __restrict__ q, int ldq,
+                                                           const float* __restrict__ k, int ldk,
+                                                           const float* __restrict__ v, int ldv,
+                                                           const float* __restrict__ dy, int lddy, int T, float scale,
+                                                           const float* __restrict__ stats, float* dk, int lddk,
+                                                           float* dv, int lddv, int accumulate) {
+    __shared__ float2 pk[4][32], pv[4][32];
+    const int j = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t base = (size_t)h * 64 + 2 * lane;
+    const float2 kj = ld2(k + (size_t)j * ldk + base);
+    const float2 vj = ld2(v + (size_t)j * ldv + base);
+    float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+#pragma unroll 4
+    for (int i = j + warp; i < T; i += 4) {
+        const float* st = stats + ((size_t)h * T + i) * 3;
+        const float2 qv = ld2(q + (size_t)i * ldq + base);
+        const float2 dyv = ld2(dy + (size_t)i * lddy + base);
+        const float s = wdot64(qv, kj) * scale;
+        const float p = expf(s - st[0]) / st[1];
+        const float d = wdot64(dyv, vj);
+        const float ds = (d - st[2]) * p * scale;
+        a.x = fmaf(ds, qv.x, a.x);
+        a.y = fmaf(ds, qv.y, a.y);
+        b.x = fmaf(p, dyv.x, b.x);
+        b.y = fmaf(p, dyv.y, b.y);
+    }
+    pk[warp][lane] = a;
+    pv[warp][lane] = b;
+    __syncthreads();
+    if (warp == 0) {
+        float2 ra = pk[0][lane], rb = pv[0][lane];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+            ra.x += pk[w][lane].x;
+            ra.y += pk[w][lane].y;
+            rb.x += pv[w][lane].x;
+            rb.y += pv[w][lane].y;
+        }
+        float2* dkp = reinterpret_cast<float2*>(dk + (size_t)j * lddk + base);
+        float2* dvp = reinterpret_cast<float2*>(dv + (size_t)j * lddv + base);
+        if (accumulate) {
+            const float2 ok = *dkp, ov = *dvp;
+            ra.x += ok.x;
+            ra.y += ok.y;
+            rb.x += ov.x;
+            rb.y += ov.y;
+        }
+        *dkp = ra;
+        *dvp = rb;
+    }
+}
+
 int grid_1d(size_t n, int block) {
     size_t g = (n + block - 1) / block;
     if (g > 148 * 16) g = 148 * 16;
@@ -623,7 +869,17 @@ cudaError_t launch_bwd_ln(const float* dY, int ldy, const float* x, int ldx, con
                           int epi, float* out, int ldo, float* dg, float* db, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if ((dg || db) && T != 1) return cudaErrorInvalidValue;
-    k_bwd_ln<<<T, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, epi, out, ldo, dg, db);
+    const int nb = (T + 7) / 8;
+    if (n <= 256)
+        k_bwd_ln_warp<8><<<nb, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
+    else if (n <= 768)
+        k_bwd_ln_warp<24><<<nb, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
+    else if (n <= 1024)
+        k_bwd_ln_warp<32><<<nb, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
+    else if (n <= 1600)
+        k_bwd_ln_warp<50><<<nb, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
+    else
+        k_bwd_ln<<<T, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, epi, out, ldo, dg, db);
     return cudaGetLastError();
 }
 
@@ -644,7 +900,11 @@ cudaError_t launch_attn_fwd_train(const float* q, int ldq, const float* k, int l
     if (T <= 0) return cudaSuccess;
     if (T > ATT_MAX_T || hd > ATT_MAX_HD || hd <= 0 || n_head <= 0) return cudaErrorInvalidValue;
     const float scale = 1.0f / sqrtf((float)hd);
-    if (hd == 64)
+    const bool even = ((ldq | ldk | ldv | ldo) & 1) == 0 &&
+                      (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 7) == 0;
+    if (hd == 64 && even)
+        k_attn_fwd_w64<<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, scale, out, ldo, ohi, olo);
+    else if (hd == 64)
         k_attn_fwd_train<64><<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, hd, scale, out, ldo, ohi, olo);
     else
         k_attn_fwd_train<0><<<dim3(T, n_head), 128, 0, st>>>(q, ldq, k, ldk, v, ldv, hd, scale, out, ldo, ohi, olo);
@@ -658,6 +918,17 @@ cudaError_t launch_attn_bwd_train(const float* q, int ldq, const float* k, int l
     if (T > ATT_MAX_T || hd > ATT_MAX_HD || hd <= 0 || n_head <= 0) return cudaErrorInvalidValue;
     const float scale = 1.0f / sqrtf((float)hd);
     const dim3 grid(T, n_head);
+    const bool even = ((ldq | ldk | ldv | lddy | lddq | lddk | lddv) & 1) == 0 &&
+                      (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)dy | (uintptr_t)dq | (uintptr_t)dk |
+                        (uintptr_t)dv) & 7) == 0;
+    if (hd == 64 && even) {
+        k_attn_bwd_rows_w64<<<grid, 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, scale, dq, lddq, stats);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        k_attn_bwd_keys_w64<<<grid, 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, scale, stats, dk, lddk, dv,
+                                                  lddv, accumulate);
+        return cudaGetLastError();
+    }
     if (hd == 64)
         k_attn_bwd_rows<64><<<grid, 128, 0, st>>>(q, ldq, k, ldk, v, ldv, dy, lddy, T, hd, scale, dq, lddq, stats);
     else
