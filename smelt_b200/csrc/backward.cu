@@ -58,35 +58,6 @@ BwdSplit bwd_split(int T, int rows, int cols) {
     return s;
 }
 
-// Four consecutive dequantised weights W[r][c..c+3] (c % 4 == 0), each exactly (float)q * scale.
-template <int ATOM>
-__device__ __forceinline__ void load_w4(const QW& w, int r, int c, float f[4]) {
-    const uint8_t* row = w.q + (size_t)r * w.qstride;
-    if (ATOM == ATOM_F32) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(row) + (c >> 2));
-        f[0] = v.x, f[1] = v.y, f[2] = v.z, f[3] = v.w;
-    } else if (ATOM == ATOM_F16) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(row) + (c >> 2));
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-        f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
-    } else if (ATOM == ATOM_Q8) {
-        const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(row) + (c >> 2));
-        i8x4_to_f32(u, f);
-        const float s = __half2float(w.s[(size_t)r * w.sstride + (c >> 5)]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) f[j] *= s;
-    } else {  // Q4: per 32-group byte j = elem j (low nibble) | elem j+16 (high nibble)
-        const int g = c >> 5, e = c & 31;
-        const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(row + g * 16 + (e & 15)));
-        float lo[4], hi[4];
-        i4x8_to_f32(u, lo, hi);
-        const float s = __half2float(w.s[(size_t)r * w.sstride + g]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) f[j] = (e < 16 ? lo[j] : hi[j]) * s;
-    }
-}
-
 // Raw weight words of W[r][c..c+3] as loaded (dequantised later, so the next batch's loads can
 // be in flight while the current batch is consumed).
 template <int ATOM>
