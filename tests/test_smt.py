@@ -192,3 +192,47 @@ def test_record_past_section_is_refused(tmp_path):
     open(q, "wb").write(bytes(buf))
     with pytest.raises(Gpt2qError, match="runs past the section"):
         smt.inspect(q, verify=False)
+
+
+def _write_safetensors(path, tensors: dict):
+    header, blobs, off = {}, [], 0
+    for name, arr in tensors.items():
+        b = np.ascontiguousarray(arr, dtype="<f4").tobytes()
+        header[name] = {"dtype": "F32", "shape": list(arr.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    h = json.dumps(header).encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)) + h + b"".join(blobs))
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+def test_packer_reads_hf_directory(tmp_path, policy):
+    """pack_smt (the bin/pack.rs counterpart): config.json + model.safetensors + tokenizer.json
+    -> SMT whose tensors equal the in-memory converter's and whose tokenizer is embedded."""
+    from smelt_b200 import pack_smt
+
+    from .helpers import hf
+    meta = TINY
+    d = tmp_path / "assets"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps({"n_embd": meta.n_embd, "n_layer": meta.n_layer,
+                                               "n_head": meta.n_head, "n_ctx": meta.n_ctx,
+                                               "vocab_size": meta.vocab, "layer_norm_epsilon": 1e-5}))
+    (d / "tokenizer.json").write_text('{"model": {"type": "BPE"}}')
+    _write_safetensors(str(d / "model.safetensors"), hf(meta))
+    out = str(tmp_path / "m.smt")
+    assert pack_smt.main([str(d), "--policy", policy, "--out", out]) == 0
+    info = smt.inspect(out, verify=True)
+    assert info["verified"]
+    back = smt_oracle.read_smt(out)
+    ref = make_pack(meta, policy)
+    assert back.meta == ref.meta
+    for name, t in ref.tensors.items():
+        assert back.tensors[name].atom == t.atom
+        assert np.array_equal(back.tensors[name].data, np.ascontiguousarray(t.data).view(np.uint8).ravel()), name
+    buf = open(out, "rb").read()
+    tok = {ty: (p, ln) for ty, _, p, ln in _sections(buf)}[smt.SEC_TOKENIZER]
+    assert buf[tok[0]:tok[0] + tok[1]] == b'{"model": {"type": "BPE"}}'
+    with pytest.raises(SystemExit):
+        pack_smt.main(["--out", out])  # neither a directory nor --synthetic
