@@ -12,6 +12,7 @@
 #include <cstdlib>
 #include <cstring>
 
+#include "kernels.h"
 #include "tcgen05.cuh"
 
 namespace gpt2q {
@@ -892,6 +893,29 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
         const bool want_logits = p.logits != nullptr && step == p.steps - 1;
         unsigned long long best = 0ull;
         unsigned long long t_wait = 0, t_rel = 0, t_dot0 = 0, t_last = trace ? globaltimer() : 0;
+        if (p.adapter) {
+            // post-ln_f plastic adapter (cu/gpt2.cu:196-215), every CTA on its own copy of the
+            // row: ah[j] = sum_i A[j][i] h[i], then h[i] += sum_j B[i][j] ah[j], both sequential
+            // fused multiply-adds in the order of k_adapter_apply (wred is free here)
+            const AdapterDesc ad = *reinterpret_cast<const AdapterDesc*>(p.adapter);
+            if (ad.r > 0) {
+                float* ah = wred;
+                for (int j = tid; j < ad.r; j += NCT) {
+                    const float* ar = ad.a + (size_t)j * d;
+                    float s = 0.f;
+                    for (int i = 0; i < d; ++i) s = fmaf(__ldg(ar + i), ln[i], s);
+                    ah[j] = s;
+                }
+                __syncthreads();
+                for (int i = tid; i < d; i += NCT) {
+                    const float* br = ad.b + (size_t)i * ad.r;
+                    float s = 0.f;
+                    for (int j = 0; j < ad.r; ++j) s = fmaf(__ldg(br + j), ah[j], s);
+                    ln[i] = ln[i] + s;
+                }
+                __syncthreads();
+            }
+        }
         // fragments of the ln_f output (B operands) for this warp's groups, kept in registers for
         // the whole head; mpart is free once the last layer's x'' arrived
         const int gsn = d >> 5;

@@ -58,6 +58,9 @@ struct MkParams {
     int* abort_flag;
     int steps;
     unsigned long long* trace;  // optional [grid][MK_TRACE] globaltimer stamps of the first step
+    // optional post-ln_f adapter h += B (A h): device descriptor {a [r][d], b [d][r], r} read at
+    // every step's head (layout of AdapterDesc, kernels.h); null or r == 0 means none
+    const void* adapter;
 };
 
 constexpr int MK_TRACE = 48;  // trace slots per CTA: stamps (globaltimer) except the counters below

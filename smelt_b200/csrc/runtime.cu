@@ -613,6 +613,7 @@ int run_persistent(gpt2q_handle* H, int steps) {
     p.abort_flag = H->mk.err + 1;
     p.steps = steps;
     p.trace = H->mk.trace;
+    p.adapter = H->adapter_on ? H->d_adapter : nullptr;
     int rc = run_kernel(H, "decode_persistent", (double)H->mk.cta_bytes * 8 * H->mk.clusters * steps,
                         [&]() { return launch_decode_persistent(H->mk, p, H->stream); });
     if (rc) return rc;
@@ -621,8 +622,8 @@ int run_persistent(gpt2q_handle* H, int steps) {
 }
 
 bool use_persistent(const gpt2q_handle* H, int B) {
-    // the persistent kernel computes ln_f itself and has no adapter stage
-    return B == 1 && H->mk.enabled && !H->capturing && H->ktime_reps == 0 && !H->adapter_on;
+    // the persistent kernel computes ln_f and the adapter stage itself
+    return B == 1 && H->mk.enabled && !H->capturing && H->ktime_reps == 0;
 }
 
 

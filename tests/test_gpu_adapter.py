@@ -66,3 +66,38 @@ def test_adapter_rcu_switch_and_clear_in_batched_decode():
             eng.set_adapter(*(gen if gen is not None else (None, None)))
             ref = oracle_prefix_logits(eng, seq[:base + k])[-1]
             assert np.abs(got[k][s] - ref).max() <= TOL, (s, k)
+
+
+def test_adapter_on_the_persistent_single_sequence_path(monkeypatch):
+    """With an adapter set, single-sequence decode stays on the persistent kernel (its head
+    applies h += B(Ah) itself) and matches the per-kernel path and the oracle, step by step and
+    across a multi-step launch; a generation switch between launches takes effect."""
+    pk = make_pack(MINI, "auto", 0, 0.02)
+    a, b = _adapter(3, 16, MINI.n_embd)
+    a2, b2 = _adapter(4, 4, MINI.n_embd)
+    ids = ((np.arange(12) * 29 + 3) % MINI.vocab).astype(np.uint32)
+    eng = oracle_engine(pk)
+    eng.set_adapter(a, b)
+    ref = oracle_prefix_logits(eng, ids)
+    with Gpu(pk) as g:
+        if not g.info()["persistent_decode"]:
+            pytest.skip("persistent decode not available: " + g.info()["persistent_why"])
+        g.set_adapter(a, b)
+        got = np.stack([g.step(int(t), p) for p, t in enumerate(ids)])
+        assert np.abs(got - ref).max() <= TOL
+        assert np.array_equal(got.argmax(-1), ref.argmax(-1))
+        g.clear_kv()
+        g.prefill([ids])
+        multi = g.decode_steps(6, 1)[:, 0]
+        g.set_adapter(a2, b2)
+        after = g.decode_steps(3, 1)[:, 0]
+    monkeypatch.setenv("GPT2Q_NO_PERSISTENT", "1")
+    with Gpu(pk) as h:
+        assert not h.info()["persistent_decode"]
+        h.set_adapter(a, b)
+        h.prefill([ids])
+        ref_multi = h.decode_steps(6, 1)[:, 0]
+        h.set_adapter(a2, b2)
+        ref_after = h.decode_steps(3, 1)[:, 0]
+    assert np.array_equal(multi, ref_multi)
+    assert np.array_equal(after, ref_after)
