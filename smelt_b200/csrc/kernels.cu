@@ -517,6 +517,16 @@ __global__ void __launch_bounds__(AD_WARPS * 32) k_attn_decode(const float* q, i
     if (threadIdx.x == 0) {
         for (int s = 0; s < AD_NST; ++s) tc::mbar_init(&full[s], 1);
         tc::fence_mbar_init();
+        // While the q/k/v kernel finishes, pull this sequence's cached K/V rows into L2. Before
+        // griddepcontrol.wait the slot and position are only a hint (they are clamped into the
+        // arena); the rows the kernel uses are read by the bulk copies after the wait.
+        const int n_ctx = (int)(g.head_stride / AD_HD);
+        const int sp = min(max(__ldcg(slot + b), 0), g.n_slots - 1);
+        const int tp = min(max(__ldcg(pos + b) + 1, 1), n_ctx);
+        const float* Kp = g.base + (size_t)sp * g.slot_stride + layer_off + (size_t)head * g.head_stride;
+        const uint32_t bytes = (uint32_t)tp * AD_HD * 4;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(Kp), "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(Kp + g.sel_stride), "r"(bytes) : "memory");
     }
     __syncthreads();
     tc::pdl_wait();

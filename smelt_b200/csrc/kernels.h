@@ -13,6 +13,7 @@ struct KVGeom {
     float* base;
     size_t slot_stride, layer_stride, sel_stride, head_stride;
     int hd;
+    int n_slots;  // slots in the arena (n_ctx = head_stride / hd)
 };
 
 // Prefill attention work item: 64 query rows of one sequence.

@@ -1045,6 +1045,7 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
 
     // KV arena [slot][layer][K|V][head][n_ctx][hd]
     H->kv.hd = hd;
+    H->kv.n_slots = c.max_seqs;
     H->kv.head_stride = (size_t)c.n_ctx * hd;
     H->kv.sel_stride = (size_t)hn * H->kv.head_stride;
     H->kv.layer_stride = 2 * H->kv.sel_stride;
