@@ -351,13 +351,14 @@ __global__ void __launch_bounds__(256) k_bwd_ln(const float* __restrict__ dY, in
 }
 
 // The same LayerNorm backward with one warp per row (rows of up to 32 * NPL features held in
-// registers, reductions by shuffles only): T rows in T / 8 CTAs.
+// registers, reductions by shuffles only), one single-warp CTA per row so the rows spread over
+// the SMs.
 template <int NPL>
-__global__ void __launch_bounds__(256) k_bwd_ln_warp(const float* __restrict__ dY, int ldy,
+__global__ void __launch_bounds__(32) k_bwd_ln_warp(const float* __restrict__ dY, int ldy,
                                                      const float* __restrict__ X, int ldx,
                                                      const float* __restrict__ g, float eps, int n, int T, int epi,
                                                      float* __restrict__ out, int ldo, float* dg, float* db) {
-    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int t = blockIdx.x, lane = threadIdx.x;
     if (t >= T) return;
     const float* x = X + (size_t)t * ldx;
     const float* dy = dY + (size_t)t * ldy;
@@ -840,15 +841,14 @@ cudaError_t launch_bwd_ln(const float* dY, int ldy, const float* x, int ldx, con
                           int epi, float* out, int ldo, float* dg, float* db, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if ((dg || db) && T != 1) return cudaErrorInvalidValue;
-    const int nb = (T + 7) / 8;
     if (n <= 256)
-        k_bwd_ln_warp<8><<<nb, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
+        k_bwd_ln_warp<8><<<T, 32, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
     else if (n <= 768)
-        k_bwd_ln_warp<24><<<nb, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
+        k_bwd_ln_warp<24><<<T, 32, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
     else if (n <= 1024)
-        k_bwd_ln_warp<32><<<nb, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
+        k_bwd_ln_warp<32><<<T, 32, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
     else if (n <= 1600)
-        k_bwd_ln_warp<50><<<nb, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
+        k_bwd_ln_warp<50><<<T, 32, 0, st>>>(dY, ldy, x, ldx, g, eps, n, T, epi, out, ldo, dg, db);
     else
         k_bwd_ln<<<T, 256, 0, st>>>(dY, ldy, x, ldx, g, eps, n, epi, out, ldo, dg, db);
     return cudaGetLastError();
