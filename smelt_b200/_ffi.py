@@ -76,7 +76,9 @@ def load(path: str | None = None):
     lib.gpt2q_reset_kv.restype = C.c_int
     lib.gpt2q_step.argtypes = [_hp, C.c_uint32, C.c_int32, _f32p]
     lib.gpt2q_step.restype = C.c_int
-    lib.gpt2q_decode.argtypes = [_hp, _u32p, _i32p, _i32p, C.c_int, _f32p, _u32p]
+    # plain addresses: the per-token call path passes array addresses as integers (cheaper than
+    # building ctypes pointer objects)
+    lib.gpt2q_decode.argtypes = [_hp, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
     lib.gpt2q_decode.restype = C.c_int
     lib.gpt2q_prefill.argtypes = [_hp, _u32p, _i32p, _i32p, C.c_int, _f32p, _u32p]
     lib.gpt2q_prefill.restype = C.c_int

@@ -308,7 +308,11 @@ bool open_smt(const char* path, bool verify, Smt& s) {
         Record rec;
         const JVal *n = r.get("name"), *a = r.get("atom"), *sh = r.get("shape"), *o = r.get("offset"),
                    *l = r.get("len"), *d = r.get("digest");
-        if (!n || !a || !sh || !o || !l || sh->kind != JVal::ARR) return s.err = "malformed tensor record", false;
+        if (!n || !a || !sh || !o || !l || sh->kind != JVal::ARR || o->kind != JVal::NUM || l->kind != JVal::NUM ||
+            o->num < 0 || l->num < 0 || o->num > 9.0e15 || l->num > 9.0e15)
+            return s.err = "malformed tensor record", false;
+        for (const JVal& x : sh->arr)
+            if (x.kind != JVal::NUM || x.num < 0 || x.num > 2147483647.0) return s.err = "malformed tensor shape", false;
         rec.name = n->str;
         rec.atom = a->str;
         for (const JVal& x : sh->arr) rec.shape.push_back((int64_t)x.num);

@@ -128,9 +128,8 @@ class Gpu:
         nxt = np.empty(n, dtype=np.uint32)
         lg = np.empty((n, self.meta.vocab), dtype=np.float32) if want_logits else None
         self._check(self._lib.gpt2q_decode(
-            self.h, tok.ctypes.data_as(_ffi._u32p), pos.ctypes.data_as(_ffi._i32p),
-            None if sl is None else sl.ctypes.data_as(_ffi._i32p), n,
-            None if lg is None else lg.ctypes.data_as(_ffi._f32p), nxt.ctypes.data_as(_ffi._u32p)))
+            self.h, tok.ctypes.data, pos.ctypes.data, None if sl is None else sl.ctypes.data, n,
+            None if lg is None else lg.ctypes.data, nxt.ctypes.data))
         return (nxt, lg) if want_logits else nxt
 
     @staticmethod
