@@ -286,6 +286,178 @@ __global__ void __launch_bounds__(256, 2) k_bwd_linear(QW w, const float* __rest
     if (tid == 0) *ticket = 0u;  // ready for the next launch
 }
 
+// ---- the same transposed product on the tensor cores (3xTF32, mma.sync m16n8k8) ----
+// Each operand is split x = hi + lo with hi = tf32(x) and lo = tf32(x - hi) (both rounded to
+// nearest); hi*hi + hi*lo + lo*hi keeps about 21 bits, the fp32-level accuracy of the CUDA-core
+// product, with fp32's exponent range (no scaling needed for small gradients). A CTA owns 64
+// positions x 128 columns and a range of W's rows; per 32-row chunk the dequantised W and dY
+// tiles are staged (split) in shared memory, the next chunk's raw loads in flight meanwhile,
+// and warp w computes rows 16 (w % 4) .. + 15 against columns 64 (w / 4) .. + 63.
+constexpr int TB_M = 64, TB_N = 128, TB_K = 32;
+constexpr int TB_WS = TB_N + 8;  // W tile row stride (words): bank = 8 k + n, conflict-free fragments
+constexpr int TB_YS = TB_K + 4;  // dY tile row stride (words): bank = 4 t + k
+constexpr int TB_SMEM = (2 * TB_K * TB_WS + 2 * TB_M * TB_YS) * 4;
+
+struct TbSplit {
+    int splits, rows_per_split, col_tiles, m_tiles;
+};
+
+TbSplit tb_split(int T, int rows, int cols) {
+    TbSplit s;
+    s.col_tiles = (cols + TB_N - 1) / TB_N;
+    s.m_tiles = (T + TB_M - 1) / TB_M;
+    const int chunks = (rows + TB_K - 1) / TB_K;
+    int want = (2 * 148 + s.col_tiles * s.m_tiles - 1) / (s.col_tiles * s.m_tiles);
+    want = want < 1 ? 1 : (want > 64 ? 64 : want);
+    if (want > chunks) want = chunks;
+    s.rows_per_split = ((chunks + want - 1) / want) * TB_K;
+    s.splits = (rows + s.rows_per_split - 1) / s.rows_per_split;
+    if (s.splits < 1) s.splits = 1;
+    return s;
+}
+
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(x - __uint_as_float(hi)));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int ATOM>
+__global__ void __launch_bounds__(256, 2) k_bwd_linear_tc(QW w, const float* __restrict__ dY, int ldy, int T,
+                                                          int rows_per_split, float* part, unsigned* counters, int epi,
+                                                          float* out, int ldo, const float* xpre, int ldx) {
+    extern __shared__ __align__(16) uint32_t tb_sm[];
+    uint32_t* Wh = tb_sm;                    // [TB_K][TB_WS]
+    uint32_t* Wl = Wh + TB_K * TB_WS;        // [TB_K][TB_WS]
+    uint32_t* Yh = Wl + TB_K * TB_WS;        // [TB_M][TB_YS]
+    uint32_t* Yl = Yh + TB_M * TB_YS;        // [TB_M][TB_YS]
+    __shared__ bool is_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    const int c0 = blockIdx.x * TB_N, m0 = blockIdx.y * TB_M;
+    const int r_begin = blockIdx.z * rows_per_split;
+    const int r_end = min(w.rows, r_begin + rows_per_split);
+    // staging roles: W row tid / 8 (of 32), columns 16 (tid % 8) .. + 15 (four quads);
+    // dY position tid / 4 (of 64), k 8 (tid % 4) .. + 7
+    const int wr = tid >> 3, wc = 16 * (tid & 7);
+    const int yt = tid >> 2, yk = 8 * (tid & 3);
+    WRaw<ATOM> raw[4];
+    float yv[8];
+    auto load = [&](int rc) {
+        const int r = rc + wr;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int c = c0 + wc + 4 * q;
+            if (r < r_end && c < w.cols)
+                raw_load<ATOM>(w, r, c, raw[q]);
+            else
+                raw_zero<ATOM>(raw[q]);
+        }
+        const int tg = m0 + yt;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int k = rc + yk + u;
+            yv[u] = (tg < T && k < r_end) ? dY[(size_t)tg * ldy + k] : 0.f;
+        }
+    };
+    auto stage = [&]() {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float f[4];
+            raw_deq<ATOM>(raw[q], c0 + wc + 4 * q, f);
+            uint4 h, l;
+            tf32_split(f[0], h.x, l.x);
+            tf32_split(f[1], h.y, l.y);
+            tf32_split(f[2], h.z, l.z);
+            tf32_split(f[3], h.w, l.w);
+            *reinterpret_cast<uint4*>(Wh + wr * TB_WS + wc + 4 * q) = h;
+            *reinterpret_cast<uint4*>(Wl + wr * TB_WS + wc + 4 * q) = l;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u += 4) {
+            uint4 h, l;
+            tf32_split(yv[u], h.x, l.x);
+            tf32_split(yv[u + 1], h.y, l.y);
+            tf32_split(yv[u + 2], h.z, l.z);
+            tf32_split(yv[u + 3], h.w, l.w);
+            *reinterpret_cast<uint4*>(Yh + yt * TB_YS + yk + u) = h;
+            *reinterpret_cast<uint4*>(Yl + yt * TB_YS + yk + u) = l;
+        }
+    };
+    float acc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[nt][j] = 0.f;
+    const int mrow = 16 * (warp & 3), ncol = 64 * (warp >> 2);
+    if (r_begin < r_end) load(r_begin);
+    for (int rc = r_begin; rc < r_end; rc += TB_K) {
+        stage();
+        __syncthreads();
+        if (rc + TB_K < r_end) load(rc + TB_K);  // next chunk's loads fly during the MMAs
+#pragma unroll
+        for (int ks = 0; ks < TB_K / 8; ++ks) {
+            const int kk = 8 * ks + t4;
+            const uint32_t ah0 = Yh[(mrow + g) * TB_YS + kk], ah1 = Yh[(mrow + g + 8) * TB_YS + kk];
+            const uint32_t ah2 = Yh[(mrow + g) * TB_YS + kk + 4], ah3 = Yh[(mrow + g + 8) * TB_YS + kk + 4];
+            const uint32_t al0 = Yl[(mrow + g) * TB_YS + kk], al1 = Yl[(mrow + g + 8) * TB_YS + kk];
+            const uint32_t al2 = Yl[(mrow + g) * TB_YS + kk + 4], al3 = Yl[(mrow + g + 8) * TB_YS + kk + 4];
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                const int n = ncol + 8 * nt + g;
+                const uint32_t bh0 = Wh[kk * TB_WS + n], bh1 = Wh[(kk + 4) * TB_WS + n];
+                const uint32_t bl0 = Wl[kk * TB_WS + n], bl1 = Wl[(kk + 4) * TB_WS + n];
+                mma_tf32(acc[nt], al0, al1, al2, al3, bh0, bh1);
+                mma_tf32(acc[nt], ah0, ah1, ah2, ah3, bl0, bl1);
+                mma_tf32(acc[nt], ah0, ah1, ah2, ah3, bh0, bh1);
+            }
+        }
+        __syncthreads();  // the tiles are restaged next
+    }
+    // C fragment: rows mrow + g (+ 8), columns ncol + 8 nt + 2 t4 (+ 1)
+    const bool split = gridDim.z > 1;
+    float* mine = part + (size_t)blockIdx.z * T * w.cols;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int tg = m0 + mrow + g + ((j & 2) ? 8 : 0);
+            const int cg = c0 + ncol + 8 * nt + 2 * t4 + (j & 1);
+            if (tg < T && cg < w.cols) {
+                if (split)
+                    mine[(size_t)tg * w.cols + cg] = acc[nt][j];
+                else
+                    bwd_epi(epi, acc[nt][j], out, ldo, xpre, ldx, tg, cg);
+            }
+        }
+    if (!split) return;
+    __threadfence();
+    __syncthreads();
+    unsigned* ticket = counters + blockIdx.y * gridDim.x + blockIdx.x;
+    if (tid == 0) is_last = atomicAdd(ticket, 1u) == gridDim.z - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const int tn = min(TB_M, T - m0);
+    for (int i = tid; i < tn * TB_N; i += blockDim.x) {
+        const int tt = i / TB_N, cc = i - tt * TB_N;
+        const int tg = m0 + tt, cg = c0 + cc;
+        if (cg < w.cols) {
+            float v = 0.f;
+            for (int z = 0; z < (int)gridDim.z; ++z) v += __ldcg(part + ((size_t)z * T + tg) * w.cols + cg);
+            bwd_epi(epi, v, out, ldo, xpre, ldx, tg, cg);
+        }
+    }
+    if (tid == 0) *ticket = 0u;  // ready for the next launch
+}
+
+
 // Sum over the block in fixed order (warp shuffles, then warp 0 over the warps' sums).
 __device__ float block_sum(float v, float* red) {
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -801,19 +973,55 @@ int grid_1d(size_t n, int block) {
 
 }  // namespace
 
+// The tensor-core kernel serves T >= 16 positions over long reductions (W with at least 8192
+// rows: the tied head). Measured at 64 positions: head 404 -> 207 us; on the per-layer weights
+// (768 .. 3072 rows) it was slower than the CUDA-core kernel (c_fc 34 -> 66 us), since the short
+// reduction gives each CTA only a few 32-row chunks and the split partials dominate.
+constexpr int BWD_TC_MIN_T = 16, BWD_TC_MIN_ROWS = 8192;
+
+bool use_tc(int T, int rows) { return T >= BWD_TC_MIN_T && rows >= BWD_TC_MIN_ROWS; }
+
 size_t bwd_linear_part_floats(int T, int rows, int cols) {
     const BwdSplit s = bwd_split(T, rows, cols);
-    return s.splits > 1 ? (size_t)s.splits * T * cols : 1;
+    const TbSplit b = tb_split(T, rows, cols);
+    const int splits = use_tc(T, rows) ? b.splits : s.splits;
+    return splits > 1 ? (size_t)splits * T * cols : 1;
 }
 
 size_t bwd_linear_counters(int T, int cols) {
-    return (size_t)((cols + BL_COLS - 1) / BL_COLS) * ((T + BL_TT - 1) / BL_TT);
+    const size_t simt = (size_t)((cols + BL_COLS - 1) / BL_COLS) * ((T + BL_TT - 1) / BL_TT);
+    const size_t tc = (size_t)((cols + TB_N - 1) / TB_N) * ((T + TB_M - 1) / TB_M);
+    return simt > tc ? simt : tc;
+}
+
+template <int ATOM>
+cudaError_t launch_bwd_tc(const QW& w, const float* dY, int ldy, int T, float* part, unsigned* counters, int epi,
+                          float* out, int ldo, const float* xpre, int ldx, cudaStream_t st) {
+    static bool attr = false;  // one attribute call per instantiation and process
+    if (!attr) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(k_bwd_linear_tc<ATOM>, cudaFuncAttributeMaxDynamicSharedMemorySize, TB_SMEM);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const TbSplit s = tb_split(T, w.rows, w.cols);
+    k_bwd_linear_tc<ATOM><<<dim3(s.col_tiles, s.m_tiles, s.splits), 256, TB_SMEM, st>>>(
+        w, dY, ldy, T, s.rows_per_split, part, counters, epi, out, ldo, xpre, ldx);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_bwd_linear(const QW& w, const float* dY, int ldy, int T, float* part, unsigned* counters, int epi,
                               float* out, int ldo, const float* xpre, int ldx, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (w.cols % 4 != 0) return cudaErrorInvalidValue;
+    if (use_tc(T, w.rows)) {
+        switch (w.atom) {
+            case ATOM_Q8: return launch_bwd_tc<ATOM_Q8>(w, dY, ldy, T, part, counters, epi, out, ldo, xpre, ldx, st);
+            case ATOM_Q4: return launch_bwd_tc<ATOM_Q4>(w, dY, ldy, T, part, counters, epi, out, ldo, xpre, ldx, st);
+            case ATOM_F16: return launch_bwd_tc<ATOM_F16>(w, dY, ldy, T, part, counters, epi, out, ldo, xpre, ldx, st);
+            default: return launch_bwd_tc<ATOM_F32>(w, dY, ldy, T, part, counters, epi, out, ldo, xpre, ldx, st);
+        }
+    }
     const BwdSplit s = bwd_split(T, w.rows, w.cols);
     const dim3 grid(s.col_tiles, s.t_tiles, s.splits), block(256);
     switch (w.atom) {

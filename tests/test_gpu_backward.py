@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 from oracle import backward_oracle as B
+from smelt_b200 import pack as P
 from smelt_b200._ffi import Gpt2qError
 from smelt_b200.backward import GpuBwdOps
 from smelt_b200.gpu import Gpu
@@ -112,3 +113,23 @@ def test_trunk_rejects_bad_arguments():
         # the handle still works afterwards
         dx, _ = g.trunk_input_grad(np.array([1, 2], np.uint32), ok)
         assert np.all(dx == 0)
+
+
+WIDE_VOCAB = P.Meta(n_embd=128, n_layer=2, n_head=2, n_ctx=64, vocab=9000)
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto", "f32"])
+def test_trunk_head_on_tensor_cores(policy):
+    """A vocabulary of >= 8192 rows with >= 16 positions takes the 3xTF32 tensor-core kernel for
+    the head's transposed product (dh = dlogits . wte); the result matches the f64 oracle."""
+    pk = make_pack(WIDE_VOCAB, policy, 0, 0.02)
+    W = B.weights64(pk)
+    rng = np.random.default_rng(21)
+    with Gpu(pk) as g:
+        for n in (16, 40, WIDE_VOCAB.n_ctx):
+            ids = rng.integers(0, WIDE_VOCAB.vocab, n).astype(np.uint32)
+            dl = (rng.standard_normal((n, WIDE_VOCAB.vocab)) * 0.01).astype(np.float32)  # dense dlogits
+            dx, _ = g.trunk_input_grad(ids, dl)
+            _, acts = B.forward_stash(W, WIDE_VOCAB, ids)
+            ref = B.trunk_input_grad(W, WIDE_VOCAB, acts, dl.astype(np.float64))
+            assert B.rel_max(dx, ref) < 2e-3, (n, B.rel_max(dx, ref))
