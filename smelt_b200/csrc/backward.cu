@@ -309,7 +309,9 @@ TbSplit tb_split(int T, int rows, int cols) {
     const int chunks = (rows + TB_K - 1) / TB_K;
     int want = (2 * 148 + s.col_tiles * s.m_tiles - 1) / (s.col_tiles * s.m_tiles);
     want = want < 1 ? 1 : (want > 64 ? 64 : want);
-    if (want > chunks) want = chunks;
+    // at least 8 chunks per CTA: the last CTA of a tile sums every split's partial tile
+    const int by_len = chunks / 8 > 1 ? chunks / 8 : 1;
+    if (want > by_len) want = by_len;
     s.rows_per_split = ((chunks + want - 1) / want) * TB_K;
     s.splits = (rows + s.rows_per_split - 1) / s.rows_per_split;
     if (s.splits < 1) s.splits = 1;
@@ -975,8 +977,9 @@ int grid_1d(size_t n, int block) {
 
 // The tensor-core kernel serves T >= 16 positions over long reductions (W with at least 8192
 // rows: the tied head). Measured at 64 positions: head 404 -> 207 us; on the per-layer weights
-// (768 .. 3072 rows) it was slower than the CUDA-core kernel (c_fc 34 -> 66 us), since the short
-// reduction gives each CTA only a few 32-row chunks and the split partials dominate.
+// (768 .. 3072 rows) it was slower than the CUDA-core kernel (c_fc 34 -> 66 us with 2 chunks per
+// CTA, 58 us with 8), its per-chunk staging and mma.sync issue costing more than the CUDA-core
+// kernel's whole pass.
 constexpr int BWD_TC_MIN_T = 16, BWD_TC_MIN_ROWS = 8192;
 
 bool use_tc(int T, int rows) { return T >= BWD_TC_MIN_T && rows >= BWD_TC_MIN_ROWS; }
