@@ -1000,12 +1000,14 @@ size_t bwd_linear_counters(int T, int cols) {
 template <int ATOM>
 cudaError_t launch_bwd_tc(const QW& w, const float* dY, int ldy, int T, float* part, unsigned* counters, int epi,
                           float* out, int ldo, const float* xpre, int ldx, cudaStream_t st) {
-    static bool attr = false;  // one attribute call per instantiation and process
-    if (!attr) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(k_bwd_linear_tc<ATOM>, cudaFuncAttributeMaxDynamicSharedMemorySize, TB_SMEM);
+    static bool attr[64] = {};  // the attribute is per device: once per instantiation and device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !attr[dev]) {
+        e = cudaFuncSetAttribute(k_bwd_linear_tc<ATOM>, cudaFuncAttributeMaxDynamicSharedMemorySize, TB_SMEM);
         if (e != cudaSuccess) return e;
-        attr = true;
+        if (dev >= 0 && dev < 64) attr[dev] = true;
     }
     const TbSplit s = tb_split(T, w.rows, w.cols);
     k_bwd_linear_tc<ATOM><<<dim3(s.col_tiles, s.m_tiles, s.splits), 256, TB_SMEM, st>>>(

@@ -435,16 +435,26 @@ __global__ void __launch_bounds__(256) k_adapter_apply(const AdapterDesc* __rest
     }
 }
 
+// Raise a kernel's dynamic shared-memory limit once per device (the attribute is per device).
+template <class K>
+cudaError_t smem_limit_once(K* kern, int smem, bool (&done)[64]) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+    return e;
+}
+
 cudaError_t launch_adapter(const AdapterDesc* desc, float* h, __half* hhi, __half* hlo, int ld, int d, int rows,
                            int max_r, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
     const size_t smem = (size_t)(d + max_r) * 4;
     if (smem > 48 * 1024) {
-        static bool attr = [smem] {
-            return cudaFuncSetAttribute(k_adapter_apply, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
-                   cudaSuccess;
-        }();
-        if (!attr) return cudaErrorInvalidValue;
+        static bool done[64] = {};
+        const cudaError_t e = smem_limit_once(k_adapter_apply, (int)smem, done);
+        if (e != cudaSuccess) return e;
     }
     return launch_pdl(k_adapter_apply, dim3(rows), dim3(256), smem, st, desc, h, hhi, hlo, ld, d);
 }
@@ -626,11 +636,9 @@ cudaError_t launch_attn_decode(const float* q, int ldq, const KVGeom& g, size_t 
                                float scale, int* err, cudaStream_t st) {
     if (B <= 0) return cudaSuccess;
     if (g.hd != AD_HD) return cudaErrorInvalidValue;
-    static bool attr = [] {
-        return cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AD_SMEM) ==
-               cudaSuccess;
-    }();
-    if (!attr) return cudaErrorInvalidValue;
+    static bool done[64] = {};
+    const cudaError_t e = smem_limit_once(k_attn_decode, (int)AD_SMEM, done);
+    if (e != cudaSuccess) return e;
     return launch_pdl(k_attn_decode, dim3(n_head, B), dim3(AD_WARPS * 32), AD_SMEM, st, q, ldq, g, layer_off, slot,
                       pos, out, ohi, olo, ldo, scale, err);
 }
