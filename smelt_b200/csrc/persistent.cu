@@ -903,6 +903,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
                 for (int j = tid; j < ad.r; j += NCT) {
                     const float* ar = ad.a + (size_t)j * d;
                     float s = 0.f;
+#pragma unroll 16
                     for (int i = 0; i < d; ++i) s = fmaf(__ldg(ar + i), ln[i], s);
                     ah[j] = s;
                 }
@@ -910,6 +911,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_persistent(const __grid_c
                 for (int i = tid; i < d; i += NCT) {
                     const float* br = ad.b + (size_t)i * ad.r;
                     float s = 0.f;
+#pragma unroll 8
                     for (int j = 0; j < ad.r; ++j) s = fmaf(__ldg(br + j), ah[j], s);
                     ln[i] = ln[i] + s;
                 }
