@@ -8,12 +8,15 @@
 //   registers) and broadcasts the staged dY values from shared memory. Row ranges are split
 //   across CTAs so the grid fills the 148 SMs; the last CTA of each tile sums the splits in
 //   fixed order and applies the epilogue (store, add, or GELU backward): deterministic.
+// * k_bwd_linear_tc: the same product on the tensor cores as 3xTF32 (mma.sync m16n8k8), used
+//   for long reductions (the tied head's 50257 rows) at 16 or more positions.
 // * k_bwd_ln_warp: one warp per row held in registers, shuffle reductions (k_bwd_ln, one CTA
 //   per row, for rows wider than 1600).
 // * attention: one CTA per (query row, head) recomputes the probability row, the row's dP and
 //   dq; one CTA per (key row, head) recomputes the column of P and dS from the saved row
 //   statistics and sums dk and dv over the later queries (strided over the CTA's thread groups,
-//   parts added in fixed order). No floating-point atomics anywhere.
+//   parts added in fixed order). For head dim 64 a whole row goes to one warp (the _w64
+//   kernels). No floating-point atomics anywhere.
 #include <cuda_runtime.h>
 
 #include <cmath>
