@@ -236,3 +236,29 @@ def test_packer_reads_hf_directory(tmp_path, policy):
     assert buf[tok[0]:tok[0] + tok[1]] == b'{"model": {"type": "BPE"}}'
     with pytest.raises(SystemExit):
         pack_smt.main(["--out", out])  # neither a directory nor --synthetic
+
+
+def test_unknown_sections_are_covered_by_the_merkle_but_ignored(tmp_path):
+    """A section type the reader does not know (e.g. a future one) is hashed into the content_id
+    like every other section (PackReader::verify walks all of them, format.rs:121-145) and
+    otherwise ignored."""
+    pk = make_pack(TINY, "auto")
+    path = str(tmp_path / "m.smt")
+    smt.write_smt(path, pk)
+    buf = bytearray(open(path, "rb").read())
+    extra = b"future section payload"
+    buf += struct.pack("<IIQ", 99, 0, len(extra)) + extra
+    # content_id over every section, the appended one included (INDEX itself is unchanged)
+    digests = sorted(smt.blake3(bytes(buf[p:p + ln])) for _, _, p, ln in _sections(bytes(buf)))
+    buf[16:48] = smt.blake3(b"".join(digests))
+    buf[48:56] = struct.pack("<Q", len(buf))
+    q = str(tmp_path / "extra.smt")
+    open(q, "wb").write(bytes(buf))
+    info = smt.inspect(q, verify=True)
+    assert info["verified"] and len(info["tensors"]) == len(pk.tensors)
+    # the same file without re-merkling fails verification
+    bad = bytearray(open(path, "rb").read()) + struct.pack("<IIQ", 99, 0, len(extra)) + extra
+    q2 = str(tmp_path / "extra_bad.smt")
+    open(q2, "wb").write(bytes(bad))
+    with pytest.raises(Gpt2qError, match="merkle"):
+        smt.inspect(q2, verify=True)
