@@ -41,3 +41,16 @@ def test_trunk_composition_matches_finite_differences(meta, policy):
     dx = B.trunk_input_grad(W, meta, acts, dl.astype(np.float64))
     rows = B.fd_embedding_check(W, meta, ids, dl, dx, acts["lnf_out"], n_coords=16)
     assert B.rel_max(rows[:, 0], rows[:, 1]) < 1e-3
+
+
+@pytest.mark.parametrize("policy", ["f32", "auto"])
+def test_f64_stash_forward_agrees_with_the_cpp_oracle(policy):
+    """The backward oracle's f64 forward (bwparity.rs forward_stash) and the C++ restatement of
+    Engine::step give the same logits on the same dequantised weights (to f32 rounding)."""
+    from .helpers import oracle_engine, oracle_prefix_logits
+
+    pk = make_pack(TINY, policy, 0, 0.02)
+    ids = np.array([3, 14, 15, 92, 65, 35, 89], np.uint32)
+    lg64, _ = B.forward_stash(B.weights64(pk), TINY, ids)
+    lg32 = oracle_prefix_logits(oracle_engine(pk), ids)
+    assert np.max(np.abs(lg64 - lg32)) < 1e-4
