@@ -262,3 +262,16 @@ def test_unknown_sections_are_covered_by_the_merkle_but_ignored(tmp_path):
     open(q2, "wb").write(bytes(bad))
     with pytest.raises(Gpt2qError, match="merkle"):
         smt.inspect(q2, verify=True)
+
+
+def test_packer_synthetic_gpt2_small(tmp_path):
+    """`python -m smelt_b200.pack_smt --synthetic small` writes a verifiable 148-tensor container."""
+    from smelt_b200 import pack_smt
+
+    out = str(tmp_path / "small.smt")
+    assert pack_smt.main(["--synthetic", "small", "--policy", "auto", "--out", out]) == 0
+    info = smt.inspect(out, verify=True)
+    assert info["verified"] and len(info["tensors"]) == 148
+    assert info["arch"] == {"n_embd": 768, "n_layer": 12, "n_head": 12, "n_ctx": 1024, "vocab_size": 50257}
+    atoms = {t["name"]: t["atom"] for t in info["tensors"]}
+    assert atoms["wte.weight"] == "core.i8.b32.f16scale" and atoms["ln_f.weight"] == "core.f16"
