@@ -275,3 +275,9 @@ def test_packer_synthetic_gpt2_small(tmp_path):
     assert info["arch"] == {"n_embd": 768, "n_layer": 12, "n_head": 12, "n_ctx": 1024, "vocab_size": 50257}
     atoms = {t["name"]: t["atom"] for t in info["tensors"]}
     assert atoms["wte.weight"] == "core.i8.b32.f16scale" and atoms["ln_f.weight"] == "core.f16"
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """No fallback: without the built library every entry point refuses to load."""
+    with pytest.raises(ImportError, match="not built"):
+        _ffi.load(str(tmp_path / "libgpt2q.so"))
