@@ -7,7 +7,11 @@ backward.cu, gpt2q_trunk_input_grad in runtime.cu) are compared against. Only te
   [-1, 1), below).
 * ``selfcheck``: the finite-difference self-checks of each backward kernel
   (gpu_backward.rs:915-1090, same seeds, sizes and tolerances, ``rel_max`` of :860-872), run
-  through any implementation of the four ops.
+  through any implementation of the four ops. The finite-difference side keeps the reference's
+  evaluation order (sequential f64 sums), so that ``MirrorOps32`` (the reference's CPU mirror,
+  gpu_backward.rs:450-590, in f32 with Rust's operation order) prints the reference's own
+  logged KCHECK lines digit for digit (docs/experiments/results/bwparity.log:6-9): the pin of
+  the Rng, the harness and rel_max.
 * ``forward_stash``: the stash of bin/bwparity.rs forward_stash (:448-580): per layer the residual
   entering the layer, the residual after attention, q|k|v with bias, the pre-GELU c_fc output;
   the input and output of ln_f; the logits.
@@ -19,6 +23,9 @@ backward.cu, gpt2q_trunk_input_grad in runtime.cu) are compared against. Only te
 Everything is float64 over the exactly dequantised weights (Engine::vec_f32).
 """
 from __future__ import annotations
+
+import math
+import sys
 
 import numpy as np
 
@@ -217,49 +224,102 @@ def fd_embedding_check(W: dict, meta, ids, dlogits, dx, lnf_out, n_coords: int =
 
 
 # ---------------------------------------------------------------- kernel self-checks
+# f64 reference forwards of the self-checks, evaluated in the reference's order (sequential
+# iterator sums, libm transcendentals), so the finite differences carry the same rounding
+def _seq_sum(vals) -> float:
+    s = 0.0
+    for v in vals:
+        s += v
+    return s
+
+
+def _f64_gelu(v: float) -> float:
+    return 0.5 * v * (1.0 + math.tanh(0.7978845608028654 * (v + 0.044715 * v * v * v)))
+
+
+def _f64_attn_add(q, k, v, t_len, hd, stride, out):
+    """gpu_backward.rs f64ref::attn_add: causal training-form attention, adds into out."""
+    scale = 1.0 / math.sqrt(hd)
+    for head in range(stride // hd):
+        base = head * hd
+        for i in range(t_len):
+            scores = []
+            for j in range(i + 1):
+                d = 0.0
+                for tt in range(hd):
+                    d += float(q[i * stride + base + tt]) * float(k[j * stride + base + tt])
+                scores.append(d * scale)
+            mx = -sys.float_info.max
+            for sc in scores:
+                mx = max(mx, sc)
+            ssum = 0.0
+            for j in range(len(scores)):
+                scores[j] = math.exp(scores[j] - mx)
+                ssum += scores[j]
+            for j in range(len(scores)):
+                scores[j] /= ssum
+            for j in range(i + 1):
+                for tt in range(hd):
+                    out[i * stride + base + tt] += scores[j] * float(v[j * stride + base + tt])
+
+
 def selfcheck(ops, which: str):
     """gpu_backward.rs:915-1090 through `ops` (an object with lin_input_grad(w, dy, rows, cols),
     ln_backward(dy, x, g, b, eps) -> (dx, dg, db), gelu_bwd(x, dy), attn_bwd_train(q, k, v, dy,
-    t, hd, stride) -> (dq, dk, dv), all float32 in and out). Returns (max_rel, tol)."""
+    t, hd, stride) -> (dq, dk, dv), all float32 in and out). Returns (max_rel, tol). The f64 side
+    follows the reference's evaluation order, so MirrorOps32 reproduces the reference's logged
+    KCHECK values for its CPU mirror."""
     if which == "k_lin_input_grad":
         r = Rng(101)
         rows, cols = 16, 24
         w = np.array([r.f32() for _ in range(rows * cols)], np.float32)
         c = np.array([r.f32() for _ in range(rows)], np.float32)
         dx = ops.lin_input_grad(w, c, rows, cols)
-        wf, cf = w.astype(np.float64).reshape(rows, cols), c.astype(np.float64)
+        wf = [float(v) for v in w]
+        cf = [float(v) for v in c]
         h = 1e-5
-        fd = np.zeros(cols)
-        y = np.zeros(cols)
+
+        def f(y):
+            acc = 0.0
+            for rr in range(rows):
+                d = 0.0
+                for j in range(cols):
+                    d += wf[rr * cols + j] * y[j]
+                acc += cf[rr] * d
+            return acc
+
+        y = [0.0] * cols
+        fd = np.zeros(cols, np.float32)
         for i in range(cols):
             y[i] += h
-            lp = float(cf @ (wf @ y))
-            y[i] -= 2 * h
-            lm = float(cf @ (wf @ y))
+            lp = f(y)
+            y[i] -= 2.0 * h
+            lm = f(y)
             y[i] += h
-            fd[i] = (lp - lm) / (2 * h)
-        return rel_max(dx, fd.astype(np.float32)), 1e-4
+            fd[i] = np.float32((lp - lm) / (2.0 * h))
+        return rel_max(dx, fd), 1e-4
     if which == "k_ln_backward":
         r = Rng(202)
         n, eps = 64, np.float32(1e-5)
         x0 = np.array([r.f32() for _ in range(n)], np.float32)
         g0 = np.array([r.f32() for _ in range(n)], np.float32)
         b0 = np.array([r.f32() for _ in range(n)], np.float32)
-        dy0 = np.array([r.f32() for _ in range(n)], np.float32).astype(np.float64)
-        dx, dg, db = ops.ln_backward(dy0.astype(np.float32), x0, g0, b0, eps)
+        dy0 = [float(r.f32()) for _ in range(n)]
+        dx, dg, db = ops.ln_backward(np.array(dy0, np.float32), x0, g0, b0, eps)
 
         def df(xx, gg, bb):
-            mean = xx.sum() / n
-            var = ((xx - mean) ** 2).sum() / n
-            return float((((xx - mean) / np.sqrt(var + float(eps)) * gg + bb) * dy0).sum())
+            mean = _seq_sum(xx) / n
+            var = _seq_sum((v - mean) * (v - mean) for v in xx) / n
+            den = math.sqrt(var + float(eps))
+            return _seq_sum(((xx[i] - mean) / den * gg[i] + bb[i]) * dy0[i] for i in range(n))
 
-        xf, gf, bf = (a.astype(np.float64) for a in (x0, g0, b0))
+        base = [[float(v) for v in a] for a in (x0, g0, b0)]
         h = 1e-6
 
         def fd_of(which_arr):
-            out = np.zeros(n, np.float32)
-            arrs = [xf.copy(), gf.copy(), bf.copy()]
+            arrs = [list(a) for a in base]
             a = arrs[which_arr]
+            out = np.zeros(n, np.float32)
             for i in range(n):
                 keep = a[i]
                 a[i] = keep + h
@@ -267,7 +327,7 @@ def selfcheck(ops, which: str):
                 a[i] = keep - h
                 lm = df(*arrs)
                 a[i] = keep
-                out[i] = np.float32((lp - lm) / (2 * h))
+                out[i] = np.float32((lp - lm) / (2.0 * h))
             return out
 
         mr = max(rel_max(dx, fd_of(0)), rel_max(dg, fd_of(1)), rel_max(db, fd_of(2)))
@@ -276,19 +336,19 @@ def selfcheck(ops, which: str):
         r = Rng(303)
         n = 32
         xp = np.array([np.float32(r.f32() * np.float32(3.0)) for _ in range(n)], np.float32)
-        dy0 = np.array([r.f32() for _ in range(n)], np.float32).astype(np.float64)
-        dx = ops.gelu_bwd(xp, dy0.astype(np.float32))
-        xx = xp.astype(np.float64)
+        dy0 = [float(r.f32()) for _ in range(n)]
+        dx = ops.gelu_bwd(xp, np.array(dy0, np.float32))
+        xx = [float(v) for v in xp]
         h = 1e-6
-        fd = np.zeros(n)
+        fd = np.zeros(n, np.float32)
         for i in range(n):
             xx[i] += h
-            lp = float((gelu(xx) * dy0).sum())
-            xx[i] -= 2 * h
-            lm = float((gelu(xx) * dy0).sum())
+            lp = _seq_sum(_f64_gelu(v) * d for v, d in zip(xx, dy0))
+            xx[i] -= 2.0 * h
+            lm = _seq_sum(_f64_gelu(v) * d for v, d in zip(xx, dy0))
             xx[i] += h
-            fd[i] = (lp - lm) / (2 * h)
-        return rel_max(dx, fd.astype(np.float32)), 1e-3
+            fd[i] = np.float32((lp - lm) / (2.0 * h))
+        return rel_max(dx, fd), 1e-3
     if which == "k_attn_bwd_train":
         r = Rng(404)
         t_len, hd, stride = 5, 8, 8
@@ -298,11 +358,12 @@ def selfcheck(ops, which: str):
         v = np.array([r.f32() for _ in range(total)], np.float32)
         dy0 = np.array([r.f32() for _ in range(total)], np.float32)
         dq, dk, dv = ops.attn_bwd_train(q, k, v, dy0, t_len, hd, stride)
+        dyl = [float(x) for x in dy0]
 
         def f(qq, kk, vv):
-            o = attn_causal(qq.astype(np.float64).reshape(t_len, stride), kk.astype(np.float64).reshape(t_len, stride),
-                            vv.astype(np.float64).reshape(t_len, stride), stride // hd)
-            return float((o.ravel() * dy0.astype(np.float64)).sum())
+            out = [0.0] * total
+            _f64_attn_add(qq, kk, vv, t_len, hd, stride, out)
+            return _seq_sum(a * d for a, d in zip(out, dyl))
 
         h = np.float32(1e-4)
 
@@ -310,15 +371,13 @@ def selfcheck(ops, which: str):
             out = np.zeros(total, np.float32)
             a = arr.copy()
             for i in range(total):
-                keep = a[i]
-                a[i] = np.float32(keep + h)
+                a[i] = np.float32(a[i] + h)
                 args = [q, k, v]
                 args[pos] = a
                 lp = f(*args)
-                a[i] = np.float32(np.float32(keep + h) - np.float32(2.0) * h)
-                args[pos] = a
+                a[i] = np.float32(a[i] - np.float32(2.0) * h)
                 lm = f(*args)
-                a[i] = keep
+                a[i] = np.float32(a[i] + h)
                 out[i] = np.float32((lp - lm) / (2.0 * float(h)))
             return out
 
@@ -348,3 +407,113 @@ class MirrorOps:
         sh = (t, stride)
         out = attn_bwd_train(*(a.astype(np.float64).reshape(sh) for a in (q, k, v, dy)), hd)
         return tuple(o.ravel().astype(np.float32) for o in out)
+
+
+class MirrorOps32:
+    """MirrorOps (gpu_backward.rs:450-590) in float32 with the Rust operation order: sequential
+    sums, separate multiply and add (Rust does not fuse), f32 transcendentals. Pure-Python
+    loops: only for the self-check sizes."""
+
+    def lin_input_grad(self, w, dy, rows, cols):
+        w = np.asarray(w, np.float32).reshape(rows, cols)
+        dy = np.asarray(dy, np.float32)
+        dx = np.zeros(cols, np.float32)
+        for i in range(cols):
+            acc = np.float32(0.0)
+            for r in range(rows):
+                acc = np.float32(acc + np.float32(w[r, i] * dy[r]))
+            dx[i] = acc
+        return dx
+
+    def ln_backward(self, dy, x, g, b, eps):
+        dy, x, g = (np.asarray(a, np.float32) for a in (dy, x, g))
+        n = x.size
+        nf = np.float32(n)
+        s = np.float32(0.0)
+        for v in x:
+            s = np.float32(s + v)
+        mean = np.float32(s / nf)
+        sq = np.float32(0.0)
+        for v in x:
+            d = np.float32(v - mean)
+            sq = np.float32(sq + np.float32(d * d))
+        var = np.float32(sq / nf)
+        rstd = np.float32(np.float32(1.0) / np.sqrt(np.float32(var + np.float32(eps))))
+        mdxh = np.float32(0.0)
+        mdxh_xh = np.float32(0.0)
+        for i in range(n):
+            dh = np.float32(dy[i] * g[i])
+            mdxh = np.float32(mdxh + dh)
+            mdxh_xh = np.float32(mdxh_xh + np.float32(np.float32(dh * np.float32(x[i] - mean)) * rstd))
+        mdxh = np.float32(mdxh / nf)
+        mdxh_xh = np.float32(mdxh_xh / nf)
+        dx = np.zeros(n, np.float32)
+        dg = np.zeros(n, np.float32)
+        db = np.zeros(n, np.float32)
+        for i in range(n):
+            xh = np.float32(np.float32(x[i] - mean) * rstd)
+            dh = np.float32(dy[i] * g[i])
+            dx[i] = np.float32(rstd * np.float32(np.float32(dh - mdxh) - np.float32(xh * mdxh_xh)))
+            dg[i] = np.float32(dg[i] + np.float32(dy[i] * xh))
+            db[i] = np.float32(db[i] + dy[i])
+        return dx, dg, db
+
+    def gelu_bwd(self, x, dy):
+        x, dy = np.asarray(x, np.float32), np.asarray(dy, np.float32)
+        c, k = np.float32(0.7978845608028654), np.float32(0.044715)
+        dx = np.zeros(x.size, np.float32)
+        for i in range(x.size):
+            v = x[i]
+            u = np.float32(c * np.float32(v + np.float32(np.float32(np.float32(k * v) * v) * v)))
+            th = np.float32(np.tanh(u))
+            sech2 = np.float32(np.float32(1.0) - np.float32(th * th))
+            t1 = np.float32(np.float32(0.5) * np.float32(np.float32(1.0) + th))
+            t2 = np.float32(np.float32(np.float32(np.float32(np.float32(0.5) * v) * sech2) * c) *
+                            np.float32(np.float32(1.0) + np.float32(np.float32(np.float32(np.float32(3.0) * k) * v) * v)))
+            dx[i] = np.float32(dy[i] * np.float32(t1 + t2))
+        return dx
+
+    def attn_bwd_train(self, q, k, v, dy, t, hd, stride):
+        q, k, v, dy = (np.asarray(a, np.float32).reshape(-1) for a in (q, k, v, dy))
+        total = t * stride
+        dq, dk, dv = np.zeros(total, np.float32), np.zeros(total, np.float32), np.zeros(total, np.float32)
+        scale = np.float32(np.float32(1.0) / np.sqrt(np.float32(hd)))
+        for head in range(stride // hd):
+            base = head * hd
+            for i in range(t):
+                scores = []
+                mx = np.float32(np.finfo(np.float32).min)
+                for j in range(i + 1):
+                    d = np.float32(0.0)
+                    for tt in range(hd):
+                        d = np.float32(d + np.float32(q[i * stride + base + tt] * k[j * stride + base + tt]))
+                    s = np.float32(d * scale)
+                    scores.append(s)
+                    mx = max(mx, s)
+                ssum = np.float32(0.0)
+                for j in range(i + 1):
+                    scores[j] = np.float32(np.exp(np.float32(scores[j] - mx)))
+                    ssum = np.float32(ssum + scores[j])
+                for j in range(i + 1):
+                    scores[j] = np.float32(scores[j] / ssum)
+                dp = []
+                rs = np.float32(0.0)
+                for j in range(i + 1):
+                    d = np.float32(0.0)
+                    for tt in range(hd):
+                        d = np.float32(d + np.float32(dy[i * stride + base + tt] * v[j * stride + base + tt]))
+                    dp.append(d)
+                    rs = np.float32(rs + np.float32(d * scores[j]))
+                ds = [np.float32(np.float32(np.float32(dp[j] - rs) * scores[j]) * scale) for j in range(i + 1)]
+                for tt in range(hd):
+                    acc = np.float32(0.0)
+                    for j in range(i + 1):
+                        acc = np.float32(acc + np.float32(ds[j] * k[j * stride + base + tt]))
+                    dq[i * stride + base + tt] = acc
+                for j in range(i + 1):
+                    for tt in range(hd):
+                        dk[j * stride + base + tt] = np.float32(dk[j * stride + base + tt] +
+                                                                np.float32(ds[j] * q[i * stride + base + tt]))
+                        dv[j * stride + base + tt] = np.float32(dv[j * stride + base + tt] +
+                                                                np.float32(scores[j] * dy[i * stride + base + tt]))
+        return dq, dk, dv

@@ -54,3 +54,26 @@ def test_f64_stash_forward_agrees_with_the_cpp_oracle(policy):
     lg64, _ = B.forward_stash(B.weights64(pk), TINY, ids)
     lg32 = oracle_prefix_logits(oracle_engine(pk), ids)
     assert np.max(np.abs(lg64 - lg32)) < 1e-4
+
+
+def _rust_e(v: float, prec: int) -> str:
+    """Rust's `{:.Ne}` formatting (no exponent padding, no '+')."""
+    mant, exp = f"{v:.{prec}e}".split("e")
+    return f"{mant}e{int(exp)}"
+
+
+def test_mirror32_reproduces_the_reference_kcheck_log():
+    """The f32 restatement of MirrorOps run through the restated self-check harness prints the
+    reference's own KCHECK lines for its CPU mirror, digit for digit
+    (docs/experiments/results/bwparity.log:6-9, copied to tests/golden/bwparity_kcheck_ref.txt).
+    This pins the Rng, the finite-difference harness and rel_max, and the mirror arithmetic."""
+    import os
+
+    samples = {"k_lin_input_grad": 24, "k_ln_backward": 192, "k_gelu_bwd": 32, "k_attn_bwd_train": 120}
+    lines = []
+    for k in B.KERNELS:
+        mr, tol = B.selfcheck(B.MirrorOps32(), k)
+        lines.append(f"KCHECK {k} [cpu-mirror] samples={samples[k]} max_rel={_rust_e(mr, 3)} "
+                     f"tol={_rust_e(tol, 0)} {'PASS' if mr < tol else 'FAIL'}")
+    ref = open(os.path.join(os.path.dirname(__file__), "golden", "bwparity_kcheck_ref.txt")).read().splitlines()
+    assert lines == ref
