@@ -77,3 +77,31 @@ def test_mirror32_reproduces_the_reference_kcheck_log():
                      f"tol={_rust_e(tol, 0)} {'PASS' if mr < tol else 'FAIL'}")
     ref = open(os.path.join(os.path.dirname(__file__), "golden", "bwparity_kcheck_ref.txt")).read().splitlines()
     assert lines == ref
+
+
+def test_per_op_entry_points_refuse_bad_arguments_before_any_device_call():
+    """The per-op backward C-ABI (gpt2q_bwd_*) checks its arguments on the host and returns
+    EARG with a message before it opens a device, so these calls need no GPU."""
+    import ctypes as C
+
+    from smelt_b200 import _ffi, build
+
+    build.build()
+    lib = _ffi.load()
+    f = np.zeros(64, np.float32)
+    p = f.ctypes.data_as(C.POINTER(C.c_float))
+    null = C.POINTER(C.c_float)()
+    cases = [
+        (lib.gpt2q_bwd_lin_input_grad, (0, p, p, 4, 6, p), "cols % 4"),      # cols not a multiple of 4
+        (lib.gpt2q_bwd_lin_input_grad, (0, p, null, 4, 8, p), "null"),
+        (lib.gpt2q_bwd_lin_input_grad, (0, p, p, 0, 8, p), "rows/cols"),
+        (lib.gpt2q_bwd_ln_backward, (0, p, p, p, p, 1e-5, 0, p, p, p), "null"),
+        (lib.gpt2q_bwd_gelu, (0, p, p, -1, p), "null"),
+        (lib.gpt2q_bwd_attn_train, (0, p, p, p, p, 4, 64, 96, p, p, p), "stride"),   # stride % hd != 0
+        (lib.gpt2q_bwd_attn_train, (0, p, p, p, p, 1025, 64, 64, p, p, p), "t <= 1024"),
+        (lib.gpt2q_bwd_attn_train, (0, p, p, p, p, 4, 256, 256, p, p, p), "hd <= 128"),
+    ]
+    for fn, args, words in cases:
+        assert fn(*args) == -1, (fn.__name__, args)
+        assert words in lib.gpt2q_last_error(None).decode(), (fn.__name__, words)
+    assert lib.gpt2q_trunk_input_grad(None, None, 1, None, None, None) == -1
