@@ -76,8 +76,10 @@ int gpt2q_create(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int 
 /* Tensor-parallel handle (no counterpart in the reference, which is single-GPU,
  * gpu.rs:76): rank `tp_rank` of `tp_size` keeps its column slice of c_attn
  * (whole heads) and c_fc and its row slice of attn/mlp c_proj; the two c_proj
- * outputs per layer are summed with an NCCL all-reduce. nccl_id points to the
- * 128-byte ncclUniqueId made by rank 0 and shared by the caller. */
+ * partial sums per layer are added by the library's own kernel from peer memory
+ * when the GPUs can map each other's memory (gpt2q_info "tp_peer_mapped"), else
+ * by an NCCL all-reduce. nccl_id points to the 128-byte ncclUniqueId made by
+ * rank 0 and shared by the caller. */
 int gpt2q_create_tp(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int n_tensors,
                     int device, int tp_size, int tp_rank, const void* nccl_id,
                     gpt2q_handle** out);

@@ -57,3 +57,18 @@ int main(void) {{
     out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert out.returncode == 0, (out.returncode, out.stderr)
     assert out.stdout.strip() == smt.blake3(b"abc").hex()
+
+
+def test_rust_stub_declares_every_function_with_the_header_arity():
+    """The gpt2q-sys extern block in INTEGRATION.md binds every function of the header, each with
+    the header's number of parameters."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    c_arity = {}
+    for name, params in re.findall(r"\b(gpt2q_\w+)\s*\(([^)]*)\)\s*;", text):
+        c_arity[name] = 0 if params.strip() in ("", "void") else params.count(",") + 1
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    block = doc[doc.index('extern "C" {'):]
+    block = block[:block.index("\n}\n")]
+    rust_arity = {name: (0 if not params.strip() else params.count(",") + 1)
+                  for name, params in re.findall(r"pub fn (gpt2q_\w+)\(([^)]*)\)", block)}
+    assert rust_arity == c_arity
