@@ -25,3 +25,14 @@ def test_reference_arm_json_line(config, unit):
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["unit"] == unit and cb["cores"] >= 1 and cb["kind"] == "port"
     assert d["e2e"] == {"value": d["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+@pytest.mark.parametrize("config", ["small-int8-b32", "small-int8-trunk-bwd"])
+def test_reference_arm_runs_on_rank_0_only(config):
+    """Under torchrun every rank but 0 exits 0 without work and prints no JSON line."""
+    env = dict(os.environ, RANK="1", LOCAL_RANK="1", WORLD_SIZE="2")
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", config, "--gpus", "2",
+                          "--steps", "1", "--warmup", "1"], cwd=ROOT, capture_output=True, text=True, timeout=300,
+                         env=env)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert not [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
