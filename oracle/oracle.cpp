@@ -12,6 +12,10 @@
 #include <thread>
 #include <vector>
 
+#if defined(__AVX2__) && defined(__FMA__)
+#include <immintrin.h>
+#endif
+
 static const char* ATOM_F16 = "core.f16";              // atoms.rs:5
 static const char* ATOM_Q8 = "core.i8.b32.f16scale";   // atoms.rs:6
 static const char* ATOM_Q4 = "core.i4.b32.f16scale";   // int4 atom (18 B / 32 values)
@@ -717,6 +721,282 @@ extern "C" int orc_engine_step(const orc_engine* e, uint32_t tok, int pos, float
         }
     }
     matmul(e, "wte.weight", x.data(), logits);
+    return 0;
+}
+
+// ---------------------------------------------------------------- batched prefill
+// T consecutive Engine::step calls (gpt2.rs:227-332, driven by the prompt loop gpt2.rs:373-381)
+// computed layer by layer over all T positions, so that long prompts check in seconds. Every
+// value goes through the same operations in the same order as in orc_engine_step; only the loop
+// nest differs (positions are SIMD lanes), so the results are bit-identical (tested against the
+// per-token step on every atom).
+namespace {
+
+// Weight row r as the fp32 values the GEMV multiplies: (float)q * f16(s) for the group atoms
+// (exact in fp32: 8 x 11 significant bits), the decoded half, or the float itself.
+void deq_row(const Tensor& t, size_t r, size_t cols, float* out) {
+    const uint8_t* p = t.data.data();
+    if (t.atom == ATOM_Q8) {
+        const uint8_t* row = p + r * (cols / 32) * 34;
+        for (size_t b = 0; b < cols / 32; ++b) {
+            float s = blk_scale(row + b * 34);
+            for (int i = 0; i < 32; ++i) out[b * 32 + i] = (float)(int8_t)row[b * 34 + 2 + i] * s;
+        }
+    } else if (t.atom == ATOM_Q4) {
+        const uint8_t* row = p + r * (cols / 32) * 18;
+        for (size_t b = 0; b < cols / 32; ++b) {
+            float s = blk_scale(row + b * 18);
+            for (int i = 0; i < 32; ++i) out[b * 32 + i] = q4_elem(row + b * 18 + 2, i) * s;
+        }
+    } else if (t.atom == ATOM_F16) {
+        const uint8_t* row = p + r * cols * 2;
+        for (size_t j = 0; j < cols; ++j) out[j] = orc_f16_to_f32((uint16_t)(row[2 * j] | (row[2 * j + 1] << 8)));
+    } else {
+        std::memcpy(out, reinterpret_cast<const float*>(p) + r * cols, cols * 4);
+    }
+}
+
+// Accumulation order of the GEMVs (atoms.rs:89-164): element j goes to accumulator j % 4 for
+// j < main_end, in increasing j; the rest goes to accumulator 0, by FMA in the group kernels
+// (gemv_q8's single-block tail) and by an unfused multiply-add in the element kernels
+// (gemv_f16's `acc += w * x` tail). The result is ((acc0 + acc1) + acc2) + acc3, added to 0.
+struct GemvOrder {
+    size_t main_end;
+    bool tail_fused;
+};
+GemvOrder order_of(const Tensor& t, size_t cols) {
+    if (t.atom == ATOM_Q8 || t.atom == ATOM_Q4) return {cols / 128 * 128, true};
+    return {cols / 4 * 4, false};
+}
+
+template <class F>
+void parallel_for(int threads, size_t n, F&& f) {
+    size_t nt = std::min<size_t>((size_t)std::max(threads, 1), std::max<size_t>(n, 1));
+    if (nt <= 1) {
+        f(0, 0, n);
+        return;
+    }
+    std::vector<std::thread> hs;
+    size_t per = (n + nt - 1) / nt;
+    for (size_t i = 0; i < nt; ++i) {
+        size_t lo = i * per, hi = std::min(n, lo + per);
+        if (lo < hi) hs.emplace_back(f, i, lo, hi);
+    }
+    for (auto& h : hs) h.join();
+}
+
+constexpr int TB = 8;  // positions per SIMD vector
+
+// Y[t][r] = matmul(W, X[t])[r] for t in [0, T): bit-identical to T calls of matmul(). X is
+// staged block-major (Xb[block][j][lane], 8 positions per block) so that a row's pass over one
+// block streams contiguous memory; two weight rows share every activation load.
+void matmul_batched(const orc_engine* e, const std::string& wname, const float* X, int T, float* Y) {
+    const Tensor& w = e->get(wname);
+    const size_t rows = (size_t)w.shape[0], cols = (size_t)w.shape[1];
+    const size_t nb = (size_t)(T + TB - 1) / TB;
+    std::vector<float> Xb(nb * cols * TB, 0.f);
+    for (int t = 0; t < T; ++t)
+        for (size_t j = 0; j < cols; ++j) Xb[((size_t)t / TB * cols + j) * TB + (size_t)t % TB] = X[(size_t)t * cols + j];
+    const GemvOrder ord = order_of(w, cols);
+    auto store = [&](size_t b, size_t r, const float* lanes) {
+        for (size_t p = 0; p < (size_t)TB && b * TB + p < (size_t)T; ++p) Y[(b * TB + p) * rows + r] = 0.f + lanes[p];
+    };
+    const size_t pairs = (rows + 1) / 2;
+    parallel_for(e->threads, pairs, [&](size_t, size_t lo, size_t hi) {
+        std::vector<float> w0(cols), w1(cols);
+        alignas(32) float out0[TB], out1[TB];
+        for (size_t pr = lo; pr < hi; ++pr) {
+            const size_t r0 = 2 * pr, r1 = r0 + 1;
+            const bool two = r1 < rows;
+            deq_row(w, r0, cols, w0.data());
+            if (two) deq_row(w, r1, cols, w1.data());
+            else std::fill(w1.begin(), w1.end(), 0.f);
+            for (size_t b = 0; b < nb; ++b) {
+                const float* xb = Xb.data() + b * cols * TB;
+#if defined(__AVX2__) && defined(__FMA__)
+                __m256 a0 = _mm256_setzero_ps(), a1 = a0, a2 = a0, a3 = a0;
+                __m256 c0 = a0, c1 = a0, c2 = a0, c3 = a0;
+                size_t j = 0;
+                for (; j < ord.main_end; j += 4) {
+                    const __m256 x0 = _mm256_loadu_ps(xb + j * TB), x1 = _mm256_loadu_ps(xb + (j + 1) * TB);
+                    const __m256 x2 = _mm256_loadu_ps(xb + (j + 2) * TB), x3 = _mm256_loadu_ps(xb + (j + 3) * TB);
+                    a0 = _mm256_fmadd_ps(_mm256_set1_ps(w0[j]), x0, a0);
+                    a1 = _mm256_fmadd_ps(_mm256_set1_ps(w0[j + 1]), x1, a1);
+                    a2 = _mm256_fmadd_ps(_mm256_set1_ps(w0[j + 2]), x2, a2);
+                    a3 = _mm256_fmadd_ps(_mm256_set1_ps(w0[j + 3]), x3, a3);
+                    c0 = _mm256_fmadd_ps(_mm256_set1_ps(w1[j]), x0, c0);
+                    c1 = _mm256_fmadd_ps(_mm256_set1_ps(w1[j + 1]), x1, c1);
+                    c2 = _mm256_fmadd_ps(_mm256_set1_ps(w1[j + 2]), x2, c2);
+                    c3 = _mm256_fmadd_ps(_mm256_set1_ps(w1[j + 3]), x3, c3);
+                }
+                for (; j < cols; ++j) {
+                    const __m256 xv = _mm256_loadu_ps(xb + j * TB);
+                    const __m256 v0 = _mm256_set1_ps(w0[j]), v1 = _mm256_set1_ps(w1[j]);
+                    if (ord.tail_fused) {
+                        a0 = _mm256_fmadd_ps(v0, xv, a0);
+                        c0 = _mm256_fmadd_ps(v1, xv, c0);
+                    } else {
+                        a0 = _mm256_add_ps(a0, _mm256_mul_ps(v0, xv));
+                        c0 = _mm256_add_ps(c0, _mm256_mul_ps(v1, xv));
+                    }
+                }
+                _mm256_store_ps(out0, _mm256_add_ps(_mm256_add_ps(_mm256_add_ps(a0, a1), a2), a3));
+                _mm256_store_ps(out1, _mm256_add_ps(_mm256_add_ps(_mm256_add_ps(c0, c1), c2), c3));
+#else
+                for (int k = 0; k < 2; ++k) {
+                    const float* wr = k ? w1.data() : w0.data();
+                    float acc[4][TB] = {};
+                    size_t j = 0;
+                    for (; j < ord.main_end; ++j)
+                        for (int p = 0; p < TB; ++p) acc[j & 3][p] = std::fma(wr[j], xb[j * TB + p], acc[j & 3][p]);
+                    for (; j < cols; ++j)
+                        for (int p = 0; p < TB; ++p)
+                            acc[0][p] = ord.tail_fused ? std::fma(wr[j], xb[j * TB + p], acc[0][p])
+                                                       : acc[0][p] + wr[j] * xb[j * TB + p];
+                    float* o = k ? out1 : out0;
+                    for (int p = 0; p < TB; ++p) o[p] = acc[0][p] + acc[1][p] + acc[2][p] + acc[3][p];
+                }
+#endif
+                store(b, r0, out0);
+                if (two) store(b, r1, out1);
+            }
+        }
+    });
+}
+
+}  // namespace
+
+// T positions pos0..pos0+T-1 of one sequence (kv rows 0..pos0-1 already written by earlier
+// steps); writes their K/V rows and the logits of the last position.
+extern "C" int orc_engine_prefill(const orc_engine* e, const uint32_t* ids, int T, int pos0, float* kv,
+                                  float* logits_last) {
+    const size_t d = (size_t)e->n_embd;
+    const size_t hd = d / (size_t)e->n_head;
+    const size_t ctxd = (size_t)e->n_ctx * d;
+    if (T <= 0 || pos0 < 0 || pos0 + T > e->n_ctx) return -1;
+    for (int t = 0; t < T; ++t)
+        if ((int)ids[t] >= e->vocab) return -1;
+    std::vector<float> X((size_t)T * d);
+    for (int t = 0; t < T; ++t) {
+        std::vector<float> x = vec_row(e, "wte.weight", ids[t]);
+        std::vector<float> wpe = vec_row(e, "wpe.weight", (uint32_t)(pos0 + t));
+        for (size_t i = 0; i < d; ++i) X[t * d + i] = x[i] + wpe[i];
+    }
+    std::vector<float> Hn((size_t)T * d), ATT((size_t)T * d), PR((size_t)T * d);
+    for (int layer = 0; layer < e->n_layer; ++layer) {
+        float* kc = kv + (size_t)layer * 2 * ctxd;
+        float* vc = kc + ctxd;
+        std::vector<float> gw = vec_f32(e, L(layer, "ln_1.weight"));
+        std::vector<float> gb = vec_f32(e, L(layer, "ln_1.bias"));
+        Hn = X;
+        for (int t = 0; t < T; ++t) layernorm(Hn.data() + t * d, d, gw.data(), gb.data(), e->ln_eps);
+        std::string qkv_name = L(layer, "attn.c_attn.weight");
+        const size_t inter3 = (size_t)e->get(qkv_name).shape[0];
+        std::vector<float> QKV((size_t)T * inter3);
+        matmul_batched(e, qkv_name, Hn.data(), T, QKV.data());
+        std::vector<float> qb = vec_f32(e, L(layer, "attn.c_attn.bias"));
+        for (int t = 0; t < T; ++t) {
+            float* qkv = QKV.data() + t * inter3;
+            for (size_t i = 0; i < inter3; ++i) qkv[i] += qb[i];
+            size_t row = (size_t)(pos0 + t) * d;
+            std::memcpy(kc + row, qkv + d, d * 4);
+            std::memcpy(vc + row, qkv + 2 * d, d * 4);
+        }
+        // attention of every (position, head), the loops of orc_engine_step; the scores of 8 keys
+        // are one vector (each lane sums q[tt] * k[tt] over tt in order, unfused, as the step does)
+        const float scale = 1.0f / std::sqrt((float)hd);
+        std::fill(ATT.begin(), ATT.end(), 0.f);
+        const size_t npos = (size_t)pos0 + (size_t)T, npos8 = (npos + 7) / 8 * 8;
+        std::vector<float> Kt((size_t)e->n_head * hd * npos8, 0.f);  // Kt[head][tt][p]
+        for (size_t p = 0; p < npos; ++p)
+            for (size_t i = 0; i < d; ++i) Kt[((i / hd) * hd + i % hd) * npos8 + p] = kc[p * d + i];
+        const size_t pairs = (size_t)T * (size_t)e->n_head;
+        const int nth = std::max(1, e->threads);
+        parallel_for(nth, (size_t)nth, [&](size_t th, size_t, size_t) {
+            std::vector<float> scores(npos8);
+            for (size_t k = th; k < pairs; k += (size_t)nth) {  // interleaved: cost grows with the position
+                const int t = (int)(k / (size_t)e->n_head), head = (int)(k % (size_t)e->n_head);
+                const int pos = pos0 + t;
+                const size_t o = (size_t)head * hd;
+                const float* q = QKV.data() + t * inter3 + o;
+                const float* kt = Kt.data() + (size_t)head * hd * npos8;
+                float* attn_out = ATT.data() + t * d;
+                float maxs = -3.40282347e+38f;  // f32::MIN
+                for (int p0 = 0; p0 <= pos; p0 += 8) {
+#if defined(__AVX2__) && defined(__FMA__)
+                    __m256 dot = _mm256_setzero_ps();
+                    for (size_t tt = 0; tt < hd; ++tt)
+                        dot = _mm256_add_ps(dot, _mm256_mul_ps(_mm256_set1_ps(q[tt]), _mm256_loadu_ps(kt + tt * npos8 + p0)));
+                    _mm256_storeu_ps(scores.data() + p0, _mm256_mul_ps(dot, _mm256_set1_ps(scale)));
+#else
+                    for (int p = p0; p < p0 + 8; ++p) {
+                        float dot = 0.f;
+                        for (size_t tt = 0; tt < hd; ++tt) dot += q[tt] * kt[tt * npos8 + p];
+                        scores[p] = dot * scale;
+                    }
+#endif
+                }
+                for (int p = 0; p <= pos; ++p) maxs = rust_max(maxs, scores[p]);
+                float sum = 0.f;
+                for (int p = 0; p <= pos; ++p) {
+                    scores[p] = std::exp(scores[p] - maxs);
+                    sum += scores[p];
+                }
+                for (int p = 0; p <= pos; ++p) scores[p] /= sum;
+                for (int p = 0; p <= pos; ++p) {
+                    const float* vp = vc + (size_t)p * d + o;
+                    for (size_t tt = 0; tt < hd; ++tt) attn_out[o + tt] += scores[p] * vp[tt];
+                }
+            }
+        });
+        matmul_batched(e, L(layer, "attn.c_proj.weight"), ATT.data(), T, PR.data());
+        std::vector<float> pb = vec_f32(e, L(layer, "attn.c_proj.bias"));
+        for (int t = 0; t < T; ++t)
+            for (size_t i = 0; i < d; ++i) X[t * d + i] += PR[t * d + i] + pb[i];
+
+        std::vector<float> gw2 = vec_f32(e, L(layer, "ln_2.weight"));
+        std::vector<float> gb2 = vec_f32(e, L(layer, "ln_2.bias"));
+        Hn = X;
+        for (int t = 0; t < T; ++t) layernorm(Hn.data() + t * d, d, gw2.data(), gb2.data(), e->ln_eps);
+        std::string fc_name = L(layer, "mlp.c_fc.weight");
+        const size_t inter = (size_t)e->get(fc_name).shape[0];
+        std::vector<float> FC((size_t)T * inter);
+        matmul_batched(e, fc_name, Hn.data(), T, FC.data());
+        std::vector<float> fb = vec_f32(e, L(layer, "mlp.c_fc.bias"));
+        for (int t = 0; t < T; ++t) {
+            float* fc = FC.data() + t * inter;
+            for (size_t i = 0; i < inter; ++i) {
+                float v = fc[i] + fb[i];
+                fc[i] = 0.5f * v * (1.0f + std::tanh(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+            }
+        }
+        matmul_batched(e, L(layer, "mlp.c_proj.weight"), FC.data(), T, PR.data());
+        std::vector<float> mb = vec_f32(e, L(layer, "mlp.c_proj.bias"));
+        for (int t = 0; t < T; ++t)
+            for (size_t i = 0; i < d; ++i) X[t * d + i] += PR[t * d + i] + mb[i];
+    }
+    // the tail of the last position's step (earlier positions' logits are not needed)
+    std::vector<float> x(X.end() - (long)d, X.end());
+    std::vector<float> wf = vec_f32(e, "ln_f.weight");
+    std::vector<float> bf = vec_f32(e, "ln_f.bias");
+    layernorm(x.data(), d, wf.data(), bf.data(), e->ln_eps);
+    if (e->ad_r > 0) {
+        const int r = e->ad_r;
+        std::vector<float> ah(r);
+        for (int j = 0; j < r; ++j) {
+            float acc = 0.f;
+            const float* ar = e->ad_a.data() + (size_t)j * d;
+            for (size_t i = 0; i < d; ++i) acc = std::fma(ar[i], x[i], acc);
+            ah[j] = acc;
+        }
+        for (size_t i = 0; i < d; ++i) {
+            float acc = 0.f;
+            const float* br = e->ad_b.data() + i * r;
+            for (int j = 0; j < r; ++j) acc = std::fma(br[j], ah[j], acc);
+            x[i] += acc;
+        }
+    }
+    matmul(e, "wte.weight", x.data(), logits_last);
     return 0;
 }
 

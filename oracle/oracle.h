@@ -81,6 +81,11 @@ void orc_engine_free(orc_engine* e);
 /* kv layout: [n_layer][2][n_ctx * n_embd] f32, caller-owned, zero-initialised. */
 size_t orc_kv_floats(const orc_engine* e);
 int orc_engine_step(const orc_engine* e, uint32_t tok, int pos, float* kv, float* logits);
+/* T consecutive steps of one sequence at positions pos0..pos0+T-1 (kv rows 0..pos0-1 written by
+ * earlier steps), computed over all positions at once with bit-identical results; writes the K/V
+ * rows and the vocab logits of the last position. */
+int orc_engine_prefill(const orc_engine* e, const uint32_t* ids, int T, int pos0, float* kv,
+                       float* logits_last);
 int orc_vec_f32(const orc_engine* e, const char* name, float* out, uint64_t n);
 int orc_vec_row(const orc_engine* e, const char* name, uint32_t row, float* out, uint64_t n);
 /* Returns number of generated tokens written to out (<= steps). */

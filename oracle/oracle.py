@@ -72,6 +72,8 @@ def _sig(lib):
     lib.orc_kv_floats.restype = C.c_size_t
     lib.orc_engine_step.argtypes = [C.c_void_p, C.c_uint32, C.c_int, _f32p, _f32p]
     lib.orc_engine_step.restype = C.c_int
+    lib.orc_engine_prefill.argtypes = [C.c_void_p, _u32p, C.c_int, C.c_int, _f32p, _f32p]
+    lib.orc_engine_prefill.restype = C.c_int
     lib.orc_vec_f32.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_uint64]
     lib.orc_vec_f32.restype = C.c_int
     lib.orc_vec_row.argtypes = [C.c_void_p, C.c_char_p, C.c_uint32, _f32p, C.c_uint64]
@@ -207,6 +209,17 @@ class Engine:
         rc = self._l.orc_engine_step(self.h, int(tok), int(pos), _p(kv, _f32p), _p(logits, _f32p))
         if rc != 0:
             raise ValueError(f"orc_engine_step rc={rc}")
+        return logits
+
+    def prefill(self, ids, kv: np.ndarray, pos0: int = 0) -> np.ndarray:
+        """len(ids) consecutive `step` calls at positions pos0.. (the prompt loop, gpt2.rs:373-381),
+        computed over all positions at once with bit-identical results: fills kv and returns the
+        logits of the last position."""
+        p = np.ascontiguousarray(ids, dtype=np.uint32)
+        logits = np.empty(self.meta["vocab"], dtype=np.float32)
+        rc = self._l.orc_engine_prefill(self.h, _p(p, _u32p), p.size, int(pos0), _p(kv, _f32p), _p(logits, _f32p))
+        if rc != 0:
+            raise ValueError(f"orc_engine_prefill rc={rc}")
         return logits
 
     def vec_f32(self, name: str) -> np.ndarray:

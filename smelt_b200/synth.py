@@ -17,7 +17,7 @@ import ctypes as C
 import numpy as np
 
 from . import _ffi
-from .pack import Meta, Pack, from_hf, hf_shapes
+from .pack import POLICIES, Meta, Pack, convert_tensor, hf_shapes
 
 
 class Rng:
@@ -40,11 +40,10 @@ def is_ln(name: str) -> bool:
     return ".ln_" in name or name.startswith("ln_")
 
 
-def hf_weights(meta: Meta, seed: int = 0, std: float = 0.02, bias_std: float = 0.0,
-               inter: int | None = None) -> dict:
-    """HF-layout fp32 tensors for `meta`, drawn in sorted-name order from Rng(seed)."""
+def iter_hf_weights(meta: Meta, seed: int = 0, std: float = 0.02, bias_std: float = 0.0,
+                    inter: int | None = None):
+    """(name, HF-layout fp32 tensor) for `meta`, drawn in sorted-name order from Rng(seed)."""
     rng = Rng(seed)
-    out = {}
     for name, shape in hf_shapes(meta, inter).items():
         n = int(np.prod(shape))
         if is_ln(name):
@@ -53,12 +52,24 @@ def hf_weights(meta: Meta, seed: int = 0, std: float = 0.02, bias_std: float = 0
             v = rng.normal_f32(n, bias_std) if bias_std > 0 else np.zeros(n, np.float32)
         else:
             v = rng.normal_f32(n, std)
-        out[name] = v.reshape(shape)
-    return out
+        yield name, v.reshape(shape)
+
+
+def hf_weights(meta: Meta, seed: int = 0, std: float = 0.02, bias_std: float = 0.0,
+               inter: int | None = None) -> dict:
+    """HF-layout fp32 tensors for `meta`, drawn in sorted-name order from Rng(seed)."""
+    return dict(iter_hf_weights(meta, seed, std, bias_std, inter))
 
 
 def synthetic_pack(meta: Meta, policy: str = "auto", seed: int = 0, bias_std: float = 0.0) -> Pack:
-    return from_hf(meta, hf_weights(meta, seed=seed, bias_std=bias_std), policy)
+    """The seeded model converted tensor by tensor (the fp32 copy of a large model is never
+    held whole); equal to from_hf(meta, hf_weights(...), policy)."""
+    if policy not in POLICIES:
+        raise ValueError(f"unknown policy {policy}; one of {POLICIES}")
+    pack = Pack(meta)
+    for name, v in iter_hf_weights(meta, seed=seed, bias_std=bias_std):
+        pack.tensors[name] = convert_tensor(name, v, policy)
+    return pack
 
 
 def prompt_ids(n: int, vocab: int, seed: int = 1) -> np.ndarray:
