@@ -59,16 +59,22 @@ int main(void) {{
     assert out.stdout.strip() == smt.blake3(b"abc").hex()
 
 
-def test_rust_stub_declares_every_function_with_the_header_arity():
-    """The gpt2q-sys extern block in INTEGRATION.md binds every function of the header, each with
-    the header's number of parameters."""
+def test_rust_sys_crate_declares_every_function_with_the_header_arity():
+    """rust/gpt2q-sys/src/lib.rs binds every function of the header, each with the header's number
+    of parameters, and the safe wrapper (rust/gpt2q) calls only functions the sys crate declares."""
     text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
     c_arity = {}
     for name, params in re.findall(r"\b(gpt2q_\w+)\s*\(([^)]*)\)\s*;", text):
         c_arity[name] = 0 if params.strip() in ("", "void") else params.count(",") + 1
-    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    block = doc[doc.index('extern "C" {'):]
+    src = open(os.path.join(ROOT, "rust", "gpt2q-sys", "src", "lib.rs")).read()
+    block = src[src.index('extern "C" {'):]
     block = block[:block.index("\n}\n")]
     rust_arity = {name: (0 if not params.strip() else params.count(",") + 1)
                   for name, params in re.findall(r"pub fn (gpt2q_\w+)\(([^)]*)\)", block)}
     assert rust_arity == c_arity
+    consts = dict(re.findall(r"pub const (GPT2Q_\w+): c_int = (-?\d+);", src))
+    for name, value in re.findall(r"#define (GPT2Q_\w+) (-?\d+)", open(HEADER).read()):
+        assert consts.get(name) == value, name
+    wrapper = open(os.path.join(ROOT, "rust", "gpt2q", "src", "lib.rs")).read()
+    used = set(re.findall(r"sys::(gpt2q_\w+)\(", wrapper))
+    assert used and used <= set(c_arity), used - set(c_arity)
