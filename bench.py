@@ -938,6 +938,15 @@ def measure_tp(args, wl, world: int, rank: int, local: int, dev, parity: bool = 
         timed_ms += ev0.elapsed_time(ev1)
     launches = g.launches - l0
     ms_max = max_over_ranks(timed_ms, world, dev)
+    # each kernel's share of one decode step, from per-launch CUDA events in profiling mode (graphs
+    # off); the tensor-parallel residual kernel's time includes its wait for the peers
+    if done >= dec:
+        g.prefill(prompts)
+    g.profile(True)
+    g.decode_steps(1, batch, want_tokens=False)
+    prof = g.profile_read()
+    g.profile(False)
+    prof_total = sum(v["ms"] for v in prof.values()) or 1.0
     weights = sum(t.data.nbytes for t in pk.tensors.values() if len(t.shape) == 2)
     hbm, peak_kind = peaks()
     per_rank = weights / world / (ms_max / args.steps / 1e3) / 1e9
@@ -947,6 +956,9 @@ def measure_tp(args, wl, world: int, rank: int, local: int, dev, parity: bool = 
         "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "int8xfp32", "data": "synthetic", "config": tp_config(wl, world),
         "gpu_launches": int(launches), "clocks": clk.summary(),
+        "kernels": {k: {"launches": v["launches"], "share_of_step": round(v["ms"] / prof_total, 4)}
+                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])[:8]},
+        "tp_reduce_ln_share": round(prof.get("tp_reduce_ln", {"ms": 0.0})["ms"] / prof_total, 4),
         "roofline": {"bound": "hbm", "kernel": "whole decode step", "achieved": per_rank, "peak": hbm,
                      "unit": "GB/s", "frac": per_rank / hbm, "traffic": None, "peak_source": peak_kind,
                      "note": "weight bytes per rank only (KV excluded)"},

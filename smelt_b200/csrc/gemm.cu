@@ -107,6 +107,7 @@ struct TcParams {
     float pre;   // 2^P
     Epi epi;
     int* err;
+    int* fault;                 // one-shot split-K stall switch (GemmPlan::fault)
     unsigned long long* trace;  // optional [grid][TC_TRACE] globaltimer stamps (one traced launch)
 };
 
@@ -527,6 +528,8 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
         const int mend = min(p.M, m0 + BN);
         // push exchange: rank r reduces token columns [r CW, r CW + CW) of the tile
         const int rank = push ? (int)tc::cluster_rank() : 0;
+        // test switch (GemmPlan::fault): rank 1 withholds its partials once
+        const bool stall = push && rank == 1 && *reinterpret_cast<volatile const int*>(p.fault) != 0;
         const int CW = push_cw(BN, p.splits);
         float* recv = reinterpret_cast<float*>(smem);  // [splits][128][CW]: slot s from split s
         const int own_w = max(0, min(BN, (rank + 1) * CW) - rank * CW);
@@ -570,7 +573,7 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
                     const float4 val = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
                     if (r == rank)
                         *reinterpret_cast<float4*>(dst) = val;
-                    else
+                    else if (!stall)
                         tc::st_async_f32x4((uint32_t)r, dst, val, recv_full);
                 }
             } else {
@@ -580,6 +583,7 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
             }
         }
         if (push) {
+            if (stall && threadIdx.x == 32) atomicExch(p.fault, 0);
             if (threadIdx.x == 32) tc_stamp(p, 13);
             const bool ok = acc_ok && (own_w == 0 || tc::mbar_wait_cluster(recv_full, 0, p.err));
             if (threadIdx.x == 32) tc_stamp(p, 14);
@@ -1051,7 +1055,12 @@ int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax) {
     if (const char* e = std::getenv("GPT2Q_TC_MIN_M")) p.min_m = std::max(1, std::atoi(e));
     p.presplit_min_m = 257;
     if (const char* e = std::getenv("GPT2Q_TC_PRESPLIT_MIN_M")) p.presplit_min_m = std::max(1, std::atoi(e));
-    if (cudaMalloc(&p.err, 4) != cudaSuccess || cudaMemset(p.err, 0, 4) != cudaSuccess) return -1;
+    if (cudaMalloc(&p.err, 8) != cudaSuccess || cudaMemset(p.err, 0, 8) != cudaSuccess) return -1;
+    p.fault = p.err + 1;
+    if (const char* e = std::getenv("GPT2Q_TEST_SPLITK_STALL")) {
+        const int one = 1;
+        if (e[0] == '1' && cudaMemcpy(p.fault, &one, 4, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    }
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     p.state = new GemmState();
     if (const char* e = std::getenv("GPT2Q_TC_TRACE")) {
@@ -1162,6 +1171,7 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
     tp.post = wt.post;
     tp.epi = e;
     tp.err = p.err;
+    tp.fault = p.fault;
     tp.trace = nullptr;
     dim3 grid(n_tiles, m_tiles, splits);
     GemmState& gs = *p.state;

@@ -26,6 +26,10 @@ struct GemmPlan {
     int presplit_min_m = 1 << 30;  // ... and reads the fp16 hi/lo weight copies for M >= this
     int Mmax = 0, Kmax = 0;
     int* err = nullptr;   // device error word (bounded-wait timeouts)
+    // One-shot test switch, next to err: while it is non-zero, the rank-1 CTA of a split-K
+    // cluster skips sending its partials, so the peers' bounded waits run out; the launch
+    // that does so clears it. Armed at creation by GPT2Q_TEST_SPLITK_STALL=1 (tests only).
+    int* fault = nullptr;
     size_t presplit_bytes = 0;
     GemmState* state = nullptr;
     bool usable(const QW& w, int M) const;

@@ -435,13 +435,17 @@ int tp_residual(gpt2q_handle* H, const char* name, const Linear& L, const In& X,
     Epi e = epi_store(tp_partial(H->tp, parity), d, H->tp_rank == 0 ? L.bias : nullptr);
     int rc = linear(H, name, L, X, M, e);
     if (rc) return rc;
+    // timed like every other kernel in profiling mode (the time includes the wait for the peers)
+    cudaEvent_t a = nullptr, ev_b = nullptr;
+    if (H->prof && !H->capturing) {
+        a = pooled_event(H);
+        ev_b = pooled_event(H);
+        cudaEventRecord(a, H->stream);
+    }
     rc = tp_reduce_ln(H->tp, parity, H->x, M, d, g, b, H->cfg.ln_eps, H->h, H->h_hi, H->h_lo, H->stream);
     if (rc) return H->fail(GPT2Q_ENCCL, tp_last_error(H->tp));
-    if (H->capturing)
-        H->capture_kernels++;
-    else
-        H->launches++;
-    return GPT2Q_OK;
+    const double bytes = (double)M * d * 4 * (H->tp_size + 3);  // partials of every rank, x in/out, LN out
+    return launched(H, "tp_reduce_ln", bytes, cudaSuccess, a, ev_b);
 }
 
 Epi epi_qkv(gpt2q_handle* H, int layer, const int* slot, const int* pos, const float* bias) {
