@@ -20,8 +20,8 @@ BUILD = os.path.join(PKG, "_build")
 LIBDIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIBDIR, "libgpt2q.so")
 
-SOURCES = ["kernels.cu", "runtime.cu", "gemm.cu", "attn_tc.cu", "persistent.cu", "tp.cu", "noalloc.cu", "synth.cpp", "blake3.cpp", "smt.cpp", "backward.cu"]
-HEADERS = ["common.cuh", "kernels.h", "gemm.h", "persistent.h", "tp.h", "tcgen05.cuh", "blake3.h", "backward.h"]
+SOURCES = ["kernels.cu", "runtime.cu", "gemm.cu", "gemm_mma.cu", "attn_tc.cu", "persistent.cu", "tp.cu", "noalloc.cu", "synth.cpp", "blake3.cpp", "smt.cpp", "backward.cu"]
+HEADERS = ["common.cuh", "kernels.h", "gemm.h", "gemm_mma.h", "persistent.h", "tp.h", "tcgen05.cuh", "blake3.h", "backward.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1,0 +1,34 @@
+// Batched-decode linear on the warp-level tensor cores (mma.sync, fp16 hi/lo split of the int8 /
+// int4 weights in registers) for 1..MMA_MAX_M tokens. See gemm_mma.cu.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "common.cuh"
+
+namespace gpt2q {
+
+constexpr int MMA_MAX_M = 64;             // tokens per launch (8 fragments of 8)
+constexpr int MMA_MAX_WARPS = 16;         // warps per CTA, each a group range of the CTA's K range
+constexpr int MMA_MAX_SPLITS = 8;         // K splits over the CTAs of a cluster
+constexpr int MMA_MAX_TILES = 1024;       // matrices of more 16-row tiles (the tied head) use the tcgen05 GEMM
+constexpr int MMA_MAX_SMEM = 225 * 1024;  // staged activations + warp and cluster partials per CTA
+
+// Per-process set-up on the current device (call when a handle is created, outside any capture).
+void mma_init();
+bool mma_usable(const QW& w, int M);
+// mma_usable, and a work layout whose staged activations fit in shared memory exists.
+bool mma_fits(const QW& w, int M);
+// Power-of-two exponent P applied to the group scales (s' = s 2^P) so that the fp16 hi/lo
+// split stays in the normal range; max_abs_w bounds |dequantised weight|.
+int mma_prescale_exp(float max_abs_w);
+// X = x_hi + x_lo, fp16 [M][ldx] written by the previous kernel; ldx % 8 == 0. err: device word
+// set when the bounded wait for the staged activations gives up.
+cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, int pexp, int* err,
+                              const Epi& e, cudaStream_t st);
+// Phase stamps of the launch selected by GPT2Q_MMA_TRACE ("" when none), as JSON.
+std::string mma_trace_json();
+
+}  // namespace gpt2q

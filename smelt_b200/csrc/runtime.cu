@@ -26,6 +26,7 @@
 
 #include "gpt2q.h"
 #include "gemm.h"
+#include "gemm_mma.h"
 #include "backward.h"
 #include "kernels.h"
 #include "persistent.h"
@@ -53,6 +54,7 @@ struct Linear {
     std::string name;
     size_t weight_bytes = 0;  // q + scale bytes read by one full pass over W
     float max_abs_w = 0.f;    // upper bound of |dequantised weight| (tensor-core prescale)
+    int mma_p = 0;            // power-of-two scale exponent of the warp-level tensor-core path
 };
 
 struct LayerW {
@@ -170,6 +172,10 @@ struct gpt2q_handle {
     std::map<std::string, ProfAgg> prof_agg;
 
     GemmPlan gemm;  // tensor-core path for large M
+    // warp-level tensor-core path (mma.sync) for mma_min_m <= M <= MMA_MAX_M tokens, and the
+    // scratch of its K split over CTAs; GPT2Q_MMA_DISABLE=1 / GPT2Q_MMA_MIN_M at creation
+    bool mma_on = true;
+    int mma_min_m = 16;
     MkPlan mk;      // persistent single-sequence decode
     TpComm* tp = nullptr;
 
@@ -348,6 +354,7 @@ int upload_linear(gpt2q_handle* H, const gpt2q_tensor_desc* t, int rows, int col
             if (sv > smax && std::isfinite(sv)) smax = sv;
         }
         L->max_abs_w = smax * qmax;
+        L->mma_p = mma_prescale_exp(L->max_abs_w);
     }
     L->rows = out_rows;
     L->cols = out_cols;
@@ -417,7 +424,9 @@ struct In {
 int linear(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int M, const Epi& e) {
     const int extra = (e.kind == EPI_RESID) ? 2 : 1;
     const double bytes = linear_bytes(L, M, extra);
-    if (X.hi && H->gemm.usable(L.w, M)) {
+    if (X.hi && H->mma_on && M >= H->mma_min_m && M <= MMA_MAX_M && X.ld % 8 == 0 && mma_fits(L.w, M)) {
+        RUN(name, bytes, launch_linear_mma(L.w, X.hi, X.lo, X.ld, M, L.mma_p, H->kerr, e, H->stream));
+    } else if (X.hi && H->gemm.usable(L.w, M)) {
         const XSplit xs{X.hi, X.lo, X.ld};
         RUN(name, bytes, launch_linear_tc(H->gemm, L.w, xs, M, e, H->stream));
     } else {
@@ -1080,6 +1089,10 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     H->f_lo = H->dalloc<__half>(M * H->fc_local * 2);
     H->best = H->dalloc<unsigned long long>((size_t)c.max_seqs * 8);
     H->kerr = H->dalloc<int>(4);
+    if (const char* e = std::getenv("GPT2Q_MMA_DISABLE")) H->mma_on = e[0] != '1';
+    if (const char* e = std::getenv("GPT2Q_MMA_MIN_M")) H->mma_min_m = std::max(1, std::atoi(e));
+    if (H->mma_on) mma_init();
+
     H->p_tok = H->dalloc<uint32_t>(M * 4);
     H->p_pos = H->dalloc<int>(M * 4);
     H->p_slot = H->dalloc<int>(M * 4);
@@ -1721,6 +1734,8 @@ int gpt2q_info(gpt2q_handle* H, char* json, size_t cap) {
     }
     const std::string gt = gemm_trace_json(H->gemm);
     if (!gt.empty()) tr += ", \"tc_trace\": " + gt;
+    const std::string mt = mma_trace_json();
+    if (!mt.empty()) tr += ", \"mma_trace\": " + mt;
     const std::string at = attn_tc_trace_json();
     if (!at.empty()) tr += ", \"attn_trace\": " + at;
     const std::string s = head + tr + "}";

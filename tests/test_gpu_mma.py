@@ -1,0 +1,97 @@
+"""Warp-level tensor-core linear (mma.sync, gemm_mma.cu) for batched decode vs the oracle and vs
+the two other linear paths.
+
+Batched decode of 1..64 sequences runs every linear of the step (q/k/v, attn c_proj, c_fc + GELU,
+mlp c_proj, the tied head) through this kernel by default for 16 <= M <= 64 tokens
+(GPT2Q_MMA_MIN_M lowers the bound). GPT2Q_MMA_DISABLE=1 falls back to the tcgen05 GEMM and,
+with GPT2Q_TC_DISABLE=1 as well, to the CUDA-core kernel. All three must give the oracle's tokens
+and logits within the split-precision bound; the mma path must be deterministic.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from smelt_b200 import pack as P
+from smelt_b200.gpu import Gpu
+
+from .helpers import MINI, TINY, make_pack, oracle_engine, oracle_prefix_logits
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 2e-2
+OBSERVED = 1e-3
+WIDE = P.Meta(n_embd=224 * 2, n_layer=2, n_head=7, n_ctx=96, vocab=3001)  # K = 448: 14 groups, 28 row tiles
+# heads of 313 row tiles take the whole-tile layout; K = 6 and 10 groups are not multiples of the
+# 8-group weight ring, so its refill runs on into the next tile mid-ring
+HEAD6 = P.Meta(n_embd=192, n_layer=2, n_head=3, n_ctx=64, vocab=5003)
+HEAD10 = P.Meta(n_embd=320, n_layer=1, n_head=5, n_ctx=64, vocab=5003)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    from smelt_b200 import build
+    build.build()
+
+
+MODES = {
+    "mma": {"GPT2Q_MMA_DISABLE": "0", "GPT2Q_TC_DISABLE": "0"},
+    "tc": {"GPT2Q_MMA_DISABLE": "1", "GPT2Q_TC_DISABLE": "0", "GPT2Q_TC_MIN_M": "16"},
+    "simt": {"GPT2Q_MMA_DISABLE": "1", "GPT2Q_TC_DISABLE": "1"},
+}
+
+
+def _run(pk, prompts, steps, monkeypatch, mode, extra=None):
+    for k, v in {**MODES[mode], **(extra or {})}.items():
+        monkeypatch.setenv(k, v)
+    with Gpu(pk, max_seqs=len(prompts)) as g:
+        nxt, lg0 = g.prefill(prompts, want_logits=True)
+        toks = g.decode_steps(steps, len(prompts))
+        nxt2, lg = g.decode(toks[-1], [p.size + steps for p in prompts], want_logits=True)
+    return nxt, lg0, toks, nxt2, lg
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+@pytest.mark.parametrize("meta", [TINY, MINI, WIDE, HEAD6, HEAD10], ids=["tiny", "mini", "wide", "head6", "head10"])
+@pytest.mark.parametrize("n_seq", [16, 17, 40, 64])
+def test_mma_decode_matches_oracle_and_other_paths(meta, policy, n_seq, monkeypatch):
+    pk = make_pack(meta, policy, 0, 0.02)
+    rng = np.random.default_rng(n_seq)
+    prompts = [rng.integers(0, meta.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, meta.n_ctx // 3, n_seq)]
+    steps = 4
+    res = {m: _run(pk, prompts, steps, monkeypatch, m) for m in MODES}
+    a = res["mma"]
+    for other in ("tc", "simt"):
+        b = res[other]
+        assert np.abs(a[1] - b[1]).max() <= OBSERVED and np.abs(a[4] - b[4]).max() <= OBSERVED, other
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[2], b[2]) and np.array_equal(a[3], b[3]), other
+    eng = oracle_engine(pk)
+    for i in (0, n_seq - 1):
+        ref = oracle_prefix_logits(eng, np.concatenate([prompts[i], [a[0][i]], a[2][:, i]]))
+        p = prompts[i].size
+        assert np.abs(a[1][i] - ref[p - 1]).max() <= OBSERVED
+        assert np.abs(a[4][i] - ref[-1]).max() <= OBSERVED
+        assert a[0][i] == O.argmax(ref[p - 1]) and a[3][i] == O.argmax(ref[-1])
+        for s in range(steps):
+            assert a[2][s, i] == O.argmax(ref[p + s])
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+@pytest.mark.parametrize("n_seq", [2, 5, 9])
+def test_mma_for_few_tokens_matches_oracle(policy, n_seq, monkeypatch):
+    """GPT2Q_MMA_MIN_M=1 sends 2..15-token decode steps through the warp-level kernel too."""
+    pk = make_pack(MINI, policy, 0, 0.02)
+    rng = np.random.default_rng(100 + n_seq)
+    prompts = [rng.integers(0, MINI.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 40, n_seq)]
+    a = _run(pk, prompts, 3, monkeypatch, "mma", {"GPT2Q_MMA_MIN_M": "1", "GPT2Q_NO_PERSISTENT": "1"})
+    b = _run(pk, prompts, 3, monkeypatch, "simt")
+    assert np.abs(a[1] - b[1]).max() <= OBSERVED and np.abs(a[4] - b[4]).max() <= OBSERVED
+    assert np.array_equal(a[2], b[2]) and np.array_equal(a[3], b[3])
+
+
+def test_mma_decode_is_deterministic_and_batch_invariant(monkeypatch):
+    pk = make_pack(MINI, "auto", 0, 0.02)
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, MINI.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 50, 32)]
+    a = _run(pk, prompts, 5, monkeypatch, "mma")
+    b = _run(pk, prompts, 5, monkeypatch, "mma")
+    for x, y in zip(a, b):
+        assert np.array_equal(np.asarray(x).view(np.uint32), np.asarray(y).view(np.uint32))

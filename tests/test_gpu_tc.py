@@ -45,6 +45,7 @@ def test_tc_batched_decode_matches_cuda_core_path(policy, monkeypatch):
     pk = make_pack(MINI, policy, 0, 0.02)
     rng = np.random.default_rng(3)
     prompts = [rng.integers(0, MINI.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 60, 40)]
+    monkeypatch.setenv("GPT2Q_MMA_DISABLE", "1")  # 16..64 tokens would take the warp-level kernel
     res = {}
     for mode in ("simt", "tc"):
         monkeypatch.setenv("GPT2Q_TC_DISABLE", "1" if mode == "simt" else "0")
@@ -110,6 +111,7 @@ def test_tc_split_k_exchange_shapes_match_cuda_core_path(batch, monkeypatch):
     pk = make_pack(MID, "auto", 1, 0.02)
     rng = np.random.default_rng(batch)
     prompts = [rng.integers(0, MID.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 50, batch)]
+    monkeypatch.setenv("GPT2Q_MMA_DISABLE", "1")  # keep the tcgen05 split-K tiles on the decode path
     res = {}
     for mode in ("simt", "tc"):
         monkeypatch.setenv("GPT2Q_TC_DISABLE", "1" if mode == "simt" else "0")

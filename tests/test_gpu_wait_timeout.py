@@ -2,7 +2,7 @@
 
 The reference only panics when the GPU misbehaves (experiments/model-lab/src/gpu.rs:76,92).
 Here every device-side wait is bounded. This test makes a real one run out, with no fault:
-GPT2Q_TEST_SPLITK_STALL=1 at creation arms a one-shot switch in the tensor-core linear. The
+GPT2Q_TEST_SPLITK_STALL=1 at creation arms a one-shot switch in the tcgen05 linear. The
 first split-K launch that reads it has the rank-1 CTA of a cluster withhold its partial sums,
 so its peers' bounded mbarrier waits (2^26 polls, about a second) give up. The kernel still
 completes every cluster-barrier phase and returns, and the host reports GPT2Q_ETIMEOUT. The next
@@ -32,6 +32,8 @@ def test_split_k_wait_timeout_is_reported_and_the_handle_recovers(monkeypatch):
     n, plen, steps = 32, 128, 4  # batched decode: d = 768 / 3072 linears run as split-K clusters
     ids = synth.prompt_ids(n * plen, pk.meta.vocab, seed=1)
     prompts = [ids[i * plen:(i + 1) * plen] for i in range(n)]
+    # the decode linears of 32 tokens on the tcgen05 GEMM (whose split-K exchange has the wait)
+    monkeypatch.setenv("GPT2Q_MMA_DISABLE", "1")
     with Gpu(pk, max_seqs=n) as clean:
         ref_next, ref_logits = clean.prefill(prompts, want_logits=True)
         ref_toks = clean.decode_steps(steps, n)
