@@ -76,3 +76,18 @@ def test_tp2_matches_single_gpu(policy):
         assert np.abs(lg_r - lg).max() <= 1e-3
         assert np.abs(lg2_r - lg2).max() <= 1e-3
         assert np.array_equal(n_r, nxt) and np.array_equal(t_r, toks) and np.array_equal(n2_r, nxt2)
+    # and the oracle's own greedy continuation (Engine::step, gpt2.rs:227-332)
+    from oracle import oracle as O
+
+    from .helpers import oracle_engine, oracle_prefix_logits
+
+    eng = oracle_engine(pk)
+    _, _, n_r, lg_r, t_r, n2_r, lg2_r, _ = res[0]
+    for i, p in enumerate(_prompts()):
+        seq = np.concatenate([p, [n_r[i]], t_r[:, i]])
+        ref = oracle_prefix_logits(eng, seq)
+        assert np.abs(lg_r[i] - ref[p.size - 1]).max() <= 1e-3
+        assert np.abs(lg2_r[i] - ref[-1]).max() <= 1e-3
+        assert n_r[i] == O.argmax(ref[p.size - 1]) and n2_r[i] == O.argmax(ref[-1])
+        for s in range(t_r.shape[0]):
+            assert t_r[s, i] == O.argmax(ref[p.size + s])
