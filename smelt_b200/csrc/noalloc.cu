@@ -13,8 +13,9 @@
 // Limits and caveats:
 //  - at most GPT2Q_NOALLOC_MAX_ROWS rows per call (8 KiB of scratch, held by every GPU
 //    that loads the library until the process exits); larger calls fail with GPT2Q_EARG;
-//  - the first call on a device looks up the array's device address; make that first
-//    call before any stream capture;
+//  - the first call on a device looks up the array's device address (and every later call
+//    made outside a stream capture looks it up again); make that first call before any
+//    stream capture;
 //  - every call shares the one array: calls whose kernels overlap on the GPU (different
 //    streams without ordering between them) race and give wrong tokens. Serialise them.
 #include <cuda_runtime.h>
@@ -38,15 +39,19 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 unsigned long long* g_dev_ptr[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device (looked up once per device).
-int scratch_for_current_device(unsigned long long** out) {
+// Device address of the scratch array on the current device. Looked up again on every call
+// made outside a stream capture (so a module reloaded after a device reset gets its new
+// address); a call during a capture uses the address cached by an earlier call.
+int scratch_for_current_device(cudaStream_t st, unsigned long long** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
         gpt2q::set_global_error("gpt2q_argmax_noalloc: no usable current CUDA device");
         return GPT2Q_ECUDA;
     }
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusNone;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_dev_ptr[dev]) {
+    if (!g_dev_ptr[dev] || cs == cudaStreamCaptureStatusNone) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_best);
         if (e != cudaSuccess || !p) {
@@ -73,10 +78,10 @@ extern "C" int gpt2q_argmax_noalloc(const float* d_logits, int vocab, int ld, in
                                 std::to_string(GPT2Q_NOALLOC_MAX_ROWS));
         return GPT2Q_EARG;
     }
-    unsigned long long* best = nullptr;
-    int rc = scratch_for_current_device(&best);
-    if (rc != GPT2Q_OK) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned long long* best = nullptr;
+    int rc = scratch_for_current_device(st, &best);
+    if (rc != GPT2Q_OK) return rc;
     // the previous call may have stopped before its finaliser cleared the slots
     cudaError_t e = cudaMemsetAsync(best, 0, (size_t)n_rows * sizeof(unsigned long long), st);
     if (e == cudaSuccess)

@@ -1,10 +1,10 @@
 """Warp-level tensor-core linear (mma.sync, gemm_mma.cu) for batched decode vs the oracle and vs
 the two other linear paths.
 
-Batched decode of 1..64 sequences runs every linear of the step (q/k/v, attn c_proj, c_fc + GELU,
-mlp c_proj, the tied head) through this kernel by default for 16 <= M <= 64 tokens
-(GPT2Q_MMA_MIN_M lowers the bound). GPT2Q_MMA_DISABLE=1 falls back to the tcgen05 GEMM and,
-with GPT2Q_TC_DISABLE=1 as well, to the CUDA-core kernel. All three must give the oracle's tokens
+Batched decode of 1..64 sequences runs the layer linears (q/k/v, attn c_proj, c_fc + GELU,
+mlp c_proj) through this kernel by default (GPT2Q_MMA_MIN_M raises the lower bound; one
+sequence alone takes the persistent kernel). GPT2Q_MMA_DISABLE=1 falls back to the tcgen05 GEMM
+(16 tokens and up) and, with GPT2Q_TC_DISABLE=1 as well, to the CUDA-core kernel. All three must give the oracle's tokens
 and logits within the split-precision bound; the mma path must be deterministic.
 """
 import numpy as np
@@ -77,7 +77,7 @@ def test_mma_decode_matches_oracle_and_other_paths(meta, policy, n_seq, monkeypa
 @pytest.mark.parametrize("policy", ["auto", "q4auto"])
 @pytest.mark.parametrize("n_seq", [2, 5, 9])
 def test_mma_for_few_tokens_matches_oracle(policy, n_seq, monkeypatch):
-    """GPT2Q_MMA_MIN_M=1 sends 2..15-token decode steps through the warp-level kernel too."""
+    """2..15-token decode steps through the warp-level kernel against the CUDA-core kernel."""
     pk = make_pack(MINI, policy, 0, 0.02)
     rng = np.random.default_rng(100 + n_seq)
     prompts = [rng.integers(0, MINI.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 40, n_seq)]

@@ -80,6 +80,29 @@ def test_argmax_noalloc_ties_row_stride_and_limit():
     assert b"exceeds the maximum" in lib.gpt2q_last_error(None)
 
 
+@pytest.mark.parametrize("n_rows,vocab", [(None, 33), (3, 3 * 4096 + 17)])
+def test_argmax_noalloc_full_array_and_wide_vocabulary(n_rows, vocab):
+    """Exactly GPT2Q_NOALLOC_MAX_ROWS rows (the whole scratch array), and a vocabulary that
+    spans several argmax blocks per row; each checked twice in a row against the oracle."""
+    import torch
+
+    lib = _ffi.load()
+    stream = torch.cuda.Stream()
+    n = n_rows or _ffi_max()
+    rng = np.random.default_rng(n + vocab)
+    for rep in range(2):
+        lg = rng.standard_normal((n, vocab)).astype(np.float32)
+        lg[::7, vocab // 2] = 50.0 + rep  # a clear maximum in the middle of some rows
+        d_logits = torch.from_numpy(lg).cuda()
+        d_next = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        assert _call(lib, d_logits, vocab, vocab, n, d_next, stream) == 0
+        stream.synchronize()
+        got = d_next.cpu().numpy().view(np.uint32)
+        ref = np.array([O.argmax(lg[i]) for i in range(n)], np.uint32)
+        assert np.array_equal(got, ref)
+
+
 def _ffi_max() -> int:
     import os
 
