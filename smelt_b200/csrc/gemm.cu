@@ -72,7 +72,6 @@ struct Cfg {
     // half by both; A_hi and A_lo each accumulate into their own TMEM block of 2 BN columns.
     static constexpr bool DUAL = BN <= 64;
     static constexpr int TMEM_COLS = DUAL ? 4 * BN : BN;
-    static constexpr int PS = BN + 4;  // split-K partial tile [128 rows][PS] fp32 (padded rows)
     // Decode tiles exchange split-K partials by pushing them (16-byte remote stores into the
     // peers' shared memory); rank r receives the block of CW token columns it reduces into an
     // area of [splits][128][CW] fp32 (splits * CW <= BN + 32) over the free operand rings.
@@ -95,8 +94,6 @@ struct Cfg {
     static_assert(SMEM <= 232448, "shared memory per CTA");
     // shallow decode tiles that fit twice in an SM's shared memory share it
     static constexpr int MIN_BLOCKS = (!DEEP && BN <= 64 && SMEM <= 232448 / 2 - 1024) ? 2 : 1;
-    // the split-K partial tile reuses the operand rings once every MMA is done
-    static_assert(PS * BM * 4 <= OFF_RAW, "partial tile must fit in the operand rings");
     static_assert(!PUSH || XCH_FLOATS * 4 <= OFF_RAW, "exchange area must fit in the operand rings");
 };
 
@@ -108,6 +105,7 @@ struct TcParams {
     Epi epi;
     int* err;
     int* fault;                 // one-shot split-K stall switch (GemmPlan::fault)
+    float4* part;               // split-K partials of the wide tiles (GemmPlan::part)
     unsigned long long* trace;  // optional [grid][TC_TRACE] globaltimer stamps (one traced launch)
 };
 
@@ -505,7 +503,7 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
             }
         }
         if (threadIdx.x == 32) tc_stamp(p, 5);
-        // ---- epilogue part 1: TMEM -> (outputs | shared-memory partial) ----
+        // ---- epilogue part 1: TMEM -> (outputs | pushed partial | L2 partial) ----
         // the bias is a weight: its load flies while the MMAs finish
         const int n_epi = n0 + (warp & 3) * 32 + lane;
         const float bias_v = (p.epi.bias && n_epi < p.w.rows) ? __ldg(p.epi.bias + n_epi) : 0.f;
@@ -524,7 +522,7 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
         const int row = quarter * 32 + lane;  // TMEM lane owned by this thread
         const int nn = n0 + row;
         const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
-        float* part = reinterpret_cast<float*>(smem);  // [128][PS], operand rings are free now
+        float4* gpart = p.part + ((size_t)(blockIdx.x + gridDim.x * blockIdx.y) * p.splits + split) * (BN / 4) * 128;
         const int mend = min(p.M, m0 + BN);
         // push exchange: rank r reduces token columns [r CW, r CW + CW) of the tile
         const int rank = push ? (int)tc::cluster_rank() : 0;
@@ -576,10 +574,13 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
                     else if (!stall)
                         tc::st_async_f32x4((uint32_t)r, dst, val, recv_full);
                 }
-            } else {
+            } else if constexpr (!C::PUSH) {
+                // wide tiles: the partial goes to L2 as [BN / 4][128 rows] float4 (a warp writes
+                // 512 contiguous bytes per store); distributed shared memory is several times
+                // slower per SM than L2 for a 128 KB partial
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
-                    *reinterpret_cast<float4*>(part + row * C::PS + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    __stcg(gpart + (size_t)((c0 + j) >> 2) * 128 + row, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
             }
         }
         if (push) {
@@ -630,59 +631,65 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
     if (!push && threadIdx.x == 32) tc_stamp(p, 12);
     if (push) {
         tc::cluster_wait();  // phase 2: no copy into or out of any CTA of the cluster is in flight
-    } else if (p.splits > 1) {
-        // ---- epilogue part 2: cluster-wide split-K reduction over distributed shared memory ----
-        tc::cluster_sync();  // every CTA's partial tile is in its shared memory
+    } else if (!C::PUSH && p.splits > 1) {  // (PUSH tiles exchange by push whenever they split)
+        // ---- epilogue part 2: split-K reduction of the partials in L2 ----
+        tc::cluster_sync();  // every CTA's partial is written (release / acquire, cluster scope)
         if (threadIdx.x == 32) tc_stamp(p, 13);
         if (warp >= 1 && warp <= 4) {
             const int row = (warp & 3) * 32 + lane;
             const int nn = n0 + row;
-            const int rank = (int)tc::cluster_rank();
-            const uint32_t local = tc::smem_u32(smem);
             const int mend = min(p.M, m0 + BN);
-            // rank r reduces and writes a contiguous block of CW columns (tokens): 16-byte
-            // remote loads, all splits of a batch in flight together, summed in rank order
+            const float4* tile_part = p.part + (size_t)(blockIdx.x + gridDim.x * blockIdx.y) * p.splits * (BN / 4) * 128;
+            // split s reduces and writes a contiguous block of CW columns (tokens). Every split's
+            // loads of a block are issued before any is summed; the sums run in split order.
             const int CW = push_cw(BN, p.splits);
-            const int cend = min(BN, (rank + 1) * CW);
-            constexpr int RJ = 8;
-            for (int cb = rank * CW; cb < cend && m0 + cb < mend; cb += RJ) {
+            const int cend = min(BN, (split + 1) * CW);
+            constexpr int RJ = 16, RQ = RJ / 4;
+            for (int cb = split * CW; cb < cend && m0 + cb < mend; cb += RJ) {
                 float acc[RJ], rp[RJ];
                 const bool resid = p.epi.kind == EPI_RESID;
-                if (resid) {  // residual loads in flight together with the remote partial loads
+                if (resid) {  // residual loads in flight together with the partial loads
 #pragma unroll
                     for (int j = 0; j < RJ; ++j) {
                         const int m = m0 + cb + j;
                         rp[j] = (nn < p.w.rows && m < mend && cb + j < cend) ? p.epi.out[(size_t)m * p.epi.ldo + nn] : 0.f;
                     }
                 }
-#pragma unroll
-                for (int j = 0; j < RJ; ++j) acc[j] = 0.f;
-                const uint32_t a0 = local + (uint32_t)((row * C::PS + cb) * 4);
-                const bool second = cb + 4 < cend;  // columns cb+4..cb+7 belong to this block
+                // unconditional loads from clamped (valid) addresses, masked afterwards: no branch
+                // separates a load from the next one
+                float4 x[MAX_SPLITS_PULL][RQ];
 #pragma unroll
                 for (int sp = 0; sp < MAX_SPLITS_PULL; ++sp) {
-                    if (sp < p.splits) {
-                        const float4 x = tc::ld_cluster_f32x4(tc::map_cluster(a0, sp));
-                        const float4 y = second ? tc::ld_cluster_f32x4(tc::map_cluster(a0 + 16, sp))
-                                                : make_float4(0.f, 0.f, 0.f, 0.f);
-                        acc[0] += x.x;
-                        acc[1] += x.y;
-                        acc[2] += x.z;
-                        acc[3] += x.w;
-                        acc[4] += y.x;
-                        acc[5] += y.y;
-                        acc[6] += y.z;
-                        acc[7] += y.w;
+                    const int spc = min(sp, p.splits - 1);
+#pragma unroll
+                    for (int q = 0; q < RQ; ++q) {
+                        const int c4 = min((cb >> 2) + q, (cend >> 2) - 1);
+                        x[sp][q] = __ldcg(tile_part + ((size_t)spc * (BN / 4) + c4) * 128 + row);
                     }
                 }
+#pragma unroll
+                for (int j = 0; j < RJ; ++j) acc[j] = 0.f;
+#pragma unroll
+                for (int sp = 0; sp < MAX_SPLITS_PULL; ++sp) {
+                    const bool keep = sp < p.splits;  // an absent split adds +0: no value changes
+#pragma unroll
+                    for (int q = 0; q < RQ; ++q) {
+                        acc[4 * q] += keep ? x[sp][q].x : 0.f;
+                        acc[4 * q + 1] += keep ? x[sp][q].y : 0.f;
+                        acc[4 * q + 2] += keep ? x[sp][q].z : 0.f;
+                        acc[4 * q + 3] += keep ? x[sp][q].w : 0.f;
+                    }
+                }
+                if (threadIdx.x == 32 && cb == split * CW) tc_stamp(p, 15);  // first block summed
                 epi_chunk<RJ>(p.epi, nn, nn < p.w.rows, acc, m0 + cb, 1, min(mend, m0 + cend), p.post,
                               resid ? rp : nullptr);
             }
         }
+        // no closing cluster barrier: the partials live in global memory, and the next launch
+        // writes them only after its dependent-launch wait, when this grid has completed
         if (threadIdx.x == 32) tc_stamp(p, 14);
-        tc::cluster_sync();  // no CTA leaves while its partial may still be read
     }
-    if (threadIdx.x == 0) tc_stamp(p, 15);
+    if (threadIdx.x == 0 && (C::PUSH || p.splits == 1)) tc_stamp(p, 15);  // (pull: see above)
     if (warp == 0) tc::tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
@@ -1061,6 +1068,12 @@ int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax) {
         const int one = 1;
         if (e[0] == '1' && cudaMemcpy(p.fault, &one, 4, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
     }
+    if (Mmax > 64) {
+        // split-K partials of the wide tiles (BN 128 / 256): fewer than 120 tiles, each split
+        // ceil(148 / tiles) ways at most, so under 268 CTAs of 128 x 256 fp32
+        p.part_floats = (size_t)268 * 128 * 256;
+        if (cudaMalloc(&p.part, p.part_floats * 4) != cudaSuccess) return -1;
+    }
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     p.state = new GemmState();
     if (const char* e = std::getenv("GPT2Q_TC_TRACE")) {
@@ -1074,6 +1087,7 @@ int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax) {
 
 void gemm_destroy(GemmPlan& p) {
     if (p.err) cudaFree(p.err);
+    if (p.part) cudaFree(p.part);
     if (p.state && p.state->trace) cudaFree(p.state->trace);
     if (p.state)
         for (void* q : p.state->owned) cudaFree(q);
@@ -1172,8 +1186,11 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
     tp.epi = e;
     tp.err = p.err;
     tp.fault = p.fault;
+    tp.part = reinterpret_cast<float4*>(p.part);
     tp.trace = nullptr;
     dim3 grid(n_tiles, m_tiles, splits);
+    if (splits > 1 && BN > 64 && (size_t)n_tiles * m_tiles * splits * 128 * BN > p.part_floats)
+        return cudaErrorInvalidValue;  // cannot happen: tiles < 120 and splits <= ceil(148 / tiles)
     GemmState& gs = *p.state;
     if (gs.trace && !gs.traced && w.rows == gs.trace_rows && w.cols == gs.trace_cols && M == gs.trace_m &&
         (size_t)grid.x * grid.y * grid.z <= 4096) {

@@ -30,6 +30,11 @@ struct GemmPlan {
     // cluster skips sending its partials, so the peers' bounded waits run out; the launch
     // that does so clears it. Armed at creation by GPT2Q_TEST_SPLITK_STALL=1 (tests only).
     int* fault = nullptr;
+    // Split-K partials of the wide tiles (more than 64 tokens), exchanged through L2; one
+    // buffer serves every launch on the stream because a launch writes it only after its
+    // dependent-launch wait, when the launch before has finished reading it.
+    float* part = nullptr;
+    size_t part_floats = 0;
     size_t presplit_bytes = 0;
     GemmState* state = nullptr;
     bool usable(const QW& w, int M) const;
