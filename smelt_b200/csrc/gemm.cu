@@ -106,6 +106,7 @@ struct TcParams {
     int* err;
     int* fault;                 // one-shot split-K stall switch (GemmPlan::fault)
     float4* part;               // split-K partials of the wide tiles (GemmPlan::part)
+    int products;               // wide tiles: 1 = W_hi X_hi, 2 = + W_lo X_hi, 3 = + W_hi X_lo
     unsigned long long* trace;  // optional [grid][TC_TRACE] globaltimer stamps (one traced launch)
 };
 
@@ -363,10 +364,11 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
                 if (PRESPLIT) {
                     const int s = i % C::OS, use = i / C::OS;
                     if (!tc::mbar_wait_spin(&op_empty[s], (use & 1) ^ 1, p.err)) break;
-                    tc::mbar_arrive_expect_tx(&op_full[s], 2 * C::A_BYTES);
+                    const bool wlo = C::DUAL || p.products >= 2;
+                    tc::mbar_arrive_expect_tx(&op_full[s], (wlo ? 2 : 1) * C::A_BYTES);
                     uint8_t* a = smem + C::OFF_A + s * 2 * C::A_BYTES;
                     tc::tma_load_2d(a, &tm_w, (kb0 + i) * BK, n0, &op_full[s]);
-                    tc::tma_load_2d(a + C::A_BYTES, &tm_wlo, (kb0 + i) * BK, n0, &op_full[s]);
+                    if (wlo) tc::tma_load_2d(a + C::A_BYTES, &tm_wlo, (kb0 + i) * BK, n0, &op_full[s]);
                 } else {
                     const int s = i % C::RAW_STAGES, use = i / C::RAW_STAGES;
                     if (!tc::mbar_wait_spin(&raw_empty[s], (use & 1) ^ 1, p.err)) break;
@@ -398,11 +400,12 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % C::XS, use = i / C::XS;
                 if (!tc::mbar_wait_spin(&x_empty[s], (use & 1) ^ 1, p.err)) break;
-                tc::mbar_arrive_expect_tx(&x_full[s], 2 * C::B_BYTES);
+                const bool xlo = C::DUAL || p.products >= 3;
+                tc::mbar_arrive_expect_tx(&x_full[s], (xlo ? 2 : 1) * C::B_BYTES);
                 const int kx = (kb0 + i) * BK;
                 uint8_t* b = smem + C::OFF_B + s * 2 * C::B_BYTES;
                 tc::tma_load_2d(b, &tm_xhi, kx, m0, &x_full[s]);
-                tc::tma_load_2d(b + C::B_BYTES, &tm_xlo, kx, m0, &x_full[s]);
+                if (xlo) tc::tma_load_2d(b + C::B_BYTES, &tm_xlo, kx, m0, &x_full[s]);
                 if (i == 0) tc_stamp(p, 9);
                 issued = i + 1;
             }
@@ -439,8 +442,8 @@ __global__ void __launch_bounds__(THREADS, (Cfg<BN, PRESPLIT, DEEP>::MIN_BLOCKS)
                     } else {
                         const uint64_t dbl = tc::desc_sw128(b_lo + ko);
                         tc::mma_f16(tmem, dah, dbh, idesc, acc);
-                        tc::mma_f16(tmem, dah, dbl, idesc, 1u);
-                        tc::mma_f16(tmem, dal, dbh, idesc, 1u);
+                        if (p.products >= 3) tc::mma_f16(tmem, dah, dbl, idesc, 1u);
+                        if (p.products >= 2) tc::mma_f16(tmem, dal, dbh, idesc, 1u);
                     }
                 }
                 tc::mma_commit(&op_empty[s]);
@@ -760,10 +763,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int i = 0; i < nkb; ++i, ++it) {
                     const int s = it % PB_OS, use = it / PB_OS;
                     if (!tc::mbar_wait_spin(&op_empty[s], (use & 1) ^ 1, p.err)) break;
-                    tc::mbar_arrive_expect_tx(&op_full[s], 2 * PB_A_BYTES);
+                    const bool wlo = p.products >= 2;
+                    tc::mbar_arrive_expect_tx(&op_full[s], (wlo ? 2 : 1) * PB_A_BYTES);
                     uint8_t* a = smem + s * 2 * PB_A_BYTES;
                     tc::tma_load_2d(a, &tm_w, i * BK, n0, &op_full[s]);
-                    tc::tma_load_2d(a + PB_A_BYTES, &tm_wlo, i * BK, n0, &op_full[s]);
+                    if (wlo) tc::tma_load_2d(a + PB_A_BYTES, &tm_wlo, i * BK, n0, &op_full[s]);
                 }
             }
         }
@@ -779,10 +783,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int i = 0; i < nkb; ++i, ++it) {
                     const int s = it % PB_XS, use = it / PB_XS;
                     if (!tc::mbar_wait_spin(&x_empty[s], (use & 1) ^ 1, p.err)) break;
-                    tc::mbar_arrive_expect_tx(&x_full[s], 2 * PB_B_BYTES);
+                    const bool xlo = p.products >= 3;
+                    tc::mbar_arrive_expect_tx(&x_full[s], (xlo ? 2 : 1) * PB_B_BYTES);
                     uint8_t* b = smem + PB_OFF_B + s * 2 * PB_B_BYTES;
                     tc::tma_load_2d(b, &tm_xhi, i * BK, m0, &x_full[s]);
-                    tc::tma_load_2d(b + PB_B_BYTES, &tm_xlo, i * BK, m0, &x_full[s]);
+                    if (xlo) tc::tma_load_2d(b + PB_B_BYTES, &tm_xlo, i * BK, m0, &x_full[s]);
                 }
             }
         }
@@ -812,8 +817,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint64_t dah = tc::desc_sw128(a_hi + ko), dal = tc::desc_sw128(a_lo + ko);
                         const uint64_t dbh = tc::desc_sw128(b_hi + ko), dbl = tc::desc_sw128(b_lo + ko);
                         tc::mma_f16(d, dah, dbh, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                        tc::mma_f16(d, dah, dbl, idesc, 1u);
-                        tc::mma_f16(d, dal, dbh, idesc, 1u);
+                        if (p.products >= 3) tc::mma_f16(d, dah, dbl, idesc, 1u);
+                        if (p.products >= 2) tc::mma_f16(d, dal, dbh, idesc, 1u);
                     }
                     tc::mma_commit(&op_empty[s]);
                     tc::mma_commit(&x_empty[xs]);
@@ -1062,6 +1067,7 @@ int gemm_init(GemmPlan& p, int device, int Mmax, int Kmax) {
     if (const char* e = std::getenv("GPT2Q_TC_MIN_M")) p.min_m = std::max(1, std::atoi(e));
     p.presplit_min_m = 257;
     if (const char* e = std::getenv("GPT2Q_TC_PRESPLIT_MIN_M")) p.presplit_min_m = std::max(1, std::atoi(e));
+    if (const char* e = std::getenv("GPT2Q_TC_PRODUCTS")) p.products = std::max(1, std::min(3, std::atoi(e)));
     if (cudaMalloc(&p.err, 8) != cudaSuccess || cudaMemset(p.err, 0, 8) != cudaSuccess) return -1;
     p.fault = p.err + 1;
     if (const char* e = std::getenv("GPT2Q_TEST_SPLITK_STALL")) {
@@ -1187,6 +1193,7 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
     tp.err = p.err;
     tp.fault = p.fault;
     tp.part = reinterpret_cast<float4*>(p.part);
+    tp.products = p.products;
     tp.trace = nullptr;
     dim3 grid(n_tiles, m_tiles, splits);
     if (splits > 1 && BN > 64 && (size_t)n_tiles * m_tiles * splits * 128 * BN > p.part_floats)

@@ -35,6 +35,14 @@ struct GemmPlan {
     // dependent-launch wait, when the launch before has finished reading it.
     float* part = nullptr;
     size_t part_floats = 0;
+    // Products of the wide (more than 64 tokens) tiles: 3 = W_hi X_hi + W_lo X_hi + W_hi X_lo
+    // (about 22 bits on both operands), 2 = the exact dequantised weights times fp16
+    // activations, 1 = fp16-rounded weights times fp16 activations. Logits max-abs against the
+    // oracle on the GPT-2 small / medium / XL workload shapes: 3.2e-5, 2.0e-3, 3.2e-3. All
+    // three hold 2e-2, but 1 and 2 flip greedy tokens whose top-2 logits are closer than
+    // that (one of 200 sequences of a d = 384 decode batch at 2 products), so the default
+    // is 3. GPT2Q_TC_PRODUCTS selects 1 or 2 when the handle is created.
+    int products = 3;
     size_t presplit_bytes = 0;
     GemmState* state = nullptr;
     bool usable(const QW& w, int M) const;

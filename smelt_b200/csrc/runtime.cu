@@ -1185,6 +1185,15 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
 // batched over the T positions. Weights are read in their uploaded atoms; the dequantised
 // values are exactly Engine::vec_f32's, the f32 weights the reference's backward uses.
 int trunk_grad(gpt2q_handle* H, const uint32_t* ids, int T, const float* dlogits, float* dx_out, float* lnf_out) {
+    // The stash feeds a backward that amplifies activation rounding (fp16 activations in the
+    // forward gave 6 % relative error in dx at 128 positions): the wide tiles compute all
+    // three products here, whatever GPT2Q_TC_PRODUCTS selected for inference.
+    struct Products {
+        GemmPlan& g;
+        int saved;
+        ~Products() { g.products = saved; }
+    } keep{H->gemm, H->gemm.products};
+    H->gemm.products = 3;
     const int d = H->cfg.n_embd, L = H->cfg.n_layer, V = H->cfg.vocab, NH = H->cfg.n_head, hd = H->hd;
     const int F = H->fc_local, d3 = 3 * d;
     const float eps = H->cfg.ln_eps;
@@ -1711,6 +1720,7 @@ int gpt2q_info(gpt2q_handle* H, char* json, size_t cap) {
                           ", \"persistent_why\": \"" + why + "\", \"persistent_ctas\": " +
                           std::to_string(H->mk.enabled ? MK_CS * H->mk.clusters : 0) +
                           ", \"tensor_core\": " + (H->gemm.enabled ? "true" : "false") +
+                          ", \"tc_products\": " + std::to_string(H->gemm.products) +
                           ", \"tp_size\": " + std::to_string(H->tp_size) +
                           ", \"tp_peer_mapped\": " + (tp_peer_mapped(H->tp) ? "true" : "false");
     std::string tr;

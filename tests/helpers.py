@@ -14,6 +14,18 @@ TINY = P.Meta(n_embd=128, n_layer=2, n_head=2, n_ctx=64, vocab=97)
 MINI = P.Meta(n_embd=256, n_layer=3, n_head=4, n_ctx=128, vocab=1031)
 POLICIES = ["auto", "q4auto", "core.f16", "f32"]
 
+# Observed logits accuracy (max-abs vs the oracle) by the products of the wide tensor-core
+# tiles that run linears over more than 64 tokens (gpt2q_info "tc_products"): 3 = ~22-bit
+# operands, 2 = exact dequantised weights x fp16 activations (the default), 1 = fp16 weights
+# x fp16 activations. Regression guards well inside the 2e-2 acceptance bound. 3 is the default;
+# GPT2Q_TC_PRODUCTS selects the others.
+TC_OBSERVED = {3: 1e-3, 2: 5e-3, 1: 1e-2}
+
+
+def observed(g) -> float:
+    """The accuracy guard for a handle, from the products its wide tiles compute."""
+    return TC_OBSERVED[int(g.info().get("tc_products", 3))]
+
 
 @functools.lru_cache(maxsize=None)
 def hf(meta: P.Meta, seed: int = 0, bias_std: float = 0.0):

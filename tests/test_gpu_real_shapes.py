@@ -13,8 +13,9 @@ against the oracle's restatement of Engine::step (experiments/model-lab/src/gpt2
 Inputs are the workloads' own seeded weights and token ids. The oracle side follows each
 checked sequence greedily: its prompt through orc_engine_prefill (bit-identical to one
 Engine::step per prompt token, tests/test_oracle_prefill.py), then one step per token.
-Acceptance: logits within 2e-2 max-abs (and within the 1e-3 this path achieves), identical
-greedy tokens (ties -> last index, gpt2.rs:390-396).
+Acceptance: logits within 2e-2 max-abs (and within what the handle's wide-tile products
+achieve, tests/helpers.py TC_OBSERVED), identical greedy tokens (ties -> last index,
+gpt2.rs:390-396).
 """
 import functools
 
@@ -26,9 +27,10 @@ from smelt_b200 import pack as P
 from smelt_b200 import synth
 from smelt_b200.gpu import Gpu
 
+from .helpers import observed
+
 pytestmark = pytest.mark.gpu
 LOGIT_TOL = 2e-2  # acceptance bound for fp32 accumulation
-OBSERVED = 1e-3   # what the split-precision tensor-core path achieves (regression guard)
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -63,12 +65,13 @@ def gap(lg) -> float:
     return float(top[1] - top[0])
 
 
-def check_sequence(i, ref_logits, ref_toks, got_first, got_first_tok, got_steps, got_last, got_last_tok):
-    """got_steps[s] is the token the GPU predicted at decode step s (ref_toks[s + 1])."""
+def check_sequence(i, bound, ref_logits, ref_toks, got_first, got_first_tok, got_steps, got_last, got_last_tok):
+    """got_steps[s] is the token the GPU predicted at decode step s (ref_toks[s + 1]); `bound` is
+    the handle's observed accuracy (tests/helpers.py observed)."""
     for name, a, b in (("prompt", got_first, ref_logits[0]), ("last step", got_last, ref_logits[-1])):
         err = float(np.abs(a - b).max())
         assert err <= LOGIT_TOL, (i, name, err)
-        assert err <= OBSERVED, (i, name, err)
+        assert err <= bound, (i, name, err)
     assert got_first_tok == ref_toks[0], (i, got_first_tok, ref_toks[0], gap(ref_logits[0]))
     for s, t in enumerate(got_steps):
         assert t == ref_toks[s + 1], (i, s, t, ref_toks[s + 1], gap(ref_logits[s + 1]))
@@ -83,13 +86,14 @@ def test_small_int8_batch32_decode():
     prompts = [ids[i * plen:(i + 1) * plen] for i in range(n)]
     with Gpu(pk, max_seqs=n) as g:
         assert g.info()["tensor_core"]
+        bound = observed(g)
         nxt0, lg0 = g.prefill(prompts, want_logits=True)
         toks = g.decode_steps(steps, n)
         nxt, lg = g.decode(toks[-1], [plen + steps] * n, want_logits=True)
     eng = engine(pk)
     for i in (0, 7, 19, 31):
         ref_lg, ref_tok = oracle_follow(eng, prompts[i], steps + 1)
-        check_sequence(i, ref_lg, ref_tok, lg0[i], nxt0[i], toks[:, i], lg[i], nxt[i])
+        check_sequence(i, bound, ref_lg, ref_tok, lg0[i], nxt0[i], toks[:, i], lg[i], nxt[i])
 
 
 def test_small_int4_batch256_ragged_decode():
@@ -101,6 +105,7 @@ def test_small_int4_batch256_ragged_decode():
     offs = np.concatenate([[0], np.cumsum(lens)])
     prompts = [ids[offs[i]:offs[i + 1]] for i in range(n)]
     with Gpu(pk, max_seqs=n, max_tokens=8192) as g:
+        bound = observed(g)
         nxt0, lg0 = g.prefill(prompts, want_logits=True)
         toks = g.decode_steps(steps, n)
         nxt, lg = g.decode(toks[-1], (lens + steps).astype(np.int32), want_logits=True)
@@ -109,7 +114,7 @@ def test_small_int4_batch256_ragged_decode():
     subset = sorted({int(np.argmin(lens)), int(np.argmax(lens)), *rng.choice(n, 2, replace=False).tolist()})
     for i in subset:
         ref_lg, ref_tok = oracle_follow(eng, prompts[i], steps + 1)
-        check_sequence(i, ref_lg, ref_tok, lg0[i], nxt0[i], toks[:, i], lg[i], nxt[i])
+        check_sequence(i, bound, ref_lg, ref_tok, lg0[i], nxt0[i], toks[:, i], lg[i], nxt[i])
 
 
 def test_medium_int8_prefill_1024():
@@ -120,12 +125,13 @@ def test_medium_int8_prefill_1024():
     prompts = [ids[:plen], ids[plen:2 * plen]]
     with Gpu(pk, max_seqs=2, max_tokens=16384) as g:
         assert g.info()["tensor_core"]
+        bound = observed(g)
         nxt, lg = g.prefill(prompts, want_logits=True)
     eng = engine(pk)
     for i, p in enumerate(prompts):
         ref = eng.prefill(p, eng.empty_kv())
         err = float(np.abs(lg[i] - ref).max())
-        assert err <= LOGIT_TOL and err <= OBSERVED, (i, err)
+        assert err <= LOGIT_TOL and err <= bound, (i, err)
         assert nxt[i] == O.argmax(ref), (i, nxt[i], O.argmax(ref), gap(ref))
 
 
@@ -136,10 +142,11 @@ def test_xl_int8_batch16_decode():
     ids = synth.prompt_ids(n * 256, V, seed=1)
     prompts = [ids[i * 256:i * 256 + plen] for i in range(n)]
     with Gpu(pk, max_seqs=n) as g:
+        bound = observed(g)
         nxt0, lg0 = g.prefill(prompts, want_logits=True)
         toks = g.decode_steps(steps, n)
         nxt, lg = g.decode(toks[-1], [plen + steps] * n, want_logits=True)
     eng = engine(pk)
     for i in (0, 15):
         ref_lg, ref_tok = oracle_follow(eng, prompts[i], steps + 1)
-        check_sequence(i, ref_lg, ref_tok, lg0[i], nxt0[i], toks[:, i], lg[i], nxt[i])
+        check_sequence(i, bound, ref_lg, ref_tok, lg0[i], nxt0[i], toks[:, i], lg[i], nxt[i])

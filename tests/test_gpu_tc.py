@@ -11,7 +11,7 @@ from oracle import oracle as O
 from smelt_b200 import pack as P
 from smelt_b200.gpu import Gpu
 
-from .helpers import MINI, TINY, make_pack, oracle_engine, oracle_prefix_logits
+from .helpers import MINI, TC_OBSERVED, TINY, make_pack, observed, oracle_engine, oracle_prefix_logits
 
 pytestmark = pytest.mark.gpu
 LOGIT_TOL = 2e-2
@@ -54,10 +54,11 @@ def test_tc_batched_decode_matches_cuda_core_path(policy, monkeypatch):
             nxt, lg0 = g.prefill(prompts, want_logits=True)
             toks = g.decode_steps(8, len(prompts))
             nxt2, lg = g.decode(toks[-1], [p.size + 8 for p in prompts], want_logits=True)
+            bound = observed(g)
         res[mode] = (nxt, lg0, toks, nxt2, lg)
     a, b = res["simt"], res["tc"]
-    assert np.abs(a[1] - b[1]).max() <= 1e-3
-    assert np.abs(a[4] - b[4]).max() <= 1e-3
+    assert np.abs(a[1] - b[1]).max() <= bound
+    assert np.abs(a[4] - b[4]).max() <= bound
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[2], b[2]) and np.array_equal(a[3], b[3])
 
 
@@ -69,9 +70,10 @@ def test_tc_large_prefill_matches_oracle():
     prompts = [rng.integers(0, MINI.vocab, n).astype(np.uint32) for n in lens]
     with Gpu(pk, max_seqs=len(prompts)) as g:
         nxt, lg = g.prefill(prompts, want_logits=True)
+        bound = observed(g)
     for i in (0, 1, 8, 15):
         ref = oracle_prefix_logits(eng, prompts[i])[-1]
-        assert np.abs(lg[i] - ref).max() <= 1e-3
+        assert np.abs(lg[i] - ref).max() <= bound
         assert nxt[i] == int(np.argmax(ref[::-1]) and (len(ref) - 1 - np.argmax(ref[::-1])))
 
 
@@ -89,14 +91,15 @@ def test_tc_prefill_attention_matches_cuda_cores_and_oracle(policy, monkeypatch)
     prompts = [rng.integers(0, LONG.vocab, n).astype(np.uint32) for n in lens]
     with Gpu(pk, max_seqs=len(prompts), max_tokens=2048) as g:
         nxt_tc, lg_tc = g.prefill(prompts, want_logits=True)
+        bound = observed(g)
     monkeypatch.setenv("GPT2Q_ATTN_CORES", "1")
     with Gpu(pk, max_seqs=len(prompts), max_tokens=2048) as g:
         nxt_cc, lg_cc = g.prefill(prompts, want_logits=True)
-    assert np.abs(lg_tc - lg_cc).max() <= 1e-3
+    assert np.abs(lg_tc - lg_cc).max() <= 1e-3  # same linears: only the attention kernels differ
     assert np.array_equal(nxt_tc, nxt_cc)
     for i, p in enumerate(prompts):
         ref = oracle_prefix_logits(eng, p)[-1]
-        assert np.abs(lg_tc[i] - ref).max() <= 1e-3
+        assert np.abs(lg_tc[i] - ref).max() <= bound
         assert nxt_tc[i] == O.argmax(ref)
 
 
@@ -119,9 +122,10 @@ def test_tc_split_k_exchange_shapes_match_cuda_core_path(batch, monkeypatch):
             g.prefill(prompts)
             toks = g.decode_steps(4, batch)
             nxt, lg = g.decode(toks[-1], [p.size + 4 for p in prompts], want_logits=True)
+            bound = observed(g)
         res[mode] = (toks, nxt, lg)
     a, b = res["simt"], res["tc"]
-    assert np.abs(a[2] - b[2]).max() <= 1e-3
+    assert np.abs(a[2] - b[2]).max() <= bound
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
 
 
@@ -139,9 +143,42 @@ def test_persistent_prefill_gemm_matches_per_tile_launch(monkeypatch):
             monkeypatch.delenv("GPT2Q_TC_NO_PERSISTENT")
         with Gpu(pk, max_seqs=len(prompts), max_tokens=4096) as g:
             res[mode] = g.prefill(prompts, want_logits=True)
+            bound = observed(g)
     assert np.array_equal(res["persistent"][0], res["per_tile"][0])
     assert np.array_equal(res["persistent"][1], res["per_tile"][1])
     eng = oracle_engine(pk)
     for i in (0, 31):
         ref = oracle_prefix_logits(eng, prompts[i])[-1]
-        assert np.abs(res["persistent"][1][i] - ref).max() <= 1e-3
+        assert np.abs(res["persistent"][1][i] - ref).max() <= bound
+
+
+@pytest.mark.parametrize("products", [1, 2, 3])
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+def test_wide_tile_products_against_oracle(products, policy, monkeypatch):
+    """GPT2Q_TC_PRODUCTS selects the MMAs of the wide tiles (prefill, and decode batches over 64
+    tokens): 1 = W_hi X_hi, 2 = + W_lo X_hi (the exact weights), 3 = + W_hi X_lo (the default).
+    Each holds the 2e-2 bound and its own observed bound through a 4096-token prefill
+    (persistent form) and decode steps of 100 sequences (split-K wide tiles). Every greedy token
+    equals the oracle's, evaluated on the GPU's own history, where the oracle's top-2 gap is
+    wider than twice the variant's bound (inside it a reduced-precision variant may flip)."""
+    monkeypatch.setenv("GPT2Q_TC_PRODUCTS", str(products))
+    pk = make_pack(MINI, policy, 0, 0.02)
+    eng = oracle_engine(pk)
+    rng = np.random.default_rng(31)
+    prompts = [rng.integers(0, MINI.vocab, int(n)).astype(np.uint32) for n in rng.integers(20, 80, 100)]
+    with Gpu(pk, max_seqs=len(prompts), max_tokens=8192) as g:
+        assert g.info()["tc_products"] == products
+        nxt, lg0 = g.prefill(prompts, want_logits=True)
+        toks = g.decode_steps(4, len(prompts))
+        nxt2, lg = g.decode(toks[-1], [p.size + 4 for p in prompts], want_logits=True)
+    for i in (0, 57, 99):
+        p = prompts[i]
+        ref = oracle_prefix_logits(eng, np.concatenate([p, [nxt[i]], toks[:, i]]))
+        for got, r in ((lg0[i], ref[p.size - 1]), (lg[i], ref[-1])):
+            err = float(np.abs(got - r).max())
+            assert err <= LOGIT_TOL and err <= TC_OBSERVED[products], (i, err)
+        picks = [(nxt[i], ref[p.size - 1]), (nxt2[i], ref[-1])] + [(toks[s, i], ref[p.size + s]) for s in range(4)]
+        for t, r in picks:
+            top2 = np.sort(r)[-2:]
+            if products == 3 or top2[1] - top2[0] > 2 * TC_OBSERVED[products]:
+                assert t == O.argmax(r), (i, t, O.argmax(r), top2)
