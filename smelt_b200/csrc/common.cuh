@@ -52,6 +52,13 @@ struct Epi {
     size_t layer_off;      // floats to this layer inside a slot
     size_t sel_stride;     // floats from K to V block inside a layer
     size_t head_stride;    // floats per head (n_ctx * hd)
+    // EPI_RESID, warp-level linear only (optional): per token and 16-row tile, the mean and the
+    // sum of squared deviations of the tile's new residual values, [token][stats_ld], and
+    // ln_g * (new value) split into out_hi / out_lo, for the LayerNorm that the next linear folds
+    // into its epilogue
+    float2* stats;
+    int stats_ld;
+    const float* ln_g;
 };
 
 __device__ __forceinline__ float gelu_tanh(float v) {

@@ -146,10 +146,16 @@ __device__ __forceinline__ void wait_staged(uint64_t* bar, int* err) {
     atomicExch(err, tc::ERR_WAIT_TIMEOUT);
 }
 
+__device__ __forceinline__ float lane_sum(float v) {  // butterfly: the same order on every lane
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
 template <int ATOM, int NB>
 __global__ void __launch_bounds__(MMA_MAX_WARPS * 32, 1)
 k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, int gps, int gpw, __half pre,
-             float post, int* err, unsigned long long* trace, Epi e) {
+             float post, int* err, unsigned long long* trace, Epi e, LnFold ln) {
     constexpr int NC = NB * 8;
     constexpr int N_OUT = TILE * NC;
     constexpr int GB = (ATOM == ATOM_Q8) ? 32 : 16;  // payload bytes per row and group
@@ -166,6 +172,7 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
     // (rows dense, stride ldx); otherwise one copy per token row at a bank-spread stride. One
     // layout for every CTA of a cluster (CTA 0's partial slots are addressed by the others): the
     // stride of the nominal range, even where the last split holds fewer groups.
+    const bool fold = ln.stats != nullptr;  // X = g * x of a LayerNorm folded into the epilogue
     const bool whole = S == 1 && G * 32 == ldx;
     const int xs = whole ? ldx : staged_stride<ATOM>(gps);
     __half* sxh = reinterpret_cast<__half*>(smem_raw);
@@ -175,6 +182,9 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
     float* red = reinterpret_cast<float*>(smem_raw);
     const size_t staged_bytes = max((size_t)2 * NC * xs * 2, (size_t)nw * N_OUT * 4);
     float* recv = reinterpret_cast<float*>(smem_raw + staged_bytes);
+    // folded LayerNorm: each token's mean and 1 / sqrt(var + eps)
+    float* smean = recv + (S > 1 ? (size_t)S * N_OUT : 0);
+    float* srstd = smean + NC;
     const int g0 = min(kg1, kg0 + warp * gpw), g1 = min(kg1, g0 + gpw);
 
     // ---- before the previous kernel finishes: this warp's first weights, the epilogue's bias ----
@@ -203,13 +213,23 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
     bool eok[EP];
     float eb[EP], er[EP];
     int esl[EP], eps[EP];
+    float ec1[EP];  // folded LayerNorm: sum_k W[n][k] g[k]; eb then holds sum_k W[n][k] b[k] + bias[n]
 #pragma unroll
     for (int k = 0; k < EP; ++k) {
         const int i = threadIdx.x + k * (int)blockDim.x;
         em[k] = i / TILE;
         en[k] = tile * TILE + i % TILE;
         eok[k] = epi_cta && i < N_OUT && em[k] < M && en[k] < w.rows;
-        eb[k] = (eok[k] && e.bias) ? __ldg(e.bias + en[k]) : 0.f;
+        eb[k] = 0.f;
+        ec1[k] = 0.f;
+        if (eok[k]) {
+            if (fold) {
+                ec1[k] = __ldg(ln.c1 + en[k]);
+                eb[k] = __ldg(ln.c2b + en[k]);
+            } else if (e.bias) {
+                eb[k] = __ldg(e.bias + en[k]);
+            }
+        }
         er[k] = 0.f;
         esl[k] = eps[k] = 0;
     }
@@ -250,6 +270,40 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
         if (e.kind == EPI_QKV && en[k] >= e.d_local) {
             esl[k] = e.slot[em[k]];
             eps[k] = e.pos[em[k]];
+        }
+    }
+    if (fold && epi_cta) {
+        // each token's LayerNorm statistics from the (mean_t, M2_t) of the T 16-element tiles of
+        // its row, in a fixed order: mean = sum(mean_t) / T, M2 = sum(M2_t + 16 (mean_t - mean)^2)
+        // (exact identities); rstd = 1 / sqrt(M2 / (16 T) + eps) as k_layernorm computes it.
+        // Every load of a warp's tokens is issued first; they fly with the activation copy.
+        constexpr int TPW = 4;  // tokens per warp (M <= 64, at least 16 warps when M > 32)
+        const int T = ln.n_tiles;
+        float2 st[TPW][4];
+#pragma unroll
+        for (int r = 0; r < TPW; ++r) {
+            const int m = warp + r * nw;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int t = lane + 32 * u;
+                st[r][u] = (m < M && t < T) ? __ldcg(ln.stats + (size_t)m * ln.stats_ld + t) : make_float2(0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < TPW; ++r) {
+            const int m = warp + r * nw;
+            const float mean = lane_sum(st[r][0].x + st[r][1].x + st[r][2].x + st[r][3].x) / (float)T;
+            float q = 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float dm = st[r][u].x - mean;
+                if (lane + 32 * u < T) q += st[r][u].y + 16.f * dm * dm;
+            }
+            const float var = lane_sum(q) / (float)(16 * T);
+            if (lane == 0 && m < M) {
+                smean[m] = mean;
+                srstd[m] = __frcp_rn(sqrtf(var + ln.eps));
+            }
         }
     }
     wait_staged(&xbar, err);
@@ -335,17 +389,27 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
         mma_stamp(trace, 6);
     }
     // ---- epilogue: every input is already in registers ----
+    float res[EP];
 #pragma unroll
     for (int k = 0; k < EP; ++k) {
+        res[k] = 0.f;
         if (!eok[k]) continue;
-        const float x = v[k] * post + eb[k];
+        // folded LayerNorm: W (g (x - mean) rstd + b) + bias = rstd (W (g x) - mean W g) + W b + bias
+        const float x = fold ? srstd[em[k]] * (v[k] * post - smean[em[k]] * ec1[k]) + eb[k] : v[k] * post + eb[k];
         const size_t o = (size_t)em[k] * e.ldo + en[k];
         switch (e.kind) {
             case EPI_STORE:
                 e.out[o] = x;
                 break;
             case EPI_RESID:
-                e.out[o] = er[k] + x;
+                res[k] = er[k] + x;
+                e.out[o] = res[k];
+                if (e.stats) {  // g * x of the next LayerNorm, the next linear's activations
+                    __half h, l;
+                    split_hl(e.ln_g[en[k]] * res[k], h, l);
+                    e.out_hi[o] = h;
+                    e.out_lo[o] = l;
+                }
                 break;
             case EPI_GELU: {
                 const float gv = gelu_tanh(x);
@@ -368,6 +432,24 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
                          (size_t)head * e.head_stride + (size_t)eps[k] * e.hd + i] = x;
                 }
             }
+        }
+    }
+    if (e.kind == EPI_RESID && e.stats) {
+        // the tile's 16 new residual values of a token sit in 16 consecutive threads: their mean
+        // and sum of squared deviations (fixed butterfly order), for the next LayerNorm
+#pragma unroll
+        for (int k = 0; k < EP; ++k) {
+            const int i = threadIdx.x + k * (int)blockDim.x;
+            if (i - (threadIdx.x & 31) >= N_OUT) break;  // warp-uniform: no outputs left
+            float s = res[k];
+#pragma unroll
+            for (int o = 1; o < TILE; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            const float mean = s * (1.0f / TILE);
+            const float dv = eok[k] ? res[k] - mean : 0.f;
+            float q = dv * dv;
+#pragma unroll
+            for (int o = 1; o < TILE; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+            if (eok[k] && i % TILE == 0) e.stats[(size_t)em[k] * e.stats_ld + tile] = make_float2(mean, q);
         }
     }
     mma_stamp(trace, 7);
@@ -412,16 +494,18 @@ struct Plan {
     size_t smem = 0;
 };
 
-size_t smem_bytes(int atom, int NB, int kgroups, int warps, int S) {
+size_t smem_bytes(int atom, int NB, int kgroups, int warps, int S, bool ln) {
     const int NC = NB * 8;
     const int xs = atom == ATOM_Q8 ? staged_stride<ATOM_Q8>(kgroups) : staged_stride<ATOM_Q4>(kgroups);
     const size_t staged = std::max((size_t)2 * NC * xs * 2, (size_t)warps * TILE * NC * 4);
-    return staged + (S > 1 ? (size_t)S * TILE * NC * 4 : 0);
+    // folded LayerNorm: each token's mean and rstd
+    const size_t lnb = ln ? (size_t)2 * NC * 4 : 0;
+    return staged + (S > 1 ? (size_t)S * TILE * NC * 4 : 0) + lnb;
 }
 
 // Work layout: K split over a cluster of S CTAs only where the row tiles alone leave most SMs
 // idle (or the staged activations of the whole K would not fit); warps of 1-2 groups each.
-bool plan(const QW& w, int M, Plan& p) {
+bool plan(const QW& w, int M, Plan& p, bool ln) {
     const int tiles = (w.rows + TILE - 1) / TILE;
     const int G = w.cols / 32;
     const int NB = (M + 7) / 8;
@@ -436,7 +520,7 @@ bool plan(const QW& w, int M, Plan& p) {
         const int wmax = tiles > sms ? MMA_MAX_WARPS / 2 : MMA_MAX_WARPS;
         const int warps = std::max(2 * NB, std::min(wmax, gps));  // 2 epilogue outputs per thread
         const int gpw = (gps + warps - 1) / warps;
-        const size_t smem = smem_bytes(w.atom, NB, gps, warps, Sx);
+        const size_t smem = smem_bytes(w.atom, NB, gps, warps, Sx, ln);
         if (smem <= (size_t)MMA_MAX_SMEM) {
             p.S = Sx;
             p.warps = warps;
@@ -451,7 +535,7 @@ bool plan(const QW& w, int M, Plan& p) {
 
 template <int ATOM, int NB>
 cudaError_t launch_nb(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, const Plan& p, __half pre,
-                      float post, int* err, const Epi& e, cudaStream_t st) {
+                      float post, int* err, const Epi& e, const LnFold& ln, cudaStream_t st) {
     auto kern = k_linear_mma<ATOM, NB>;
     // the dynamic shared-memory limit is raised once per device for each instantiation
     static unsigned long long raised = 0;
@@ -493,21 +577,21 @@ cudaError_t launch_nb(const QW& w, const __half* xhi, const __half* xlo, int ldx
         ts.traced = true;
         ts.grid = grid;
     }
-    return cudaLaunchKernelEx(&cfg, kern, w, xhi, xlo, ldx, M, p.gps, p.gpw, pre, post, err, tr, e);
+    return cudaLaunchKernelEx(&cfg, kern, w, xhi, xlo, ldx, M, p.gps, p.gpw, pre, post, err, tr, e, ln);
 }
 
 template <int ATOM>
 cudaError_t launch_atom(int NB, const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, const Plan& p,
-                        __half pre, float post, int* err, const Epi& e, cudaStream_t st) {
+                        __half pre, float post, int* err, const Epi& e, const LnFold& ln, cudaStream_t st) {
     switch (NB) {
-        case 1: return launch_nb<ATOM, 1>(w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
-        case 2: return launch_nb<ATOM, 2>(w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
-        case 3: return launch_nb<ATOM, 3>(w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
-        case 4: return launch_nb<ATOM, 4>(w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
-        case 5: return launch_nb<ATOM, 5>(w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
-        case 6: return launch_nb<ATOM, 6>(w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
-        case 7: return launch_nb<ATOM, 7>(w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
-        default: return launch_nb<ATOM, 8>(w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
+        case 1: return launch_nb<ATOM, 1>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
+        case 2: return launch_nb<ATOM, 2>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
+        case 3: return launch_nb<ATOM, 3>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
+        case 4: return launch_nb<ATOM, 4>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
+        case 5: return launch_nb<ATOM, 5>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
+        case 6: return launch_nb<ATOM, 6>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
+        case 7: return launch_nb<ATOM, 7>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
+        default: return launch_nb<ATOM, 8>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
     }
 }
 
@@ -531,21 +615,32 @@ void mma_init() {
     num_sms();
 }
 
-bool mma_fits(const QW& w, int M) {
+bool mma_fits(const QW& w, int M, bool ln) {
     Plan p;
-    return mma_usable(w, M) && plan(w, M, p);
+    return mma_usable(w, M) && plan(w, M, p, ln);
 }
 
 cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, int pexp, int* err,
-                              const Epi& e, cudaStream_t st) {
+                              const Epi& e, cudaStream_t st, const LnFold* ln) {
     if (M <= 0) return cudaSuccess;
     Plan p;
-    if (!mma_usable(w, M) || ldx % 8 != 0 || !err || !plan(w, M, p)) return cudaErrorInvalidValue;
+    if (!mma_usable(w, M) || ldx % 8 != 0 || !err || !plan(w, M, p, ln != nullptr)) return cudaErrorInvalidValue;
+    LnFold lf{};
+    if (ln) {
+        // the row's statistics in at most 128 tiles of 16; four tokens per warp at most
+        const int warps = p.warps;
+        if (!ln->stats || !ln->c1 || !ln->c2b || ln->n_tiles * 16 != w.cols || ln->n_tiles > 128 ||
+            ln->stats_ld < ln->n_tiles || 4 * warps < M)
+            return cudaErrorInvalidValue;
+        lf = *ln;
+    }
+    if (e.kind == EPI_RESID && e.stats && (w.rows % TILE != 0 || e.stats_ld * TILE < w.rows || !e.ln_g || !e.out_hi || !e.out_lo))
+        return cudaErrorInvalidValue;
     const __half pre = __float2half_rn(std::ldexp(1.0f, pexp));
     const float post = std::ldexp(1.0f, -pexp);
     const int NB = (M + 7) / 8;
-    if (w.atom == ATOM_Q8) return launch_atom<ATOM_Q8>(NB, w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
-    return launch_atom<ATOM_Q4>(NB, w, xhi, xlo, ldx, M, p, pre, post, err, e, st);
+    if (w.atom == ATOM_Q8) return launch_atom<ATOM_Q8>(NB, w, xhi, xlo, ldx, M, p, pre, post, err, e, lf, st);
+    return launch_atom<ATOM_Q4>(NB, w, xhi, xlo, ldx, M, p, pre, post, err, e, lf, st);
 }
 
 std::string mma_trace_json() {

@@ -19,15 +19,29 @@ constexpr int MMA_MAX_SMEM = 225 * 1024;  // staged activations + warp and clust
 // Per-process set-up on the current device (call when a handle is created, outside any capture).
 void mma_init();
 bool mma_usable(const QW& w, int M);
-// mma_usable, and a work layout whose staged activations fit in shared memory exists.
-bool mma_fits(const QW& w, int M);
+// mma_usable, and a work layout whose staged activations fit in shared memory exists (with room
+// for a folded LayerNorm's statistics when `ln`).
+bool mma_fits(const QW& w, int M, bool ln = false);
 // Power-of-two exponent P applied to the group scales (s' = s 2^P) so that the fp16 hi/lo
 // split stays in the normal range; max_abs_w bounds |dequantised weight|.
 int mma_prescale_exp(float max_abs_w);
+// A LayerNorm folded into the linear that consumes it: with X = g * x (the gain applied by the
+// residual linear that produced x, Epi::ln_g), W LN(x) + bias = rstd (W X - mean W g) + W b + bias
+// per token, the mean and rstd combined from the (mean, M2) of 16-element tiles that the
+// producer wrote (Epi::stats), and c1 = W g, c2b = W b + bias precomputed per output row.
+struct LnFold {
+    const float2* stats;  // [token][stats_ld]: tiles 0..n_tiles-1 of a token contiguous
+    int stats_ld, n_tiles;
+    float eps;
+    const float* c1;   // [rows]
+    const float* c2b;  // [rows]
+};
+
 // X = x_hi + x_lo, fp16 [M][ldx] written by the previous kernel; ldx % 8 == 0. err: device word
-// set when the bounded wait for the staged activations gives up.
+// set when the bounded wait for the staged activations gives up. With `ln`, X = g * x and the
+// epilogue completes the LayerNorm (see LnFold).
 cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, int pexp, int* err,
-                              const Epi& e, cudaStream_t st);
+                              const Epi& e, cudaStream_t st, const LnFold* ln = nullptr);
 // Phase stamps of the launch selected by GPT2Q_MMA_TRACE ("" when none), as JSON.
 std::string mma_trace_json();
 

@@ -828,6 +828,36 @@ __global__ void k_dequant(QW w, float* __restrict__ out) {
         out[i] = deq_elem(w, (int)(i / w.cols), (int)(i % w.cols));
 }
 
+// Constants of a LayerNorm folded into the linear after it, per output row n (in double, from the
+// exactly dequantised weights): c1 = sum_k W[n][k] g[k], c2b = sum_k W[n][k] b[k] + bias[n].
+__global__ void k_ln_fold(const QW w, const float* __restrict__ g, const float* __restrict__ b,
+                          const float* __restrict__ bias, float* __restrict__ c1, float* __restrict__ c2b) {
+    const int n = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (n >= w.rows) return;
+    double s1 = 0.0, s2 = 0.0;
+    for (int k = lane; k < w.cols; k += 32) {
+        const double wv = (double)deq_elem(w, n, k);
+        s1 += wv * (double)g[k];
+        s2 += wv * (double)b[k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (lane == 0) {
+        c1[n] = (float)s1;
+        c2b[n] = (float)(s2 + (bias ? (double)bias[n] : 0.0));
+    }
+}
+
+cudaError_t launch_ln_fold(const QW& w, const float* g, const float* b, const float* bias, float* c1, float* c2b,
+                           cudaStream_t st) {
+    if (w.rows <= 0) return cudaSuccess;
+    k_ln_fold<<<(unsigned)(((size_t)w.rows * 32 + 255) / 256), 256, 0, st>>>(w, g, b, bias, c1, c2b);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_dequant(const QW& w, float* out, cudaStream_t st) {
     k_dequant<<<148 * 8, 256, 0, st>>>(w, out);
     return cudaGetLastError();

@@ -70,6 +70,10 @@ cudaError_t launch_argmax(const float* logits, int V, int ld, int B, unsigned lo
 // Programmatic dependent launch on/off (GPT2Q_NO_PDL=1 disables it).
 bool pdl_enabled();
 cudaError_t launch_dequant(const QW& w, float* out, cudaStream_t st);
+// c1[n] = sum_k W[n][k] g[k], c2b[n] = sum_k W[n][k] b[k] + bias[n] (bias may be null): the
+// constants of a LayerNorm folded into the linear W that follows it (computed in double).
+cudaError_t launch_ln_fold(const QW& w, const float* g, const float* b, const float* bias, float* c1, float* c2b,
+                           cudaStream_t st);
 // Upload-time layout conversion from the SMT payload (raw, on device).
 cudaError_t launch_repack_q8(const uint8_t* raw, int rows, int cols, uint8_t* q, __half* s, int sstride,
                              cudaStream_t st);

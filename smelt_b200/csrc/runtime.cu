@@ -55,6 +55,9 @@ struct Linear {
     size_t weight_bytes = 0;  // q + scale bytes read by one full pass over W
     float max_abs_w = 0.f;    // upper bound of |dequantised weight| (tensor-core prescale)
     int mma_p = 0;            // power-of-two scale exponent of the warp-level tensor-core path
+    // the LayerNorm before this linear folded into its epilogue: W g and W b + bias per row
+    float* ln_c1 = nullptr;
+    float* ln_c2b = nullptr;
 };
 
 struct LayerW {
@@ -176,6 +179,11 @@ struct gpt2q_handle {
     // scratch of its K split over CTAs; GPT2Q_MMA_DISABLE=1 / GPT2Q_MMA_MIN_M at creation
     bool mma_on = true;
     int mma_min_m = 1;  // measured 2.7-4.4x faster than the CUDA-core GEMV at 2-12 tokens
+    // LayerNorms inside a layer folded into the warp-level linear that consumes them, from the
+    // per-tile statistics the residual linear before them writes ([MMA_MAX_M][n_embd / 16]);
+    // GPT2Q_LN_FUSE=0 at creation keeps the LayerNorm launches
+    bool ln_fuse = true;
+    float2* ln_stats = nullptr;
     MkPlan mk;      // persistent single-sequence decode
     TpComm* tp = nullptr;
 
@@ -421,10 +429,20 @@ struct In {
     int ld;
 };
 
-int linear(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int M, const Epi& e) {
+// The linear runs on the warp-level tensor-core kernel (with room for an applied LayerNorm).
+bool takes_mma(const gpt2q_handle* H, const Linear& L, const In& X, int M, bool ln) {
+    return X.hi && H->mma_on && M >= H->mma_min_m && M <= MMA_MAX_M && X.ld % 8 == 0 && mma_fits(L.w, M, ln);
+}
+
+// With `ln` the warp-level kernel completes the LayerNorm folded into it (the caller checked
+// ln_fusable).
+int linear(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int M, const Epi& e,
+           const LnFold* ln = nullptr) {
     const int extra = (e.kind == EPI_RESID) ? 2 : 1;
     const double bytes = linear_bytes(L, M, extra);
-    if (X.hi && H->mma_on && M >= H->mma_min_m && M <= MMA_MAX_M && X.ld % 8 == 0 && mma_fits(L.w, M)) {
+    if (ln) {
+        RUN(name, bytes, launch_linear_mma(L.w, X.hi, X.lo, X.ld, M, L.mma_p, H->kerr, e, H->stream, ln));
+    } else if (takes_mma(H, L, X, M, false)) {
         RUN(name, bytes, launch_linear_mma(L.w, X.hi, X.lo, X.ld, M, L.mma_p, H->kerr, e, H->stream));
     } else if (X.hi && H->gemm.usable(L.w, M)) {
         const XSplit xs{X.hi, X.lo, X.ld};
@@ -475,6 +493,16 @@ Epi epi_qkv(gpt2q_handle* H, int layer, const int* slot, const int* pos, const f
     return e;
 }
 
+// A LayerNorm between the residual linear `prod` and the linear `cons` that consumes it is
+// folded into `cons` when both take the warp-level kernel: prod writes the per-tile statistics
+// of its new residual rows and g * x as cons's activations; cons's epilogue completes the
+// LayerNorm with its precomputed W g and W b + bias.
+bool ln_fusable(const gpt2q_handle* H, const Linear& prod, const In& pin, const Linear& cons, const In& cin, int M) {
+    const int d = H->cfg.n_embd;
+    return H->ln_fuse && H->tp_size == 1 && cons.ln_c1 && d % 16 == 0 && d / 16 <= 128 &&
+           takes_mma(H, prod, pin, M, false) && takes_mma(H, cons, cin, M, true);
+}
+
 // One transformer block over M activation rows (gpt2.rs:238-322). attn_fn runs the
 // attention of this layer (decode or prefill form).
 template <class AttnFn>
@@ -485,13 +513,21 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     const In hin{H->h, H->h_hi, H->h_lo, d};
     const In ain{H->att, H->att_hi, H->att_lo, H->d_local};
     const In fin{H->f, H->f_hi, H->f_lo, H->fc_local};
+    // LN1 (after the previous layer's mlp c_proj) and LN2 (after attn c_proj) folded into qkv and
+    // c_fc where the kernels allow it
+    const bool fuse1 = layer > 0 && ln_fusable(H, H->layers[layer - 1].mproj, fin, Lw.attn, hin, M);
+    const bool fuse2 = ln_fusable(H, Lw.proj, ain, Lw.fc, hin, M);
+    const LayerW* next = layer + 1 < H->cfg.n_layer ? &H->layers[layer + 1] : nullptr;
+    const bool fuse1_next = next && ln_fusable(H, Lw.mproj, fin, next->attn, hin, M);
+    const LnFold ln1{H->ln_stats, d / 16, d / 16, eps, Lw.attn.ln_c1, Lw.attn.ln_c2b};
+    const LnFold ln2{H->ln_stats, d / 16, d / 16, eps, Lw.fc.ln_c1, Lw.fc.ln_c2b};
     // under tensor parallelism every LayerNorm after the first is applied by the residual
     // reduction before it
     const bool tp = H->tp_size > 1;
-    if (!(tp && layer > 0))
+    if (!(tp && layer > 0) && !fuse1)
         RUN("layernorm", (double)M * d * 8,
             launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln1_g, Lw.ln1_b, d, eps, M, H->stream));
-    int rc = linear(H, "linear_qkv", Lw.attn, hin, M, epi_qkv(H, layer, slot, pos, Lw.attn.bias));
+    int rc = linear(H, "linear_qkv", Lw.attn, hin, M, epi_qkv(H, layer, slot, pos, Lw.attn.bias), fuse1 ? &ln1 : nullptr);
     if (rc) return rc;
     rc = attn_fn(layer);
     if (rc) return rc;
@@ -500,10 +536,17 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     } else {
         Epi e = epi_store(H->x, d, Lw.proj.bias);
         e.kind = EPI_RESID;
+        if (fuse2) {
+            e.stats = H->ln_stats;
+            e.stats_ld = d / 16;
+            e.ln_g = Lw.ln2_g;
+            e.out_hi = H->h_hi;
+            e.out_lo = H->h_lo;
+        }
         rc = linear(H, "linear_attn_proj", Lw.proj, ain, M, e);
     }
     if (rc) return rc;
-    if (!tp)
+    if (!tp && !fuse2)
         RUN("layernorm", (double)M * d * 8,
             launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln2_g, Lw.ln2_b, d, eps, M, H->stream));
     {
@@ -511,7 +554,7 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
         e.kind = EPI_GELU;
         e.out_hi = H->f_hi;
         e.out_lo = H->f_lo;
-        rc = linear(H, "linear_fc_gelu", Lw.fc, hin, M, e);
+        rc = linear(H, "linear_fc_gelu", Lw.fc, hin, M, e, fuse2 ? &ln2 : nullptr);
         if (rc) return rc;
     }
     if (tp) {
@@ -523,6 +566,13 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     } else {
         Epi e = epi_store(H->x, d, Lw.mproj.bias);
         e.kind = EPI_RESID;
+        if (fuse1_next) {
+            e.stats = H->ln_stats;
+            e.stats_ld = d / 16;
+            e.ln_g = next->ln1_g;
+            e.out_hi = H->h_hi;
+            e.out_lo = H->h_lo;
+        }
         rc = linear(H, "linear_mlp_proj", Lw.mproj, fin, M, e);
     }
     return rc;
@@ -1092,6 +1142,8 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     if (const char* e = std::getenv("GPT2Q_MMA_DISABLE")) H->mma_on = e[0] != '1';
     if (const char* e = std::getenv("GPT2Q_MMA_MIN_M")) H->mma_min_m = std::max(1, std::atoi(e));
     if (H->mma_on) mma_init();
+    if (const char* e = std::getenv("GPT2Q_LN_FUSE")) H->ln_fuse = e[0] != '0';
+    H->ln_stats = H->dalloc<float2>((size_t)((d + 15) / 16) * MMA_MAX_M * 8);
 
     H->p_tok = H->dalloc<uint32_t>(M * 4);
     H->p_pos = H->dalloc<int>(M * 4);
@@ -1133,6 +1185,24 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
             if (gemm_register_weight(H->gemm, L->w, L->max_abs_w, presplit, H->stream) != 0) {
                 H->err = "tensor map for " + kv.first + " failed";
                 return bail(GPT2Q_ECUDA);
+            }
+        }
+    }
+    if (tp_size == 1 && H->mma_on && H->ln_fuse) {
+        // the constants of LN1 / LN2 folded into qkv / c_fc on the warp-level decode path
+        for (auto& L : H->layers) {
+            const std::pair<Linear*, std::pair<const float*, const float*>> pairs[2] = {
+                {&L.attn, {L.ln1_g, L.ln1_b}}, {&L.fc, {L.ln2_g, L.ln2_b}}};
+            for (const auto& pr : pairs) {
+                Linear* lin = pr.first;
+                const float* g = pr.second.first;
+                const float* b = pr.second.second;
+                if ((lin->w.atom != ATOM_Q8 && lin->w.atom != ATOM_Q4) || !g || !b) continue;
+                lin->ln_c1 = H->dalloc<float>((size_t)lin->rows * 4);
+                lin->ln_c2b = H->dalloc<float>((size_t)lin->rows * 4);
+                if (!lin->ln_c1 || !lin->ln_c2b) return bail(GPT2Q_EOOM);
+                if (launch_ln_fold(lin->w, g, b, lin->bias, lin->ln_c1, lin->ln_c2b, H->stream) != cudaSuccess)
+                    return bail(GPT2Q_ECUDA);
             }
         }
     }

@@ -100,3 +100,24 @@ def test_mma_decode_is_deterministic_and_batch_invariant(monkeypatch):
     b = _run(pk, prompts, 5, monkeypatch, "mma")
     for x, y in zip(a, b):
         assert np.array_equal(np.asarray(x).view(np.uint32), np.asarray(y).view(np.uint32))
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+@pytest.mark.parametrize("meta", [MINI, WIDE], ids=["mini", "wide"])
+def test_layernorm_applied_by_the_linear_matches_layernorm_launches(meta, policy, monkeypatch):
+    """LN1 (from layer 1 on) and LN2 applied by the warp-level qkv / c_fc launches from the
+    per-tile statistics that the residual linears write, against the same decode with the
+    LayerNorm launches (GPT2Q_LN_FUSE=0): the same tokens, logits equal to rounding, and the
+    oracle's logits within the bound."""
+    pk = make_pack(meta, policy, 0, 0.02)
+    rng = np.random.default_rng(77)
+    prompts = [rng.integers(0, meta.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 12, 32)]
+    fused = _run(pk, prompts, 6, monkeypatch, "mma")  # the decode steps of 32 tokens apply the LayerNorms
+    plain = _run(pk, prompts, 6, monkeypatch, "mma", {"GPT2Q_LN_FUSE": "0"})
+    assert np.abs(fused[1] - plain[1]).max() <= 1e-4 and np.abs(fused[4] - plain[4]).max() <= 1e-4
+    assert np.array_equal(fused[0], plain[0]) and np.array_equal(fused[2], plain[2]) and np.array_equal(fused[3], plain[3])
+    eng = oracle_engine(pk)
+    for i in (0, 31):
+        ref = oracle_prefix_logits(eng, np.concatenate([prompts[i], [fused[0][i]], fused[2][:, i]]))
+        assert np.abs(fused[4][i] - ref[-1]).max() <= bounds["mma"]
+        assert fused[3][i] == O.argmax(ref[-1])
