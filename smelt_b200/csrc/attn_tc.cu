@@ -1,12 +1,12 @@
-// Causal prefill attention on the tensor cores (tcgen05 / TMEM), one CTA per
-// (128-query tile, head), two CTAs per SM (97 KB shared memory, 256 TMEM columns each), so
+// Causal prefill attention on the tensor cores (tcgen05 / TMEM), one CTA of 256 threads per
+// (128-query tile, head), two CTAs per SM (98 KB shared memory, 256 TMEM columns each), so
 // one CTA's softmax and operand conversion overlap the other's MMAs.
 //
 // Per key block of 64 positions:
 //   S  = (Q * 2^-3) K^T          tcgen05.mma kind::f16, M = 128 queries, N = 64 keys, K = 64
-//   P  = exp(S - m_new)          one thread per query row (TMEM lane), online softmax in fp32
+//   P  = exp(S - m_new)          two threads per query row (TMEM lane), online softmax in fp32
 //   PV = P V                     tcgen05.mma, M = 128, N = 64 (head dim), K = 64 keys
-//   O  = O * exp(m_old - m_new) + PV   (O in registers)
+//   O  = O * exp(m_old - m_new) + PV   (O in registers, 32 dimensions per thread)
 // Both products use the fp16x3 split of gemm.cu: every fp32 operand x is held as
 // x_hi + x_lo (fp16 pair, ~22 bits) and A_hi B_hi + A_hi B_lo + A_lo B_hi accumulate in fp32
 // TMEM, so scores and outputs keep fp32-class accuracy (the dropped lo*lo term is ~2^-22
@@ -17,11 +17,15 @@
 // [2^13, 2^14): Q per query row, K and V per key block, P by 2^14. The scales are undone
 // exactly on S and PV, together with the attention scale 1/sqrt(64) = 2^-3.
 //
-// Operands are K-major tiles with the 128-byte swizzle (rows of 64 fp16; 8-row groups 1024
-// bytes apart), as in gemm.cu: Q [128 q][64], K [64 keys][64], P [128 q][64 keys] and
-// V^T [64 dims][64 keys] (V is transposed while it is converted). Threads 0-63 convert the K
-// rows, threads 64-127 the V rows of a block. Reference semantics: gpt2.rs:261-291
-// (softmax(q.K^T / sqrt(hd)) . V over positions 0..t), per query position t of the prompt.
+// Operands are tiles with the 128-byte swizzle (rows of 64 fp16; 8-row groups 1024 bytes
+// apart), as in gemm.cu: Q [128 q][64], K [64 keys][64] and P [128 q][64 keys] K-major, V
+// [64 keys][64 dims] the same bytes read as an MN-major B operand. The raw fp32 rows of a key
+// block (16 KB each for K and V, contiguous in the cache) arrive by one 1-D bulk copy into the
+// very area their hi/lo tiles occupy, issued as soon as that area is free: K's after the S MMAs
+// of the previous block, V's after its PV MMAs. A block's conversion then reads shared memory
+// (four threads per key row), holds its values in registers across the block maximum's barrier
+// and writes the tiles in place. Reference semantics: gpt2.rs:261-291 (softmax(q.K^T / sqrt(hd))
+// . V over positions 0..t), per query position t of the prompt.
 #include <cuda_fp16.h>
 
 #include <cstdlib>
@@ -37,7 +41,7 @@ namespace {
 constexpr int QT = 128;  // queries per CTA (TMEM lanes)
 constexpr int KB = 64;   // keys per block
 constexpr int HD = 64;
-constexpr int THREADS = 128;
+constexpr int THREADS = 256;  // two threads per query row
 constexpr int TILE_Q = QT * 128;   // bytes of one [128][64] fp16 tile
 constexpr int TILE_K = KB * 128;   // bytes of one [64][64] fp16 tile
 constexpr int OFF_QH = 0, OFF_QL = OFF_QH + TILE_Q;
@@ -46,7 +50,8 @@ constexpr int OFF_KH = OFF_QL + TILE_Q, OFF_KL = OFF_KH + TILE_K;
 constexpr int OFF_VH = OFF_KL + TILE_K, OFF_VL = OFF_VH + TILE_K;
 constexpr int OFF_PH = OFF_VL + TILE_K, OFF_PL = OFF_PH + TILE_Q;
 constexpr int OFF_BAR = OFF_PL + TILE_Q;
-constexpr int SMEM = OFF_BAR + 64 + 1024;  // barriers, TMEM slot, block-max scratch, alignment slack
+constexpr int OFF_XCH = OFF_BAR + 128;              // [2][QT] floats: the halves of a query row
+constexpr int SMEM = OFF_XCH + 2 * QT * 4 + 1024;  // + alignment slack
 static_assert(SMEM <= 232448 / 2 - 1024, "two CTAs per SM");
 // S: columns 0..127 (Q_hi K_hi | Q_hi K_lo, Q_lo K_hi added to the first half);
 // PV: 128..255 (P_hi V_hi | P_hi V_lo, P_lo V_hi added to the first half)
@@ -74,24 +79,6 @@ __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
     return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
 }
 
-// Row r of a [rows][64] tile from 64 fp32 values (times `mul`, a power of two): hi and lo.
-__device__ __forceinline__ void put_row64(uint8_t* hi, uint8_t* lo, int r, const float* v, float mul) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        uint32_t h[4], l[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            __half2 h2, l2;
-            split_hl2(v[8 * c + 2 * j] * mul, v[8 * c + 2 * j + 1] * mul, h2, l2);
-            h[j] = *reinterpret_cast<uint32_t*>(&h2);
-            l[j] = *reinterpret_cast<uint32_t*>(&l2);
-        }
-        const uint32_t o = sw_off(r, c);
-        *reinterpret_cast<uint4*>(hi + o) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(lo + o) = make_uint4(l[0], l[1], l[2], l[3]);
-    }
-}
-
 // 2^e as a float, e in [-126, 127].
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
@@ -102,42 +89,17 @@ __device__ __forceinline__ int scale_exp(float m) {
     return max(-60, min(60, 13 - (b - 127)));
 }
 
-__device__ __forceinline__ float row_absmax(const float* v) {
-    float m = 0.f;
+// Maximum over the THREADS threads of the CTA (red: 8 floats of shared memory).
+__device__ __forceinline__ float block_max(float a, float* red) {
 #pragma unroll
-    for (int i = 0; i < 64; ++i) m = fmaxf(m, fabsf(v[i]));
-    return m;
-}
-
-// Maxima over the 128 threads of the CTA of two values at once (red: 8 floats of shared memory).
-__device__ __forceinline__ float2 block_max2(float a, float b, float* red) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
-    }
-    if ((threadIdx.x & 31) == 0) {
-        red[threadIdx.x >> 5] = a;
-        red[4 + (threadIdx.x >> 5)] = b;
-    }
+    for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
     __syncthreads();
-    const float2 r = make_float2(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])),
-                                 fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+    float r = red[0];
+#pragma unroll
+    for (int w = 1; w < THREADS / 32; ++w) r = fmaxf(r, red[w]);
     __syncthreads();  // red is reused by the next call
     return r;
-}
-
-__device__ __forceinline__ void load_row64(const float* src, bool ok, float* v) {
-#pragma unroll
-    for (int i = 0; i < 64; i += 4) {
-        // coherent loads: q and K/V come from the preceding kernel, and a non-coherent (__ldg)
-        // load could be scheduled above griddepcontrol.wait
-        float4 x = ok ? __ldcg(reinterpret_cast<const float4*>(src + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[i] = x.x;
-        v[i + 1] = x.y;
-        v[i + 2] = x.z;
-        v[i + 3] = x.w;
-    }
 }
 
 __global__ void __launch_bounds__(THREADS, 2)
@@ -148,13 +110,23 @@ __global__ void __launch_bounds__(THREADS, 2)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
     uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* bar_pv = bar_s + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
-    float* red = reinterpret_cast<float*>(bar_s + 3);  // [8]
-    const int tid = threadIdx.x, warp = tid >> 5;
+    uint64_t* bar_k = bar_s + 2;  // raw K rows of a block landed in the K area
+    uint64_t* bar_v = bar_s + 3;  // raw V rows landed in the V area
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 4);
+    float* red = reinterpret_cast<float*>(bar_s + 6);        // [8] block maxima
+    float* xch = reinterpret_cast<float*>(smem + OFF_XCH);   // [2][QT]: the two halves of a query row
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // query row r (TMEM lane) of this thread, and its half: keys 32h..32h+31 of each block in
+    // the softmax, head dimensions 32h..32h+31 of the output (a warp reads only its own lane
+    // quarter of TMEM: warps w and w + 4 share lanes 32 (w % 4) ..)
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
 
     if (tid == 0) {
         tc::mbar_init(bar_s, 1);
         tc::mbar_init(bar_pv, 1);
+        tc::mbar_init(bar_k, 1);
+        tc::mbar_init(bar_v, 1);
         tc::fence_mbar_init();
     }
     if (warp == 0) {
@@ -166,7 +138,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     tc::pdl_trigger();  // after the TMEM allocation: dependents never hold columns this CTA waits for
-    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lanes
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);  // this warp's TMEM lanes
 
     tc::pdl_wait();  // q and the K/V rows were written by the preceding kernels
     atr_stamp(trace, 0);
@@ -174,68 +146,116 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int head = blockIdx.x;
     const float* Kc = g.base + (size_t)tile.slot * g.slot_stride + layer_off + (size_t)head * g.head_stride;
     const float* Vc = Kc + g.sel_stride;
-    const int qpos = tile.q0 + tid;  // this thread's query position (TMEM lane tid)
+    const int qpos = tile.q0 + r;  // this thread's query position
     const bool qvalid = qpos < tile.T;
+    const int kend = min(tile.T, tile.q0 + QT);  // keys past the last query of the tile are masked
+    const int nkb = (kend + KB - 1) / KB;
+    // raw fp32 K (or V) rows of key block kb into the K (V) operand area: 64 rows x 256 bytes =
+    // the 16 KB of its hi/lo tiles, contiguous in the cache
+    auto fetch = [&](uint64_t* bar, int area, const float* src, int kb) {
+        const uint32_t bytes = (uint32_t)min(KB, kend - kb * KB) * HD * 4;
+        tc::mbar_arrive_expect_tx(bar, bytes);
+        tc::bulk_load_1d(smem + area, src + (size_t)kb * KB * HD, bytes, bar);
+    };
+    if (tid == 0 && nkb > 0) {
+        fetch(bar_k, OFF_KH, Kc, 0);
+        fetch(bar_v, OFF_VH, Vc, 0);
+    }
 
-    // ---- Q tile, row scaled by 2^eq ----
+    // ---- Q tile, row scaled by 2^eq (the row maximum over both halves) ----
     int eq;
     {
-        float v[64];
-        load_row64(q + (size_t)(tile.row0 + (qvalid ? qpos : 0)) * ldq + head * HD, qvalid, v);
-        eq = scale_exp(row_absmax(v));
-        put_row64(smem + OFF_QH, smem + OFF_QL, tid, v, pow2f(eq));
+        float v[32];
+        const float* src = q + (size_t)(tile.row0 + (qvalid ? qpos : 0)) * ldq + head * HD + half * 32;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            // coherent loads: q comes from the preceding kernel, and a non-coherent (__ldg) load
+            // could be scheduled above griddepcontrol.wait
+            const float4 x = qvalid ? __ldcg(reinterpret_cast<const float4*>(src + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[i] = x.x;
+            v[i + 1] = x.y;
+            v[i + 2] = x.z;
+            v[i + 3] = x.w;
+        }
+        float am = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(v[i]));
+        xch[half * QT + r] = am;
+        __syncthreads();
+        eq = scale_exp(fmaxf(xch[r], xch[QT + r]));
+        __syncthreads();  // xch is reused
+        const float sq = pow2f(eq);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t h[4], lo[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                __half2 h2, l2;
+                split_hl2(v[8 * c + 2 * j] * sq, v[8 * c + 2 * j + 1] * sq, h2, l2);
+                h[j] = *reinterpret_cast<uint32_t*>(&h2);
+                lo[j] = *reinterpret_cast<uint32_t*>(&l2);
+            }
+            const uint32_t o = sw_off(r, 4 * half + c);
+            *reinterpret_cast<uint4*>(smem + OFF_QH + o) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4*>(smem + OFF_QL + o) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
     }
     atr_stamp(trace, 1);
 
     constexpr uint32_t idesc_s2 = tc::idesc_f16_f32(QT, 2 * KB);  // Q_hi [K_hi; K_lo]
     constexpr uint32_t idesc_s = tc::idesc_f16_f32(QT, KB);
-    constexpr uint32_t idesc_pv2 = tc::idesc_f16_f32(QT, 2 * HD);  // P_hi [V^T_hi; V^T_lo]
-    constexpr uint32_t idesc_pv = tc::idesc_f16_f32(QT, HD);
-    float o[64];
+    // V tiles are [keys][64 dims] rows, an MN-major B operand; V_lo follows V_hi as a second
+    // 64-wide atom along N: P_hi [V_hi | V_lo] is one MMA of N = 128
+    constexpr uint32_t idesc_pv2 = tc::idesc_f16_f32_bmn(QT, 2 * HD);
+    constexpr uint32_t idesc_pv = tc::idesc_f16_f32_bmn(QT, HD);
+    float o[32];  // output dimensions 32 half .. 32 half + 31 of query row r
 #pragma unroll
-    for (int i = 0; i < 64; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    const int kend = min(tile.T, tile.q0 + QT);  // keys past the last query of the tile are masked
-    const int nkb = (kend + KB - 1) / KB;
-    const bool is_k = tid < KB;        // threads 0-63: K row tid; 64-127: V row tid - 64
-    const int krow = tid & (KB - 1);
+    for (int i = 0; i < 32; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
+    // block conversion: four threads per key row, 16 values each
+    const int krow = tid >> 2, kq = tid & 3;
     bool ok = true;
-    for (int kb = 0; kb < nkb; ++kb) {
-        const int k0 = kb * KB;
-        // ---- K tile and V^T tile of keys k0..k0+63, each scaled by 2^ek / 2^ev of the block ----
-        int ek, ev;
-        {
-            const int kp = k0 + krow;
-            const bool kvalid = kp < kend;
-            float v[64];
-            load_row64((is_k ? Kc : Vc) + (size_t)(kvalid ? kp : 0) * HD, kvalid, v);
-            const float am = row_absmax(v);
-            const float2 mx = block_max2(is_k ? am : 0.f, is_k ? 0.f : am, red);
-            ek = scale_exp(mx.x);
-            ev = scale_exp(mx.y);
-            if (is_k) {
-                put_row64(smem + OFF_KH, smem + OFF_KL, krow, v, pow2f(ek));
-            } else {
-                // V^T column krow: element (dim d, key) -> row d
-                const float sv = pow2f(ev);
+    // ---- K of block kb: raw rows (prefetched) -> scaled by 2^ek of the block -> hi/lo tiles in
+    // place (every thread holds its values before the block maximum's barrier); returns ek ----
+    auto convert_k = [&](int kb) {
+        const bool kvalid = kb * KB + krow < kend;
+        ok = tc::mbar_wait_spin(bar_k, (uint32_t)(kb & 1), err) && ok;
+        float v[16];
+        const float* src = reinterpret_cast<const float*>(smem + OFF_KH) + krow * HD + kq * 16;
 #pragma unroll
-                for (int dd = 0; dd < 64; dd += 2) {
-                    __half2 h, lo;
-                    split_hl2(v[dd] * sv, v[dd + 1] * sv, h, lo);
-                    const uint32_t off0 = sw_off(dd, krow >> 3) + (uint32_t)((krow & 7) * 2);
-                    const uint32_t off1 = sw_off(dd + 1, krow >> 3) + (uint32_t)((krow & 7) * 2);
-                    *reinterpret_cast<__half*>(smem + OFF_VH + off0) = __low2half(h);
-                    *reinterpret_cast<__half*>(smem + OFF_VL + off0) = __low2half(lo);
-                    *reinterpret_cast<__half*>(smem + OFF_VH + off1) = __high2half(h);
-                    *reinterpret_cast<__half*>(smem + OFF_VL + off1) = __high2half(lo);
-                }
+        for (int i = 0; i < 16; i += 4) {
+            const float4 x = kvalid ? *reinterpret_cast<const float4*>(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[i] = x.x;
+            v[i + 1] = x.y;
+            v[i + 2] = x.z;
+            v[i + 3] = x.w;
+        }
+        float am = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) am = fmaxf(am, fabsf(v[i]));
+        const int e = scale_exp(block_max(am, red));
+        const float sk = pow2f(e);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            uint32_t h[4], lo[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                __half2 h2, l2;
+                split_hl2(v[8 * c + 2 * j] * sk, v[8 * c + 2 * j + 1] * sk, h2, l2);
+                h[j] = *reinterpret_cast<uint32_t*>(&h2);
+                lo[j] = *reinterpret_cast<uint32_t*>(&l2);
             }
+            const uint32_t off = sw_off(krow, 2 * kq + c);
+            *reinterpret_cast<uint4*>(smem + OFF_KH + off) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4*>(smem + OFF_KL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
         tc::fence_proxy_async_smem();
         tc::tc_fence_before();
         __syncthreads();
-        atr_stamp(trace, 2 + 4 * kb);
-        // ---- S = Q K^T ----
+        return e;
+    };
+    // ---- S = Q K^T of the block in the K area (one thread issues) ----
+    auto issue_s = [&]() {
         if (tid == 0) {
             tc::tc_fence_after();
             const uint32_t qh = tc::smem_u32(smem + OFF_QH), ql = tc::smem_u32(smem + OFF_QL);
@@ -248,33 +268,44 @@ __global__ void __launch_bounds__(THREADS, 2)
             }
             tc::mma_commit(bar_s);
         }
+    };
+    int ek = 0;
+    if (nkb > 0) {
+        ek = convert_k(0);
+        issue_s();
+    }
+    for (int kb = 0; kb < nkb; ++kb) {
+        const int k0 = kb * KB;
+        const bool kvalid = k0 + krow < kend;
+        atr_stamp(trace, 2 + 4 * kb);
         ok = tc::mbar_wait_spin(bar_s, (uint32_t)(kb & 1), err) && ok;
         tc::tc_fence_after();
+        // the K area is free until the next block's conversion: its raw rows fly meanwhile
+        if (tid == 0 && kb + 1 < nkb) fetch(bar_k, OFF_KH, Kc, kb + 1);
         atr_stamp(trace, 3 + 4 * kb);
-        // ---- online softmax of this thread's query row ----
-        float s[KB];
+        // ---- online softmax: keys 32 half .. 32 half + 31 of query row r ----
+        float s[32];
         {
             float u[32];
-            tc::tmem_ld32x2(t_lane, t_lane + KB, *reinterpret_cast<float(*)[32]>(s), u);
+            tc::tmem_ld32x2(t_lane + 32 * half, t_lane + KB + 32 * half, s, u);
 #pragma unroll
             for (int j = 0; j < 32; ++j) s[j] += u[j];
-            tc::tmem_ld32x2(t_lane + 32, t_lane + KB + 32, *reinterpret_cast<float(*)[32]>(s + 32), u);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) s[32 + j] += u[j];
         }
         const float s_unscale = pow2f(-(eq + ek) - 3);  // operand scales and 1/sqrt(64)
         float bmax = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < KB; ++j) {
-            const int kp = k0 + j;
+        for (int j = 0; j < 32; ++j) {
+            const int kp = k0 + 32 * half + j;
             s[j] = (kp > qpos || kp >= tile.T) ? -INFINITY : s[j] * s_unscale;
             bmax = fmaxf(bmax, s[j]);
         }
-        const float mnew = fmaxf(m, bmax);
+        xch[half * QT + r] = bmax;  // the row maximum over both halves
+        __syncthreads();
+        const float mnew = fmaxf(m, fmaxf(xch[r], xch[QT + r]));
         const float alpha = (mnew == -INFINITY) ? 1.f : __expf(m - mnew);
         float psum = 0.f;
 #pragma unroll
-        for (int c = 0; c < KB / 8; ++c) {  // 8 chunks of 8 keys
+        for (int c = 0; c < 4; ++c) {  // 4 chunks of 8 keys
             uint32_t h[4], lo[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -286,12 +317,47 @@ __global__ void __launch_bounds__(THREADS, 2)
                 h[j] = *reinterpret_cast<uint32_t*>(&h2);
                 lo[j] = *reinterpret_cast<uint32_t*>(&l2);
             }
-            const uint32_t off = sw_off(tid, c);
+            const uint32_t off = sw_off(r, 4 * half + c);
             *reinterpret_cast<uint4*>(smem + OFF_PH + off) = make_uint4(h[0], h[1], h[2], h[3]);
             *reinterpret_cast<uint4*>(smem + OFF_PL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
         l = l * alpha + psum;
         m = mnew;
+        // ---- V of the block: raw rows (prefetched) -> scaled by 2^ev -> hi/lo tiles in place, rows
+        // of keys as for K ----
+        int ev;
+        {
+            ok = tc::mbar_wait_spin(bar_v, (uint32_t)(kb & 1), err) && ok;
+            float v[16];
+            const float* src = reinterpret_cast<const float*>(smem + OFF_VH) + krow * HD + kq * 16;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+                const float4 x = kvalid ? *reinterpret_cast<const float4*>(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[i] = x.x;
+                v[i + 1] = x.y;
+                v[i + 2] = x.z;
+                v[i + 3] = x.w;
+            }
+            float am = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) am = fmaxf(am, fabsf(v[i]));
+            ev = scale_exp(block_max(am, red));  // its first barrier also orders xch's reads above
+            const float sv = pow2f(ev);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t h[4], lo[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    __half2 h2, l2;
+                    split_hl2(v[8 * c + 2 * j] * sv, v[8 * c + 2 * j + 1] * sv, h2, l2);
+                    h[j] = *reinterpret_cast<uint32_t*>(&h2);
+                    lo[j] = *reinterpret_cast<uint32_t*>(&l2);
+                }
+                const uint32_t off = sw_off(krow, 2 * kq + c);
+                *reinterpret_cast<uint4*>(smem + OFF_VH + off) = make_uint4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<uint4*>(smem + OFF_VL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+        }
         tc::fence_proxy_async_smem();
         tc::tc_fence_before();
         __syncthreads();
@@ -303,43 +369,53 @@ __global__ void __launch_bounds__(THREADS, 2)
             const uint32_t vh = tc::smem_u32(smem + OFF_VH);
 #pragma unroll
             for (int ks = 0; ks < KB / 16; ++ks) {
-                const uint32_t ko = ks * 32;
-                tc::mma_f16(tmem + 128, tc::desc_sw128(ph + ko), tc::desc_sw128(vh + ko), idesc_pv2, ks > 0 ? 1u : 0u);
-                tc::mma_f16(tmem + 128, tc::desc_sw128(pl + ko), tc::desc_sw128(vh + ko), idesc_pv, 1u);
+                const uint32_t ko = ks * 32;           // 16 keys of P's K-major rows
+                const uint32_t vo = ks * 16 * 128;     // 16 key rows of V (two 8-row groups)
+                const uint64_t dv = tc::desc_sw128_mn(vh + vo, OFF_VL - OFF_VH);
+                tc::mma_f16(tmem + 128, tc::desc_sw128(ph + ko), dv, idesc_pv2, ks > 0 ? 1u : 0u);
+                tc::mma_f16(tmem + 128, tc::desc_sw128(pl + ko), dv, idesc_pv, 1u);
             }
             tc::mma_commit(bar_pv);
         }
+        // the next block's K conversion and S MMAs run while this block's PV MMAs do (S and PV
+        // accumulate in disjoint TMEM columns)
+        if (kb + 1 < nkb) {
+            ek = convert_k(kb + 1);
+            issue_s();
+        }
         ok = tc::mbar_wait_spin(bar_pv, (uint32_t)(kb & 1), err) && ok;
         tc::tc_fence_after();
+        if (tid == 0 && kb + 1 < nkb) fetch(bar_v, OFF_VH, Vc, kb + 1);  // the V area is free now
         atr_stamp(trace, 5 + 4 * kb);
-        float pv[HD];
+        float pv[32];
         {
             float u[32];
-            tc::tmem_ld32x2(t_lane + 128, t_lane + 128 + HD, *reinterpret_cast<float(*)[32]>(pv), u);
+            tc::tmem_ld32x2(t_lane + 128 + 32 * half, t_lane + 128 + HD + 32 * half, pv, u);
 #pragma unroll
             for (int j = 0; j < 32; ++j) pv[j] += u[j];
-            tc::tmem_ld32x2(t_lane + 160, t_lane + 160 + HD, *reinterpret_cast<float(*)[32]>(pv + 32), u);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) pv[32 + j] += u[j];
         }
         const float pv_unscale = pow2f(-14 - ev);
 #pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha, pv[i] * pv_unscale);
+        for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], alpha, pv[i] * pv_unscale);
     }
-    // ---- out = O / l (fp32 and the fp16 hi/lo copy for the c_proj GEMM) ----
+    // ---- out = O / l, l the sum of both halves' shares (fp32 and the fp16 hi/lo copy for the
+    // c_proj GEMM) ----
+    xch[half * QT + r] = l;
+    __syncthreads();
+    l = xch[r] + xch[QT + r];
     if (qvalid && ok) {
-        const size_t base = (size_t)(tile.row0 + qpos) * ldo + head * HD;
+        const size_t base = (size_t)(tile.row0 + qpos) * ldo + head * HD + half * 32;
         const float inv = 1.0f / l;
 #pragma unroll
-        for (int i = 0; i < HD; i += 4) {
-            float r[4];
+        for (int i = 0; i < 32; i += 4) {
+            float rr[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) r[j] = o[i + j] * inv;
-            *reinterpret_cast<float4*>(out + base + i) = make_float4(r[0], r[1], r[2], r[3]);
+            for (int j = 0; j < 4; ++j) rr[j] = o[i + j] * inv;
+            *reinterpret_cast<float4*>(out + base + i) = make_float4(rr[0], rr[1], rr[2], rr[3]);
             if (ohi) {
                 __half h[4], lo[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) split_hl(r[j], h[j], lo[j]);
+                for (int j = 0; j < 4; ++j) split_hl(rr[j], h[j], lo[j]);
                 *reinterpret_cast<uint2*>(ohi + base + i) = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
                 *reinterpret_cast<uint2*>(olo + base + i) = make_uint2(pack_h2(lo[0], lo[1]), pack_h2(lo[2], lo[3]));
             }

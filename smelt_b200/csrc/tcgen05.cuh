@@ -260,6 +260,19 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// MN-major operand with the 128-byte swizzle: rows of 64 fp16 along M/N (one swizzle atom wide),
+// 8-row groups along K 1024 bytes apart (SBO), further 64-wide atoms along M/N lbo_bytes apart.
+// The same bytes as a K-major tile whose rows run along K.
+__device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t smem_addr, uint32_t lbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
     return (1u << 4)                       // D = f32
            | (0u << 7) | (0u << 10)        // A, B = f16
@@ -267,6 +280,9 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
            | ((uint32_t)(N >> 3) << 17)    // N
            | ((uint32_t)(M >> 4) << 24);   // M
 }
+
+// As idesc_f16_f32 with B MN-major (bit 16).
+__host__ __device__ constexpr uint32_t idesc_f16_f32_bmn(int M, int N) { return idesc_f16_f32(M, N) | (1u << 16); }
 
 }  // namespace tc
 }  // namespace gpt2q
