@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(THREADS, 2)
             float rr[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) rr[j] = o[i + j] * inv;
-            *reinterpret_cast<float4*>(out + base + i) = make_float4(rr[0], rr[1], rr[2], rr[3]);
+            if (out) *reinterpret_cast<float4*>(out + base + i) = make_float4(rr[0], rr[1], rr[2], rr[3]);
             if (ohi) {
                 __half h[4], lo[4];
 #pragma unroll

@@ -83,7 +83,7 @@ __device__ __forceinline__ void epi_apply(const Epi& e, int m, int n, float acc)
             if (e.bias) v += e.bias[n];
             const float gv = gelu_tanh(v);
             const size_t o = (size_t)m * e.ldo + n;
-            e.out[o] = gv;
+            if (e.out) e.out[o] = gv;  // null: the consumer reads only the hi/lo pair
             if (e.out_hi) {
                 const __half h = __float2half_rn(gv);
                 e.out_hi[o] = h;

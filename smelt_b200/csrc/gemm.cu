@@ -242,7 +242,7 @@ __device__ __forceinline__ void epi_chunk(const Epi& e, int nn, bool row_ok, con
                 const float gv = gelu_tanh(v);
                 const size_t o = (size_t)(mbase + j * mstep) * e.ldo + nn;
                 if (ok[j]) {
-                    e.out[o] = gv;
+                    if (e.out) e.out[o] = gv;  // null: the consumer reads only the hi/lo pair
                     if (e.out_hi) {
                         const __half h = __float2half_rn(gv);
                         e.out_hi[o] = h;

@@ -413,7 +413,7 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
                 break;
             case EPI_GELU: {
                 const float gv = gelu_tanh(x);
-                e.out[o] = gv;
+                if (e.out) e.out[o] = gv;  // null: the consumer reads only the hi/lo pair
                 if (e.out_hi) {
                     const __half h = __float2half_rn(gv);
                     e.out_hi[o] = h;
@@ -510,9 +510,13 @@ bool plan(const QW& w, int M, Plan& p, bool ln) {
     const int G = w.cols / 32;
     const int NB = (M + 7) / 8;
     const int sms = num_sms();
-    // whole rows per CTA (one bulk copy per operand) unless that leaves three quarters of the SMs
-    // idle or does not fit
-    int S = tiles >= sms / 4 ? 1 : std::max(1, std::min({MMA_MAX_SPLITS, (sms - 8 + tiles - 1) / tiles, G / 2}));
+    // whole rows per CTA (one bulk copy per operand) unless that leaves more than 1 - 1 / F of the
+    // SMs idle (F = 4; GPT2Q_MMA_SPLIT_F overrides it for tuning) or does not fit
+    static const int F = [] {
+        const char* e = std::getenv("GPT2Q_MMA_SPLIT_F");
+        return e ? std::max(1, std::atoi(e)) : 4;
+    }();
+    int S = tiles >= sms / F ? 1 : std::max(1, std::min({MMA_MAX_SPLITS, (sms - 8 + tiles - 1) / tiles, G / 2}));
     for (; S <= MMA_MAX_SPLITS && S <= G; ++S) {
         const int gps = (G + S - 1) / S;
         const int Sx = (G + gps - 1) / gps;  // no empty split

@@ -147,9 +147,9 @@ __global__ void __launch_bounds__(128) k_layernorm(const float* x, int ldx, cons
         for (int e = 0; e < VEC; ++e) o[e] = (v[j][e] - mean) * rstd * gg[j][e] + bb[j][e];
         const int i0 = (lane + 32 * j) * VEC;
         if (VEC == 4) {
-            *reinterpret_cast<float4*>(yr + i0) = vec_make4(o);
+            if (y) *reinterpret_cast<float4*>(yr + i0) = vec_make4(o);
         } else {
-            *reinterpret_cast<float2*>(yr + i0) = make_float2(o[0], o[1]);
+            if (y) *reinterpret_cast<float2*>(yr + i0) = make_float2(o[0], o[1]);
         }
         if (yhi) {
             __half h[VEC], l[VEC];
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(128) k_layernorm_any(const float* x, int ldx,
     const float rstd = __frcp_rn(sqrtf(warp_sum(q) / (float)d + eps));
     for (int i = lane; i < d; i += 32) {
         const float o = (xr[i] - mean) * rstd * g[i] + b[i];
-        y[(size_t)warp * ldy + i] = o;
+        if (y) y[(size_t)warp * ldy + i] = o;
         if (yhi) split_hl(o, yhi[(size_t)warp * ldy + i], ylo[(size_t)warp * ldy + i]);
     }
 }
@@ -632,7 +632,7 @@ __global__ void __launch_bounds__(AD_WARPS * 32) k_attn_decode(const float* q, i
         }
         const float r = O / L;
         const size_t o = (size_t)b * ldo + head * AD_HD + threadIdx.x;
-        out[o] = r;
+        if (out) out[o] = r;
         if (ohi) split_hl(r, ohi[o], olo[o]);
     }
 }
@@ -737,7 +737,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill(const float* q, int ldq, K
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
             const float r = o[i] * inv;
-            out[base + i] = r;
+            if (out) out[base + i] = r;
             if (ohi) split_hl(r, ohi[base + i], olo[base + i]);
         }
     }

@@ -434,6 +434,12 @@ bool takes_mma(const gpt2q_handle* H, const Linear& L, const In& X, int M, bool 
     return X.hi && H->mma_on && M >= H->mma_min_m && M <= MMA_MAX_M && X.ld % 8 == 0 && mma_fits(L.w, M, ln);
 }
 
+// The linear reads the fp32 copy of its activations only on the CUDA-core path; their producer
+// (LayerNorm, attention, the c_fc GELU epilogue) skips that copy otherwise.
+bool reads_f32(const gpt2q_handle* H, const Linear& L, const In& X, int M) {
+    return !(X.hi && (takes_mma(H, L, X, M, false) || H->gemm.usable(L.w, M)));
+}
+
 // With `ln` the warp-level kernel completes the LayerNorm folded into it (the caller checked
 // ln_fusable).
 int linear(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int M, const Epi& e,
@@ -526,7 +532,8 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     const bool tp = H->tp_size > 1;
     if (!(tp && layer > 0) && !fuse1)
         RUN("layernorm", (double)M * d * 8,
-            launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln1_g, Lw.ln1_b, d, eps, M, H->stream));
+            launch_layernorm(H->x, d, nullptr, reads_f32(H, Lw.attn, hin, M) ? H->h : nullptr, d, H->h_hi, H->h_lo,
+                             Lw.ln1_g, Lw.ln1_b, d, eps, M, H->stream));
     int rc = linear(H, "linear_qkv", Lw.attn, hin, M, epi_qkv(H, layer, slot, pos, Lw.attn.bias), fuse1 ? &ln1 : nullptr);
     if (rc) return rc;
     rc = attn_fn(layer);
@@ -548,9 +555,10 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     if (rc) return rc;
     if (!tp && !fuse2)
         RUN("layernorm", (double)M * d * 8,
-            launch_layernorm(H->x, d, nullptr, H->h, d, H->h_hi, H->h_lo, Lw.ln2_g, Lw.ln2_b, d, eps, M, H->stream));
+            launch_layernorm(H->x, d, nullptr, reads_f32(H, Lw.fc, hin, M) ? H->h : nullptr, d, H->h_hi, H->h_lo,
+                             Lw.ln2_g, Lw.ln2_b, d, eps, M, H->stream));
     {
-        Epi e = epi_store(H->f, H->fc_local, Lw.fc.bias);
+        Epi e = epi_store(reads_f32(H, Lw.mproj, fin, M) ? H->f : nullptr, H->fc_local, Lw.fc.bias);
         e.kind = EPI_GELU;
         e.out_hi = H->f_hi;
         e.out_lo = H->f_lo;
@@ -596,9 +604,11 @@ int enqueue_decode(gpt2q_handle* H, int B) {
     for (int b = 0; b < B && b < (int)H->hpos.size(); ++b) kv_bytes += 2.0 * (H->hpos[b] + 1) * H->d_local * 4;
     for (int l = 0; l < H->cfg.n_layer; ++l) {
         int rc = block(H, l, B, H->d_slot, H->d_pos, [&](int layer) {
+            const In ain{H->att, H->att_hi, H->att_lo, H->d_local};
+            float* att32 = reads_f32(H, H->layers[layer].proj, ain, B) ? H->att : nullptr;
             RUN("attn_decode", kv_bytes + (double)B * H->d_local * 8,
                 launch_attn_decode(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->d_slot,
-                                   H->d_pos, H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, B, scale,
+                                   H->d_pos, att32, H->att_hi, H->att_lo, H->d_local, H->H_local, B, scale,
                                    H->kerr, H->stream));
             return GPT2Q_OK;
         });
@@ -803,15 +813,17 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
     RUN("embed", (double)M * d * 6, launch_embed(H->wte.w, H->wpe.w, H->p_tok, H->p_pos, H->x, d, M, H->stream));
     for (int l = 0; l < H->cfg.n_layer; ++l) {
         rc = block(H, l, M, H->p_slot, H->p_pos, [&](int layer) {
+            const In ain{H->att, H->att_hi, H->att_lo, H->d_local};
+            float* att32 = reads_f32(H, H->layers[layer].proj, ain, M) ? H->att : nullptr;
             if (attn_tc)
                 RUN("attn_prefill_tc", kv_bytes + (double)M * H->d_local * 8,
                     launch_attn_prefill_tc(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->p_tiles,
-                                           nt, H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, H->gemm.err,
+                                           nt, att32, H->att_hi, H->att_lo, H->d_local, H->H_local, H->gemm.err,
                                            H->stream));
             else
                 RUN("attn_prefill", kv_bytes + (double)M * H->d_local * 8,
                     launch_attn_prefill(H->qb, H->d_local, H->kv, (size_t)layer * H->kv.layer_stride, H->p_tiles, nt,
-                                        H->att, H->att_hi, H->att_lo, H->d_local, H->H_local, scale, H->stream));
+                                        att32, H->att_hi, H->att_lo, H->d_local, H->H_local, scale, H->stream));
             return GPT2Q_OK;
         });
         if (rc) return rc;
