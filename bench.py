@@ -393,7 +393,9 @@ def measure_decode(args, name: str, wl, world: int, rank: int, local: int, dev) 
     g = Gpu(pk, device=local, max_seqs=n_local, max_tokens=max(8192, max(p.size for p in prompts)))
     stream = torch.cuda.Stream(device=dev)
     g.set_stream(stream.cuda_stream)
-    fill = max(int(stagger(n_local, span, k1).max()) - 1, max(args.warmup, 3))
+    # every chunk of the timed region starts from offsets <= span - 1 (a shorter last chunk
+    # staggers further in), so the fill decodes the whole span up to that
+    fill = max(span - 2, max(args.warmup, 3))
     run = DecodeRun(g, prompts, span, fill)
     barrier(world)
     if args.profile_one_step:
