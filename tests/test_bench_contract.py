@@ -79,3 +79,19 @@ def test_staggered_offsets_cover_the_span(n, span, k):
     assert abs(timed.mean() - span / 2) <= 1.0  # the middle of the decode offsets 0..span-1
     with pytest.raises(ValueError):
         bench.stagger(n, span, span)
+
+
+@pytest.mark.parametrize("n,span,steps", [(1, 64, 100), (1, 64, 20), (32, 128, 100), (256, 256, 100), (5, 10, 23)])
+def test_every_timed_chunk_starts_inside_the_fill(n, span, steps):
+    """The timed region runs `steps` decode steps in chunks of at most span - 1, each from a
+    rewind to staggered offsets; a shorter last chunk staggers further in. Every rewind feeds
+    the token decoded at offset o - 1, which the untimed fill must hold."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    k1 = min(steps, span - 1)
+    chunks = [k1] * (steps // k1) + ([steps % k1] if steps % k1 else [])
+    fill = max(span - 2, 3)  # as measure_decode
+    for k in chunks:
+        off = bench.stagger(n, span, k)
+        assert 1 <= off.min() and off.max() - 1 <= fill and off.max() + k - 1 <= span - 1
