@@ -1161,9 +1161,24 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
     const WeightTc& wt = wi->second;
     const int K = w.cols;
     const bool presplit = wt.has_split && M >= p.presplit_min_m;
-    const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
-    const int m_tiles = (M + BN - 1) / BN;
+    // tokens per tile; GPT2Q_TC_BN_MAX caps it (tuning)
+    static const int bn_max = [] {
+        const char* e = std::getenv("GPT2Q_TC_BN_MAX");
+        const int v = e ? std::atoi(e) : 256;
+        return v >= 256 ? 256 : (v >= 128 ? 128 : (v >= 64 ? 64 : 32));
+    }();
     const int n_tiles = (w.rows + BM - 1) / BM;
+    int BN = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
+    if (M > 64 && !presplit && n_tiles * ((M + BN - 1) / BN) < 120) {
+        // 65..256 tokens on raw weights, too few tiles for a wave: the wide tiles would split K
+        // and exchange 64-128 KB partials per CTA. Measured on GPT-2 small at 256 tokens (µs per
+        // launch, tile width 256 -> chosen): qkv 15.2 -> 14.4 and c_fc 28.2 -> 17.1 with 32-token
+        // tiles (a wave of tiles, no split), attn c_proj 12.3 -> 9.0 and mlp c_proj 15.1 -> 12.3
+        // with 128-token tiles (smaller partials); the tied head (393 x 1 tiles) keeps 256.
+        BN = n_tiles * ((M + 31) / 32) >= 120 ? 32 : std::min(BN, 128);
+    }
+    BN = std::min(bn_max, BN);
+    const int m_tiles = (M + BN - 1) / BN;
     const int nkb = (K + BK - 1) / BK;
     int splits = 1, kb_per = nkb;
     const int tiles = m_tiles * n_tiles;
