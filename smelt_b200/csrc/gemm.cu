@@ -1015,6 +1015,185 @@ cudaError_t launch_bn(int BN, const CUtensorMap& tw, const CUtensorMap& twlo, co
     }
 }
 
+// ---------------------------------------------------------------- int8 lm head for decode batches
+// The tied head over 16..64 tokens on kind::i8. k_head_pieces splits the ln_f output of every
+// token and 32-group exactly into three int8 pieces, x = 2^-S (p0 + p1 2^-7 + p2 2^-14) + r with
+// |r| <= 2^-20 of the group's largest |x|, laid out as B operands. The int8 weights enter as they
+// are stored, so one MMA of N = 3 MP per group gives the exact integer dot products of 128 rows
+// with every piece of every token (four f16 MMAs per group on the hi/lo path). Groups carry
+// their own scales (f16 per row for W, 2^-S per token for x), so each group's product lands in
+// one of two TMEM buffers and the epilogue warps fold it in, v = d0 + d1 2^-7 + d2 2^-14,
+// acc += (v 2^-S) s_w, while the next group's MMA runs.
+constexpr int HI_RS = 4;  // raw weight stages of 128 rows x 64 bytes (two groups each)
+
+template <int MP>
+struct HeadCfg {
+    static constexpr int N = 3 * MP;          // MMA columns: piece-major, then token
+    static constexpr int B_GROUP = N * 32;    // bytes of one group's pieces
+    static constexpr int A_STAGE = BM * 64;
+    static constexpr int OFF_B = HI_RS * A_STAGE;
+    static constexpr uint32_t TMEM_COLS = N <= 128 ? 256 : 512;  // two buffers of N columns
+    static size_t smem(int G) {
+        return (size_t)OFF_B + (size_t)G * B_GROUP + (size_t)MP * G * 4 + (2 * HI_RS + 5) * 8 + 16 + 1024;
+    }
+};
+
+template <int MP>
+__global__ void __launch_bounds__(THREADS, MP == 32 ? 2 : 1)
+    k_head_i8(const __grid_constant__ CUtensorMap tm_w, const uint8_t* __restrict__ pieces,
+              const float* __restrict__ xscale, QW w, int M, float* __restrict__ out, int ldo, int* err) {
+    using C = HeadCfg<MP>;
+    extern __shared__ __align__(1024) uint8_t smem_raw_[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw_) + 1023) & ~uintptr_t(1023));
+    const int G = w.cols / 32, nkb = G / 2;
+    float* sxs = reinterpret_cast<float*>(smem + C::OFF_B + (size_t)G * C::B_GROUP);  // [MP][G]: 2^-S
+    uint64_t* full = reinterpret_cast<uint64_t*>(sxs + ((MP * G + 1) & ~1));
+    uint64_t* empty = full + HI_RS;
+    uint64_t* xbar = empty + HI_RS;  // pieces and scales landed
+    uint64_t* mfull = xbar + 1;      // [2] a group's product is in TMEM buffer b
+    uint64_t* tempty = mfull + 2;    // [2] the epilogue has read buffer b
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BM;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < HI_RS; ++i) {
+            tc::mbar_init(&full[i], 1);
+            tc::mbar_init(&empty[i], 1);
+        }
+        tc::mbar_init(xbar, 1);
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&mfull[b], 1);
+            tc::mbar_init(&tempty[b], 128);
+        }
+        tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    tc::pdl_trigger();  // after the TMEM allocation (see k_linear_tc)
+
+    if (warp == 0) {
+        // ---------------- weight tiles: 64 bytes of K (two groups) x 128 rows per stage ----------------
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_w);
+            int issued = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int st = kb % HI_RS, use = kb / HI_RS;
+                if (!tc::mbar_wait_spin(&empty[st], (use & 1) ^ 1, err)) break;
+                tc::mbar_arrive_expect_tx(&full[st], C::A_STAGE);
+                tc::tma_load_2d(smem + st * C::A_STAGE, &tm_w, kb * 64, n0, &full[st]);
+                issued = kb + 1;
+            }
+            for (int kb = (issued > HI_RS ? issued - HI_RS : 0); kb < issued; ++kb)
+                tc::mbar_wait(&full[kb % HI_RS], (kb / HI_RS) & 1, err);  // nothing in flight at exit
+        }
+    } else if (warp == 6) {
+        // ---------------- the pieces and scales of every token (written by k_head_pieces) ----------------
+        if (lane == 0) {
+            tc::pdl_wait();
+            const uint32_t pb = (uint32_t)G * C::B_GROUP, sb = (uint32_t)(MP * G * 4);
+            tc::mbar_arrive_expect_tx(xbar, pb + sb);
+            tc::bulk_load_1d(smem + C::OFF_B, pieces, pb, xbar);
+            tc::bulk_load_1d(sxs, xscale, sb, xbar);
+            tc::mbar_wait(xbar, 0, err);
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer: one kind::i8 MMA per group ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_s8_s32(BM, C::N);
+            bool ok = tc::mbar_wait_spin(xbar, 0, err);
+            for (int g = 0; g < G && ok; ++g) {
+                const int kb = g >> 1, st = kb % HI_RS, use = kb / HI_RS;
+                const int b = g & 1, bu = g >> 1;
+                if ((g & 1) == 0) ok = tc::mbar_wait_spin(&full[st], use & 1, err);
+                ok = ok && tc::mbar_wait_spin(&tempty[b], (bu & 1) ^ 1, err);
+                if (!ok) break;
+                tc::tc_fence_after();
+                const uint64_t ad = tc::desc_sw64(tc::smem_u32(smem + st * C::A_STAGE) + (uint32_t)(g & 1) * 32);
+                const uint64_t bd = tc::desc_noswz(tc::smem_u32(smem + C::OFF_B + (size_t)g * C::B_GROUP), 128, 256);
+                tc::mma_i8(tmem + (uint32_t)(b * C::N), ad, bd, idesc, 0u);
+                tc::mma_commit(&mfull[b]);
+                if ((g & 1) == 1) tc::mma_commit(&empty[st]);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 1-4): one weight row per thread ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const int nn = n0 + row;
+        const bool row_ok = nn < w.rows;
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+        const __half* srow = w.s + (size_t)(row_ok ? nn : 0) * w.sstride;
+        float acc[MP];
+#pragma unroll
+        for (int t = 0; t < MP; ++t) acc[t] = 0.f;
+        // polled waits: a suspended try_wait resumes microseconds late, once per group here
+        bool ok = tc::mbar_wait_spin(xbar, 0, err);
+        float sw = row_ok ? __half2float(srow[0]) : 0.f;
+        for (int g = 0; g < G && ok; ++g) {
+            const int b = g & 1, bu = g >> 1;
+            const float sw_next = (row_ok && g + 1 < G) ? __half2float(srow[g + 1]) : 0.f;
+            ok = tc::mbar_wait_spin(&mfull[b], bu & 1, err);
+            if (!ok) break;
+            tc::tc_fence_after();
+            float v[MP];
+#pragma unroll
+            for (int c = 0; c < MP / 32; ++c) {
+                float d0[32], d1[32], d2[32];
+                tc::tmem_ld32x2(taddr + b * C::N + c * 32, taddr + b * C::N + MP + c * 32, d0, d1);
+                tc::tmem_ld32(taddr + b * C::N + 2 * MP + c * 32, d2);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float p0 = (float)__float_as_int(d0[j]);
+                    const float p1 = (float)__float_as_int(d1[j]);
+                    const float p2 = (float)__float_as_int(d2[j]);
+                    v[c * 32 + j] = fmaf(p2, 1.0f / 16384.0f, fmaf(p1, 1.0f / 128.0f, p0));
+                }
+            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&tempty[b]);
+#pragma unroll
+            for (int t = 0; t < MP; ++t) acc[t] = fmaf(v[t] * sxs[t * G + g], sw, acc[t]);
+            sw = sw_next;
+        }
+        if (row_ok && ok) {
+#pragma unroll
+            for (int t = 0; t < MP; ++t)
+                if (t < M) out[(size_t)t * ldo + nn] = acc[t];
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+template <int MP>
+cudaError_t launch_head_i8_mp(const CUtensorMap& tw, const uint8_t* pieces, const float* xscale, const QW& w, int M,
+                              float* out, int ldo, int* err, cudaStream_t st) {
+    auto kern = k_head_i8<MP>;
+    const size_t smem = HeadCfg<MP>::smem(w.cols / 32);
+    if (smem > 232448) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((w.rows + BM - 1) / BM);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, tw, pieces, xscale, w, M, out, ldo, err);
+}
+
 }  // namespace
 
 struct WeightTc {
@@ -1230,6 +1409,20 @@ cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, in
     }
     if (w.atom == ATOM_Q8) return launch_bn<ATOM_Q8, false>(BN, wt.raw, wt.raw, *xh, *xl, tp, grid, st);
     return launch_bn<ATOM_Q4, false>(BN, wt.raw, wt.raw, *xh, *xl, tp, grid, st);
+}
+
+bool head_i8_usable(const GemmPlan& p, const QW& w, int M) {
+    if (!p.enabled || w.atom != ATOM_Q8 || M < 1 || M > 64 || w.cols % 64 != 0) return false;
+    if (p.state->w.find(w.q) == p.state->w.end()) return false;
+    return (M <= 32 ? HeadCfg<32>::smem(w.cols / 32) : HeadCfg<64>::smem(w.cols / 32)) <= 232448;
+}
+
+cudaError_t launch_head_i8(const GemmPlan& p, const QW& w, const uint8_t* pieces, const float* xscale, int M,
+                           float* out, int ldo, cudaStream_t st) {
+    if (!head_i8_usable(p, w, M)) return cudaErrorInvalidValue;
+    const WeightTc& wt = p.state->w.find(w.q)->second;
+    if (M <= 32) return launch_head_i8_mp<32>(wt.raw, pieces, xscale, w, M, out, ldo, p.err, st);
+    return launch_head_i8_mp<64>(wt.raw, pieces, xscale, w, M, out, ldo, p.err, st);
 }
 
 std::string gemm_trace_json(const GemmPlan& p) {

@@ -56,6 +56,11 @@ void gemm_destroy(GemmPlan& p);
 int gemm_register_weight(GemmPlan& p, const QW& w, float max_abs_w, bool presplit, cudaStream_t st);
 cudaError_t launch_linear_tc(const GemmPlan& p, const QW& w, const XSplit& x, int M, const Epi& e,
                              cudaStream_t st);
+// The tied lm head over 1..64 tokens on kind::i8 (int8 weights registered with this plan, K a
+// multiple of 64): pieces / xscale as written by launch_head_pieces with MP = 32 (M <= 32) or 64.
+bool head_i8_usable(const GemmPlan& p, const QW& w, int M);
+cudaError_t launch_head_i8(const GemmPlan& p, const QW& w, const uint8_t* pieces, const float* xscale, int M,
+                           float* out, int ldo, cudaStream_t st);
 // Phase stamps of the launch selected by GPT2Q_TC_TRACE ("" when none), as JSON.
 std::string gemm_trace_json(const GemmPlan& p);
 // Reads and clears the device error word (0 = no error). Synchronises `st`.

@@ -828,6 +828,61 @@ __global__ void k_dequant(QW w, float* __restrict__ out) {
         out[i] = deq_elem(w, (int)(i / w.cols), (int)(i % w.cols));
 }
 
+// The ln_f output of tokens 0..MP-1 split per 32-group into three exact int8 pieces for the
+// kind::i8 lm head (gemm.cu k_head_i8): x = 2^-S (p0 + p1 2^-7 + p2 2^-14) + r, with S such that
+// the group's largest |x| scales into [32, 64), so every piece is an integer in [-64, 64] and
+// |r| <= 2^-15 2^-S <= 2^-20 of that largest |x|. Every step is exact in fp32 (scaling by powers of
+// two, rounding to integers, subtracting values of equal exponent range). Tokens M..MP-1 get zero
+// pieces. B operand layout of group g: row n = p MP + t, 32 bytes of K, in 8-row x 16-byte core
+// matrices: byte (n, e) at g 3 MP 32 + (n / 8) 256 + (e / 16) 128 + (n % 8) 16 + e % 16.
+// One warp per (token, group); xscale[t][g] = 2^-S.
+__global__ void __launch_bounds__(256) k_head_pieces(const float* h, int ldh, int M, int K, int MP,
+                                                      int8_t* __restrict__ pieces, float* __restrict__ xscale) {
+    tc::pdl_trigger();
+    tc::pdl_wait();
+    const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    const int G = K / 32;
+    if (warp >= MP * G) return;
+    const int t = warp / G, g = warp - t * G;
+    const float x = t < M ? __ldcg(h + (size_t)t * ldh + 32 * g + lane) : 0.f;
+    const float m = warp_max(fabsf(x));
+    float up = 0.f, down = 0.f;  // 2^S, 2^-S
+    if (m >= 1e-30f && m <= 3e38f) {
+        const int S = 5 - (((__float_as_int(m) >> 23) & 0xff) - 127);
+        up = __int_as_float((S + 127) << 23);
+        down = __int_as_float((127 - S) << 23);
+    }
+    const float y = x * up;
+    const float p0 = rintf(y);
+    const float r1 = (y - p0) * 128.0f;
+    const float p1 = rintf(r1);
+    const float p2 = rintf((r1 - p1) * 128.0f);
+    const float pv[3] = {p0, p1, p2};
+    int8_t* base = pieces + (size_t)g * 3 * MP * 32 + (lane >> 4) * 128 + (lane & 15);
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        const int n = p * MP + t;
+        base[(n >> 3) * 256 + (n & 7) * 16] = (int8_t)(int)pv[p];
+    }
+    if (lane == 0) xscale[(size_t)t * G + g] = down;
+}
+
+cudaError_t launch_head_pieces(const float* h, int ldh, int M, int K, int MP, int8_t* pieces, float* xscale,
+                               cudaStream_t st) {
+    if (M < 1 || M > MP || K % 32 != 0) return cudaErrorInvalidValue;
+    const size_t threads = (size_t)MP * (K / 32) * 32;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_head_pieces, h, ldh, M, K, MP, pieces, xscale);
+}
+
 // Constants of a LayerNorm folded into the linear after it, per output row n (in double, from the
 // exactly dequantised weights): c1 = sum_k W[n][k] g[k], c2b = sum_k W[n][k] b[k] + bias[n].
 __global__ void k_ln_fold(const QW w, const float* __restrict__ g, const float* __restrict__ b,

@@ -70,6 +70,10 @@ cudaError_t launch_argmax(const float* logits, int V, int ld, int B, unsigned lo
 // Programmatic dependent launch on/off (GPT2Q_NO_PDL=1 disables it).
 bool pdl_enabled();
 cudaError_t launch_dequant(const QW& w, float* out, cudaStream_t st);
+// ln_f rows 0..M-1 of h ([M][ldh], K wide) as the int8 pieces and 2^-S scales of the kind::i8 lm
+// head (gemm.h launch_head_i8), for MP = 32 or 64 token slots.
+cudaError_t launch_head_pieces(const float* h, int ldh, int M, int K, int MP, int8_t* pieces, float* xscale,
+                               cudaStream_t st);
 // c1[n] = sum_k W[n][k] g[k], c2b[n] = sum_k W[n][k] b[k] + bias[n] (bias may be null): the
 // constants of a LayerNorm folded into the linear W that follows it (computed in double).
 cudaError_t launch_ln_fold(const QW& w, const float* g, const float* b, const float* bias, float* c1, float* c2b,

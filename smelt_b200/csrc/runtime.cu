@@ -184,6 +184,12 @@ struct gpt2q_handle {
     // GPT2Q_LN_FUSE=0 at creation keeps the LayerNorm launches
     bool ln_fuse = true;
     float2* ln_stats = nullptr;
+    // the tied head on kind::i8 (int8 head weights) where the tcgen05 head does not run (fewer
+    // than its minimum of 16 rows): pieces of the ln_f output [d/32][3][64][32] and their scales
+    // [64][d/32]. GPT2Q_HEAD_I8 at creation: 0 = never, 2 = for every 1..64 rows (tests)
+    int head_i8 = 1;
+    int8_t* head_pieces = nullptr;
+    float* head_xscale = nullptr;
     MkPlan mk;      // persistent single-sequence decode
     TpComm* tp = nullptr;
 
@@ -586,6 +592,26 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
     return rc;
 }
 
+// The tied head over rows 0..M-1 of h into out (row stride vocab). Below the tcgen05 head's 16
+// rows it runs on kind::i8 over exact int8 pieces of h (int8 head weights), instead of the
+// CUDA-core GEMV: measured at 2 and 8 rows, 124 and 223 us -> 35 us per head. From 16 rows the
+// f16 hi/lo tile is faster (28.5 us at 32 rows against 36 us): each of the i8 path's 24 groups
+// per tile needs its own TMEM drain and scaling in the epilogue.
+int head(gpt2q_handle* H, int M, float* out) {
+    const int d = H->cfg.n_embd, V = H->cfg.vocab;
+    const bool want = H->head_i8 == 2 || (H->head_i8 == 1 && !H->gemm.usable(H->wte.w, M));
+    if (want && H->head_pieces && head_i8_usable(H->gemm, H->wte.w, M)) {
+        const int MP = M <= 32 ? 32 : 64;
+        RUN("head_pieces", (double)M * d * 4 + (double)MP * d * 3,
+            launch_head_pieces(H->h, d, M, d, MP, H->head_pieces, H->head_xscale, H->stream));
+        RUN("linear_head", (double)H->wte.weight_bytes + (double)M * V * 4,
+            launch_head_i8(H->gemm, H->wte.w, reinterpret_cast<const uint8_t*>(H->head_pieces), H->head_xscale, M,
+                           out, V, H->stream));
+        return GPT2Q_OK;
+    }
+    return linear(H, "linear_head", H->wte, In{H->h, H->h_hi, H->h_lo, d}, M, epi_store(out, V, nullptr));
+}
+
 // The published adapter, applied to `rows` rows of h after ln_f (gpu.rs:364-367).
 int apply_adapter(gpt2q_handle* H, int rows) {
     if (!H->adapter_on) return GPT2Q_OK;
@@ -619,8 +645,7 @@ int enqueue_decode(gpt2q_handle* H, int B) {
                          H->stream));
     int rc = apply_adapter(H, B);
     if (rc) return rc;
-    rc = linear(H, "linear_head", H->wte, In{H->h, H->h_hi, H->h_lo, d}, B,
-                    epi_store(H->logits, H->cfg.vocab, nullptr));
+    rc = head(H, B, H->logits);
     if (rc) return rc;
     RUN("argmax", (double)B * H->cfg.vocab * 4,
         launch_argmax(H->logits, H->cfg.vocab, H->cfg.vocab, B, H->best, H->d_next, H->d_genlog, H->d_pos,
@@ -836,7 +861,7 @@ int prefill_chunk(gpt2q_handle* H, const uint32_t* tokens, const int32_t* offs, 
     rc = apply_adapter(H, ns);
     if (rc) return rc;
     float* lg = H->logits + (size_t)s0 * H->cfg.vocab;
-    rc = linear(H, "linear_head", H->wte, In{H->h, H->h_hi, H->h_lo, d}, ns, epi_store(lg, H->cfg.vocab, nullptr));
+    rc = head(H, ns, lg);
     if (rc) return rc;
     RUN("argmax", (double)ns * H->cfg.vocab * 4,
         launch_argmax(lg, H->cfg.vocab, H->cfg.vocab, ns, H->best + s0, H->d_next + s0,
@@ -1155,6 +1180,15 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     if (const char* e = std::getenv("GPT2Q_MMA_MIN_M")) H->mma_min_m = std::max(1, std::atoi(e));
     if (H->mma_on) mma_init();
     if (const char* e = std::getenv("GPT2Q_LN_FUSE")) H->ln_fuse = e[0] != '0';
+    if (const char* e = std::getenv("GPT2Q_HEAD_I8")) H->head_i8 = std::atoi(e);
+    if (d % 32 == 0) {
+        const size_t pb = (size_t)(d / 32) * 3 * 64 * 32, sb = (size_t)64 * (d / 32) * 4;
+        H->head_pieces = H->dalloc<int8_t>(pb);
+        H->head_xscale = H->dalloc<float>(sb);
+        if (!H->head_pieces || !H->head_xscale || cudaMemset(H->head_pieces, 0, pb) != cudaSuccess ||
+            cudaMemset(H->head_xscale, 0, sb) != cudaSuccess)
+            return bail(GPT2Q_EOOM);
+    }
     H->ln_stats = H->dalloc<float2>((size_t)((d + 15) / 16) * MMA_MAX_M * 8);
 
     H->p_tok = H->dalloc<uint32_t>(M * 4);

@@ -260,6 +260,40 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// K-major operand with the 64-byte swizzle (TMA SWIZZLE_64B tiles): rows of 64 bytes, 8-row groups
+// 512 bytes apart.
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;           // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(512 >> 4) << 32;  // SBO: 8 rows x 64 B
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;           // SWIZZLE_64B
+    return d;
+}
+
+// K-major operand without swizzle: 8-row x 16-byte core matrices (rows 16 bytes apart), the next
+// 16 bytes of K lbo_bytes away, the next 8 rows sbo_bytes away.
+__device__ __forceinline__ uint64_t desc_noswz(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    return d;  // layout type 0: no swizzle
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::i8 (signed 8-bit operands, s32 accumulator).
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem), "l"(a_desc), "l"(b_desc),
+        "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // MN-major operand with the 128-byte swizzle: rows of 64 fp16 along M/N (one swizzle atom wide),
 // 8-row groups along K 1024 bytes apart (SBO), further 64-wide atoms along M/N lbo_bytes apart.
 // The same bytes as a K-major tile whose rows run along K.
@@ -279,6 +313,14 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
            | (0u << 15) | (0u << 16)       // both K-major
            | ((uint32_t)(N >> 3) << 17)    // N
            | ((uint32_t)(M >> 4) << 24);   // M
+}
+
+// kind::i8 instruction descriptor: signed 8-bit A and B, both K-major, s32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
+    return (2u << 4)                      // D = s32
+           | (1u << 7) | (1u << 10)       // A, B = signed 8-bit
+           | ((uint32_t)(N >> 3) << 17)   // N
+           | ((uint32_t)(M >> 4) << 24);  // M
 }
 
 // As idesc_f16_f32 with B MN-major (bit 16).
