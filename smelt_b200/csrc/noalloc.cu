@@ -1,21 +1,18 @@
 // gpt2q_argmax_noalloc: greedy argmax over device logits that allocates nothing.
 //
 // Some callers of this library cannot allocate device memory at the moment they need a
-// greedy pick: a serving loop that is being captured into a CUDA graph (an allocation
-// is not a stream operation and cannot be recorded into the graph), code that must not
-// stall the device (cudaMalloc / cudaFree can synchronise the whole device, which breaks
-// latency budgets of a running decode loop), and hosts whose device memory is owned by
-// another framework's pool, where a stray cudaMalloc can fail even though memory is
-// nominally free. For them this entry point runs the same two argmax kernels as the
+// greedy pick: code that must not stall the device (cudaMalloc / cudaFree can synchronise
+// the whole device, which breaks latency budgets of a running decode loop), and hosts whose
+// device memory is owned by another framework's pool, where a stray cudaMalloc can fail
+// even though memory is nominally free. For them this entry point runs the same two argmax kernels as the
 // decode path, but their per-row scratch slot lives in a fixed array compiled into the
 // library instead of a buffer allocated by a handle.
 //
 // Limits and caveats:
 //  - at most GPT2Q_NOALLOC_MAX_ROWS rows per call (8 KiB of scratch, held by every GPU
 //    that loads the library until the process exits); larger calls fail with GPT2Q_EARG;
-//  - the first call on a device looks up the array's device address (and every later call
-//    made outside a stream capture looks it up again); make that first call before any
-//    stream capture;
+//  - a call looks up the array's device address, except while `stream` reports an active
+//    capture, when it uses the address an earlier call found;
 //  - every call shares the one array: calls whose kernels overlap on the GPU (different
 //    streams without ordering between them) race and give wrong tokens. Serialise them.
 #include <cuda_runtime.h>
@@ -39,9 +36,9 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 unsigned long long* g_dev_ptr[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device. Looked up again on every call
-// made outside a stream capture (so a module reloaded after a device reset gets its new
-// address); a call during a capture uses the address cached by an earlier call.
+// Device address of the scratch array on the current device, looked up on every call (so a
+// module reloaded after a device reset gets its new address) except while the stream reports
+// an active capture, when the address an earlier call found is used.
 int scratch_for_current_device(cudaStream_t st, unsigned long long** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {

@@ -1,8 +1,7 @@
 """gpt2q_argmax_noalloc: the greedy argmax for callers that cannot allocate device memory.
 
-Callers capturing a decode loop into a CUDA graph, loops that must never stall the
-device on cudaMalloc/cudaFree, or code running under another framework's memory pool
-cannot let the library allocate scratch at call time. This entry point keeps its scratch
+Loops that must never stall the device on cudaMalloc/cudaFree, or code running under
+another framework's memory pool, cannot let the library allocate scratch at call time. This entry point keeps its scratch
 in a fixed array inside the library; the caller passes device logits in and gets device
 token ids out. The test checks it against the tokens the regular decode path returns,
 on two calls in a row (the shared scratch must come back clean after each call).
