@@ -58,8 +58,9 @@ static_assert(SMEM <= 232448 / 2 - 1024, "two CTAs per SM");
 constexpr uint32_t TMEM_COLS = 256;
 
 // Phase trace of one launch (GPT2Q_ATTN_TRACE set at the first launch): globaltimer stamps of
-// thread 0 of the first ATR_CTAS CTAs: start, Q staged, then per key block kb < 8: K/V staged,
-// S ready, P staged, PV ready.
+// thread 0 of the first ATR_CTAS CTAs: start, Q staged, then per key block kb < 8: iteration
+// start (its K converted, S issued), S ready, P and V staged, PV ready (the next block's K
+// converted and S issued meanwhile).
 constexpr int ATR_CTAS = 128, ATR_N = 2 + 4 * 8;
 __device__ unsigned long long g_attn_trace[ATR_CTAS * ATR_N];
 
