@@ -6,13 +6,13 @@
 // split-K exchange), not by HBM or the tensor pipe. mma.sync keeps operands and accumulators in
 // registers, so a CTA's warps can each take a sliver of K and meet in shared memory.
 //
-// Exactness (the same ~22 bits as the tcgen05 path): every weight w = q * s is split as
-// hi + lo in fp16 with hi = fp16(q * s') and lo = fma(q, s', -hi) = the exact residual, where
-// s' = s * 2^P is the group scale times a per-matrix power of two; both are computed in fp16
-// with one rounding (q is an exact fp16 integer, the residual has at most 7 significant bits on
-// the grid of ulp(s')). Activations arrive split the same way by their producer (x = x_hi + x_lo).
-// Each 16 x 8 x 16 step issues W_hi x_hi, W_hi x_lo and W_lo x_hi into fp32 accumulators; the
-// dropped W_lo x_lo is below 2^-22 of the product.
+// Exactness: the integer weights q (|q| <= 128) are exact fp16 values, and the activations
+// arrive from their producer as an fp16 pair x = x_hi + x_lo (~22 bits). For each 32-group a
+// warp issues q x_hi and q x_lo (products exact in the fp32 accumulators) and then adds s times
+// the group's sum to its fp32 accumulator, s the group's fp16 scale: one rounding per group, no
+// product dropped. Four 16 x 8 x 16 MMAs per group and 8 tokens; splitting q s into an fp16
+// hi/lo pair instead (three products, W_lo x_lo dropped) took six and was 4 % slower per decode
+// step at 32 sequences.
 //
 // K permutation: a dot product does not depend on the order of its terms, so the k-slots of an
 // mma fragment are fed any permutation of K, the same for both operands. Thread (g, t) of a warp
@@ -20,15 +20,18 @@
 // 4t..4t+3 and 16+4t..16+4t+3) and the matching 16 contiguous bytes of each token's activation
 // row, so both operands load as plain vectors with no shuffles.
 //
-// Work layout: grid (16-row tiles, S), clusters of the S CTAs of a tile. A CTA stages the
-// activations of its K range ([NB*8 tokens][K/S], hi and lo) by bulk copies, its warps take
-// consecutive group ranges of that range, and the warp partials meet in shared memory (fixed
-// order). With S > 1 the other CTAs of the cluster store their tile partials into CTA 0's shared
-// memory, and after one cluster barrier CTA 0 sums them in rank order and runs the epilogue, so
-// results do not depend on scheduling.
+// Work layout: grid (tile groups of T consecutive 16-row tiles, S), clusters of the S CTAs of a
+// tile group. A CTA stages the activations of its K range ([NB*8 tokens][K/S], hi and lo) by bulk
+// copies once for its T tiles; each tile is a team of warps / T warps taking consecutive group
+// ranges of that range, and a team's warp partials meet in shared memory (fixed order). With
+// S > 1 the other CTAs of the cluster store their partials into CTA 0's shared memory, and after
+// one cluster barrier CTA 0 sums them in rank order and runs the epilogue, so results do not
+// depend on scheduling. T > 1 serves matrices of more tiles than SMs, or whose one-tile layout
+// would need a second wave of CTAs (plan()).
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -62,46 +65,37 @@ __device__ __forceinline__ __half2 bytes_to_h2(uint32_t u, uint32_t sel, uint32_
     return __hsub2(u2h(__byte_perm(u, 0x64646464u, sel)), u2h(magic2));
 }
 
-// hi/lo split of two weights q * s' (see the file comment).
-__device__ __forceinline__ void split_w(__half2 q, __half2 s, uint32_t& hi, uint32_t& lo) {
-    const __half2 h = __hmul2(q, s);
-    hi = h2u(h);
-    lo = h2u(__hfma2(q, s, __hneg2(h)));
-}
-
-// A fragments (hi and lo, two k16 steps) of one 32-group from the thread's raw weight bytes of
-// rows g (ra) and g + 8 (rb): step 0 takes K 8t..8t+3 (int4: 4t..4t+3), step 1 K 8t+4..8t+7
-// (int4: 16+4t..16+4t+3). Register order of m16n8k16's A: {row g, slots 2t,2t+1},
+// A fragments (two k16 steps) of one 32-group as exact fp16 integers q, from the thread's raw
+// weight bytes of rows g (ra) and g + 8 (rb): step 0 takes K 8t..8t+3 (int4: 4t..4t+3), step 1
+// K 8t+4..8t+7 (int4: 16+4t..16+4t+3). Register order of m16n8k16's A: {row g, slots 2t,2t+1},
 // {row g+8, 2t,2t+1}, {row g, 2t+8,2t+9}, {row g+8, 2t+8,2t+9}.
 template <int ATOM>
-__device__ __forceinline__ void dequant_group(uint2 ra, uint2 rb, __half sa, __half sb, __half pre,
-                                              uint32_t (&hi)[2][4], uint32_t (&lo)[2][4]) {
-    const __half2 s0 = __half2half2(__hmul(sa, pre)), s1 = __half2half2(__hmul(sb, pre));
+__device__ __forceinline__ void dequant_q(uint2 ra, uint2 rb, uint32_t (&aq)[2][4]) {
     if constexpr (ATOM == ATOM_Q8) {
         const uint32_t m = 0x64806480u;  // 1152 = 1024 + 128
         const uint32_t a0 = ra.x ^ 0x80808080u, a1 = ra.y ^ 0x80808080u;
         const uint32_t b0 = rb.x ^ 0x80808080u, b1 = rb.y ^ 0x80808080u;
-        split_w(bytes_to_h2(a0, 0x4140u, m), s0, hi[0][0], lo[0][0]);
-        split_w(bytes_to_h2(b0, 0x4140u, m), s1, hi[0][1], lo[0][1]);
-        split_w(bytes_to_h2(a0, 0x4342u, m), s0, hi[0][2], lo[0][2]);
-        split_w(bytes_to_h2(b0, 0x4342u, m), s1, hi[0][3], lo[0][3]);
-        split_w(bytes_to_h2(a1, 0x4140u, m), s0, hi[1][0], lo[1][0]);
-        split_w(bytes_to_h2(b1, 0x4140u, m), s1, hi[1][1], lo[1][1]);
-        split_w(bytes_to_h2(a1, 0x4342u, m), s0, hi[1][2], lo[1][2]);
-        split_w(bytes_to_h2(b1, 0x4342u, m), s1, hi[1][3], lo[1][3]);
+        aq[0][0] = h2u(bytes_to_h2(a0, 0x4140u, m));
+        aq[0][1] = h2u(bytes_to_h2(b0, 0x4140u, m));
+        aq[0][2] = h2u(bytes_to_h2(a0, 0x4342u, m));
+        aq[0][3] = h2u(bytes_to_h2(b0, 0x4342u, m));
+        aq[1][0] = h2u(bytes_to_h2(a1, 0x4140u, m));
+        aq[1][1] = h2u(bytes_to_h2(b1, 0x4140u, m));
+        aq[1][2] = h2u(bytes_to_h2(a1, 0x4342u, m));
+        aq[1][3] = h2u(bytes_to_h2(b1, 0x4342u, m));
     } else {
         const uint32_t m = 0x64086408u;  // 1032 = 1024 + 8
         // ra.x: bytes 4t..4t+3 of row g's group; low nibbles are elements 4t+i, high 16+4t+i
         const uint32_t al = (ra.x & 0x0F0F0F0Fu) ^ 0x08080808u, ah = ((ra.x >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
         const uint32_t bl = (rb.x & 0x0F0F0F0Fu) ^ 0x08080808u, bh = ((rb.x >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
-        split_w(bytes_to_h2(al, 0x4140u, m), s0, hi[0][0], lo[0][0]);
-        split_w(bytes_to_h2(bl, 0x4140u, m), s1, hi[0][1], lo[0][1]);
-        split_w(bytes_to_h2(al, 0x4342u, m), s0, hi[0][2], lo[0][2]);
-        split_w(bytes_to_h2(bl, 0x4342u, m), s1, hi[0][3], lo[0][3]);
-        split_w(bytes_to_h2(ah, 0x4140u, m), s0, hi[1][0], lo[1][0]);
-        split_w(bytes_to_h2(bh, 0x4140u, m), s1, hi[1][1], lo[1][1]);
-        split_w(bytes_to_h2(ah, 0x4342u, m), s0, hi[1][2], lo[1][2]);
-        split_w(bytes_to_h2(bh, 0x4342u, m), s1, hi[1][3], lo[1][3]);
+        aq[0][0] = h2u(bytes_to_h2(al, 0x4140u, m));
+        aq[0][1] = h2u(bytes_to_h2(bl, 0x4140u, m));
+        aq[0][2] = h2u(bytes_to_h2(al, 0x4342u, m));
+        aq[0][3] = h2u(bytes_to_h2(bl, 0x4342u, m));
+        aq[1][0] = h2u(bytes_to_h2(ah, 0x4140u, m));
+        aq[1][1] = h2u(bytes_to_h2(bh, 0x4140u, m));
+        aq[1][2] = h2u(bytes_to_h2(ah, 0x4342u, m));
+        aq[1][3] = h2u(bytes_to_h2(bh, 0x4342u, m));
     }
 }
 
@@ -154,8 +148,8 @@ __device__ __forceinline__ float lane_sum(float v) {  // butterfly: the same ord
 
 template <int ATOM, int NB>
 __global__ void __launch_bounds__(MMA_MAX_WARPS * 32, 1)
-k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, int gps, int gpw, __half pre,
-             float post, int* err, unsigned long long* trace, Epi e, LnFold ln) {
+k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, int T, int gps, int gpw, int* err,
+             unsigned long long* trace, Epi e, LnFold ln) {
     constexpr int NC = NB * 8;
     constexpr int N_OUT = TILE * NC;
     constexpr int GB = (ATOM == ATOM_Q8) ? 32 : 16;  // payload bytes per row and group
@@ -166,7 +160,13 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int G = w.cols / 32;
-    const int tile = blockIdx.x, split = blockIdx.y, S = gridDim.y;
+    // T consecutive 16-row tiles per CTA, one team of nw / T warps each (left-over warps idle in
+    // the MMA phase); every team reads the same staged activations
+    const int tile0 = blockIdx.x * T, split = blockIdx.y, S = gridDim.y;
+    const int n_out = T * N_OUT;  // the CTA's outputs
+    const int wt = nw / T, team = warp / wt, wr = warp - team * wt;
+    const int mytile = tile0 + min(team, T - 1);
+    const bool active = team < T && mytile * TILE < w.rows;
     const int kg0 = split * gps, kg1 = min(G, kg0 + gps);
     // A CTA that covers whole activation rows stages them with one bulk copy per operand
     // (rows dense, stride ldx); otherwise one copy per token row at a bank-spread stride. One
@@ -183,14 +183,14 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
     const size_t staged_bytes = max((size_t)2 * NC * xs * 2, (size_t)nw * N_OUT * 4);
     float* recv = reinterpret_cast<float*>(smem_raw + staged_bytes);
     // folded LayerNorm: each token's mean and 1 / sqrt(var + eps)
-    float* smean = recv + (S > 1 ? (size_t)S * N_OUT : 0);
+    float* smean = recv + (S > 1 ? (size_t)S * n_out : 0);
     float* srstd = smean + NC;
-    const int g0 = min(kg1, kg0 + warp * gpw), g1 = min(kg1, g0 + gpw);
+    const int g0 = active ? min(kg1, kg0 + wr * gpw) : kg1, g1 = min(kg1, g0 + gpw);
 
     // ---- before the previous kernel finishes: this warp's first weights, the epilogue's bias ----
     uint2 wa[PF], wb[PF];
     __half ws_a[PF], ws_b[PF];
-    const int ra = min(tile * TILE + g, w.rows - 1), rb = min(tile * TILE + g + 8, w.rows - 1);
+    const int ra = min(mytile * TILE + g, w.rows - 1), rb = min(mytile * TILE + g + 8, w.rows - 1);
     const uint8_t* qa = w.q + (size_t)ra * w.qstride;
     const uint8_t* qb = w.q + (size_t)rb * w.qstride;
     auto load_slot = [&](int u, int gr) {
@@ -207,7 +207,8 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
 #pragma unroll
     for (int u = 0; u < PF; ++u)
         if (g0 + u < g1) load_slot(u, g0 + u);
-    // epilogue outputs of this thread: i = threadIdx.x + k * blockDim.x -> token i / 16, row i % 16
+    // epilogue outputs of this thread: i = threadIdx.x + k * blockDim.x -> tile i / N_OUT, token
+    // (i % N_OUT) / 16, row i % 16
     const bool epi_cta = split == 0;
     int em[EP], en[EP];
     bool eok[EP];
@@ -217,9 +218,9 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
 #pragma unroll
     for (int k = 0; k < EP; ++k) {
         const int i = threadIdx.x + k * (int)blockDim.x;
-        em[k] = i / TILE;
-        en[k] = tile * TILE + i % TILE;
-        eok[k] = epi_cta && i < N_OUT && em[k] < M && en[k] < w.rows;
+        em[k] = (i % N_OUT) / TILE;
+        en[k] = (tile0 + i / N_OUT) * TILE + i % TILE;
+        eok[k] = epi_cta && i < n_out && em[k] < M && en[k] < w.rows;
         eb[k] = 0.f;
         ec1[k] = 0.f;
         if (eok[k]) {
@@ -309,37 +310,38 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
     wait_staged(&xbar, err);
     mma_stamp(trace, 3);
 
-    // ---- MMAs: up to 32 tokens, two accumulator sets (x_hi products; x_lo and w_lo products)
-    // halve the dependent chains; more tokens have chains enough and keep the registers ----
+    // ---- MMAs: up to 32 tokens, the x_hi and x_lo sums of a group in two accumulator sets
+    // (halving the dependent chains); more tokens have chains enough and keep the registers ----
     constexpr bool TWO = NB <= 4;
-    float acc[NB][4], acd[NB][4];
+    float acc[NB][4];
 #pragma unroll
     for (int j = 0; j < NB; ++j)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) acc[j][q] = acd[j][q] = 0.f;
+        for (int q = 0; q < 4; ++q) acc[j][q] = 0.f;
     for (int base = g0; base < g1; base += PF) {
 #pragma unroll
         for (int u = 0; u < PF; ++u) {
             const int gr = base + u;
             if (gr < g1) {
-                uint32_t ahi[2][4], alo[2][4];
-                dequant_group<ATOM>(wa[u], wb[u], ws_a[u], ws_b[u], pre, ahi, alo);
+                uint32_t aq[2][4];
+                dequant_q<ATOM>(wa[u], wb[u], aq);
+                const float sa = __half2float(ws_a[u]), sb = __half2float(ws_b[u]);
                 if (gr + PF < g1) load_slot(u, gr + PF);  // slot u holds the groups = g0 + u mod PF
                 const int kofs = (gr - kg0) * 32;
-                uint4 xh[NB], xl[NB];
 #pragma unroll
                 for (int j = 0; j < NB; ++j) {
-                    xh[j] = load_x<ATOM>(sxh + (size_t)(8 * j + g) * xs + kofs, t);
-                    xl[j] = load_x<ATOM>(sxl + (size_t)(8 * j + g) * xs + kofs, t);
-                }
-#pragma unroll
-                for (int j = 0; j < NB; ++j) {
-                    mma16816(acc[j], ahi[0], xh[j].x, xh[j].y);
-                    mma16816(TWO ? acd[j] : acc[j], ahi[0], xl[j].x, xl[j].y);
-                    mma16816(acc[j], ahi[1], xh[j].z, xh[j].w);
-                    mma16816(TWO ? acd[j] : acc[j], alo[0], xh[j].x, xh[j].y);
-                    mma16816(TWO ? acd[j] : acc[j], ahi[1], xl[j].z, xl[j].w);
-                    mma16816(TWO ? acd[j] : acc[j], alo[1], xh[j].z, xh[j].w);
+                    const uint4 xh = load_x<ATOM>(sxh + (size_t)(8 * j + g) * xs + kofs, t);
+                    const uint4 xl = load_x<ATOM>(sxl + (size_t)(8 * j + g) * xs + kofs, t);
+                    // the group's q x_hi and q x_lo sums (exact products), then its scale
+                    float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(th, aq[0], xh.x, xh.y);
+                    mma16816(TWO ? tl : th, aq[0], xl.x, xl.y);
+                    mma16816(th, aq[1], xh.z, xh.w);
+                    mma16816(TWO ? tl : th, aq[1], xl.z, xl.w);
+                    acc[j][0] = fmaf(sa, TWO ? th[0] + tl[0] : th[0], acc[j][0]);
+                    acc[j][1] = fmaf(sa, TWO ? th[1] + tl[1] : th[1], acc[j][1]);
+                    acc[j][2] = fmaf(sb, TWO ? th[2] + tl[2] : th[2], acc[j][2]);
+                    acc[j][3] = fmaf(sb, TWO ? th[3] + tl[3] : th[3], acc[j][3]);
                 }
             }
         }
@@ -350,20 +352,22 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
     float* mine = red + (size_t)warp * N_OUT;
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
-        mine[(8 * j + 2 * t) * TILE + g] = TWO ? acc[j][0] + acd[j][0] : acc[j][0];
-        mine[(8 * j + 2 * t + 1) * TILE + g] = TWO ? acc[j][1] + acd[j][1] : acc[j][1];
-        mine[(8 * j + 2 * t) * TILE + g + 8] = TWO ? acc[j][2] + acd[j][2] : acc[j][2];
-        mine[(8 * j + 2 * t + 1) * TILE + g + 8] = TWO ? acc[j][3] + acd[j][3] : acc[j][3];
+        mine[(8 * j + 2 * t) * TILE + g] = acc[j][0];
+        mine[(8 * j + 2 * t + 1) * TILE + g] = acc[j][1];
+        mine[(8 * j + 2 * t) * TILE + g + 8] = acc[j][2];
+        mine[(8 * j + 2 * t + 1) * TILE + g + 8] = acc[j][3];
     }
     __syncthreads();
-    // the CTA's partial, warps summed in order
+    // the CTA's partials, each tile's team summed in warp order
     float v[EP];
 #pragma unroll
     for (int k = 0; k < EP; ++k) {
         const int i = threadIdx.x + k * (int)blockDim.x;
         v[k] = 0.f;
-        if (i < N_OUT)
-            for (int wq = 0; wq < nw; ++wq) v[k] += red[(size_t)wq * N_OUT + i];
+        if (i < n_out) {
+            const int tt = i / N_OUT, j = i - tt * N_OUT;
+            for (int wq = tt * wt; wq < tt * wt + wt; ++wq) v[k] += red[(size_t)wq * N_OUT + j];
+        }
     }
     mma_stamp(trace, 5);
     if (S > 1) {
@@ -372,8 +376,8 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
 #pragma unroll
             for (int k = 0; k < EP; ++k) {
                 const int i = threadIdx.x + k * (int)blockDim.x;
-                if (i < N_OUT) {
-                    const uint32_t dst = tc::map_cluster(tc::smem_u32(recv + (size_t)split * N_OUT + i), 0);
+                if (i < n_out) {
+                    const uint32_t dst = tc::map_cluster(tc::smem_u32(recv + (size_t)split * n_out + i), 0);
                     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst), "f"(v[k]) : "memory");
                 }
             }
@@ -383,8 +387,8 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
 #pragma unroll
         for (int k = 0; k < EP; ++k) {
             const int i = threadIdx.x + k * (int)blockDim.x;
-            if (i < N_OUT)
-                for (int s2 = 1; s2 < S; ++s2) v[k] += recv[(size_t)s2 * N_OUT + i];
+            if (i < n_out)
+                for (int s2 = 1; s2 < S; ++s2) v[k] += recv[(size_t)s2 * n_out + i];
         }
         mma_stamp(trace, 6);
     }
@@ -395,7 +399,7 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
         res[k] = 0.f;
         if (!eok[k]) continue;
         // folded LayerNorm: W (g (x - mean) rstd + b) + bias = rstd (W (g x) - mean W g) + W b + bias
-        const float x = fold ? srstd[em[k]] * (v[k] * post - smean[em[k]] * ec1[k]) + eb[k] : v[k] * post + eb[k];
+        const float x = fold ? srstd[em[k]] * (v[k] - smean[em[k]] * ec1[k]) + eb[k] : v[k] + eb[k];
         const size_t o = (size_t)em[k] * e.ldo + en[k];
         switch (e.kind) {
             case EPI_STORE:
@@ -440,7 +444,7 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
 #pragma unroll
         for (int k = 0; k < EP; ++k) {
             const int i = threadIdx.x + k * (int)blockDim.x;
-            if (i - (threadIdx.x & 31) >= N_OUT) break;  // warp-uniform: no outputs left
+            if (i - (threadIdx.x & 31) >= n_out) break;  // warp-uniform: no outputs left
             float s = res[k];
 #pragma unroll
             for (int o = 1; o < TILE; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -449,17 +453,19 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
             float q = dv * dv;
 #pragma unroll
             for (int o = 1; o < TILE; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-            if (eok[k] && i % TILE == 0) e.stats[(size_t)em[k] * e.stats_ld + tile] = make_float2(mean, q);
+            if (eok[k] && i % TILE == 0)
+                e.stats[(size_t)em[k] * e.stats_ld + tile0 + i / N_OUT] = make_float2(mean, q);
         }
     }
     mma_stamp(trace, 7);
 }
 
-// The launch traced when GPT2Q_MMA_TRACE=<rows>x<cols>x<M> is set: the first one of that shape.
+// The launch traced when GPT2Q_MMA_TRACE=<rows>x<cols>x<M>[x<skip>] is set: the first one of that
+// shape after `skip` others.
 constexpr size_t MMA_TRACE_CTAS = 4096;
 struct MmaTraceState {
     unsigned long long* buf = nullptr;
-    int rows = 0, cols = 0, m = 0;
+    int rows = 0, cols = 0, m = 0, skip = 0;
     bool traced = false;
     dim3 grid;
 };
@@ -469,7 +475,7 @@ MmaTraceState& trace_state() {
     if (!init) {
         init = true;
         if (const char* e = std::getenv("GPT2Q_MMA_TRACE"))
-            if (std::sscanf(e, "%dx%dx%d", &st.rows, &st.cols, &st.m) == 3 &&
+            if (std::sscanf(e, "%dx%dx%dx%d", &st.rows, &st.cols, &st.m, &st.skip) >= 3 &&
                 cudaMalloc(&st.buf, MMA_TRACE_CTAS * MMA_TRACE * 8) == cudaSuccess)
                 cudaMemset(st.buf, 0, MMA_TRACE_CTAS * MMA_TRACE * 8);
     }
@@ -490,22 +496,106 @@ int num_sms() {
 }
 
 struct Plan {
-    int S = 1, warps = 1, gps = 0, gpw = 0;
+    int T = 1, S = 1, warps = 1, gps = 0, gpw = 0;
     size_t smem = 0;
 };
 
-size_t smem_bytes(int atom, int NB, int kgroups, int warps, int S, bool ln) {
+size_t smem_bytes(int atom, int NB, int kgroups, int warps, int S, bool ln, int T = 1) {
     const int NC = NB * 8;
     const int xs = atom == ATOM_Q8 ? staged_stride<ATOM_Q8>(kgroups) : staged_stride<ATOM_Q4>(kgroups);
     const size_t staged = std::max((size_t)2 * NC * xs * 2, (size_t)warps * TILE * NC * 4);
     // folded LayerNorm: each token's mean and rstd
     const size_t lnb = ln ? (size_t)2 * NC * 4 : 0;
-    return staged + (S > 1 ? (size_t)S * TILE * NC * 4 : 0) + lnb;
+    return staged + (S > 1 ? (size_t)S * T * TILE * NC * 4 : 0) + lnb;
 }
 
-// Work layout: K split over a cluster of S CTAs only where the row tiles alone leave most SMs
-// idle (or the staged activations of the whole K would not fit); warps of 1-2 groups each.
-bool plan(const QW& w, int M, Plan& p, bool ln) {
+// Residency of this kernel (at most 128 registers a thread): one 16-warp CTA or two 8-warp CTAs
+// per SM, fewer where shared memory runs out; clusters of S CTAs fit in a GPC, so how many run
+// at once is asked of the runtime when a handle is created (never during a graph capture).
+struct Residency {
+    bool init = false;
+    int smem_per_sm = 228 * 1024;
+    int clusters[3][MMA_MAX_SPLITS + 1] = {};  // [CTAs per SM][S]: clusters resident at once
+};
+Residency g_res[64];
+
+Residency& residency() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return g_res[dev & 63];
+}
+
+void init_residency() {
+    Residency& r = residency();
+    if (r.init) return;
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) == cudaSuccess && v > 0)
+        r.smem_per_sm = v;
+    const int sms = num_sms();
+    auto kern = k_linear_mma<ATOM_Q8, 4>;
+    const bool raised = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_MAX_SMEM) ==
+                        cudaSuccess;
+    for (int per_sm = 1; per_sm <= 2; ++per_sm) {
+        for (int S = 2; S <= MMA_MAX_SPLITS; ++S) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(1, S);
+            cfg.blockDim = dim3(32 * MMA_MAX_WARPS / per_sm);
+            cfg.dynamicSmemBytes = per_sm == 1 ? 150 * 1024 : 100 * 1024;
+            cudaLaunchAttribute at;
+            at.id = cudaLaunchAttributeClusterDimension;
+            at.val.clusterDim.x = 1;
+            at.val.clusterDim.y = S;
+            at.val.clusterDim.z = 1;
+            cfg.attrs = &at;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (!raised || cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+                cudaGetLastError();
+                n = sms * per_sm / S;
+            }
+            r.clusters[per_sm][S] = n;
+        }
+    }
+    r.init = true;
+}
+
+// Modelled time of a work layout, in ns, used only to choose among layouts. The constants come
+// from the measured phases of one launch:
+//  - ~10 ns of an SM's issue for one group of one tile and 8 tokens (six 16x8x16 MMAs, their
+//    dequantisation and operand loads from shared memory);
+//  - ~100 ns per group on one warp's dependent chain;
+//  - ~12 ns per KB of activations staged into one SM;
+//  - ~1.5 us of launch, reduction and epilogue per wave;
+//  - ~0.4 us per CTA of a split-K cluster exchange.
+int ctas_per_sm(const Plan& p) {
+    const int by_smem = (int)(residency().smem_per_sm / (p.smem + 1024));  // 1 KB reserved per CTA
+    return std::max(1, std::min(p.warps > MMA_MAX_WARPS / 2 ? 1 : 2, by_smem));
+}
+
+long wave_capacity(const Plan& p) {  // CTAs resident at once
+    const Residency& r = residency();
+    const int sms = num_sms(), per_sm = ctas_per_sm(p);
+    if (p.S == 1) return (long)sms * per_sm;
+    return (long)std::max(1, r.init ? r.clusters[per_sm][p.S] : sms * per_sm / p.S) * p.S;
+}
+
+double plan_cost(const Plan& p, int tiles, int M, int NB) {
+    const int sms = num_sms(), per_sm = ctas_per_sm(p);
+    const long cap = wave_capacity(p);
+    const long ctas = (long)((tiles + p.T - 1) / p.T) * p.S;
+    const long waves = (ctas + cap - 1) / cap;
+    const long cps = std::min<long>(per_sm, (std::min(ctas, cap) + sms - 1) / sms);
+    const double mma = 10.0 * p.T * p.gps * NB, chain = 100.0 * p.gpw;
+    const double stage = 12.0 * (double)M * p.gps * 128 / 1024;
+    return (double)waves * (1500.0 + std::max((double)cps * mma, chain) + (double)cps * stage +
+                            (p.S > 1 ? 400.0 * p.S : 0.0));
+}
+
+// Work layout with one 16-row tile per CTA: K split over a cluster of S CTAs only where the row
+// tiles alone leave most SMs idle (or the staged activations of the whole K would not fit); warps
+// of 1-2 groups each.
+bool plan_one_tile(const QW& w, int M, Plan& p, bool ln) {
     const int tiles = (w.rows + TILE - 1) / TILE;
     const int G = w.cols / 32;
     const int NB = (M + 7) / 8;
@@ -526,6 +616,7 @@ bool plan(const QW& w, int M, Plan& p, bool ln) {
         const int gpw = (gps + warps - 1) / warps;
         const size_t smem = smem_bytes(w.atom, NB, gps, warps, Sx, ln);
         if (smem <= (size_t)MMA_MAX_SMEM) {
+            p.T = 1;
             p.S = Sx;
             p.warps = warps;
             p.gps = gps;
@@ -537,9 +628,64 @@ bool plan(const QW& w, int M, Plan& p, bool ln) {
     return false;
 }
 
+int env_int(const char* name, int dflt) {
+    const char* e = std::getenv(name);
+    return e && *e ? std::atoi(e) : dflt;
+}
+
+// Where one tile per CTA needs more than one wave of CTAs, or more tiles than SMs (two CTAs per
+// SM then stage the same activations twice), T tiles per CTA share one staged copy: the layout
+// (T, S, warps) of least modelled time among those that fit. GPT2Q_MMA_MULTI=0 keeps one tile;
+// GPT2Q_MMA_TILES=<T> takes the best layout of exactly T tiles per CTA where one fits (tests and
+// tuning). Both are read at every plan, so a handle created after a change sees it.
+bool plan(const QW& w, int M, Plan& p, bool ln) {
+    const bool multi = env_int("GPT2Q_MMA_MULTI", 1) != 0;
+    const int force_t = std::min(8, std::max(0, env_int("GPT2Q_MMA_TILES", 0)));
+    Plan base;
+    const bool have = plan_one_tile(w, M, base, ln);
+    const int tiles = (w.rows + TILE - 1) / TILE, G = w.cols / 32, NB = (M + 7) / 8;
+    const int sms = num_sms();
+    if (!force_t && (!multi || (have && tiles <= sms && (long)tiles * base.S <= wave_capacity(base)))) {
+        if (!have) return false;
+        p = base;
+        return true;
+    }
+    Plan best = base;
+    double best_cost = have && !force_t ? plan_cost(base, tiles, M, NB) : 1e30;
+    for (int T = force_t ? force_t : 1; T <= (force_t ? force_t : 8); ++T) {
+        for (int S = 1; S <= MMA_MAX_SPLITS && S <= G; ++S) {
+            const int gps = (G + S - 1) / S;
+            if ((G + gps - 1) / gps != S) continue;  // no empty split
+            for (int warps = MMA_MAX_WARPS; warps >= MMA_MAX_WARPS / 2; warps -= MMA_MAX_WARPS / 2) {
+                const int wt = warps / T;
+                if (wt < 1 || 2 * NB * T > warps || (ln && 4 * warps < M)) continue;
+                Plan c;
+                c.T = T;
+                c.S = S;
+                c.warps = warps;
+                c.gps = gps;
+                c.gpw = (gps + wt - 1) / wt;
+                c.smem = smem_bytes(w.atom, NB, gps, warps, S, ln, T);
+                if (c.smem > (size_t)MMA_MAX_SMEM) continue;
+                const double cost = plan_cost(c, tiles, M, NB);
+                if (cost < best_cost) {
+                    best_cost = cost;
+                    best = c;
+                }
+            }
+        }
+    }
+    if (best_cost >= 1e30) {  // no layout of the forced T fits
+        if (!have) return false;
+        best = base;
+    }
+    p = best;
+    return true;
+}
+
 template <int ATOM, int NB>
-cudaError_t launch_nb(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, const Plan& p, __half pre,
-                      float post, int* err, const Epi& e, const LnFold& ln, cudaStream_t st) {
+cudaError_t launch_nb(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, const Plan& p, int* err,
+                      const Epi& e, const LnFold& ln, cudaStream_t st) {
     auto kern = k_linear_mma<ATOM, NB>;
     // the dynamic shared-memory limit is raised once per device for each instantiation
     static unsigned long long raised = 0;
@@ -551,7 +697,7 @@ cudaError_t launch_nb(const QW& w, const __half* xhi, const __half* xlo, int ldx
         if (ae != cudaSuccess) return ae;
         raised |= bit;
     }
-    const dim3 grid((w.rows + TILE - 1) / TILE, p.S);
+    const dim3 grid(((w.rows + TILE - 1) / TILE + p.T - 1) / p.T, p.S);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(32 * p.warps);
@@ -576,26 +722,26 @@ cudaError_t launch_nb(const QW& w, const __half* xhi, const __half* xlo, int ldx
     unsigned long long* tr = nullptr;
     MmaTraceState& ts = trace_state();
     if (ts.buf && !ts.traced && w.rows == ts.rows && w.cols == ts.cols && M == ts.m &&
-        (size_t)grid.x * grid.y <= MMA_TRACE_CTAS) {
+        (size_t)grid.x * grid.y <= MMA_TRACE_CTAS && ts.skip-- <= 0) {
         tr = ts.buf;
         ts.traced = true;
         ts.grid = grid;
     }
-    return cudaLaunchKernelEx(&cfg, kern, w, xhi, xlo, ldx, M, p.gps, p.gpw, pre, post, err, tr, e, ln);
+    return cudaLaunchKernelEx(&cfg, kern, w, xhi, xlo, ldx, M, p.T, p.gps, p.gpw, err, tr, e, ln);
 }
 
 template <int ATOM>
 cudaError_t launch_atom(int NB, const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, const Plan& p,
-                        __half pre, float post, int* err, const Epi& e, const LnFold& ln, cudaStream_t st) {
+                        int* err, const Epi& e, const LnFold& ln, cudaStream_t st) {
     switch (NB) {
-        case 1: return launch_nb<ATOM, 1>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
-        case 2: return launch_nb<ATOM, 2>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
-        case 3: return launch_nb<ATOM, 3>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
-        case 4: return launch_nb<ATOM, 4>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
-        case 5: return launch_nb<ATOM, 5>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
-        case 6: return launch_nb<ATOM, 6>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
-        case 7: return launch_nb<ATOM, 7>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
-        default: return launch_nb<ATOM, 8>(w, xhi, xlo, ldx, M, p, pre, post, err, e, ln, st);
+        case 1: return launch_nb<ATOM, 1>(w, xhi, xlo, ldx, M, p, err, e, ln, st);
+        case 2: return launch_nb<ATOM, 2>(w, xhi, xlo, ldx, M, p, err, e, ln, st);
+        case 3: return launch_nb<ATOM, 3>(w, xhi, xlo, ldx, M, p, err, e, ln, st);
+        case 4: return launch_nb<ATOM, 4>(w, xhi, xlo, ldx, M, p, err, e, ln, st);
+        case 5: return launch_nb<ATOM, 5>(w, xhi, xlo, ldx, M, p, err, e, ln, st);
+        case 6: return launch_nb<ATOM, 6>(w, xhi, xlo, ldx, M, p, err, e, ln, st);
+        case 7: return launch_nb<ATOM, 7>(w, xhi, xlo, ldx, M, p, err, e, ln, st);
+        default: return launch_nb<ATOM, 8>(w, xhi, xlo, ldx, M, p, err, e, ln, st);
     }
 }
 
@@ -607,24 +753,23 @@ bool mma_usable(const QW& w, int M) {
            w.rows >= 1 && (w.rows + TILE - 1) / TILE <= MMA_MAX_TILES;
 }
 
-int mma_prescale_exp(float max_abs_w) {
-    // largest |hi| at most 1024: hi and lo stay normal fp16 for scales within 2^10 of the largest
-    if (!(max_abs_w > 0.f) || !std::isfinite(max_abs_w)) return 0;
-    const int p = (int)std::floor(std::log2(1024.0 / (double)max_abs_w));
-    return std::max(-14, std::min(15, p));
-}
+std::atomic<int> g_tiles_max{0};
 
 void mma_init() {
     trace_state();  // the trace buffer, if any, is allocated here, never during a graph capture
     num_sms();
+    init_residency();
+    g_tiles_max = 0;
 }
+
+int mma_tiles_per_cta_max() { return g_tiles_max.load(); }
 
 bool mma_fits(const QW& w, int M, bool ln) {
     Plan p;
     return mma_usable(w, M) && plan(w, M, p, ln);
 }
 
-cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, int pexp, int* err,
+cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, int* err,
                               const Epi& e, cudaStream_t st, const LnFold* ln) {
     if (M <= 0) return cudaSuccess;
     Plan p;
@@ -640,11 +785,11 @@ cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo,
     }
     if (e.kind == EPI_RESID && e.stats && (w.rows % TILE != 0 || e.stats_ld * TILE < w.rows || !e.ln_g || !e.out_hi || !e.out_lo))
         return cudaErrorInvalidValue;
-    const __half pre = __float2half_rn(std::ldexp(1.0f, pexp));
-    const float post = std::ldexp(1.0f, -pexp);
+    for (int cur = g_tiles_max.load(); p.T > cur && !g_tiles_max.compare_exchange_weak(cur, p.T);) {
+    }
     const int NB = (M + 7) / 8;
-    if (w.atom == ATOM_Q8) return launch_atom<ATOM_Q8>(NB, w, xhi, xlo, ldx, M, p, pre, post, err, e, lf, st);
-    return launch_atom<ATOM_Q4>(NB, w, xhi, xlo, ldx, M, p, pre, post, err, e, lf, st);
+    if (w.atom == ATOM_Q8) return launch_atom<ATOM_Q8>(NB, w, xhi, xlo, ldx, M, p, err, e, lf, st);
+    return launch_atom<ATOM_Q4>(NB, w, xhi, xlo, ldx, M, p, err, e, lf, st);
 }
 
 std::string mma_trace_json() {

@@ -1,5 +1,5 @@
-// Batched-decode linear on the warp-level tensor cores (mma.sync, fp16 hi/lo split of the int8 /
-// int4 weights in registers) for 1..MMA_MAX_M tokens. See gemm_mma.cu.
+// Batched-decode linear on the warp-level tensor cores (mma.sync over the exact fp16 values of the
+// int8 / int4 weights, group scales applied in fp32) for 1..MMA_MAX_M tokens. See gemm_mma.cu.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -22,9 +22,6 @@ bool mma_usable(const QW& w, int M);
 // mma_usable, and a work layout whose staged activations fit in shared memory exists (with room
 // for a folded LayerNorm's statistics when `ln`).
 bool mma_fits(const QW& w, int M, bool ln = false);
-// Power-of-two exponent P applied to the group scales (s' = s 2^P) so that the fp16 hi/lo
-// split stays in the normal range; max_abs_w bounds |dequantised weight|.
-int mma_prescale_exp(float max_abs_w);
 // A LayerNorm folded into the linear that consumes it: with X = g * x (the gain applied by the
 // residual linear that produced x, Epi::ln_g), W LN(x) + bias = rstd (W X - mean W g) + W b + bias
 // per token, the mean and rstd combined from the (mean, M2) of 16-element tiles that the
@@ -40,8 +37,11 @@ struct LnFold {
 // X = x_hi + x_lo, fp16 [M][ldx] written by the previous kernel; ldx % 8 == 0. err: device word
 // set when the bounded wait for the staged activations gives up. With `ln`, X = g * x and the
 // epilogue completes the LayerNorm (see LnFold).
-cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, int pexp, int* err,
+cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, int* err,
                               const Epi& e, cudaStream_t st, const LnFold* ln = nullptr);
+// Largest number of 16-row tiles per CTA among the launches since the last mma_init (one count
+// for the process).
+int mma_tiles_per_cta_max();
 // Phase stamps of the launch selected by GPT2Q_MMA_TRACE ("" when none), as JSON.
 std::string mma_trace_json();
 

@@ -54,7 +54,6 @@ struct Linear {
     std::string name;
     size_t weight_bytes = 0;  // q + scale bytes read by one full pass over W
     float max_abs_w = 0.f;    // upper bound of |dequantised weight| (tensor-core prescale)
-    int mma_p = 0;            // power-of-two scale exponent of the warp-level tensor-core path
     // the LayerNorm before this linear folded into its epilogue: W g and W b + bias per row
     float* ln_c1 = nullptr;
     float* ln_c2b = nullptr;
@@ -368,7 +367,6 @@ int upload_linear(gpt2q_handle* H, const gpt2q_tensor_desc* t, int rows, int col
             if (sv > smax && std::isfinite(sv)) smax = sv;
         }
         L->max_abs_w = smax * qmax;
-        L->mma_p = mma_prescale_exp(L->max_abs_w);
     }
     L->rows = out_rows;
     L->cols = out_cols;
@@ -453,9 +451,9 @@ int linear(gpt2q_handle* H, const char* name, const Linear& L, const In& X, int 
     const int extra = (e.kind == EPI_RESID) ? 2 : 1;
     const double bytes = linear_bytes(L, M, extra);
     if (ln) {
-        RUN(name, bytes, launch_linear_mma(L.w, X.hi, X.lo, X.ld, M, L.mma_p, H->kerr, e, H->stream, ln));
+        RUN(name, bytes, launch_linear_mma(L.w, X.hi, X.lo, X.ld, M, H->kerr, e, H->stream, ln));
     } else if (takes_mma(H, L, X, M, false)) {
-        RUN(name, bytes, launch_linear_mma(L.w, X.hi, X.lo, X.ld, M, L.mma_p, H->kerr, e, H->stream));
+        RUN(name, bytes, launch_linear_mma(L.w, X.hi, X.lo, X.ld, M, H->kerr, e, H->stream));
     } else if (X.hi && H->gemm.usable(L.w, M)) {
         const XSplit xs{X.hi, X.lo, X.ld};
         RUN(name, bytes, launch_linear_tc(H->gemm, L.w, xs, M, e, H->stream));
@@ -1837,6 +1835,7 @@ int gpt2q_info(gpt2q_handle* H, char* json, size_t cap) {
                           std::to_string(H->mk.enabled ? MK_CS * H->mk.clusters : 0) +
                           ", \"tensor_core\": " + (H->gemm.enabled ? "true" : "false") +
                           ", \"tc_products\": " + std::to_string(H->gemm.products) +
+                          ", \"mma_tiles_per_cta_max\": " + std::to_string(mma_tiles_per_cta_max()) +
                           ", \"tp_size\": " + std::to_string(H->tp_size) +
                           ", \"tp_peer_mapped\": " + (tp_peer_mapped(H->tp) ? "true" : "false");
     std::string tr;

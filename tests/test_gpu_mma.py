@@ -46,10 +46,12 @@ def _run(pk, prompts, steps, monkeypatch, mode, extra=None):
         toks = g.decode_steps(steps, len(prompts))
         nxt2, lg = g.decode(toks[-1], [p.size + steps for p in prompts], want_logits=True)
         bounds[mode] = observed(g)  # prompts over 64 tokens in all go through the wide tiles
+        tiles_per_cta[mode] = g.info()["mma_tiles_per_cta_max"]
     return nxt, lg0, toks, nxt2, lg
 
 
 bounds = {}
+tiles_per_cta = {}
 
 
 @pytest.mark.parametrize("policy", ["auto", "q4auto"])
@@ -121,3 +123,31 @@ def test_layernorm_applied_by_the_linear_matches_layernorm_launches(meta, policy
         ref = oracle_prefix_logits(eng, np.concatenate([prompts[i], [fused[0][i]], fused[2][:, i]]))
         assert np.abs(fused[4][i] - ref[-1]).max() <= bounds["mma"]
         assert fused[3][i] == O.argmax(ref[-1])
+
+
+@pytest.mark.parametrize("policy", ["auto", "q4auto"])
+@pytest.mark.parametrize("tiles,n_seq", [(2, 32), (3, 16), (5, 8), (8, 6)])
+def test_multi_tile_layouts_match_one_tile(tiles, n_seq, policy, monkeypatch):
+    """CTAs of 2, 3, 5 and 8 row tiles (GPT2Q_MMA_TILES), each tile a team of warps over one staged
+    copy of the activations, against one tile per CTA (GPT2Q_MMA_MULTI=0). On WIDE, 3 and 5 tiles
+    leave a ragged last CTA (112 c_fc tiles, 28 mlp c_proj tiles); the K-split clusters of the
+    28-tile linears carry the tiles' partials too. The folded LayerNorms read and write their
+    per-tile statistics through the same index arithmetic. Same tokens, logits within the bound,
+    and the oracle's tokens and logits."""
+    pk = make_pack(WIDE, policy, 0, 0.02)
+    rng = np.random.default_rng(300 + tiles)
+    prompts = [rng.integers(0, WIDE.vocab, int(n)).astype(np.uint32) for n in rng.integers(1, 30, n_seq)]
+    few = {"GPT2Q_MMA_MIN_M": "1", "GPT2Q_NO_PERSISTENT": "1"}
+    one = _run(pk, prompts, 4, monkeypatch, "mma", {**few, "GPT2Q_MMA_MULTI": "0"})
+    assert tiles_per_cta["mma"] == 1
+    monkeypatch.delenv("GPT2Q_MMA_MULTI")
+    multi = _run(pk, prompts, 4, monkeypatch, "mma", {**few, "GPT2Q_MMA_TILES": str(tiles)})
+    assert tiles_per_cta["mma"] == tiles
+    bound = bounds["mma"]
+    assert np.abs(one[1] - multi[1]).max() <= bound and np.abs(one[4] - multi[4]).max() <= bound
+    assert np.array_equal(one[0], multi[0]) and np.array_equal(one[2], multi[2]) and np.array_equal(one[3], multi[3])
+    eng = oracle_engine(pk)
+    for i in (0, n_seq - 1):
+        ref = oracle_prefix_logits(eng, np.concatenate([prompts[i], [multi[0][i]], multi[2][:, i]]))
+        assert np.abs(multi[4][i] - ref[-1]).max() <= bound
+        assert multi[3][i] == O.argmax(ref[-1])
