@@ -190,7 +190,8 @@ int gpt2q_info(gpt2q_handle* h, char* json, size_t cap);
  * framework's memory pool). No counterpart in the reference. Limit: n_rows <=
  * GPT2Q_NOALLOC_MAX_ROWS, else GPT2Q_EARG. A call looks up the scratch array's device
  * address (cudaGetSymbolAddress) unless `stream` reports an active capture, when it uses
- * the address an earlier call found. All calls share the scratch, so calls that overlap on
+ * the address an earlier call found; the first call on a device therefore does the set-up and
+ * should come before any stream capture. All calls share the scratch, so calls that overlap on
  * the GPU race; serialise them. Errors are reported by gpt2q_last_error(NULL). */
 #define GPT2Q_NOALLOC_MAX_ROWS 1024
 int gpt2q_argmax_noalloc(const float* d_logits, int vocab, int ld, int n_rows, uint32_t* d_next, void* stream);

@@ -12,7 +12,8 @@
 //  - at most GPT2Q_NOALLOC_MAX_ROWS rows per call (8 KiB of scratch, held by every GPU
 //    that loads the library until the process exits); larger calls fail with GPT2Q_EARG;
 //  - a call looks up the array's device address, except while `stream` reports an active
-//    capture, when it uses the address an earlier call found;
+//    capture, when it uses the address an earlier call found: the first call on a device does
+//    this set-up and should come before any stream capture;
 //  - every call shares the one array: calls whose kernels overlap on the GPU (different
 //    streams without ordering between them) race and give wrong tokens. Serialise them.
 #include <cuda_runtime.h>
