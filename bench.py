@@ -11,8 +11,10 @@ Sequences are independent, so N GPUs each run their own 32 sequences with no
 data-path collective (weak scaling). The default run also reports, in
 `workloads`, the single-sequence decode (`small-int8-b1`, prompt 64, decode 64)
 and the int4 decode of 256 ragged prompts of 16..512 tokens (`small-int4-b256`,
-decode 256, sequences split across the ranks); `--only` skips them. With N >= 2
-it adds `xl-int8-tp`, GPT-2 XL tensor parallel over the N ranks.
+decode 256, sequences split across the ranks), and the GPT-2 medium int8 prefill of
+64 prompts of 1024 tokens (`medium-int8-prefill`, min(K, 5) timed prefill steps,
+prompts split across the ranks); `--only` skips them. With N >= 2 it adds
+`xl-int8-tp`, GPT-2 XL tensor parallel over the N ranks.
 
 Timed decode steps are spread over each workload's whole decode span: before the
 timed region every sequence is rewound to its own start offset o_i (spread over
@@ -516,6 +518,9 @@ def run_decode(args, wl):
         line["workloads"] = {}
         for name in SUB_WORKLOADS:
             line["workloads"][name] = measure_decode(args, name, WORKLOADS[name], world, rank, local, dev)
+        pname = "medium-int8-prefill"
+        line["workloads"][pname] = measure_prefill(args, pname, WORKLOADS[pname], world, rank, local, dev,
+                                                   steps=min(args.steps, PREFILL_SUB_STEPS))
         if world > 1:
             line["workloads"]["xl-int8-tp"] = measure_tp(args, WORKLOADS["xl-int8-tp"], world, rank, local, dev,
                                                          parity=True)
@@ -576,7 +581,7 @@ def reference_decode(args, name: str, wl, world: int) -> dict:
     }
 
 
-def reference_prefill(args, wl, world: int) -> dict:
+def reference_prefill(args, name: str, wl, world: int, steps: int | None = None) -> dict:
     """Prefill as the reference does it, one Engine::step per prompt token (gpt2.rs:373-381):
     each step times 8 consecutive prompt tokens of one sequence."""
     model, policy, batch, plen, _dec, scaling = wl
@@ -584,6 +589,8 @@ def reference_prefill(args, wl, world: int) -> dict:
     ids = generator(True).prompt_ids(batch * plen, meta["vocab"], seed=1)
     kv = eng.empty_kv()
     per_step, pos = 8, 0
+    steps = args.steps if steps is None else steps
+    warmup = min(args.warmup, steps)
 
     def one():
         nonlocal pos
@@ -591,20 +598,20 @@ def reference_prefill(args, wl, world: int) -> dict:
             eng.step(int(ids[pos % ids.size]), pos % plen, kv)
             pos += 1
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         one()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         one()
     dt = time.perf_counter() - t0
-    tok_s = args.steps * per_step / dt
+    tok_s = steps * per_step / dt
     return {
-        "impl": "reference", "metric": METRICS[args.config], "value": tok_s, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
+        "impl": "reference", "metric": METRICS[name], "value": tok_s, "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": dt * 1e3 / steps, "higher_is_better": True,
         "scaling": scaling, "vs_baseline": None, "dtype": "int8xfp32", "data": "synthetic",
-        "config": prefill_config(args.config, wl, world),
+        "config": prefill_config(name, wl, world),
         "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": REF_THREADS, "kind": "port",
-                         "sample": f"{args.steps} steps x {per_step} consecutive prompt tokens of one sequence, "
+                         "sample": f"{steps} steps x {per_step} consecutive prompt tokens of one sequence, "
                                    f"oracle C++ restatement of gpt2.rs step, {REF_THREADS}-thread row split"},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -648,13 +655,16 @@ def run_reference(args, wl):
     if args.config == "small-int8-trunk-bwd":
         line = reference_trunk(args, wl, world)
     elif args.config == "medium-int8-prefill":
-        line = reference_prefill(args, wl, world)
+        line = reference_prefill(args, args.config, wl, world)
     elif args.config == "xl-int8-tp":
         line = reference_tp(args, wl, world)
     else:
         line = reference_decode(args, args.config, wl, world)
         if not args.only and args.config == "small-int8-b32" and args.batch == 0:
             line["workloads"] = {n: reference_decode(args, n, WORKLOADS[n], world) for n in SUB_WORKLOADS}
+            pname = "medium-int8-prefill"
+            line["workloads"][pname] = reference_prefill(args, pname, WORKLOADS[pname], world,
+                                                         steps=min(args.steps, PREFILL_SUB_STEPS))
             if world > 1:
                 line["workloads"]["xl-int8-tp"] = reference_tp(args, WORKLOADS["xl-int8-tp"], world)
     print(json.dumps(line), flush=True)
@@ -801,17 +811,20 @@ def prefill_config(name: str, wl, world: int) -> dict:
             "l2": f"no flush: inputs larger than L2 ({batch * plen * 1024 * 4 / 1e6:.0f} MB of activations per layer)"}
 
 
-def run_prefill(args, wl):
-    """GPT-2 medium int8 prefill, 64 prompts of 1024 tokens; a step is their prefill and the greedy token
-    after each (generate_greedy with one step), sequences split across ranks (strong
-    scaling); tensor-core bound."""
+PREFILL_SUB_STEPS = 5  # timed prefill steps (64 x 1024 tokens each) of the sub-result in the default line
+
+
+def measure_prefill(args, name: str, wl, world: int, rank: int, local: int, dev, steps: int | None = None) -> dict:
+    """GPT-2 medium int8 prefill, 64 prompts of 1024 tokens; a step is their prefill and the greedy
+    token after each (generate_greedy with one step), sequences split across ranks (strong
+    scaling); tensor-core bound. Returns the rank-0 record."""
     import torch
 
     from smelt_b200 import shard, synth
     from smelt_b200.gpu import Gpu
 
     model, policy, batch, plen, _dec, scaling = wl
-    world, rank, local, dev = dist_setup()
+    steps = args.steps if steps is None else steps
     pk = build_pack(model, policy)
     meta = pk.meta
     ids = synth.prompt_ids(batch * plen, meta.vocab, seed=1)
@@ -820,14 +833,16 @@ def run_prefill(args, wl):
     g = Gpu(pk, device=local, max_seqs=max(1, len(prompts)), max_tokens=16384)
     stream = torch.cuda.Stream(device=dev)
     g.set_stream(stream.cuda_stream)
-    for _ in range(max(args.warmup, 3)):
+    warmup = max(args.warmup, 3) if steps == args.steps else 3
+    for _ in range(warmup):
         g.prefill(prompts)
     barrier(world)
     with ClockSampler(dev) as clk:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = g.launches
         t0 = time.perf_counter()
         ev0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             # the single greedy step is the token predicted from the last prompt position,
             # which the prefill returns
             g.prefill(prompts)
@@ -835,29 +850,49 @@ def run_prefill(args, wl):
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         ms = ev0.elapsed_time(ev1)
+        launches = g.launches - l0
     ms_max = max_over_ranks(ms, world, dev)
     wall_max = max_over_ranks(wall, world, dev)
-    tokens = batch * plen * args.steps
+    tokens = batch * plen * steps
     flops_rank = sum(prefill_flops(meta.n_embd, meta.n_layer, meta.vocab, p.size) for p in prompts)
     peak, peak_kind = bf16_sustained()
-    achieved = flops_rank / (ms / args.steps / 1e3) / 1e12 if prompts else 0.0
+    achieved = flops_rank / (ms / steps / 1e3) / 1e12 if prompts else 0.0
     line = {
-        "metric": METRICS[args.config], "value": tokens / (ms_max / 1e3), "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "metric": METRICS[name], "value": tokens / (ms_max / 1e3), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms_max / steps,
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "int8xfp32 (fp16 split tensor)",
-        "data": "synthetic", "config": prefill_config(args.config, wl, world),
+        "data": "synthetic", "config": prefill_config(name, wl, world),
         "roofline": {"bound": "tensor", "kernel": "whole prefill step", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
                      "flops_per_step_rank": flops_rank,
                      "note": "algorithmic FLOPs (2MNK); the fp16 hi/lo split issues more MMAs than that"},
         "e2e": {"value": tokens / wall_max, "unit": "tokens/s", "h2d_bytes_per_step": sum(p.size for p in prompts) * 4,
                 "d2h_bytes_per_step": len(prompts) * 4, "api": "gpt2q_prefill"},
-        "gpu_launches": None, "clocks": clk.summary(),
+        "gpu_launches": int(launches), "clocks": clk.summary(),
     }
     g.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+
+        eng = O.Engine(meta.as_dict(), {n: (t.shape, t.atom, t.data) for n, t in pk.tensors.items()}, REF_THREADS)
+        sample = np.linspace(0, plen - 1, max(2, args.cpu_sample_steps // 2)).round().astype(np.int64)
+        tok_s, dt = cpu_decode_rate(eng, sample, meta.vocab)
+        line["cpu_baseline"] = {
+            "value": tok_s, "unit": "tokens/s", "cores": REF_THREADS, "kind": "port",
+            "sample": f"{sample.size} single-token steps at prompt positions {int(sample.min())}..{int(sample.max())} "
+                      f"spread evenly ({dt:.1f} s; the reference prefills one token per step), oracle C++ "
+                      f"restatement of the reference step, {REF_THREADS}-thread row split per matmul"}
+    return line
+
+
+def run_prefill(args, wl):
+    world, rank, local, dev = dist_setup()
+    line = measure_prefill(args, args.config, wl, world, rank, local, dev)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        import torch
+
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
