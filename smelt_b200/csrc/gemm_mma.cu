@@ -460,6 +460,131 @@ k_linear_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, i
     mma_stamp(trace, 7);
 }
 
+// The tied lm head for 1..64 tokens: logits[m][n] = sum_k W[n][k] x[m][k] over the vocabulary's
+// 16-row tiles. Unlike the layer linears, the head has thousands of tiles (3142 for GPT-2), so
+// one CTA per SM stages the activations once (one bulk copy per operand) and every warp then
+// runs whole tiles over the full K, storing each tile's outputs straight from its accumulator
+// fragments: no cross-warp reduction and one staging per SM. Same arithmetic as k_linear_mma:
+// exact integer weights against x_hi and x_lo, the group's fp32 sum scaled once. Measured on
+// GPT-2 small: 22 us at 8 tokens against 35 + 1.3 us for the int8 head (kind::i8, one TMEM
+// drain per group), but 36 us at 32 tokens against 28.7 us for the tcgen05 f16 hi/lo tile, so
+// it serves the batches the tcgen05 head does not take (fewer than 16 rows). Its weights stream
+// at under 2 TB/s whether or not each load asks L2 for the 256 bytes around it.
+// CTA c owns tiles [c * tpc, (c + 1) * tpc); warp w takes tiles w, w + warps, ... of them, as
+// one stream of (tile, group) units with HPF units of weights in registers ahead of use.
+template <int ATOM, int NB>
+__global__ void __launch_bounds__(MMA_MAX_WARPS * 32, 1)
+k_head_mma(const QW w, const __half* xhi, const __half* xlo, int ldx, int M, int tpc, float* out, int ldo,
+           int* err) {
+    constexpr int NC = NB * 8;
+    constexpr int GB = (ATOM == ATOM_Q8) ? 32 : 16;  // payload bytes per row and group
+    constexpr int HPF = 4;                           // units of weights in flight per warp
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t xbar;
+    tc::pdl_trigger();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int G = w.cols / 32;
+    const int tiles = (w.rows + TILE - 1) / TILE;
+    const int t0 = blockIdx.x * tpc, t1 = min(tiles, t0 + tpc);
+    const int my_tiles = t0 + warp < t1 ? (t1 - t0 - warp + nw - 1) / nw : 0;
+    const int units = my_tiles * G;
+    __half* sxh = reinterpret_cast<__half*>(smem_raw);
+    __half* sxl = sxh + (size_t)NC * ldx;
+
+    // ---- before the previous kernel finishes: this warp's first weights ----
+    uint2 wa[HPF], wb[HPF];
+    __half ws_a[HPF], ws_b[HPF];
+    auto load_unit = [&](int slot, int u) {
+        const int k = u / G, gr = u - k * G;
+        const int tile = t0 + warp + k * nw;
+        const int ra = min(tile * TILE + g, w.rows - 1), rb = min(tile * TILE + g + 8, w.rows - 1);
+        const uint8_t* qa = w.q + (size_t)ra * w.qstride + (size_t)gr * GB;
+        const uint8_t* qb = w.q + (size_t)rb * w.qstride + (size_t)gr * GB;
+        if constexpr (ATOM == ATOM_Q8) {
+            wa[slot] = __ldg(reinterpret_cast<const uint2*>(qa + 8 * t));
+            wb[slot] = __ldg(reinterpret_cast<const uint2*>(qb + 8 * t));
+        } else {
+            wa[slot] = make_uint2(__ldg(reinterpret_cast<const uint32_t*>(qa + 4 * t)), 0u);
+            wb[slot] = make_uint2(__ldg(reinterpret_cast<const uint32_t*>(qb + 4 * t)), 0u);
+        }
+        ws_a[slot] = __ldg(w.s + (size_t)ra * w.sstride + gr);
+        ws_b[slot] = __ldg(w.s + (size_t)rb * w.sstride + gr);
+    };
+#pragma unroll
+    for (int s = 0; s < HPF; ++s)
+        if (s < units) load_unit(s, s);
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&xbar, 1);
+        tc::fence_mbar_init();
+    }
+    __syncthreads();
+    tc::pdl_wait();
+    // ---- the activations of tokens 0..M-1, rows dense at stride ldx ----
+    if (threadIdx.x == 0) {
+        const uint32_t bytes = (uint32_t)M * (uint32_t)ldx * 2u;
+        tc::mbar_arrive_expect_tx(&xbar, 2u * bytes);
+        tc::bulk_load_1d(sxh, xhi, bytes, &xbar);
+        tc::bulk_load_1d(sxl, xlo, bytes, &xbar);
+    }
+    wait_staged(&xbar, err);
+
+    // ---- units: 4 MMAs per group and 8 tokens into two accumulator sets (x_hi, x_lo) ----
+    constexpr bool TWO = NB <= 4;
+    float acc[NB][4];
+    for (int base = 0; base < units; base += HPF) {
+#pragma unroll
+        for (int s = 0; s < HPF; ++s) {
+            const int u = base + s;
+            if (u < units) {
+                const int k = u / G, gr = u - k * G;
+                if (gr == 0) {
+#pragma unroll
+                    for (int j = 0; j < NB; ++j)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) acc[j][q] = 0.f;
+                }
+                uint32_t aq[2][4];
+                dequant_q<ATOM>(wa[s], wb[s], aq);
+                const float sa = __half2float(ws_a[s]), sb = __half2float(ws_b[s]);
+                if (u + HPF < units) load_unit(s, u + HPF);  // slot s holds the units = s mod HPF
+                const int kofs = gr * 32;
+#pragma unroll
+                for (int j = 0; j < NB; ++j) {
+                    const uint4 xh = load_x<ATOM>(sxh + (size_t)(8 * j + g) * ldx + kofs, t);
+                    const uint4 xl = load_x<ATOM>(sxl + (size_t)(8 * j + g) * ldx + kofs, t);
+                    float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(th, aq[0], xh.x, xh.y);
+                    mma16816(TWO ? tl : th, aq[0], xl.x, xl.y);
+                    mma16816(th, aq[1], xh.z, xh.w);
+                    mma16816(TWO ? tl : th, aq[1], xl.z, xl.w);
+                    acc[j][0] = fmaf(sa, TWO ? th[0] + tl[0] : th[0], acc[j][0]);
+                    acc[j][1] = fmaf(sa, TWO ? th[1] + tl[1] : th[1], acc[j][1]);
+                    acc[j][2] = fmaf(sb, TWO ? th[2] + tl[2] : th[2], acc[j][2]);
+                    acc[j][3] = fmaf(sb, TWO ? th[3] + tl[3] : th[3], acc[j][3]);
+                }
+                if (gr == G - 1) {
+                    // C fragment: {row g, tokens 2t, 2t+1}, {row g+8, tokens 2t, 2t+1} of each n8 block
+                    const int tile = t0 + warp + k * nw;
+                    const int na = tile * TILE + g, nb = na + 8;
+#pragma unroll
+                    for (int j = 0; j < NB; ++j) {
+                        const int m0 = 8 * j + 2 * t, m1 = m0 + 1;
+                        if (na < w.rows) {
+                            if (m0 < M) out[(size_t)m0 * ldo + na] = acc[j][0];
+                            if (m1 < M) out[(size_t)m1 * ldo + na] = acc[j][1];
+                        }
+                        if (nb < w.rows) {
+                            if (m0 < M) out[(size_t)m0 * ldo + nb] = acc[j][2];
+                            if (m1 < M) out[(size_t)m1 * ldo + nb] = acc[j][3];
+                        }
+                    }
+                }
+            }
+        }
+    }
+}
+
 // The launch traced when GPT2Q_MMA_TRACE=<rows>x<cols>x<M>[x<skip>] is set: the first one of that
 // shape after `skip` others.
 constexpr size_t MMA_TRACE_CTAS = 4096;
@@ -751,6 +876,66 @@ bool mma_usable(const QW& w, int M) {
     // matrices of many row tiles (the tied head) stay on the tcgen05 GEMM
     return M >= 1 && M <= MMA_MAX_M && (w.atom == ATOM_Q8 || w.atom == ATOM_Q4) && w.cols % 32 == 0 &&
            w.rows >= 1 && (w.rows + TILE - 1) / TILE <= MMA_MAX_TILES;
+}
+
+bool head_mma_usable(const QW& w, int M, int ldx) {
+    const size_t staged = (size_t)((M + 7) / 8) * 8 * (size_t)ldx * 4;  // hi and lo rows of NB * 8 tokens
+    return M >= 1 && M <= MMA_MAX_M && (w.atom == ATOM_Q8 || w.atom == ATOM_Q4) && w.cols % 32 == 0 &&
+           w.rows >= 1 && ldx % 8 == 0 && ldx >= w.cols && staged <= (size_t)MMA_MAX_SMEM;
+}
+
+namespace {
+template <int ATOM, int NB>
+cudaError_t launch_head_nb(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, float* out, int ldo,
+                           int* err, cudaStream_t st) {
+    auto kern = k_head_mma<ATOM, NB>;
+    static unsigned long long raised = 0;  // dynamic shared-memory limit raised once per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(raised & bit)) {
+        const cudaError_t ae = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_MAX_SMEM);
+        if (ae != cudaSuccess) return ae;
+        raised |= bit;
+    }
+    const int tiles = (w.rows + TILE - 1) / TILE;
+    const int tpc = (tiles + num_sms() - 1) / num_sms();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((tiles + tpc - 1) / tpc);
+    cfg.blockDim = dim3(32 * MMA_MAX_WARPS);
+    cfg.dynamicSmemBytes = (size_t)NB * 8 * ldx * 4;
+    cfg.stream = st;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, w, xhi, xlo, ldx, M, tpc, out, ldo, err);
+}
+
+template <int ATOM>
+cudaError_t launch_head_atom(int NB, const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, float* out,
+                             int ldo, int* err, cudaStream_t st) {
+    switch (NB) {
+        case 1: return launch_head_nb<ATOM, 1>(w, xhi, xlo, ldx, M, out, ldo, err, st);
+        case 2: return launch_head_nb<ATOM, 2>(w, xhi, xlo, ldx, M, out, ldo, err, st);
+        case 3: return launch_head_nb<ATOM, 3>(w, xhi, xlo, ldx, M, out, ldo, err, st);
+        case 4: return launch_head_nb<ATOM, 4>(w, xhi, xlo, ldx, M, out, ldo, err, st);
+        case 5: return launch_head_nb<ATOM, 5>(w, xhi, xlo, ldx, M, out, ldo, err, st);
+        case 6: return launch_head_nb<ATOM, 6>(w, xhi, xlo, ldx, M, out, ldo, err, st);
+        case 7: return launch_head_nb<ATOM, 7>(w, xhi, xlo, ldx, M, out, ldo, err, st);
+        default: return launch_head_nb<ATOM, 8>(w, xhi, xlo, ldx, M, out, ldo, err, st);
+    }
+}
+}  // namespace
+
+cudaError_t launch_head_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, float* out, int ldo,
+                            int* err, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    if (!head_mma_usable(w, M, ldx) || !xhi || !xlo || !out || !err || ldo < w.rows) return cudaErrorInvalidValue;
+    const int NB = (M + 7) / 8;
+    if (w.atom == ATOM_Q8) return launch_head_atom<ATOM_Q8>(NB, w, xhi, xlo, ldx, M, out, ldo, err, st);
+    return launch_head_atom<ATOM_Q4>(NB, w, xhi, xlo, ldx, M, out, ldo, err, st);
 }
 
 std::atomic<int> g_tiles_max{0};

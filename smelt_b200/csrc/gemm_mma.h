@@ -39,6 +39,13 @@ struct LnFold {
 // epilogue completes the LayerNorm (see LnFold).
 cudaError_t launch_linear_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, int* err,
                               const Epi& e, cudaStream_t st, const LnFold* ln = nullptr);
+// The tied lm head on the warp-level tensor cores for 1..MMA_MAX_M tokens (k_head_mma): one CTA
+// per SM stages x = x_hi + x_lo (fp16 [M][ldx], ldx % 8 == 0) once and its warps run whole 16-row
+// tiles of W over the full K; out[m][n] for n < w.rows (row stride ldo >= w.rows). `usable` when
+// the atom is int8 / int4 and the staged rows fit in shared memory.
+bool head_mma_usable(const QW& w, int M, int ldx);
+cudaError_t launch_head_mma(const QW& w, const __half* xhi, const __half* xlo, int ldx, int M, float* out, int ldo,
+                            int* err, cudaStream_t st);
 // Largest number of 16-row tiles per CTA among the launches since the last mma_init (one count
 // for the process).
 int mma_tiles_per_cta_max();

@@ -187,6 +187,10 @@ struct gpt2q_handle {
     // than its minimum of 16 rows): pieces of the ln_f output [d/32][3][64][32] and their scales
     // [64][d/32]. GPT2Q_HEAD_I8 at creation: 0 = never, 2 = for every 1..64 rows (tests)
     int head_i8 = 1;
+    // the tied head on the warp-level tensor cores (k_head_mma), ahead of the i8 head: 0 = never,
+    // 1 = where the tcgen05 head does not run (fewer than 16 rows), 2 = for every 1..64 rows
+    // (tests). GPT2Q_HEAD_MMA at creation; off under GPT2Q_MMA_DISABLE=1 and GPT2Q_HEAD_I8=2
+    int head_mma = 1;
     int8_t* head_pieces = nullptr;
     float* head_xscale = nullptr;
     MkPlan mk;      // persistent single-sequence decode
@@ -591,12 +595,19 @@ int block(gpt2q_handle* H, int layer, int M, const int* slot, const int* pos, At
 }
 
 // The tied head over rows 0..M-1 of h into out (row stride vocab). Below the tcgen05 head's 16
-// rows it runs on kind::i8 over exact int8 pieces of h (int8 head weights), instead of the
-// CUDA-core GEMV: measured at 2 and 8 rows, 124 and 223 us -> 35 us per head. From 16 rows the
-// f16 hi/lo tile is faster (28.5 us at 32 rows against 36 us): each of the i8 path's 24 groups
-// per tile needs its own TMEM drain and scaling in the epilogue.
+// rows it runs on the warp-level tensor cores (k_head_mma; 8 rows: 22 us), else on kind::i8 over
+// exact int8 pieces of h (int8 head weights), instead of the CUDA-core GEMV: measured at 2 and 8
+// rows, 124 and 223 us -> 35 us per head. From 16 rows the f16 hi/lo tile is faster (28.5 us at
+// 32 rows against 36 us for either): each of the i8 path's 24 groups per tile needs its own TMEM
+// drain and scaling in the epilogue.
 int head(gpt2q_handle* H, int M, float* out) {
     const int d = H->cfg.n_embd, V = H->cfg.vocab;
+    const bool mma = H->head_mma == 2 || (H->head_mma == 1 && !H->gemm.usable(H->wte.w, M));
+    if (mma && H->mma_on && H->head_i8 != 2 && H->h_hi && head_mma_usable(H->wte.w, M, d)) {
+        RUN("linear_head", linear_bytes(H->wte, M, 1),
+            launch_head_mma(H->wte.w, H->h_hi, H->h_lo, d, M, out, V, H->kerr, H->stream));
+        return GPT2Q_OK;
+    }
     const bool want = H->head_i8 == 2 || (H->head_i8 == 1 && !H->gemm.usable(H->wte.w, M));
     if (want && H->head_pieces && head_i8_usable(H->gemm, H->wte.w, M)) {
         const int MP = M <= 32 ? 32 : 64;
@@ -1179,6 +1190,7 @@ int create_common(const gpt2q_config* cfg, const gpt2q_tensor_desc* tensors, int
     if (H->mma_on) mma_init();
     if (const char* e = std::getenv("GPT2Q_LN_FUSE")) H->ln_fuse = e[0] != '0';
     if (const char* e = std::getenv("GPT2Q_HEAD_I8")) H->head_i8 = std::atoi(e);
+    if (const char* e = std::getenv("GPT2Q_HEAD_MMA")) H->head_mma = std::max(0, std::min(2, std::atoi(e)));
     if (d % 32 == 0) {
         const size_t pb = (size_t)(d / 32) * 3 * 64 * 32, sb = (size_t)64 * (d / 32) * 4;
         H->head_pieces = H->dalloc<int8_t>(pb);

@@ -30,6 +30,7 @@ def _built():
 
 def _run(pk, prompts, steps, monkeypatch, i8):
     monkeypatch.setenv("GPT2Q_HEAD_I8", "2" if i8 else "0")  # 2: every batch size, 0: never
+    monkeypatch.setenv("GPT2Q_HEAD_MMA", "0")  # the comparison is with the f16 tensor-core head
     with Gpu(pk, max_seqs=len(prompts)) as g:
         nxt, lg0 = g.prefill(prompts, want_logits=True)
         toks = g.decode_steps(steps, len(prompts))
