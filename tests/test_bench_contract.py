@@ -12,7 +12,8 @@ import pytest
 ROOT = os.path.join(os.path.dirname(__file__), "..")
 
 
-@pytest.mark.parametrize("config,unit", [("small-int8-b1", "tokens/s"), ("small-int8-trunk-bwd", "positions/s")])
+@pytest.mark.parametrize("config,unit", [("small-int8-b1", "tokens/s"), ("small-int8-trunk-bwd", "positions/s"),
+                                         ("medium-int8-prefill", "tokens/s")])
 def test_reference_arm_json_line(config, unit):
     out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", config, "--steps", "1",
                           "--warmup", "1"], cwd=ROOT, capture_output=True, text=True, timeout=900)
